@@ -1,0 +1,376 @@
+"""Benchmark of the compressed-integer linear path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--bits 8|6]
+
+Workload: one hybrid layer's full linear set at batch-1
+decode, hidden 5120 -- attention q/k/v/o, Gated-DeltaNet in_proj_qkv/in_proj_z/
+out_proj, MLP gate/up/down -- on synthetic 27B-shape compressed weights (random
+code words, seeded N(0,1) value table, row scales ~0.02; bits=8 is the format's
+4-bit width, bits=6 the lowest). One step = the six operator calls of the layer
+(q/k/v, o, qkv/z, out, gate/up, down; matrices sharing an input go in one call):
+quantise x -> exact int64 weighted sums -> restore + output H512, captured in one
+CUDA graph. The metric is HBM throughput of the compressed weights:
+algorithmic bytes per step / step time. Codes per step (243.8 MB at bits=8) exceed
+the 126 MB L2, so no L2 flush is needed between steps.
+
+`--impl reference` times the CPU path instead: the C restatement (oracle/) of the
+reference's CPU engine (crates/yskn-engine kernel + pool, crates/yskn-ref quantiser
+and restore), on all host threads, rank 0 only.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "yasakani-for-mac_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+import numpy as np  # noqa: E402
+
+# (name, rows, cols); the reference model's shapes, docs/spec/01_MODEL_ARCHITECTURE.md:101-131
+LAYER = [("q_proj", 12288, 5120), ("k_proj", 1024, 5120), ("v_proj", 1024, 5120), ("o_proj", 5120, 6144),
+         ("in_proj_qkv", 10240, 5120), ("in_proj_z", 6144, 5120), ("out_proj", 5120, 6144),
+         ("gate_proj", 17408, 5120), ("up_proj", 17408, 5120), ("down_proj", 5120, 17408)]
+CALLS = [["q_proj", "k_proj", "v_proj"], ["o_proj"], ["in_proj_qkv", "in_proj_z"], ["out_proj"],
+         ["gate_proj", "up_proj"], ["down_proj"]]
+METRIC = "compressed GEMV HBM TB/s (one hybrid layer's linear set, batch-1 decode)"
+UNIT = "TB/s"
+
+
+def make_weights(bits, seed0=1000):
+    import fixtures
+    import oracle as O
+    out = {}
+    for i, (name, rows, cols) in enumerate(LAYER):
+        words, lut16, sc16 = fixtures.model_matrix(rows, cols, bits, seed0 + 17 * i)
+        out[name] = dict(rows=rows, cols=cols, words=words, lut16=lut16, sc16=sc16,
+                         s_in=O.signs("mulberry32_7919_13", 7, 0, cols),
+                         s_out=O.signs("mulberry32_7919_13", 7, cols, rows))
+    return out
+
+
+def make_inputs(M):
+    import fixtures
+    return [fixtures.normal(500 + j, M * LAYER_COLS[c[0]]).reshape(M, LAYER_COLS[c[0]]) for j, c in enumerate(CALLS)]
+
+
+LAYER_COLS = {n: c for n, _, c in LAYER}
+LAYER_ROWS = {n: r for n, r, _ in LAYER}
+
+
+def algorithmic_bytes(bits, M):
+    """Minimum bytes one step must move: codes + int8 table + f32 row scales + signs
+    (in and out) per matrix, f32 input per call, f32 output per matrix."""
+    total = 0
+    for name, rows, cols in LAYER:
+        total += rows * cols * bits // 16 + 8192 + 4 * rows + rows + 4 * M * rows
+    for c in CALLS:
+        total += 4 * M * LAYER_COLS[c[0]] + LAYER_COLS[c[0]]
+    return total
+
+
+def gemv_bytes(name, bits, M):
+    """Algorithmic bytes of one weighted-sums launch: codes + int8 table + int8
+    activations + int32 group scales + int64 sums."""
+    rows, cols = LAYER_ROWS[name], LAYER_COLS[name]
+    return rows * cols * bits // 16 + 8192 + M * cols + 4 * M * (cols // 512) + 8 * M * rows
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.proc, self.lines = index, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.index)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=lambda: self.lines.extend(iter(self.proc.stdout.readline, "")))
+            self.thread.daemon = True
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clocks not sampled"]}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_layer_step(W, xs, fraction=1.0, threads=None):
+    """The CPU path for one step (the reference's CPU engine restated in C):
+    quantise, threaded weighted sums (first `fraction` of each matrix's rows), restore."""
+    import oracle as O
+    nbytes = 0
+    for c, x in zip(CALLS, xs):
+        act, _, A, rq = O.quantize_activation(x, W[c[0]]["s_in"])
+        for name in c:
+            w = W[name]
+            rows = max(32, int(w["rows"] * fraction) // 32 * 32)
+            ws = O.fast_weighted_sums(w["words"], "warp", w["rows"], w["cols"], w["bits"], w["lut8"], act, A,
+                                      rows=rows, threads=threads)
+            if rows == w["rows"]:
+                O.restore(ws, rq, w["tau"], w["s_out"])
+            nbytes += rows * w["cols"] * w["bits"] // 16
+    return nbytes
+
+
+def prepare_cpu(W, bits):
+    import oracle as O
+    for w in W.values():
+        w["lut8"], w["tau"] = O.quantize_weight_table(w["lut16"], w["sc16"])
+        w["bits"] = bits
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    W = make_weights(args.bits)
+    prepare_cpu(W, args.bits)
+    xs = make_inputs(1)
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    cpu_layer_step(W, xs, 1.0, threads)
+    t_full = time.perf_counter() - t0
+    budget = 90.0
+    fraction = min(1.0, budget / max(1e-9, (args.steps + args.warmup) * t_full))
+    for _ in range(args.warmup):
+        cpu_layer_step(W, xs, fraction, threads)
+    t0 = time.perf_counter()
+    nbytes = 0
+    for _ in range(args.steps):
+        nbytes += cpu_layer_step(W, xs, fraction, threads)
+    dt = time.perf_counter() - t0
+    value = nbytes / dt / 1e12
+    sample = ("each step: all 10 matrices of the layer set, first %.1f%% of rows (codes %.1f MB), quantise + "
+              "threaded int64 sums%s" % (100 * fraction, nbytes / args.steps / 1e6,
+                                         " + restore" if fraction >= 1.0 else ""))
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "i8", "data": "synthetic",
+            "config": config(args),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def config(args):
+    return {"workload": "one hybrid layer's full linear set (q,k,v,o; GDN in_proj_qkv,in_proj_z,out_proj; "
+                        "gate,up,down), batch-1 decode, hidden 5120",
+            "bits": args.bits, "bits_per_weight": args.bits / 2, "M": 1,
+            "codes_mb_per_step": sum(r * c * args.bits // 16 for _, r, c in LAYER) / 1e6,
+            "l2": "inputs larger than L2: every step streams all codes (>126 MB); no flush",
+            "parallelism": "replicas" if args.gpus > 1 else "single"}
+
+
+def run_b200(args, rank, world, local_rank):
+    import torch
+    import yskn_b200 as Y
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    W = make_weights(args.bits, 1000 + 101 * rank)
+    mats, keep = {}, []
+    for name, w in W.items():
+        dw = torch.from_numpy(w["words"].view(np.int32)).to(dev)
+        mats[name] = Y.Matrix(dw, "warp", w["rows"], w["rows"], w["cols"], args.bits, w["lut16"], w["sc16"],
+                              w["s_in"], w["s_out"])
+        del dw
+    M = 1
+    xs_host = make_inputs(M)
+    xs = [torch.from_numpy(x).to(dev) for x in xs_host]
+    group = [[mats[n] for n in c] for c in CALLS]
+    works = [torch.empty(Y.linear_work_bytes(g, M), dtype=torch.uint8, device=dev) for g in group]
+    ys = [[torch.empty((M, LAYER_ROWS[n]), dtype=torch.float32, device=dev) for n in c] for c in CALLS]
+    stream = torch.cuda.Stream(dev)
+
+    def step():
+        for g, x, wk, y in zip(group, xs, works, ys):
+            Y.linear(g, x, wk, y, stream=stream)
+
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize()
+    Y.check(Y.status(stream), "status")
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            graph.replay()
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    ids = [v.strip() for v in visible.split(",") if v.strip()]
+    sampler = ClockSampler(ids[local_rank] if local_rank < len(ids) else str(local_rank))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with sampler:
+        barrier()
+        e0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(args.steps):
+                graph.replay()
+        e1.record(stream)
+        barrier()
+        ms = e0.elapsed_time(e1)
+        # Dominant kernel: time the weighted-sums launches alone, same matrices, same order.
+        acts = [torch.empty((M, x.shape[1]), dtype=torch.int8, device=dev) for x in xs]
+        scs = [torch.empty((M, x.shape[1] // 512), dtype=torch.int32, device=dev) for x in xs]
+        wss = [[torch.empty((M, LAYER_ROWS[n]), dtype=torch.int64, device=dev) for n in c] for c in CALLS]
+        for g, x, a, s in zip(group, xs, acts, scs):
+            al = torch.empty((M, x.shape[1] // 512), dtype=torch.float32, device=dev)
+            rq = torch.empty(M, dtype=torch.float32, device=dev)
+            Y.quantize(x, g[0].signs_in_ptr, a, al, s, rq, stream=stream)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in CALLS]
+        reps = max(20, min(200, args.steps))
+        gemv_ms = [0.0] * len(CALLS)
+        with torch.cuda.stream(stream):
+            for r in range(reps + 3):
+                for j, (g, a, s, o) in enumerate(zip(group, acts, scs, wss)):
+                    if r >= 3:
+                        ev[j][0].record(stream)
+                    Y.weighted_sums(g, a, s, o, stream=stream)
+                    if r >= 3:
+                        ev[j][1].record(stream)
+                stream.synchronize()
+                if r >= 3:
+                    for j in range(len(CALLS)):
+                        gemv_ms[j] += ev[j][0].elapsed_time(ev[j][1]) / reps
+        # End to end through the public API: pinned host input in, host output back, every step.
+        xh = [torch.from_numpy(x).pin_memory() for x in xs_host]
+        yh = [[torch.empty((M, LAYER_ROWS[n]), dtype=torch.float32).pin_memory() for n in c] for c in CALLS]
+        e2e_steps = max(10, min(args.steps, 500))
+        barrier()
+        t0 = time.perf_counter()
+        e2 = torch.cuda.Event(enable_timing=True)
+        e3 = torch.cuda.Event(enable_timing=True)
+        e2.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(e2e_steps):
+                for g, x, xd, wk, y, yhh in zip(group, xh, xs, works, ys, yh):
+                    xd.copy_(x, non_blocking=True)
+                    Y.linear(g, xd, wk, y, stream=stream)
+                    for a, b in zip(yhh, y):
+                        a.copy_(b, non_blocking=True)
+        e3.record(stream)
+        barrier()
+        e2e_ms = e2.elapsed_time(e3)
+    Y.check(Y.status(stream), "status")
+    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms, e2e_ms = t.tolist()
+    if rank != 0:
+        return
+    step_bytes = algorithmic_bytes(args.bits, M)
+    value = world * step_bytes * args.steps / (ms * 1e-3) / 1e12
+    e2e_value = world * step_bytes * e2e_steps / (e2e_ms * 1e-3) / 1e12
+    with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) \
+            else open(os.devnull) as f:
+        try:
+            peaks = json.load(f)
+        except ValueError:
+            peaks = {}
+    peak = peaks.get("hbm_gbs", 6650.0)
+    gemv_total_bytes = sum(gemv_bytes(n, args.bits, M) for c in CALLS for n in c)
+    achieved = gemv_total_bytes / (sum(gemv_ms) * 1e-3) / 1e9
+    h2d = sum(4 * M * LAYER_COLS[c[0]] for c in CALLS)
+    d2h = sum(4 * M * LAYER_ROWS[n] for c in CALLS for n in c)
+    # CPU baseline (rank 0, N=1 only): the oracle port on a bounded sample.
+    cpu = None
+    if world == 1 and not args.skip_cpu:
+        prepare_cpu(W, args.bits)
+        threads = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        n = 0
+        nbytes = 0
+        while time.perf_counter() - t0 < 10.0 or n < 2:
+            nbytes += cpu_layer_step(W, xs_host, 1.0, threads)
+            n += 1
+        dt = time.perf_counter() - t0
+        cpu = {"value": nbytes / dt / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": "%d full layer-set steps (quantise + threaded int64 sums + restore), %.1f s" % (n, dt)}
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "i8", "data": "synthetic", "config": config(args),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "kernel": "gemv_kernel (weighted sums, 6 launches per step incl. output zeroing)",
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": args.steps * sum(2 + len(c) for c in CALLS),
+            "clocks": sampler.summary(),
+            "step_bytes": step_bytes, "gemv_us_per_call": [round(1e3 * x, 2) for x in gemv_ms]}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--bits", type=int, default=8, choices=[6, 8])
+    ap.add_argument("--skip-cpu", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import datetime
+        import torch
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local_rank))
+    try:
+        run_b200(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,146 @@
+/*
+ * yskn_b200.h -- C ABI of the B200 (sm_100a) compressed-integer linear path.
+ *
+ * Drop-in surface for the reference's compressed linear operator (YASAKANI
+ * `.yskn` weights: trellis-coded 3/4-bit codes, a 4096-pair value table and one
+ * scale per row, Hadamard-512 rotations; int8 activations; exact int64 sums).
+ *
+ * Conventions (as the reference's include/yskn_abi.h and src/c_api.cpp:11-14):
+ *   - every call returns int: 0 on success, a negative YSKN_E* code on failure;
+ *     yskn_b200_last_error() gives a thread-local message for the last failure;
+ *   - device pointers are caller-owned; work is ordered on the caller's CUDA
+ *     stream (`void* stream`, NULL = legacy default stream) with no hidden
+ *     synchronisation, except in the *_host helpers and yskn_b200_status();
+ *   - the hot calls (weighted_sums, quantize, restore, linear) allocate nothing;
+ *     matrix handles own their device copies, created once at load time;
+ *   - one call at a time per matrix handle and stream (crates/yskn-engine/src/pool.rs:29).
+ * Plain C types only: a Rust `Backend::Cuda`, Go cgo or Python ctypes binds it directly.
+ */
+#ifndef YSKN_B200_H
+#define YSKN_B200_H
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(_WIN32)
+#define YSKN_B200_API __declspec(dllexport)
+#else
+#define YSKN_B200_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define YSKN_OK 0
+#define YSKN_EINVAL (-1)      /* bad shape, pointer or argument (reference: -1)            */
+#define YSKN_ECUDA (-2)       /* a CUDA runtime error                                      */
+#define YSKN_EOVERFLOW (-3)   /* integer accumulation exceeds i64 (compressed_linear.rs:245) */
+#define YSKN_ENONFINITE (-4)  /* a non-finite activation / restored value (compressed_linear.rs:82,100,342) */
+#define YSKN_ETIMEDOUT (-5)   /* a bounded device wait gave up                             */
+#define YSKN_ENOMEM (-6)      /* device allocation failed (create-time only)               */
+
+#define YSKN_LAYOUT_ROW 0     /* docs/FORMAT.md:141-151 */
+#define YSKN_LAYOUT_WARP 1
+
+#define YSKN_SIGNS_SPLITMIX64 0 /* docs/FORMAT.md:159-180 */
+#define YSKN_SIGNS_MULBERRY32 1
+
+typedef struct yskn_b200_matrix yskn_b200_matrix;
+
+/* Thread-local message of the last failure (src/c_api.cpp:11-14 `yskn_last_error`). */
+YSKN_B200_API const char* yskn_b200_last_error(void);
+
+/* Synchronise `stream`, then read and clear the device-side error word that kernels
+ * raise for conditions only the device sees (non-finite activations, i64 overflow,
+ * timed-out waits). Returns 0 or the first YSKN_E* code raised since the last call. */
+YSKN_B200_API int yskn_b200_status(void* stream);
+
+/* Replaces include/yskn_abi.h:19 / src/repack.cu:21-26: identical permutation of
+ * warp-layout code words into the reference's "frag" order; -1 unless rows%64==0
+ * and wps%4==0; asynchronous on `cuda_stream`. */
+YSKN_B200_API int yskn_repack_warp_to_frag(const uint32_t* d_words, uint32_t* d_frag, int rows, int seqs, int wps,
+                                           void* cuda_stream);
+/* Replaces include/yskn_abi.h:20 / src/repack.cu:27-32: host buffers in and out. */
+YSKN_B200_API int yskn_repack_warp_to_frag_host(const uint32_t* h_words, uint32_t* h_frag, int rows, int seqs,
+                                                int wps);
+
+/* Host helper: n signs (+1/-1) at positions offset.. of the stream `rule`/`seed`
+ * defines. Replaces src/signs.hpp:9-31 (crates/yskn-format/src/signs.rs:12-38). */
+YSKN_B200_API int yskn_b200_signs(int rule, uint64_t seed, uint64_t offset, int64_t n, int8_t* h_out);
+
+/* Bytes of the B200 streaming layout for a matrix (warp order, rows padded to 32). */
+YSKN_B200_API int64_t yskn_b200_pack_bytes(int physical_rows, int cols, int bits);
+
+/* Layout transform of one matrix's code words (row or warp layout, device memory)
+ * into the B200 streaming layout (d_out, yskn_b200_pack_bytes() bytes). Replaces the
+ * load-time reorder src/repack.cu + src/lnord.cu:58-88 (lnord_build). */
+YSKN_B200_API int yskn_b200_pack(const uint32_t* d_words, int layout, int physical_rows, int cols, int bits,
+                                 void* d_out, void* stream);
+
+/* Load one compressed matrix (replaces src/loader.cpp:19-60 Model::upload_linear +
+ * lnord_build; the Rust side is crates/yskn-engine/src/mapped.rs:78-186):
+ *   d_codes       the tensor's code stream as stored (`layout`), in device memory;
+ *   lut16_host    8192 binary16 table values; scale16_host: physical_rows binary16 scales;
+ *   signs_in_host cols signs; signs_out_host physical_rows signs or NULL (no output rotation).
+ * Builds the int8 table and effective row scales (compressed_linear.rs:138-158) and
+ * packs the codes. Synchronous (load time). NULL on failure (see last_error). */
+YSKN_B200_API yskn_b200_matrix* yskn_b200_matrix_create(const uint32_t* d_codes, int layout, int rows,
+                                                        int physical_rows, int cols, int bits,
+                                                        const uint16_t* lut16_host, const uint16_t* scale16_host,
+                                                        const int8_t* signs_in_host, const int8_t* signs_out_host);
+YSKN_B200_API void yskn_b200_matrix_destroy(yskn_b200_matrix* m);
+/* rows, physical_rows, cols, bits, has_output_rotation, packed bytes. */
+YSKN_B200_API int yskn_b200_matrix_info(const yskn_b200_matrix* m, int64_t* out6);
+/* Device copies owned by the handle: int8 table (8192 B), effective row scales
+ * (f32[physical_rows]), input signs (i8[cols]), output signs (i8[physical_rows] or NULL). */
+YSKN_B200_API const int8_t* yskn_b200_matrix_lut8(const yskn_b200_matrix* m);
+YSKN_B200_API const float* yskn_b200_matrix_tau(const yskn_b200_matrix* m);
+YSKN_B200_API const int8_t* yskn_b200_matrix_signs_in(const yskn_b200_matrix* m);
+YSKN_B200_API const int8_t* yskn_b200_matrix_signs_out(const yskn_b200_matrix* m);
+
+/* Exact weighted integer sums (the operator core). Replaces
+ * crates/yskn-engine/src/model.rs:948-962 `Compute::weighted_sums` (bit-identical to
+ * crates/yskn-ref/src/compressed_linear.rs:205-252) and the reference's launch_lnord /
+ * launch_pfa / launch_q35_g6 / launch_gemv / launch_gemm (src/kernels.hpp:52-63).
+ *   mats     n_mats (1..3) matrices sharing one input of `cols` columns;
+ *   d_act    int8 [M][cols] row-major; d_scales int32 [M][cols/512];
+ *   d_out[i] int64 [M][physical_rows_i] row-major (overwritten).
+ * Any M >= 1. Returns YSKN_EOVERFLOW (synchronously detected) only for cols >= 262144. */
+YSKN_B200_API int yskn_b200_weighted_sums(const yskn_b200_matrix* const* mats, int n_mats, const int8_t* d_act,
+                                          const int32_t* d_scales, int M, int64_t* const* d_out, void* stream);
+/* The first n_rows rows only: d_out int64 [M][n_rows] (crates/yskn-engine/src/pool.rs:227-244). */
+YSKN_B200_API int yskn_b200_weighted_sums_prefix(const yskn_b200_matrix* mat, const int8_t* d_act,
+                                                 const int32_t* d_scales, int M, int n_rows, int64_t* d_out,
+                                                 void* stream);
+
+/* Activation quantiser (replaces src/a8_prologue.cuh:64-81,122-133 and the fused
+ * prologues of src/q35_kernels.cu:1402-1474; crates/yskn-ref/src/compressed_linear.rs:57-135):
+ * x f32 [M][Kc] -> act int8 [M][Kc], alpha f32 [M][Kc/512], scales int32 [M][Kc/512],
+ * row_quantum f32 [M]. Bit-exact. Non-finite inputs raise YSKN_ENONFINITE in the
+ * device error word (read with yskn_b200_status). */
+YSKN_B200_API int yskn_b200_quantize(const float* d_x, const int8_t* d_signs, int M, int Kc, int8_t* d_act,
+                                     float* d_alpha, int32_t* d_scales, float* d_row_quantum, void* stream);
+
+/* Restore + output rotation (replaces src/a8_prologue.cuh:10-15 xsum_combine and the
+ * restore part of src/q35_kernels.cu:1402-1474; compressed_linear.rs:288-370):
+ * y[m][r] = f32(ws)*row_quantum[m] (*inv_rms[m]) *tau[r]; then, if rotate_out, per
+ * 512-row block H512, *0.0441941738, *s_out. d_inv_rms may be NULL. d_y f32 [M][n_rows].
+ * If clear_ws != 0 the consumed int64 accumulators are zeroed (the reference clears
+ * its shared accumulator when it consumes it). */
+YSKN_B200_API int yskn_b200_restore(int64_t* d_ws, const float* d_row_quantum, const float* d_inv_rms,
+                                    const yskn_b200_matrix* mat, int M, int rotate_out, int n_rows, int clear_ws,
+                                    float* d_y, void* stream);
+
+/* Whole operator for up to 3 matrices sharing one input: quantise x with the first
+ * matrix's input signs, weighted sums, restore (with each matrix's output rotation
+ * if it has one). Replaces CompressedLinear::project (compressed_linear.rs:254-285)
+ * and Engine35::gemv + its post step (src/engine35.cpp:403-430).
+ * d_work: caller scratch of yskn_b200_linear_work_bytes(mats, n_mats, M) bytes. */
+YSKN_B200_API int64_t yskn_b200_linear_work_bytes(const yskn_b200_matrix* const* mats, int n_mats, int M);
+YSKN_B200_API int yskn_b200_linear(const yskn_b200_matrix* const* mats, int n_mats, const float* d_x, int M,
+                                   const float* d_inv_rms, void* d_work, float* const* d_y, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* YSKN_B200_H */

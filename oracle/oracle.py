@@ -1,0 +1,186 @@
+"""TEST INFRASTRUCTURE ONLY: ctypes front end of the C oracle (oracle/yskn_oracle.c).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import this
+module, as the checker. Each function names the reference code it restates.
+"""
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "build", "libyskn_oracle.so")
+RULES = {"splitmix64": 0, "mulberry32_7919_13": 1}
+LAYOUTS = {"row": 0, "warp": 1}
+_lib = None
+
+
+def build():
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        src = os.path.join(HERE, "yskn_oracle.c")
+        if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(src):
+            build()
+        _lib = C.CDLL(LIB_PATH)
+        _lib.orc_f16_to_f32.restype = C.c_float
+        _lib.orc_f16_to_f32.argtypes = [C.c_uint16]
+        _lib.orc_f32_to_f16.restype = C.c_uint16
+        _lib.orc_f32_to_f16.argtypes = [C.c_float]
+        _lib.orc_f32_to_bf16.restype = C.c_uint16
+        _lib.orc_f32_to_bf16.argtypes = [C.c_float]
+        _lib.orc_state.restype = C.c_uint16
+        _lib.orc_state.argtypes = [C.c_void_p, C.c_int, C.c_int64, C.c_int64, C.c_int, C.c_int64, C.c_int64, C.c_int]
+        _lib.orc_hadamard512.argtypes = [C.c_void_p]
+    return _lib
+
+
+def _p(a):
+    return C.c_void_p(a.ctypes.data)
+
+
+class OracleError(RuntimeError):
+    pass
+
+
+def _check(rc, what):
+    if rc == -2:
+        raise OverflowError("%s: compressed integer accumulation exceeds i64" % what)
+    if rc != 0:
+        raise OracleError("%s failed (%d)" % (what, rc))
+
+
+def signs(rule, seed, offset, n):
+    """crates/yskn-format/src/signs.rs:12-38."""
+    out = np.empty(n, np.int8)
+    _check(lib().orc_signs(C.c_int(RULES[rule]), C.c_uint64(seed), C.c_uint64(offset), C.c_int64(n), _p(out)), "signs")
+    return out
+
+
+def tensor_signs(rot, n):
+    return None if rot is None else signs(rot["rule"], rot["seed"], rot["offset"], n)
+
+
+def f16_to_f32(bits):
+    return lib().orc_f16_to_f32(int(bits))
+
+
+def f32_to_f16(value):
+    return lib().orc_f32_to_f16(float(value))
+
+
+def f32_to_bf16(value):
+    return lib().orc_f32_to_bf16(float(value))
+
+
+def states(words, layout, phys_rows, cols, bits):
+    """tensor.rs:385-428: uint16 [phys_rows, cols/256, 128]."""
+    words = np.ascontiguousarray(words, np.uint32)
+    out = np.empty((phys_rows, cols // 256, 128), np.uint16)
+    _check(lib().orc_states_all(_p(words), C.c_int(LAYOUTS[layout]), C.c_int64(phys_rows), C.c_int64(cols),
+                                C.c_int(bits), _p(out)), "states")
+    return out
+
+
+def quantize_weight_table(lut16, scale16):
+    """compressed_linear.rs:138-158 -> (int8 lut8[8192], f32 tau[N])."""
+    lut16 = np.ascontiguousarray(lut16, np.uint16)
+    scale16 = np.ascontiguousarray(scale16, np.uint16)
+    lut8 = np.empty(8192, np.int8)
+    tau = np.empty(scale16.size, np.float32)
+    _check(lib().orc_quantize_weight_table(_p(lut16), _p(scale16), C.c_int64(scale16.size), _p(lut8), _p(tau)),
+           "quantize_weight_table")
+    return lut8, tau
+
+
+def hadamard512(v):
+    v = np.array(v, np.float32).copy()
+    lib().orc_hadamard512(_p(v))
+    return v
+
+
+def quantize_activation(x, signs_in):
+    """compressed_linear.rs:57-135 for each row of x [M, Kc] -> (act8, alpha, A, row_quantum)."""
+    x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+    signs_in = np.ascontiguousarray(signs_in, np.int8)
+    M, K = x.shape
+    G = K // 512
+    act8 = np.empty((M, K), np.int8)
+    alpha = np.empty((M, G), np.float32)
+    A = np.empty((M, G), np.int32)
+    rq = np.empty(M, np.float32)
+    _check(lib().orc_quantize_activation(_p(x), _p(signs_in), C.c_int64(M), C.c_int64(K), _p(act8), _p(alpha),
+                                         _p(A), _p(rq)), "quantize_activation")
+    return act8, alpha, A, rq
+
+
+def weighted_sums(words, layout, phys_rows, cols, bits, lut8, act8, A, rows=None):
+    """compressed_linear.rs:205-252 (scalar, checked) -> int64 [M, rows]."""
+    words = np.ascontiguousarray(words, np.uint32)
+    act8 = np.ascontiguousarray(np.atleast_2d(act8), np.int8)
+    A = np.ascontiguousarray(np.atleast_2d(A), np.int32)
+    lut8 = np.ascontiguousarray(lut8, np.int8)
+    rows = phys_rows if rows is None else rows
+    M = act8.shape[0]
+    out = np.empty((M, rows), np.int64)
+    _check(lib().orc_weighted_sums(_p(words), C.c_int(LAYOUTS[layout]), C.c_int64(phys_rows), C.c_int64(cols),
+                                   C.c_int(bits), _p(lut8), _p(act8), _p(A), C.c_int64(M), C.c_int64(rows), _p(out)),
+           "weighted_sums")
+    return out
+
+
+def fast_weighted_sums(words, layout, phys_rows, cols, bits, lut8, act8, A, rows=None, threads=None):
+    """crates/yskn-engine/src/kernel.rs:92-233 + pool.rs:248-344 restated with pthreads."""
+    words = np.ascontiguousarray(words, np.uint32)
+    act8 = np.ascontiguousarray(np.atleast_2d(act8), np.int8)
+    A = np.ascontiguousarray(np.atleast_2d(A), np.int32)
+    lut8 = np.ascontiguousarray(lut8, np.int8)
+    rows = phys_rows if rows is None else rows
+    threads = threads or os.cpu_count() or 1
+    M = act8.shape[0]
+    out = np.empty((M, rows), np.int64)
+    _check(lib().orc_fast_weighted_sums(_p(words), C.c_int(LAYOUTS[layout]), C.c_int64(phys_rows), C.c_int64(cols),
+                                        C.c_int(bits), _p(lut8), _p(act8), _p(A), C.c_int64(M), C.c_int64(rows),
+                                        _p(out), C.c_int(threads)), "fast_weighted_sums")
+    return out
+
+
+def restore(ws, row_quantum, tau, signs_out=None, inv_rms=None, rows=None):
+    """compressed_linear.rs:288-370 -> float32 [M, rows]."""
+    ws = np.ascontiguousarray(np.atleast_2d(ws), np.int64)
+    M, N = ws.shape
+    rows = N if rows is None else rows
+    rq = np.ascontiguousarray(row_quantum, np.float32).reshape(M)
+    tau = np.ascontiguousarray(tau, np.float32)
+    so = None if signs_out is None else np.ascontiguousarray(signs_out, np.int8)
+    if so is not None and so.size != N:
+        raise OracleError("restore: output signs must have one entry per physical row")
+    if tau.size != N:
+        raise OracleError("restore: one row scale per physical row")
+    ir = None if inv_rms is None else np.ascontiguousarray(inv_rms, np.float32).reshape(M)
+    out = np.empty((M, rows), np.float32)
+    _check(lib().orc_restore(_p(ws), C.c_int64(M), C.c_int64(N), _p(rq), None if ir is None else _p(ir), _p(tau),
+                             None if so is None else _p(so), C.c_int64(rows), _p(out)), "restore")
+    return out
+
+
+def repack_warp_to_frag(words, rows, seqs, wps):
+    """src/repack.cu:10-18."""
+    words = np.ascontiguousarray(words, np.uint32)
+    out = np.empty_like(words)
+    _check(lib().orc_repack_warp_to_frag(_p(words), _p(out), C.c_int(rows), C.c_int(seqs), C.c_int(wps)), "repack")
+    return out
+
+
+def linear(words, layout, phys_rows, cols, bits, lut16, scale16, x, signs_in, signs_out=None, inv_rms=None,
+           rows=None):
+    """The whole operator y = D_out H (M (H D_in x)) as CompressedLinear::project
+    (compressed_linear.rs:254-285) runs it."""
+    lut8, tau = quantize_weight_table(lut16, scale16)
+    act8, _, A, rq = quantize_activation(x, signs_in)
+    ws = weighted_sums(words, layout, phys_rows, cols, bits, lut8, act8, A)
+    return restore(ws, rq, tau, signs_out, inv_rms, rows)

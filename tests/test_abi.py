@@ -1,0 +1,62 @@
+"""The C ABI library loads and exports every symbol include/yskn_b200.h declares
+(no GPU needed: only host-side entry points are called here)."""
+import os
+import re
+
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import ROOT
+
+
+def _declared():
+    names = set()
+    with open(os.path.join(ROOT, "include", "yskn_b200.h")) as f:
+        text = f.read()
+    for m in re.finditer(r"YSKN_B200_API\s+[^;{]*?\b(yskn_\w+)\s*\(", text):
+        names.add(m.group(1))
+    return names
+
+
+def test_header_declares_the_reference_repack_exports():
+    names = _declared()
+    assert {"yskn_repack_warp_to_frag", "yskn_repack_warp_to_frag_host"} <= names
+    assert "yskn_b200_weighted_sums" in names and "yskn_b200_last_error" in names
+
+
+def test_library_exports_every_declared_symbol():
+    import yskn_b200
+    L = yskn_b200.lib()
+    declared = _declared()
+    for name in declared:
+        assert hasattr(L, name), name
+    assert declared == set(yskn_b200.exported_symbols())
+
+
+@pytest.mark.parametrize("rule", ["splitmix64", "mulberry32_7919_13"])
+def test_host_sign_streams_match_the_oracle(rule):
+    import yskn_b200
+    for seed, offset, n in [(7, 0, 5120), (11, 1024, 512), (0, 3, 64), (2 ** 40 + 5, 2 ** 33, 1000)]:
+        assert np.array_equal(yskn_b200.signs(rule, seed, offset, n), O.signs(rule, seed, offset, n))
+
+
+def test_shape_errors_are_returned_not_trapped():
+    import yskn_b200
+    L = yskn_b200.lib()
+    assert L.yskn_b200_pack_bytes(17408, 5120, 8) == 17408 * 20 * 8 * 16
+    assert L.yskn_b200_pack_bytes(13, 512, 6) == 32 * 2 * 6 * 16
+    assert L.yskn_b200_pack_bytes(16, 500, 8) == -1
+    assert L.yskn_b200_pack_bytes(16, 512, 9) == -1
+    # The reference's repack rejects rows % 64 and wps % 4 with -1 before touching memory.
+    assert L.yskn_repack_warp_to_frag(None, None, 65, 2, 32, None) == -1
+    assert L.yskn_repack_warp_to_frag(None, None, 64, 2, 30, None) == -1
+    lut = np.zeros(8192, np.uint16)
+    sc = np.zeros(16, np.uint16)
+    si = np.ones(512, np.int8)
+    for args in [(1, 13, 16, 500, 8), (1, 13, 16, 512, 3), (1, 17, 16, 512, 8), (1, 13, 11, 512, 8)]:
+        layout, rows, phys, cols, bits = args
+        h = L.yskn_b200_matrix_create(None, layout, rows, phys, cols, bits, lut.ctypes.data, sc.ctypes.data,
+                                      si.ctypes.data, None)
+        assert not h
+        assert yskn_b200.last_error()

@@ -1,0 +1,413 @@
+// The C ABI (include/yskn_b200.h): matrix handles, argument checks, dispatch.
+//
+// Host-side arithmetic here (the int8 table and the effective row scales) follows
+// crates/yskn-ref/src/compressed_linear.rs:138-158 and the reference loader
+// src/loader.cpp:19-25; it is compiled with -ffp-contract=off so each binary32
+// operation rounds once, as the Rust reference does.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+
+namespace yskn {
+
+__device__ unsigned g_device_error = 0;
+
+unsigned* device_error_word() {
+  static unsigned* words[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (!words[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) == cudaSuccess) words[dev] = reinterpret_cast<unsigned*>(p);
+  }
+  return words[dev];
+}
+
+static thread_local std::string t_last_error;
+
+int fail(int code, const std::string& msg) {
+  t_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  if (e == cudaSuccess) return YSKN_OK;
+  t_last_error = std::string(where) + ": " + cudaGetErrorString(e);
+  return YSKN_ECUDA;
+}
+
+static float f16_to_f32(uint16_t bits) {  // crates/yskn-format/src/floats.rs:4-19
+  const uint32_t sign = (uint32_t)(bits & 0x8000u) << 16;
+  const uint32_t exponent = (bits >> 10) & 0x1fu, fraction = bits & 0x3ffu;
+  uint32_t out;
+  if (exponent == 0 && fraction == 0) {
+    out = sign;
+  } else if (exponent == 0) {
+    const uint32_t shift = (uint32_t)__builtin_clz(fraction) - 21u;
+    out = sign | ((113u - shift) << 23) | (((fraction << shift) & 0x3ffu) << 13);
+  } else if (exponent == 31) {
+    out = sign | 0x7f800000u | (fraction << 13);
+  } else {
+    out = sign | ((exponent + 112u) << 23) | (fraction << 13);
+  }
+  float f;
+  std::memcpy(&f, &out, 4);
+  return f;
+}
+
+static void sign_stream(int rule, uint64_t seed, uint64_t offset, int64_t n, int8_t* out) {
+  for (int64_t i = 0; i < n; ++i) {
+    const uint64_t position = offset + (uint64_t)i + 1u;
+    bool positive;
+    if (rule == YSKN_SIGNS_SPLITMIX64) {
+      uint64_t v = seed + position * 0x9e3779b97f4a7c15ull;
+      v = (v ^ (v >> 30)) * 0xbf58476d1ce4e5b9ull;
+      v = (v ^ (v >> 27)) * 0x94d049bb133111ebull;
+      v ^= v >> 31;
+      positive = (v >> 63) != 0;
+    } else {
+      uint32_t s0 = (uint32_t)seed * 7919u + 13u;
+      if (s0 == 0) s0 = 0x9e3779b9u;
+      uint32_t v = s0 + (uint32_t)position * 0x6d2b79f5u;
+      v = (v ^ (v >> 15)) * (v | 1u);
+      v ^= v + (v ^ (v >> 7)) * (v | 61u);
+      v ^= v >> 14;
+      positive = v >= 0x80000000u;
+    }
+    out[i] = positive ? 1 : -1;
+  }
+}
+
+}  // namespace yskn
+
+using namespace yskn;
+
+struct yskn_b200_matrix {
+  MatrixDev dev{};
+  void* codes = nullptr;
+  void* small = nullptr;  // lut8 | tau | s_in | s_out in one allocation
+  int64_t packed_bytes = 0;
+  bool has_rot = false;
+};
+
+static cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+extern "C" {
+
+YSKN_B200_API const char* yskn_b200_last_error(void) { return t_last_error.c_str(); }
+
+YSKN_B200_API int yskn_b200_status(void* stream) {
+  cudaError_t e = cudaStreamSynchronize(as_stream(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "yskn_b200_status");
+  unsigned bits = 0;
+  const unsigned zero = 0;
+  e = cudaMemcpyFromSymbol(&bits, g_device_error, sizeof bits);
+  if (e == cudaSuccess && bits) e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof zero);
+  if (e != cudaSuccess) return cuda_fail(e, "yskn_b200_status");
+  if (bits & DERR_TIMEOUT) return fail(YSKN_ETIMEDOUT, "a bounded device wait timed out");
+  if (bits & DERR_OVERFLOW) return fail(YSKN_EOVERFLOW, "compressed integer accumulation exceeds i64");
+  if (bits & DERR_NONFINITE) return fail(YSKN_ENONFINITE, "non-finite activation or restored value");
+  return YSKN_OK;
+}
+
+YSKN_B200_API int yskn_repack_warp_to_frag(const uint32_t* d_words, uint32_t* d_frag, int rows, int seqs, int wps,
+                                           void* cuda_stream) {
+  if (rows % 64 || wps % 4) return -1;  // src/repack.cu:22
+  if (rows <= 0 || seqs <= 0 || wps <= 0 || !d_words || !d_frag) return fail(YSKN_EINVAL, "repack: bad arguments");
+  return launch_repack_frag(d_words, d_frag, rows, seqs, wps, as_stream(cuda_stream));
+}
+
+YSKN_B200_API int yskn_repack_warp_to_frag_host(const uint32_t* h_words, uint32_t* h_frag, int rows, int seqs,
+                                                int wps) {
+  if (rows % 64 || wps % 4) return -1;
+  if (rows <= 0 || seqs <= 0 || wps <= 0 || !h_words || !h_frag) return fail(YSKN_EINVAL, "repack: bad arguments");
+  const size_t bytes = (size_t)rows * seqs * wps * 4;
+  uint32_t *dw = nullptr, *df = nullptr;
+  cudaError_t e = cudaMalloc(&dw, bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&df, bytes);
+  if (e == cudaSuccess) e = cudaMemcpy(dw, h_words, bytes, cudaMemcpyHostToDevice);
+  int rc = e == cudaSuccess ? launch_repack_frag(dw, df, rows, seqs, wps, nullptr) : cuda_fail(e, "repack_host");
+  if (rc == YSKN_OK) {
+    e = cudaMemcpy(h_frag, df, bytes, cudaMemcpyDeviceToHost);
+    rc = cuda_fail(e, "repack_host");
+  }
+  cudaFree(dw);
+  cudaFree(df);
+  return rc;
+}
+
+YSKN_B200_API int yskn_b200_signs(int rule, uint64_t seed, uint64_t offset, int64_t n, int8_t* h_out) {
+  if ((rule != YSKN_SIGNS_SPLITMIX64 && rule != YSKN_SIGNS_MULBERRY32) || n < 0 || (n && !h_out))
+    return fail(YSKN_EINVAL, "signs: bad arguments");
+  sign_stream(rule, seed, offset, n, h_out);
+  return YSKN_OK;
+}
+
+YSKN_B200_API int64_t yskn_b200_pack_bytes(int physical_rows, int cols, int bits) {
+  if (physical_rows <= 0 || cols <= 0 || cols % 512 || bits < 4 || bits > 8) return -1;
+  return ceil_div(physical_rows, 32) * 32 * (int64_t)(cols / 256) * bits * 16;
+}
+
+static int check_shape(int layout, int phys, int cols, int bits) {
+  if (cols <= 0 || cols % 512 || phys <= 0 || bits < 4 || bits > 8 ||
+      (layout != YSKN_LAYOUT_ROW && layout != YSKN_LAYOUT_WARP))
+    return fail(YSKN_EINVAL, "invalid matrix dimensions, bits or layout");
+  if (layout == YSKN_LAYOUT_WARP && ((int64_t)phys * (cols / 256)) % 32)
+    return fail(YSKN_EINVAL, "warp layout requires a multiple of 32 sequences");
+  return YSKN_OK;
+}
+
+YSKN_B200_API int yskn_b200_pack(const uint32_t* d_words, int layout, int physical_rows, int cols, int bits,
+                                 void* d_out, void* stream) {
+  if (int rc = check_shape(layout, physical_rows, cols, bits)) return rc;
+  if (!d_words || !d_out || !aligned16(d_words) || !aligned16(d_out))
+    return fail(YSKN_EINVAL, "pack: pointers must be non-null and 16-byte aligned");
+  return launch_pack(d_words, layout, physical_rows, cols, bits, reinterpret_cast<uint4*>(d_out), as_stream(stream));
+}
+
+YSKN_B200_API yskn_b200_matrix* yskn_b200_matrix_create(const uint32_t* d_codes, int layout, int rows,
+                                                        int physical_rows, int cols, int bits,
+                                                        const uint16_t* lut16_host, const uint16_t* scale16_host,
+                                                        const int8_t* signs_in_host, const int8_t* signs_out_host) {
+  if (check_shape(layout, physical_rows, cols, bits)) return nullptr;
+  if (rows <= 0 || rows > physical_rows) return fail(YSKN_EINVAL, "rows must be in 1..physical_rows"), nullptr;
+  if (!d_codes || !aligned16(d_codes) || !lut16_host || !scale16_host || !signs_in_host)
+    return fail(YSKN_EINVAL, "matrix_create: missing or misaligned input"), nullptr;
+  if (signs_out_host && physical_rows % 512)
+    return fail(YSKN_EINVAL, "an output rotation needs whole 512-row blocks"), nullptr;
+  for (int i = 0; i < cols; ++i)
+    if (signs_in_host[i] != 1 && signs_in_host[i] != -1) return fail(YSKN_EINVAL, "signs must be -1 or +1"), nullptr;
+  if (signs_out_host)
+    for (int i = 0; i < physical_rows; ++i)
+      if (signs_out_host[i] != 1 && signs_out_host[i] != -1)
+        return fail(YSKN_EINVAL, "signs must be -1 or +1"), nullptr;
+
+  // compressed_linear.rs:138-158: one table maximum over all 8192 values.
+  float table_maximum = 0.0f;
+  for (int i = 0; i < 8192; ++i) {
+    const float v = f16_to_f32(lut16_host[i]);
+    if (!std::isfinite(v)) return fail(YSKN_EINVAL, "non-finite weight lookup table"), nullptr;
+    table_maximum = std::fmax(table_maximum, std::fabs(v));
+  }
+  if (table_maximum == 0.0f)
+    return fail(YSKN_EINVAL, "a compressed projection cannot use an all-zero lookup table (LIN-01)"), nullptr;
+  const float table_scale = table_maximum / 127.0f;
+  std::vector<int8_t> lut8(8192);
+  for (int i = 0; i < 8192; ++i) {
+    float r = std::nearbyint(f16_to_f32(lut16_host[i]) / table_scale);
+    r = std::fmin(127.0f, std::fmax(-127.0f, r));
+    lut8[i] = (int8_t)r;
+  }
+  std::vector<float> tau(physical_rows);
+  for (int r = 0; r < physical_rows; ++r) {
+    const float s = f16_to_f32(scale16_host[r]);
+    tau[r] = s * table_scale;
+    if (!std::isfinite(s) || !std::isfinite(tau[r]))
+      return fail(YSKN_EINVAL, "non-finite weight row scales"), nullptr;
+  }
+
+  std::unique_ptr<yskn_b200_matrix> m(new yskn_b200_matrix);
+  const int64_t packed = yskn_b200_pack_bytes(physical_rows, cols, bits);
+  const size_t off_tau = 8192, off_sin = off_tau + ceil_div(4 * (int64_t)physical_rows, 256) * 256;
+  const size_t off_sout = off_sin + ceil_div(cols, 256) * 256;
+  const size_t small_bytes = off_sout + ceil_div(physical_rows, 256) * 256;
+  cudaError_t e = cudaMalloc(&m->codes, (size_t)packed);
+  if (e == cudaSuccess) e = cudaMalloc(&m->small, small_bytes);
+  if (e != cudaSuccess) {
+    cudaFree(m->codes);
+    cuda_fail(e, "matrix_create: cudaMalloc");
+    return nullptr;
+  }
+  char* small = reinterpret_cast<char*>(m->small);
+  e = cudaMemcpy(small, lut8.data(), 8192, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(small + off_tau, tau.data(), 4 * (size_t)physical_rows, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(small + off_sin, signs_in_host, cols, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && signs_out_host)
+    e = cudaMemcpy(small + off_sout, signs_out_host, physical_rows, cudaMemcpyHostToDevice);
+  int rc = e == cudaSuccess ? launch_pack(d_codes, layout, physical_rows, cols, bits,
+                                          reinterpret_cast<uint4*>(m->codes), nullptr)
+                            : cuda_fail(e, "matrix_create: copy");
+  if (rc == YSKN_OK) rc = cuda_fail(cudaDeviceSynchronize(), "matrix_create: pack");
+  if (rc != YSKN_OK) {
+    cudaFree(m->codes);
+    cudaFree(m->small);
+    return nullptr;
+  }
+  m->packed_bytes = packed;
+  m->has_rot = signs_out_host != nullptr;
+  MatrixDev& d = m->dev;
+  d.codes = reinterpret_cast<const uint4*>(m->codes);
+  d.lut8 = reinterpret_cast<const uint16_t*>(small);
+  d.tau = reinterpret_cast<const float*>(small + off_tau);
+  d.s_in = reinterpret_cast<const int8_t*>(small + off_sin);
+  d.s_out = m->has_rot ? reinterpret_cast<const int8_t*>(small + off_sout) : nullptr;
+  d.rows = rows;
+  d.phys = physical_rows;
+  d.phys_pad = (int)ceil_div(physical_rows, 32) * 32;
+  d.cols = cols;
+  d.bits = bits;
+  return m.release();
+}
+
+YSKN_B200_API void yskn_b200_matrix_destroy(yskn_b200_matrix* m) {
+  if (!m) return;
+  cudaFree(m->codes);
+  cudaFree(m->small);
+  delete m;
+}
+
+YSKN_B200_API int yskn_b200_matrix_info(const yskn_b200_matrix* m, int64_t* out6) {
+  if (!m || !out6) return fail(YSKN_EINVAL, "matrix_info: null argument");
+  out6[0] = m->dev.rows;
+  out6[1] = m->dev.phys;
+  out6[2] = m->dev.cols;
+  out6[3] = m->dev.bits;
+  out6[4] = m->has_rot ? 1 : 0;
+  out6[5] = m->packed_bytes;
+  return YSKN_OK;
+}
+
+YSKN_B200_API const int8_t* yskn_b200_matrix_lut8(const yskn_b200_matrix* m) {
+  return m ? reinterpret_cast<const int8_t*>(m->dev.lut8) : nullptr;
+}
+YSKN_B200_API const float* yskn_b200_matrix_tau(const yskn_b200_matrix* m) { return m ? m->dev.tau : nullptr; }
+YSKN_B200_API const int8_t* yskn_b200_matrix_signs_in(const yskn_b200_matrix* m) { return m ? m->dev.s_in : nullptr; }
+YSKN_B200_API const int8_t* yskn_b200_matrix_signs_out(const yskn_b200_matrix* m) {
+  return m ? m->dev.s_out : nullptr;
+}
+
+static int check_group(const yskn_b200_matrix* const* mats, int n_mats) {
+  if (!mats || n_mats < 1 || n_mats > 3) return fail(YSKN_EINVAL, "1 to 3 matrices per call");
+  for (int i = 0; i < n_mats; ++i) {
+    if (!mats[i]) return fail(YSKN_EINVAL, "null matrix");
+    if (mats[i]->dev.cols != mats[0]->dev.cols || mats[i]->dev.bits != mats[0]->dev.bits)
+      return fail(YSKN_EINVAL, "grouped matrices must share cols and bits");
+  }
+  return YSKN_OK;
+}
+
+static int finish_checked(int cols, void* stream) {
+  // Overflow is only possible with at least 512 groups: |dot| < 2^23, |A| <= 2^31.
+  if (cols / 512 < 512) return YSKN_OK;
+  return yskn_b200_status(stream);
+}
+
+YSKN_B200_API int yskn_b200_weighted_sums(const yskn_b200_matrix* const* mats, int n_mats, const int8_t* d_act,
+                                          const int32_t* d_scales, int M, int64_t* const* d_out, void* stream) {
+  if (int rc = check_group(mats, n_mats)) return rc;
+  if (M < 1 || !d_act || !d_scales || !d_out || !aligned16(d_act) || !aligned16(d_scales))
+    return fail(YSKN_EINVAL, "weighted_sums: bad activation arguments");
+  MatrixDev devs[3];
+  int rows[3];
+  for (int i = 0; i < n_mats; ++i) {
+    if (!d_out[i]) return fail(YSKN_EINVAL, "weighted_sums: null output");
+    devs[i] = mats[i]->dev;
+    rows[i] = mats[i]->dev.phys;
+  }
+  if (int rc = launch_gemv(devs, n_mats, d_act, d_scales, M, d_out, rows, as_stream(stream))) return rc;
+  return finish_checked(mats[0]->dev.cols, stream);
+}
+
+YSKN_B200_API int yskn_b200_weighted_sums_prefix(const yskn_b200_matrix* mat, const int8_t* d_act,
+                                                 const int32_t* d_scales, int M, int n_rows, int64_t* d_out,
+                                                 void* stream) {
+  if (!mat) return fail(YSKN_EINVAL, "null matrix");
+  if (M < 1 || !d_act || !d_scales || !d_out || !aligned16(d_act) || !aligned16(d_scales))
+    return fail(YSKN_EINVAL, "weighted_sums_prefix: bad activation arguments");
+  if (n_rows < 1 || n_rows > mat->dev.phys)
+    return fail(YSKN_EINVAL, "requested projection rows exceed the physical row count");
+  int rows = n_rows;
+  if (int rc = launch_gemv(&mat->dev, 1, d_act, d_scales, M, &d_out, &rows, as_stream(stream))) return rc;
+  return finish_checked(mat->dev.cols, stream);
+}
+
+YSKN_B200_API int yskn_b200_quantize(const float* d_x, const int8_t* d_signs, int M, int Kc, int8_t* d_act,
+                                     float* d_alpha, int32_t* d_scales, float* d_row_quantum, void* stream) {
+  if (M < 1 || Kc <= 0 || Kc % 512)
+    return fail(YSKN_EINVAL, "activation and input signs must have matching, nonzero multiples of 512 elements");
+  if (!d_x || !d_signs || !d_act || !d_alpha || !d_scales || !d_row_quantum || !aligned16(d_x) ||
+      !aligned16(d_signs) || !aligned16(d_act))
+    return fail(YSKN_EINVAL, "quantize: null or misaligned pointer");
+  return launch_quantize(d_x, d_signs, M, Kc, d_act, d_alpha, d_scales, d_row_quantum, as_stream(stream));
+}
+
+YSKN_B200_API int yskn_b200_restore(int64_t* d_ws, const float* d_row_quantum, const float* d_inv_rms,
+                                    const yskn_b200_matrix* mat, int M, int rotate_out, int n_rows, int clear_ws,
+                                    float* d_y, void* stream) {
+  if (!mat || M < 1 || !d_ws || !d_row_quantum || !d_y || !aligned16(d_ws))
+    return fail(YSKN_EINVAL, "restore: bad arguments");
+  if (n_rows < 1 || n_rows > mat->dev.phys) return fail(YSKN_EINVAL, "restore: row count out of range");
+  if (rotate_out && !mat->dev.s_out)
+    return fail(YSKN_EINVAL, "a body projection requires complete 512-row output rotations");
+  return launch_restore(d_ws, mat->dev.phys, d_row_quantum, d_inv_rms, mat->dev.tau, rotate_out ? mat->dev.s_out : nullptr,
+                        M, mat->dev.phys, n_rows, clear_ws, d_y, as_stream(stream));
+}
+
+// Work area of yskn_b200_linear: act8 | alpha | scales | row_quantum | ws[i].
+struct LinearWork {
+  size_t act, alpha, scales, rq, ws[3], total;
+};
+
+static LinearWork linear_work(const yskn_b200_matrix* const* mats, int n_mats, int M) {
+  LinearWork w{};
+  auto up = [](size_t x) { return (x + 255) / 256 * 256; };
+  const int Kc = mats[0]->dev.cols, G = Kc / 512;
+  size_t o = 0;
+  w.act = o; o += up((size_t)M * Kc);
+  w.alpha = o; o += up(4 * (size_t)M * G);
+  w.scales = o; o += up(4 * (size_t)M * G);
+  w.rq = o; o += up(4 * (size_t)M);
+  for (int i = 0; i < n_mats; ++i) {
+    w.ws[i] = o;
+    o += up(8 * (size_t)M * mats[i]->dev.phys);
+  }
+  w.total = o;
+  return w;
+}
+
+YSKN_B200_API int64_t yskn_b200_linear_work_bytes(const yskn_b200_matrix* const* mats, int n_mats, int M) {
+  if (check_group(mats, n_mats) || M < 1) return -1;
+  return (int64_t)linear_work(mats, n_mats, M).total;
+}
+
+YSKN_B200_API int yskn_b200_linear(const yskn_b200_matrix* const* mats, int n_mats, const float* d_x, int M,
+                                   const float* d_inv_rms, void* d_work, float* const* d_y, void* stream) {
+  if (int rc = check_group(mats, n_mats)) return rc;
+  if (M < 1 || !d_x || !d_work || !d_y || !aligned16(d_x) || !aligned16(d_work))
+    return fail(YSKN_EINVAL, "linear: bad arguments");
+  const LinearWork w = linear_work(mats, n_mats, M);
+  char* base = reinterpret_cast<char*>(d_work);
+  int8_t* act = reinterpret_cast<int8_t*>(base + w.act);
+  float* alpha = reinterpret_cast<float*>(base + w.alpha);
+  int32_t* scales = reinterpret_cast<int32_t*>(base + w.scales);
+  float* rq = reinterpret_cast<float*>(base + w.rq);
+  const int Kc = mats[0]->dev.cols;
+  cudaStream_t st = as_stream(stream);
+  if (int rc = launch_quantize(d_x, mats[0]->dev.s_in, M, Kc, act, alpha, scales, rq, st)) return rc;
+  MatrixDev devs[3];
+  int rows[3];
+  int64_t* ws[3];
+  for (int i = 0; i < n_mats; ++i) {
+    if (!d_y[i]) return fail(YSKN_EINVAL, "linear: null output");
+    devs[i] = mats[i]->dev;
+    rows[i] = mats[i]->dev.phys;
+    ws[i] = reinterpret_cast<int64_t*>(base + w.ws[i]);
+  }
+  if (int rc = launch_gemv(devs, n_mats, act, scales, M, ws, rows, st)) return rc;
+  for (int i = 0; i < n_mats; ++i) {
+    const MatrixDev& d = mats[i]->dev;
+    if (int rc = launch_restore(ws[i], d.phys, rq, d_inv_rms, d.tau, d.s_out, M, d.phys, d.rows, 0, d_y[i], st))
+      return rc;
+  }
+  return finish_checked(Kc, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,56 @@
+// Shared declarations of the B200 compressed-linear library (sm_100a only).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "yskn_b200.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "this library is written for sm_100a (B200) only"
+#endif
+
+namespace yskn {
+
+// Device-side error word: kernels OR in one of these bits; yskn_b200_status()
+// reads and clears it. Never a trap, never a fault.
+enum : unsigned {
+  DERR_NONFINITE = 1u,
+  DERR_OVERFLOW = 2u,
+  DERR_TIMEOUT = 4u,
+};
+// Address of this device's error word (a __device__ variable in api.cu).
+unsigned* device_error_word();
+
+__device__ __forceinline__ void raise_device_error(unsigned* word, unsigned bits) { atomicOr(word, bits); }
+
+// Thread-local error message (src/c_api.cpp:11-14 keeps one per thread as well).
+int fail(int code, const std::string& msg);
+int cuda_fail(cudaError_t e, const char* where);
+
+// 1/sqrt(512) as the binary32 literal 0.044194173824159216f (bits 0x3d3504f3).
+constexpr float kHadamardNorm = 0.044194173824159216f;
+
+struct MatrixDev {
+  const uint4* codes;    // B200 streaming layout (see pack.cu)
+  const uint16_t* lut8;  // 4096 entries: int8 pair (component 0 low byte, component 1 high byte)
+  const float* tau;      // effective row scale, f32[physical_rows]
+  const int8_t* s_in;    // i8[cols]
+  const int8_t* s_out;   // i8[physical_rows] or nullptr
+  int rows, phys, phys_pad, cols, bits;
+};
+
+// Launchers (one per .cu file).
+int launch_gemv(const MatrixDev* mats, int n_mats, const int8_t* act, const int32_t* scales, int M, int64_t* const* out,
+                const int* out_rows, cudaStream_t st);
+int launch_quantize(const float* x, const int8_t* signs, int M, int Kc, int8_t* act, float* alpha, int32_t* scales,
+                    float* row_quantum, cudaStream_t st);
+int launch_restore(int64_t* ws, int ws_ld, const float* row_quantum, const float* inv_rms, const float* tau,
+                   const int8_t* s_out, int M, int phys, int n_rows, int clear_ws, float* y, cudaStream_t st);
+int launch_pack(const uint32_t* words, int layout, int phys, int cols, int bits, uint4* out, cudaStream_t st);
+int launch_repack_frag(const uint32_t* w, uint32_t* f, int rows, int seqs, int wps, cudaStream_t st);
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+}  // namespace yskn

@@ -1,0 +1,191 @@
+"""ctypes binding of libyskn_b200.so (include/yskn_b200.h).
+
+This mirrors how the reference's Python front end binds its native library
+(python/yasakani/_native.py:26-39): a CDLL with declared argument types, integer
+status codes and a thread-local error string. Device buffers are torch tensors
+(plumbing only); every computation runs in the CUDA library. Import fails loudly
+if the library has not been built; there is no fallback path.
+"""
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.dirname(HERE)
+LIB_PATH = os.path.join(PKG, "libyskn_b200.so")
+
+OK, EINVAL, ECUDA, EOVERFLOW, ENONFINITE, ETIMEDOUT, ENOMEM = 0, -1, -2, -3, -4, -5, -6
+LAYOUT_ROW, LAYOUT_WARP = 0, 1
+LAYOUTS = {"row": LAYOUT_ROW, "warp": LAYOUT_WARP}
+SIGN_RULES = {"splitmix64": 0, "mulberry32_7919_13": 1}
+
+_vp, _i, _i64, _u64 = C.c_void_p, C.c_int, C.c_int64, C.c_uint64
+
+_SIGNATURES = {
+    "yskn_b200_last_error": (C.c_char_p, []),
+    "yskn_b200_status": (_i, [_vp]),
+    "yskn_repack_warp_to_frag": (_i, [_vp, _vp, _i, _i, _i, _vp]),
+    "yskn_repack_warp_to_frag_host": (_i, [_vp, _vp, _i, _i, _i]),
+    "yskn_b200_signs": (_i, [_i, _u64, _u64, _i64, _vp]),
+    "yskn_b200_pack_bytes": (_i64, [_i, _i, _i]),
+    "yskn_b200_pack": (_i, [_vp, _i, _i, _i, _i, _vp, _vp]),
+    "yskn_b200_matrix_create": (_vp, [_vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
+    "yskn_b200_matrix_destroy": (None, [_vp]),
+    "yskn_b200_matrix_info": (_i, [_vp, _vp]),
+    "yskn_b200_matrix_lut8": (_vp, [_vp]),
+    "yskn_b200_matrix_tau": (_vp, [_vp]),
+    "yskn_b200_matrix_signs_in": (_vp, [_vp]),
+    "yskn_b200_matrix_signs_out": (_vp, [_vp]),
+    "yskn_b200_weighted_sums": (_i, [_vp, _i, _vp, _vp, _i, _vp, _vp]),
+    "yskn_b200_weighted_sums_prefix": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp]),
+    "yskn_b200_quantize": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp]),
+    "yskn_b200_restore": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
+    "yskn_b200_linear_work_bytes": (_i64, [_vp, _i, _i]),
+    "yskn_b200_linear": (_i, [_vp, _i, _vp, _i, _vp, _vp, _vp, _vp]),
+}
+
+_lib = None
+
+
+class YsknError(RuntimeError):
+    def __init__(self, code, message):
+        super().__init__("%s (code %d)" % (message, code))
+        self.code = code
+
+
+def lib():
+    """Load the library and declare every exported symbol of include/yskn_b200.h."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError("libyskn_b200.so is not built (run yasakani-for-mac_b200/build.py)")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def exported_symbols():
+    return sorted(_SIGNATURES)
+
+
+def last_error():
+    msg = lib().yskn_b200_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(rc, what=""):
+    if rc != OK:
+        raise YsknError(rc, "%s: %s" % (what, last_error()))
+    return rc
+
+
+def _ptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream(stream):
+    if stream is None:
+        import torch
+        stream = torch.cuda.current_stream()
+    return C.c_void_p(stream.cuda_stream)
+
+
+def signs(rule, seed, offset, n):
+    import numpy as np
+    out = np.empty(n, np.int8)
+    check(lib().yskn_b200_signs(SIGN_RULES[rule], seed, offset, n, out.ctypes.data), "signs")
+    return out
+
+
+class Matrix:
+    """One compressed matrix on the device (yskn_b200_matrix_create)."""
+
+    def __init__(self, d_codes, layout, rows, physical_rows, cols, bits, lut16, scale16, signs_in, signs_out=None):
+        import numpy as np
+        lut16 = np.ascontiguousarray(lut16, np.uint16)
+        scale16 = np.ascontiguousarray(scale16, np.uint16)
+        signs_in = np.ascontiguousarray(signs_in, np.int8)
+        so = None if signs_out is None else np.ascontiguousarray(signs_out, np.int8)
+        h = lib().yskn_b200_matrix_create(_ptr(d_codes), LAYOUTS.get(layout, layout), rows, physical_rows, cols, bits,
+                                          lut16.ctypes.data, scale16.ctypes.data, signs_in.ctypes.data,
+                                          None if so is None else so.ctypes.data)
+        if not h:
+            raise YsknError(EINVAL, "matrix_create: " + last_error())
+        self.handle = C.c_void_p(h)
+        self.rows, self.physical_rows, self.cols, self.bits = rows, physical_rows, cols, bits
+        self.has_rotation = so is not None
+
+    def info(self):
+        out = (C.c_int64 * 6)()
+        check(lib().yskn_b200_matrix_info(self.handle, out), "matrix_info")
+        return list(out)
+
+    def close(self):
+        if self.handle:
+            lib().yskn_b200_matrix_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def signs_in_ptr(self):
+        return lib().yskn_b200_matrix_signs_in(self.handle)
+
+
+def _handles(mats):
+    arr = (C.c_void_p * len(mats))(*[m.handle for m in mats])
+    return arr
+
+
+def weighted_sums(mats, act, scales, outs, stream=None):
+    """int64 [M][physical_rows] per matrix (yskn_b200_weighted_sums)."""
+    M = act.shape[0]
+    outp = (C.c_void_p * len(outs))(*[o.data_ptr() for o in outs])
+    check(lib().yskn_b200_weighted_sums(_handles(mats), len(mats), _ptr(act), _ptr(scales), M, outp, _stream(stream)),
+          "weighted_sums")
+
+
+def weighted_sums_prefix(mat, act, scales, n_rows, out, stream=None):
+    check(lib().yskn_b200_weighted_sums_prefix(mat.handle, _ptr(act), _ptr(scales), act.shape[0], n_rows, _ptr(out),
+                                               _stream(stream)), "weighted_sums_prefix")
+
+
+def quantize(x, signs_dev_ptr, act, alpha, scales, row_quantum, stream=None):
+    M, K = x.shape
+    check(lib().yskn_b200_quantize(_ptr(x), signs_dev_ptr, M, K, _ptr(act), _ptr(alpha), _ptr(scales),
+                                   _ptr(row_quantum), _stream(stream)), "quantize")
+
+
+def restore(ws, row_quantum, inv_rms, mat, rotate_out, n_rows, clear_ws, y, stream=None):
+    check(lib().yskn_b200_restore(_ptr(ws), _ptr(row_quantum), _ptr(inv_rms), mat.handle, ws.shape[0],
+                                  int(rotate_out), n_rows, int(clear_ws), _ptr(y), _stream(stream)), "restore")
+
+
+def linear_work_bytes(mats, M):
+    return lib().yskn_b200_linear_work_bytes(_handles(mats), len(mats), M)
+
+
+def linear(mats, x, work, ys, inv_rms=None, stream=None):
+    yp = (C.c_void_p * len(ys))(*[y.data_ptr() for y in ys])
+    check(lib().yskn_b200_linear(_handles(mats), len(mats), _ptr(x), x.shape[0], _ptr(inv_rms), _ptr(work), yp,
+                                 _stream(stream)), "linear")
+
+
+def status(stream=None):
+    return lib().yskn_b200_status(_stream(stream))
+
+
+def repack_warp_to_frag(words, frag, rows, seqs, wps, stream=None):
+    return lib().yskn_repack_warp_to_frag(_ptr(words), _ptr(frag), rows, seqs, wps, _stream(stream))
+
+
+def pack(words, layout, physical_rows, cols, bits, out, stream=None):
+    check(lib().yskn_b200_pack(_ptr(words), LAYOUTS.get(layout, layout), physical_rows, cols, bits, _ptr(out),
+                               _stream(stream)), "pack")
