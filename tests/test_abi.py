@@ -45,7 +45,7 @@ def test_shape_errors_are_returned_not_trapped():
     import yskn_b200
     L = yskn_b200.lib()
     assert L.yskn_b200_pack_bytes(17408, 5120, 8) == 17408 * 20 * 8 * 16
-    assert L.yskn_b200_pack_bytes(13, 512, 6) == 32 * 2 * 6 * 16
+    assert L.yskn_b200_pack_bytes(13, 512, 6) == 16 * 2 * 6 * 16
     assert L.yskn_b200_pack_bytes(16, 500, 8) == -1
     assert L.yskn_b200_pack_bytes(16, 512, 9) == -1
     # The reference's repack rejects rows % 64 and wps % 4 with -1 before touching memory.

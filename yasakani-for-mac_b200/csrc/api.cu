@@ -7,7 +7,9 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <algorithm>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -30,6 +32,51 @@ unsigned* device_error_word() {
 }
 
 static thread_local std::string t_last_error;
+
+// Per-device scratch of the GEMV reduction, sized at matrix-creation time so the
+// hot calls never allocate. Grows (synchronously) when a larger matrix is loaded.
+struct DeviceScratch {
+  GemvScratch s{};
+  void* block = nullptr;
+};
+static DeviceScratch g_scratch[64];
+static std::mutex g_scratch_mutex;
+
+static int ensure_scratch(int row_blocks) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return fail(YSKN_EINVAL, "device index out of range");
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  DeviceScratch& d = g_scratch[dev];
+  const int64_t want_counters = std::max<int64_t>(3 * (int64_t)row_blocks, 4096);
+  const int64_t want_warps = gemv_max_warps();
+  if (d.block && d.s.n_counters >= want_counters && d.s.max_warps >= want_warps) return YSKN_OK;
+  const int64_t n_counters = std::max(want_counters, d.s.n_counters);
+  const size_t part_bytes = (size_t)want_warps * 2 * 32 * 4 * sizeof(long long);
+  const size_t bytes = part_bytes + (size_t)n_counters * sizeof(unsigned);
+  void* block = nullptr;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMalloc(&block, bytes);
+  if (e == cudaSuccess) e = cudaMemset(reinterpret_cast<char*>(block) + part_bytes, 0, bytes - part_bytes);
+  if (e != cudaSuccess) {
+    if (block) cudaFree(block);
+    return cuda_fail(e, "gemv scratch");
+  }
+  if (d.block) cudaFree(d.block);
+  d.block = block;
+  d.s.partials = reinterpret_cast<long long*>(block);
+  d.s.counters = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(block) + part_bytes);
+  d.s.n_counters = n_counters;
+  d.s.max_warps = want_warps;
+  return YSKN_OK;
+}
+
+static const GemvScratch* current_scratch() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !g_scratch[dev].block) return nullptr;
+  return &g_scratch[dev].s;
+}
 
 int fail(int code, const std::string& msg) {
   t_last_error = msg;
@@ -153,7 +200,7 @@ YSKN_B200_API int yskn_b200_signs(int rule, uint64_t seed, uint64_t offset, int6
 
 YSKN_B200_API int64_t yskn_b200_pack_bytes(int physical_rows, int cols, int bits) {
   if (physical_rows <= 0 || cols <= 0 || cols % 512 || bits < 4 || bits > 8) return -1;
-  return ceil_div(physical_rows, 32) * 32 * (int64_t)(cols / 256) * bits * 16;
+  return ceil_div(physical_rows, 8) * 8 * (int64_t)(cols / 256) * bits * 16;
 }
 
 static int check_shape(int layout, int phys, int cols, int bits) {
@@ -170,7 +217,8 @@ YSKN_B200_API int yskn_b200_pack(const uint32_t* d_words, int layout, int physic
   if (int rc = check_shape(layout, physical_rows, cols, bits)) return rc;
   if (!d_words || !d_out || !aligned16(d_words) || !aligned16(d_out))
     return fail(YSKN_EINVAL, "pack: pointers must be non-null and 16-byte aligned");
-  return launch_pack(d_words, layout, physical_rows, cols, bits, reinterpret_cast<uint4*>(d_out), as_stream(stream));
+  return launch_pack(d_words, layout, physical_rows, cols, bits, reinterpret_cast<uint32_t*>(d_out),
+                     as_stream(stream));
 }
 
 YSKN_B200_API yskn_b200_matrix* yskn_b200_matrix_create(const uint32_t* d_codes, int layout, int rows,
@@ -214,6 +262,7 @@ YSKN_B200_API yskn_b200_matrix* yskn_b200_matrix_create(const uint32_t* d_codes,
       return fail(YSKN_EINVAL, "non-finite weight row scales"), nullptr;
   }
 
+  if (ensure_scratch((int)ceil_div(physical_rows, 8))) return nullptr;
   std::unique_ptr<yskn_b200_matrix> m(new yskn_b200_matrix);
   const int64_t packed = yskn_b200_pack_bytes(physical_rows, cols, bits);
   const size_t off_tau = 8192, off_sin = off_tau + ceil_div(4 * (int64_t)physical_rows, 256) * 256;
@@ -233,7 +282,7 @@ YSKN_B200_API yskn_b200_matrix* yskn_b200_matrix_create(const uint32_t* d_codes,
   if (e == cudaSuccess && signs_out_host)
     e = cudaMemcpy(small + off_sout, signs_out_host, physical_rows, cudaMemcpyHostToDevice);
   int rc = e == cudaSuccess ? launch_pack(d_codes, layout, physical_rows, cols, bits,
-                                          reinterpret_cast<uint4*>(m->codes), nullptr)
+                                          reinterpret_cast<uint32_t*>(m->codes), nullptr)
                             : cuda_fail(e, "matrix_create: copy");
   if (rc == YSKN_OK) rc = cuda_fail(cudaDeviceSynchronize(), "matrix_create: pack");
   if (rc != YSKN_OK) {
@@ -244,14 +293,14 @@ YSKN_B200_API yskn_b200_matrix* yskn_b200_matrix_create(const uint32_t* d_codes,
   m->packed_bytes = packed;
   m->has_rot = signs_out_host != nullptr;
   MatrixDev& d = m->dev;
-  d.codes = reinterpret_cast<const uint4*>(m->codes);
+  d.codes = reinterpret_cast<const uint32_t*>(m->codes);
   d.lut8 = reinterpret_cast<const uint16_t*>(small);
   d.tau = reinterpret_cast<const float*>(small + off_tau);
   d.s_in = reinterpret_cast<const int8_t*>(small + off_sin);
   d.s_out = m->has_rot ? reinterpret_cast<const int8_t*>(small + off_sout) : nullptr;
   d.rows = rows;
   d.phys = physical_rows;
-  d.phys_pad = (int)ceil_div(physical_rows, 32) * 32;
+  d.phys_pad8 = (int)ceil_div(physical_rows, 8) * 8;
   d.cols = cols;
   d.bits = bits;
   return m.release();
@@ -312,7 +361,9 @@ YSKN_B200_API int yskn_b200_weighted_sums(const yskn_b200_matrix* const* mats, i
     devs[i] = mats[i]->dev;
     rows[i] = mats[i]->dev.phys;
   }
-  if (int rc = launch_gemv(devs, n_mats, d_act, d_scales, M, d_out, rows, as_stream(stream))) return rc;
+  const GemvScratch* sc = current_scratch();
+  if (!sc) return fail(YSKN_EINVAL, "weighted_sums: no matrix was created on this device");
+  if (int rc = launch_gemv(devs, n_mats, d_act, d_scales, M, d_out, rows, *sc, as_stream(stream))) return rc;
   return finish_checked(mats[0]->dev.cols, stream);
 }
 
@@ -325,7 +376,9 @@ YSKN_B200_API int yskn_b200_weighted_sums_prefix(const yskn_b200_matrix* mat, co
   if (n_rows < 1 || n_rows > mat->dev.phys)
     return fail(YSKN_EINVAL, "requested projection rows exceed the physical row count");
   int rows = n_rows;
-  if (int rc = launch_gemv(&mat->dev, 1, d_act, d_scales, M, &d_out, &rows, as_stream(stream))) return rc;
+  const GemvScratch* sc = current_scratch();
+  if (!sc) return fail(YSKN_EINVAL, "weighted_sums: no matrix was created on this device");
+  if (int rc = launch_gemv(&mat->dev, 1, d_act, d_scales, M, &d_out, &rows, *sc, as_stream(stream))) return rc;
   return finish_checked(mat->dev.cols, stream);
 }
 
@@ -401,7 +454,9 @@ YSKN_B200_API int yskn_b200_linear(const yskn_b200_matrix* const* mats, int n_ma
     rows[i] = mats[i]->dev.phys;
     ws[i] = reinterpret_cast<int64_t*>(base + w.ws[i]);
   }
-  if (int rc = launch_gemv(devs, n_mats, act, scales, M, ws, rows, st)) return rc;
+  const GemvScratch* sc = current_scratch();
+  if (!sc) return fail(YSKN_EINVAL, "linear: no matrix was created on this device");
+  if (int rc = launch_gemv(devs, n_mats, act, scales, M, ws, rows, *sc, st)) return rc;
   for (int i = 0; i < n_mats; ++i) {
     const MatrixDev& d = mats[i]->dev;
     if (int rc = launch_restore(ws[i], d.phys, rq, d_inv_rms, d.tau, d.s_out, M, d.phys, d.rows, 0, d_y[i], st))

@@ -33,22 +33,34 @@ int cuda_fail(cudaError_t e, const char* where);
 constexpr float kHadamardNorm = 0.044194173824159216f;
 
 struct MatrixDev {
-  const uint4* codes;    // B200 streaming layout (see pack.cu)
-  const uint16_t* lut8;  // 4096 entries: int8 pair (component 0 low byte, component 1 high byte)
-  const float* tau;      // effective row scale, f32[physical_rows]
-  const int8_t* s_in;    // i8[cols]
-  const int8_t* s_out;   // i8[physical_rows] or nullptr
-  int rows, phys, phys_pad, cols, bits;
+  const uint32_t* codes;  // B200 streaming layout (see pack.cu)
+  const uint16_t* lut8;   // 4096 entries: int8 pair (component 0 low byte, component 1 high byte)
+  const float* tau;       // effective row scale, f32[physical_rows]
+  const int8_t* s_in;     // i8[cols]
+  const int8_t* s_out;    // i8[physical_rows] or nullptr
+  int rows, phys, phys_pad8, cols, bits;
 };
+
+// Scratch of the decode GEMV's split-row-block reduction (gemv.cu): per-warp i64
+// partials and one arrival counter per 8-row block (zero between launches).
+struct GemvScratch {
+  long long* partials;  // [2 * max_warps][32][4]
+  unsigned* counters;   // [n_counters], zeroed at allocation, reset by the kernel
+  int64_t n_counters;
+  int64_t max_warps;
+};
+
+constexpr int GEMV_WARPS = 16;  // warps per persistent GEMV CTA (one CTA per SM)
+int gemv_max_warps();
 
 // Launchers (one per .cu file).
 int launch_gemv(const MatrixDev* mats, int n_mats, const int8_t* act, const int32_t* scales, int M, int64_t* const* out,
-                const int* out_rows, cudaStream_t st);
+                const int* out_rows, const GemvScratch& scratch, cudaStream_t st);
 int launch_quantize(const float* x, const int8_t* signs, int M, int Kc, int8_t* act, float* alpha, int32_t* scales,
                     float* row_quantum, cudaStream_t st);
 int launch_restore(int64_t* ws, int ws_ld, const float* row_quantum, const float* inv_rms, const float* tau,
                    const int8_t* s_out, int M, int phys, int n_rows, int clear_ws, float* y, cudaStream_t st);
-int launch_pack(const uint32_t* words, int layout, int phys, int cols, int bits, uint4* out, cudaStream_t st);
+int launch_pack(const uint32_t* words, int layout, int phys, int cols, int bits, uint32_t* out, cudaStream_t st);
 int launch_repack_frag(const uint32_t* w, uint32_t* f, int rows, int seqs, int wps, cudaStream_t st);
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }

@@ -6,18 +6,36 @@
 // with an i32 dot per 512-column group and i64 across groups. Integer adds are
 // associative, so any split of the groups across warps gives identical bits.
 //
-// B200 design. The hot loop is an HBM stream of the code words. The streaming
-// layout (pack.cu) puts the 32 rows of a row group side by side in 16-byte
-// chunks, so lane l of a warp owns row 32*rg + l: it loads its sequence's
-// 4*bits words with bits 16-byte loads (each warp-wide load is one contiguous
-// 512-byte segment), rebuilds its 128 trellis states with constant shifts,
-// looks the int8 pairs up in a shared-memory copy of the table and feeds dp4a.
-// No lane ever needs another lane's data: there are no shuffles and no partial
-// sums to reduce inside a warp. The work unit is (row group, 512-column group);
-// each warp takes a contiguous run of units in row-group-major order, keeps i64
-// sums in registers while the row group stays the same, and adds them to the
-// output with one 64-bit atomic per row when it leaves the row group (the output
-// is zeroed first). The grid is sized to the SM count times the resident blocks.
+// B200 design
+// -----------
+// * Streaming layout (pack.cu): tiles of 8 rows x one 256-column sequence. Lane
+//   (n = lane/4, q = lane%4) of a warp owns the q-th quarter (32 trellis steps,
+//   `bits` words) of row n's sequence; the two tiles of a 512-column group are
+//   adjacent, and a warp's run of units is one contiguous byte range of HBM.
+// * Decode: each lane rebuilds its 32 states with constant shifts (the
+//   12-bit window of its first step reaches into the previous quarter: one
+//   shfl_up of the neighbour's last word), and looks the int8 pairs up in
+//   shared memory. The table is stored 16 times (two lanes per copy, four lanes
+//   per group of 4 banks), so a warp-wide lookup costs about 3 shared-memory
+//   wavefronts instead of ~3.6 for one shared copy, and the address is one shift
+//   (a funnel shift only where the 12-bit window straddles two words) plus one
+//   LOP3. B200's integer pipe (16 lanes/clk per SM sub-partition) is as scarce
+//   as shared-memory bandwidth here, so the layout is chosen for fewer integer
+//   ops per lookup rather than fewer bank conflicts.
+// * Math: the 8 decoded weights of a lane per 32-column chunk are exactly its
+//   B fragment of mma.sync.m16n8k32.s8 (n = row, k = 8 consecutive columns of its
+//   quarter); the activations (A, 16 token rows) are loaded in the same column
+//   permutation, so one MMA replaces 4*M dp4a and M = 1..16 cost the same.
+//   The i32 accumulator is scaled by the token's integer group scale into i64
+//   after each 512-column group.
+// * Work: one persistent CTA per SM; CTAs are split between the (up to 3)
+//   matrices of a call in proportion to their work; each warp streams a
+//   contiguous run of (8-row block, group) units, prefetching the next unit's
+//   codes while it computes the current one. A row block whose groups are split
+//   between warps is reduced without atomics on the output: every contributor
+//   writes its i64 partial to scratch, and the last one to arrive (a counter per
+//   row block) adds the partials and stores the result, then resets the counter.
+//   The output is written exactly once, so it needs no zeroing.
 #include <algorithm>
 #include <mutex>
 
@@ -25,243 +43,431 @@
 
 namespace yskn {
 
-constexpr int GEMV_WARPS = 8;
 constexpr int GEMV_MAX_SEG = 3;
+constexpr int LUT_COPY_BYTES = 128 * 1024;  // 16 copies x 4096 entries x 2 bytes
+constexpr int LUT_RAW_BYTES = 8192;         // the table as stored, staged for the expansion
 
 struct GemvSeg {
-  const uint4* codes;
+  const uint32_t* codes;
   const uint16_t* lut;
   int64_t* out;
-  int64_t unit_begin;  // first unit of this segment
-  int rowgroups;       // phys_pad / 32
-  int out_rows;        // rows written (<= phys)
-  int out_ld;          // leading dimension of out (elements per activation row)
+  unsigned* counters;  // one per row block, zero between launches
+  int64_t units;       // row blocks * G
+  int row_blocks;
+  int out_rows;        // rows written (<= physical rows)
+  int out_ld;
+  int cta_begin;       // first CTA of this segment
+  int n_ctas;
+  int base, rem;       // balanced unit ranges of the segment's warps
 };
 
 struct GemvParams {
   GemvSeg seg[GEMV_MAX_SEG];
   int n_seg;
-  int G;  // 512-column groups per row (cols / 512)
+  int G;
+  int S;  // sequences per row (cols / 256)
   int Kc;
   const int8_t* act;
   const int32_t* scales;
-  int mv;  // valid activation rows in this pass (<= MT)
-  int64_t total_units;
-  int checked;  // 1: one warp owns whole rows and checks every i64 add (cols >= 262144)
+  int mv;  // valid activation rows (1..16)
+  int checked;
+  long long* partials;  // [2 * warps][32 lanes][4] i64
   unsigned* err;
 };
 
-__device__ __forceinline__ uint4 ld_stream(const uint4* p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-
-// State of step j (docs/FORMAT.md:121-128): the 12 code bits ending at bits*(j+1),
-// zeros before the start of the sequence. j is a compile-time constant after unrolling.
 template <int BITS>
-__device__ __forceinline__ uint32_t state_at(const uint32_t (&w)[4 * BITS], int j) {
-  const int end = BITS * (j + 1);
-  if (end < 12) return (w[0] << (12 - end)) & 0xfffu;
-  const int start = end - 12, wi = start >> 5, sh = start & 31;
-  if (sh + 12 <= 32) return (w[wi] >> sh) & 0xfffu;
-  return __funnelshift_r(w[wi], w[wi + 1], sh) & 0xfffu;
-}
+struct Unit {
+  static constexpr int U = (BITS % 4 == 0) ? 4 : (BITS % 2 == 0 ? 2 : 1);
+  uint32_t w[2][BITS];
+};
 
-template <int BITS, int MT>
-__device__ __forceinline__ void sequence_dot(const uint32_t (&w)[4 * BITS], const uint16_t* __restrict__ lut,
-                                             const int8_t* __restrict__ act, int Kc, int mv, int (&dot)[MT]) {
+template <int BITS>
+__device__ __forceinline__ void load_unit(Unit<BITS>& u, const uint32_t* tile0, int lane) {
+  constexpr int U = Unit<BITS>::U;
 #pragma unroll
-  for (int qb = 0; qb < 16; ++qb) {
-    uint32_t wq[4];
+  for (int s = 0; s < 2; ++s) {
+    const uint32_t* t = tile0 + s * (BITS * 32);
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      const int j0 = qb * 8 + 2 * t;
-      const uint32_t lo = lut[state_at<BITS>(w, j0)];
-      const uint32_t hi = lut[state_at<BITS>(w, j0 + 1)];
-      wq[t] = __byte_perm(lo, hi, 0x5410);
-    }
-#pragma unroll
-    for (int m = 0; m < MT; ++m) {
-      const int mm = m < mv ? m : mv - 1;
-      const uint4 a = __ldg(reinterpret_cast<const uint4*>(act + (int64_t)mm * Kc) + qb);
-      dot[m] = __dp4a((int)wq[0], (int)a.x, dot[m]);
-      dot[m] = __dp4a((int)wq[1], (int)a.y, dot[m]);
-      dot[m] = __dp4a((int)wq[2], (int)a.z, dot[m]);
-      dot[m] = __dp4a((int)wq[3], (int)a.w, dot[m]);
+    for (int j = 0; j < BITS / U; ++j) {
+      const uint32_t* p = t + (j * 32 + lane) * U;
+      if constexpr (U == 4) {
+        uint4 v;
+        asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+        u.w[s][4 * j] = v.x; u.w[s][4 * j + 1] = v.y; u.w[s][4 * j + 2] = v.z; u.w[s][4 * j + 3] = v.w;
+      } else if constexpr (U == 2) {
+        uint2 v;
+        asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+        u.w[s][2 * j] = v.x; u.w[s][2 * j + 1] = v.y;
+      } else {
+        uint32_t v;
+        asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+        u.w[s][j] = v;
+      }
     }
   }
 }
 
-template <int BITS, int MT>
-__global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_kernel(const __grid_constant__ GemvParams p) {
-  __shared__ uint16_t s_lut[GEMV_MAX_SEG][4096];
-  for (int s = 0; s < p.n_seg; ++s)
-    for (int i = threadIdx.x; i < 2048; i += blockDim.x)
-      reinterpret_cast<uint32_t*>(s_lut[s])[i] = __ldg(reinterpret_cast<const uint32_t*>(p.seg[s].lut) + i);
+// Bits [LO, HI) of the 32-bit window of V = [carry | w0 .. w_{BITS-1} | 0]
+// starting at bit p (other bits of the result are unspecified). Everything is a
+// compile-time constant after unrolling; a funnel shift (half rate on B200) is
+// used only when the needed bits straddle two words, otherwise one plain shift.
+template <int BITS, int LO, int HI>
+__device__ __forceinline__ uint32_t window(uint32_t carry, const uint32_t (&w)[BITS], int p) {
+  const int i = p >> 5, sh = p & 31;
+  const uint32_t lo = i == 0 ? carry : w[i - 1];
+  const uint32_t hi = i >= BITS ? 0u : w[i];
+  if (sh == 0) return lo;
+  if (sh + HI <= 32) return lo >> sh;         // only the low word contributes
+  if (sh + LO >= 32) return hi << (32 - sh);  // only the high word contributes
+  return __funnelshift_r(lo, hi, sh);
+}
+
+// Shared-memory byte address of state(step i) in this lane's table copy. The
+// table is 4096 slots of 32 bytes (slot s holds 16 copies of entry s), so the
+// state lands in address bits 5..16 with one shift and one LOP3, and the copy
+// (lane/2) in bits 1..4. Four lanes share the 4 banks {c, c+8, c+16, c+24}
+// picked by the state's two low bits: ~3 wavefronts per 32 random lookups,
+// against ~2 for a layout that needs two shifted fields; on B200 the integer
+// pipe, not shared memory, was the tighter limit of the two-field form.
+template <int BITS>
+__device__ __forceinline__ uint32_t lut_addr(uint32_t carry, const uint32_t (&w)[BITS], int i, uint32_t copy_off) {
+  const int P = 32 + BITS * (i + 1) - 12;  // first bit of the state in V
+  return (window<BITS, 5, 17>(carry, w, P - 5) & 0x1ffe0u) | copy_off;
+}
+
+// lo | hi << 16 on the FMA pipe (lo, hi are zero-extended 16-bit entries).
+__device__ __forceinline__ uint32_t pack_pair(uint32_t lo, uint32_t hi) {
+  uint32_t r;
+  asm("mad.lo.u32 %0, %1, 65536, %2;" : "=r"(r) : "r"(hi), "r"(lo));
+  return r;
+}
+
+__device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// One sequence of one tile: 8 MMAs (k = 32 each) over this lane's quarter.
+// a0p / a1p: the 64 activation bytes of quarter q for tokens n and n + 8 (shared
+// memory or global, same column permutation as the B fragments).
+template <int BITS, bool M1>
+__device__ __forceinline__ void sequence_mma(const uint32_t (&w)[BITS], int lane, const uint8_t* __restrict__ lut,
+                                             uint32_t copy_off, const uint4* a0p, const uint4* a1p, int (&c)[4]) {
+  uint32_t carry = __shfl_up_sync(0xffffffffu, w[BITS - 1], 1);
+  if ((lane & 3) == 0) carry = 0u;  // zeros before the start of the sequence (docs/FORMAT.md:121-128)
+#pragma unroll
+  for (int tp = 0; tp < 4; ++tp) {
+    // Activations of two 32-column chunks, loaded before the 16 lookups that hide their latency.
+    uint4 x0 = make_uint4(0, 0, 0, 0), x1 = make_uint4(0, 0, 0, 0);
+    if (M1) {
+      if (lane < 4) x0 = a0p[tp];
+    } else {
+      x0 = a0p[tp];
+      x1 = a1p[tp];
+    }
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int t = 2 * tp + half;
+      uint32_t b[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int i0 = 4 * t + 2 * h;
+        const uint32_t lo = *reinterpret_cast<const uint16_t*>(lut + lut_addr<BITS>(carry, w, i0, copy_off));
+        const uint32_t hi = *reinterpret_cast<const uint16_t*>(lut + lut_addr<BITS>(carry, w, i0 + 1, copy_off));
+        b[h] = pack_pair(lo, hi);
+      }
+      const uint32_t a0 = half ? x0.z : x0.x, a2 = half ? x0.w : x0.y;
+      const uint32_t a1 = half ? x1.z : x1.x, a3 = half ? x1.w : x1.y;
+      mma_s8(c, a0, a1, a2, a3, b[0], b[1]);
+    }
+  }
+}
+
+// Balanced contiguous ranges: warp w of a segment owns units
+// [w*base + min(w, rem), (w+1)*base + min(w+1, rem)), base = units / warps.
+struct Ranges {
+  int base, rem;
+  __device__ __forceinline__ int begin(int w) const { return w * base + min(w, rem); }
+  __device__ __forceinline__ int owner(int u) const {
+    const int cut = rem * (base + 1);
+    return u < cut ? u / (base + 1) : rem + (u - cut) / base;
+  }
+};
+
+// ACT_SMEM: activations and scales staged once per CTA in shared memory after
+// the table (rows padded by 16 bytes so the 8 token rows fall in different banks).
+template <int BITS, bool M1, bool ACT_SMEM>
+__global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
+  extern __shared__ __align__(16) uint8_t s_lut[];
+  // Which matrix this CTA serves.
+  int si = 0;
+  while (si + 1 < p.n_seg && (int)blockIdx.x >= p.seg[si + 1].cta_begin) ++si;
+  const GemvSeg& S = p.seg[si];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int G = p.G, Kc = p.Kc, act_ld = Kc + 16;
+  int8_t* s_act = reinterpret_cast<int8_t*>(s_lut + LUT_COPY_BYTES + LUT_RAW_BYTES);
+  int32_t* s_scale = reinterpret_cast<int32_t*>(s_lut + LUT_COPY_BYTES + LUT_RAW_BYTES + (size_t)p.mv * act_ld);
+
+  // 16 copies of the int8-pair table: slot s (32 bytes) holds entry s 16 times.
+  // The raw 8 KiB table is staged once (one 16-byte load per thread), then each
+  // thread writes 16-byte chunks k = tid + 512*i, so a warp's stores cover 512
+  // consecutive bytes (no bank conflicts) and every load is issued up front.
+  uint16_t* s_raw = reinterpret_cast<uint16_t*>(s_lut + LUT_COPY_BYTES);
+  {
+    static_assert(GEMV_WARPS * 32 == 512, "the fill assumes 512 threads");
+    reinterpret_cast<uint4*>(s_raw)[threadIdx.x] = __ldg(reinterpret_cast<const uint4*>(S.lut) + threadIdx.x);
+    if (ACT_SMEM) {
+      // Batches of 8 independent 16-byte loads per thread before their stores.
+      const int vec = Kc / 16, total = p.mv * vec;
+      for (int base = 0; base < total; base += 8 * GEMV_WARPS * 32) {
+        uint4 v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int idx = base + threadIdx.x + k * GEMV_WARPS * 32;
+          if (idx < total) v[k] = __ldg(reinterpret_cast<const uint4*>(p.act + (size_t)(idx / vec) * Kc) + idx % vec);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int idx = base + threadIdx.x + k * GEMV_WARPS * 32;
+          if (idx < total) reinterpret_cast<uint4*>(s_act + (idx / vec) * act_ld)[idx % vec] = v[k];
+        }
+      }
+      for (int idx = threadIdx.x; idx < p.mv * G; idx += blockDim.x) s_scale[idx] = __ldg(p.scales + idx);
+    }
+  }
+  __syncthreads();
+#pragma unroll 4
+  for (int i = 0; i < LUT_COPY_BYTES / 16 / 512; ++i) {
+    const int k = threadIdx.x + 512 * i;  // 16-byte chunk k = half (k & 1) of slot k >> 1
+    const uint32_t h = s_raw[k >> 1];
+    const uint32_t v = h | (h << 16);
+    reinterpret_cast<uint4*>(s_lut)[k] = make_uint4(v, v, v, v);
+  }
   __syncthreads();
 
-  const int lane = threadIdx.x & 31;
-  const int64_t gw = (int64_t)blockIdx.x * GEMV_WARPS + (threadIdx.x >> 5);
-  const int64_t nw = (int64_t)gridDim.x * GEMV_WARPS;
-  (void)nw;
-  int64_t u, u_end;
+  const int nw = S.n_ctas * GEMV_WARPS;
+  const int w_id = (blockIdx.x - S.cta_begin) * GEMV_WARPS + warp;
+  const Ranges R{S.base, S.rem};
+  int u, u_end;
   if (p.checked) {
-    // One warp per row group, groups in ascending order: every i64 add is
+    // One warp per whole row block, groups in ascending order: every i64 add is
     // checked in the reference's order (compressed_linear.rs:229-248).
-    u = gw * p.G;
-    u_end = std::min<int64_t>(u + p.G, p.total_units);
+    if (w_id >= S.row_blocks) return;
+    u = w_id * G;
+    u_end = u + G;
   } else {
-    u = gw * p.total_units / nw;
-    u_end = (gw + 1) * p.total_units / nw;
+    u = R.begin(w_id);
+    u_end = R.begin(w_id + 1);
   }
   if (u >= u_end) return;
+  const int my_begin = u;
 
-  int seg = 0;
-  while (seg + 1 < p.n_seg && u >= p.seg[seg + 1].unit_begin) ++seg;
-  int64_t local = u - p.seg[seg].unit_begin;
-  int rg = (int)(local / p.G), g = (int)(local % p.G);
-  long long acc[MT];
-#pragma unroll
-  for (int m = 0; m < MT; ++m) acc[m] = 0;
+  const uint32_t copy_off = (uint32_t)(lane >> 1) << 1;
+  const int q = lane & 3, n = lane >> 2;
+  const int tok0 = n < p.mv ? n : p.mv - 1;
+  const int tok1 = n + 8 < p.mv ? n + 8 : p.mv - 1;
+  const int8_t* act0 = ACT_SMEM ? s_act + tok0 * act_ld : p.act + (size_t)tok0 * Kc;
+  const int8_t* act1 = ACT_SMEM ? s_act + tok1 * act_ld : p.act + (size_t)tok1 * Kc;
+  const int32_t* sc0 = ACT_SMEM ? s_scale + tok0 * G : p.scales + (size_t)tok0 * G;
+  const int32_t* sc1 = ACT_SMEM ? s_scale + tok1 * G : p.scales + (size_t)tok1 * G;
+  constexpr int TILE_WORDS = BITS * 32;
+
+  int rb = u / G, g = u % G;
+  long long acc[4] = {0, 0, 0, 0};
   bool overflow = false;
+  // Units are consecutive in memory: (rb, g) -> (rb, g+1) -> (rb+1, 0) is a
+  // stride of two tiles, so the walk needs no division.
+  const uint32_t* ptr = S.codes + ((size_t)rb * p.S + 2 * g) * TILE_WORDS;
+  Unit<BITS> ua, ub;
+  load_unit<BITS>(ua, ptr, lane);
 
-  for (;;) {
-    const GemvSeg& S = p.seg[seg];
-    int dot[MT];
-#pragma unroll
-    for (int m = 0; m < MT; ++m) dot[m] = 0;
-    uint32_t w0[4 * BITS], w1[4 * BITS];
-    const uint4* c0 = S.codes + ((int64_t)(2 * g) * S.rowgroups + rg) * (BITS * 32) + lane;
-    const uint4* c1 = S.codes + ((int64_t)(2 * g + 1) * S.rowgroups + rg) * (BITS * 32) + lane;
-#pragma unroll
-    for (int c = 0; c < BITS; ++c) {
-      const uint4 v = ld_stream(c0 + c * 32);
-      w0[4 * c] = v.x; w0[4 * c + 1] = v.y; w0[4 * c + 2] = v.z; w0[4 * c + 3] = v.w;
+  // One unit: prefetch the next one into `nxt`, compute `cur`; true when done.
+  // The loop below alternates the two buffers, so no registers are copied.
+  auto step = [&](Unit<BITS>& cur, Unit<BITS>& nxt) -> bool {
+    const bool has_next = u + 1 < u_end;
+    int rbn = rb, gn = g + 1;
+    if (gn == G) {
+      gn = 0;
+      ++rbn;
     }
+    ptr += 2 * TILE_WORDS;
+    if (has_next) load_unit<BITS>(nxt, ptr, lane);
+    int c[4] = {0, 0, 0, 0};
+    const int col = g * 512 + q * 64;
+    const uint4* a0p = reinterpret_cast<const uint4*>(act0 + col);
+    const uint4* a1p = reinterpret_cast<const uint4*>(act1 + col);
+    sequence_mma<BITS, M1>(cur.w[0], lane, s_lut, copy_off, a0p, a1p, c);
+    sequence_mma<BITS, M1>(cur.w[1], lane, s_lut, copy_off, a0p + 16, a1p + 16, c);
+    const long long s0 = sc0[g], s1 = sc1[g];
+    const long long t[4] = {s0 * c[0], s0 * c[1], s1 * c[2], s1 * c[3]};
+    if (p.checked) {
 #pragma unroll
-    for (int c = 0; c < BITS; ++c) {
-      const uint4 v = ld_stream(c1 + c * 32);
-      w1[4 * c] = v.x; w1[4 * c + 1] = v.y; w1[4 * c + 2] = v.z; w1[4 * c + 3] = v.w;
-    }
-    const int8_t* a0 = p.act + (int64_t)g * 512;
-    sequence_dot<BITS, MT>(w0, s_lut[seg], a0, p.Kc, p.mv, dot);
-    sequence_dot<BITS, MT>(w1, s_lut[seg], a0 + 256, p.Kc, p.mv, dot);
+      for (int i = 0; i < 4; ++i) {
+        const long long r = (long long)((unsigned long long)acc[i] + (unsigned long long)t[i]);
+        overflow |= ((acc[i] ^ r) & (t[i] ^ r)) < 0;
+        acc[i] = r;
+      }
+    } else {
 #pragma unroll
-    for (int m = 0; m < MT; ++m) {
-      const int mm = m < p.mv ? m : p.mv - 1;
-      const long long t = (long long)__ldg(p.scales + (int64_t)mm * p.G + g) * (long long)dot[m];
-      const long long r = (long long)((unsigned long long)acc[m] + (unsigned long long)t);
-      overflow |= ((acc[m] ^ r) & (t ^ r)) < 0;
-      acc[m] = r;
+      for (int i = 0; i < 4; ++i) acc[i] += t[i];  // cannot overflow below 512 groups
     }
 
     ++u;
-    const bool done = u >= u_end;
-    int nseg = seg, nrg = rg, ng = g + 1;
-    if (ng == p.G) {
-      ng = 0;
-      ++nrg;
-      if (nrg == S.rowgroups) {
-        nrg = 0;
-        ++nseg;
-      }
-    }
-    if (done || nrg != rg || nseg != seg) {
-      const int row = rg * 32 + lane;
-      if (row < S.out_rows) {
+    if (!has_next || rbn != rb) {
+      // Rows 2q, 2q+1 of the block for tokens n and n+8 (the C fragment).
+      const int row0 = rb * 8 + 2 * q;
+      const int first = rb * G, last = first + G - 1;
+      const bool sole = p.checked || (my_begin <= first && u_end > last);
+      if (sole) {
 #pragma unroll
-        for (int m = 0; m < MT; ++m)
-          if (m < p.mv)
-            atomicAdd(reinterpret_cast<unsigned long long*>(S.out + (int64_t)m * S.out_ld + row),
-                      (unsigned long long)acc[m]);
+        for (int i = 0; i < 4; ++i) {
+          const int tok = n + (i >> 1) * 8, row = row0 + (i & 1);
+          if (tok < p.mv && row < S.out_rows) S.out[(size_t)tok * S.out_ld + row] = acc[i];
+        }
+      } else {
+        // Split row block: publish this warp's partial; the last of the
+        // contributing warps (consecutive, all non-empty) adds them up.
+        const int gw = blockIdx.x * GEMV_WARPS + warp;  // global warp id: scratch slot owner
+        const int slot_kind = my_begin >= first ? 0 : 1;
+        long long* mine = p.partials + ((size_t)(gw * 2 + slot_kind) * 32 + lane) * 4;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) __stcg(mine + i, acc[i]);
+        __threadfence();
+        __syncwarp();
+        const int wf = R.owner(first), wl = R.owner(last);
+        unsigned prev = 0;
+        if (lane == 0) prev = atomicAdd(S.counters + rb, 1u);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        if (prev == (unsigned)(wl - wf)) {
+          __threadfence();
+          long long sum[4] = {0, 0, 0, 0};
+          for (int cw = wf; cw <= wl; ++cw) {
+            const int kind = R.begin(cw) >= first ? 0 : 1;
+            const int cgw = S.cta_begin * GEMV_WARPS + cw;
+            const long long* src = p.partials + ((size_t)(cgw * 2 + kind) * 32 + lane) * 4;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) sum[i] += __ldcg(src + i);
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int tok = n + (i >> 1) * 8, row = row0 + (i & 1);
+            if (tok < p.mv && row < S.out_rows) S.out[(size_t)tok * S.out_ld + row] = sum[i];
+          }
+          if (lane == 0) S.counters[rb] = 0u;
+        }
       }
 #pragma unroll
-      for (int m = 0; m < MT; ++m) acc[m] = 0;
+      for (int i = 0; i < 4; ++i) acc[i] = 0;
     }
-    if (done) break;
-    seg = nseg;
-    rg = nrg;
-    g = ng;
+    rb = rbn;
+    g = gn;
+    return !has_next;
+  };
+  for (;;) {
+    if (step(ua, ub)) break;
+    if (step(ub, ua)) break;
   }
   if (p.checked && __any_sync(0xffffffffu, overflow) && lane == 0) raise_device_error(p.err, DERR_OVERFLOW);
+  (void)nw;
 }
 
-template <int BITS, int MT>
-static int launch_one(const GemvParams& p, cudaStream_t st) {
-  static int grid_per_sm = 0;
-  static int sm_count = 0;
+static int sm_count() {
+  static int n = 0;
   static std::once_flag once;
   std::call_once(once, [] {
     int dev = 0;
     cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&grid_per_sm, gemv_kernel<BITS, MT>, GEMV_WARPS * 32, 0);
-    if (grid_per_sm < 1) grid_per_sm = 1;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   });
-  int64_t grid;
-  if (p.checked) {
-    // One warp per whole row group: ranges are multiples of G units.
-    grid = ceil_div(p.total_units / p.G, GEMV_WARPS);
-  } else {
-    grid = std::min<int64_t>((int64_t)sm_count * grid_per_sm, ceil_div(p.total_units, GEMV_WARPS));
-  }
-  if (grid < 1) grid = 1;
-  gemv_kernel<BITS, MT><<<(unsigned)grid, GEMV_WARPS * 32, 0, st>>>(p);
+  return n;
+}
+
+int gemv_max_warps() { return (sm_count() + 8) * GEMV_WARPS; }
+
+constexpr int SMEM_LIMIT = 232448;  // opt-in shared memory per CTA on B200
+
+static size_t act_smem_bytes(int mv, int Kc) { return (size_t)mv * (Kc + 16) + 4 * (size_t)mv * (Kc / 512); }
+static size_t table_smem_bytes() { return LUT_COPY_BYTES + LUT_RAW_BYTES; }
+
+template <int BITS, bool M1, bool ACT_SMEM>
+static int launch_one(const GemvParams& p, int grid, cudaStream_t st) {
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(gemv_kernel<BITS, M1, ACT_SMEM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    SMEM_LIMIT);
+  });
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "gemv_kernel attributes");
+  const size_t smem = table_smem_bytes() + (ACT_SMEM ? act_smem_bytes(p.mv, p.Kc) : 0);
+  gemv_kernel<BITS, M1, ACT_SMEM><<<grid, GEMV_WARPS * 32, smem, st>>>(p);
   return cuda_fail(cudaGetLastError(), "gemv_kernel");
 }
 
 template <int BITS>
-static int launch_bits(const GemvParams& p, int mt, cudaStream_t st) {
-  switch (mt) {
-    case 1: return launch_one<BITS, 1>(p, st);
-    case 2: return launch_one<BITS, 2>(p, st);
-    case 4: return launch_one<BITS, 4>(p, st);
-    case 8: return launch_one<BITS, 8>(p, st);
-    default: return launch_one<BITS, 16>(p, st);
-  }
+static int launch_bits(const GemvParams& p, int grid, cudaStream_t st) {
+  const bool fits = table_smem_bytes() + act_smem_bytes(p.mv, p.Kc) <= (size_t)SMEM_LIMIT;
+  if (p.mv == 1) return fits ? launch_one<BITS, true, true>(p, grid, st) : launch_one<BITS, true, false>(p, grid, st);
+  return fits ? launch_one<BITS, false, true>(p, grid, st) : launch_one<BITS, false, false>(p, grid, st);
 }
 
 int launch_gemv(const MatrixDev* mats, int n_mats, const int8_t* act, const int32_t* scales, int M, int64_t* const* out,
-                const int* out_rows, cudaStream_t st) {
+                const int* out_rows, const GemvScratch& scratch, cudaStream_t st) {
   const int Kc = mats[0].cols, G = Kc / 512, bits = mats[0].bits;
+  const int sms = sm_count();
   GemvParams p{};
   p.n_seg = n_mats;
   p.G = G;
+  p.S = Kc / 256;
   p.Kc = Kc;
   p.checked = G >= 512 ? 1 : 0;
+  p.partials = scratch.partials;
   p.err = device_error_word();
-  int64_t units = 0;
+  // Split the CTAs between the matrices in proportion to their units.
+  int64_t total = 0;
+  for (int i = 0; i < n_mats; ++i) total += (int64_t)(mats[i].phys_pad8 / 8) * G;
+  if (total >= (int64_t)1 << 31) return fail(YSKN_EINVAL, "gemv: matrix too large for one call");
+  int grid = 0;
+  unsigned* cnt = scratch.counters;
   for (int i = 0; i < n_mats; ++i) {
-    p.seg[i].codes = mats[i].codes;
-    p.seg[i].lut = mats[i].lut8;
-    p.seg[i].unit_begin = units;
-    p.seg[i].rowgroups = mats[i].phys_pad / 32;
-    p.seg[i].out_rows = out_rows[i];
-    p.seg[i].out_ld = out_rows[i];
-    units += (int64_t)p.seg[i].rowgroups * G;
+    GemvSeg& s = p.seg[i];
+    s.codes = mats[i].codes;
+    s.lut = mats[i].lut8;
+    s.row_blocks = mats[i].phys_pad8 / 8;
+    s.units = (int64_t)s.row_blocks * G;
+    s.out_rows = out_rows[i];
+    s.out_ld = out_rows[i];
+    s.counters = cnt;
+    cnt += s.row_blocks;
+    int64_t want = std::max<int64_t>(1, (int64_t)((double)sms * s.units / total + 0.5));
+    want = std::max<int64_t>(1, std::min<int64_t>(want, ceil_div(s.units, GEMV_WARPS)));
+    if (p.checked) want = ceil_div(s.row_blocks, GEMV_WARPS);  // one warp per row block, no partials
+    s.cta_begin = grid;
+    s.n_ctas = (int)want;
+    const int64_t nw = want * GEMV_WARPS;
+    s.base = (int)(s.units / nw);
+    s.rem = (int)(s.units % nw);
+    grid += (int)want;
   }
-  p.total_units = units;
-  for (int i = 0; i < n_mats; ++i) {
-    cudaError_t e = cudaMemsetAsync(out[i], 0, sizeof(int64_t) * (size_t)M * out_rows[i], st);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
-  }
+  if ((int64_t)(cnt - scratch.counters) > scratch.n_counters ||
+      (!p.checked && (int64_t)grid * GEMV_WARPS > scratch.max_warps))
+    return fail(YSKN_EINVAL, "gemv: scratch too small for this call");
   for (int m0 = 0; m0 < M; m0 += 16) {
     const int mv = std::min(16, M - m0);
-    const int mt = mv == 1 ? 1 : mv == 2 ? 2 : mv <= 4 ? 4 : mv <= 8 ? 8 : 16;
     p.act = act + (int64_t)m0 * Kc;
     p.scales = scales + (int64_t)m0 * G;
     p.mv = mv;
     for (int i = 0; i < n_mats; ++i) p.seg[i].out = out[i] + (int64_t)m0 * out_rows[i];
     int rc;
     switch (bits) {
-      case 4: rc = launch_bits<4>(p, mt, st); break;
-      case 5: rc = launch_bits<5>(p, mt, st); break;
-      case 6: rc = launch_bits<6>(p, mt, st); break;
-      case 7: rc = launch_bits<7>(p, mt, st); break;
-      default: rc = launch_bits<8>(p, mt, st); break;
+      case 4: rc = launch_bits<4>(p, grid, st); break;
+      case 5: rc = launch_bits<5>(p, grid, st); break;
+      case 6: rc = launch_bits<6>(p, grid, st); break;
+      case 7: rc = launch_bits<7>(p, grid, st); break;
+      default: rc = launch_bits<8>(p, grid, st); break;
     }
     if (rc) return rc;
   }

@@ -1,13 +1,15 @@
 // Load-time layout transforms of the code stream.
 //
 //  * pack: the file's row or warp layout (docs/FORMAT.md:139-151) -> the B200
-//    streaming layout. The streaming layout IS the format's warp layout, taken
-//    with the physical row count rounded up to a multiple of 32 (padding rows are
-//    zero codes whose sums are never written out). Every 16-byte chunk of 32
-//    sequences is one fully coalesced 512-byte segment, and the two sequences of a
-//    512-column group for one 32-row group are two contiguous bits*512-byte runs,
-//    which is exactly what the GEMV streams with 16-byte loads (gemv.cu). So the
-//    warp-layout files of the released models need no reorder beyond a copy.
+//    streaming layout the decode GEMV reads (gemv.cu). Physical rows are padded
+//    to a multiple of 8 with zero codes (their sums are never written). Tiles of
+//    8 rows x one 256-column sequence are stored row-block-major, sequence-minor,
+//    so the two tiles of a 512-column group are adjacent. Inside a tile, lane
+//    (n = row%8, q = quarter) owns words q*bits .. q*bits+bits-1 of row n's
+//    sequence (its 32 trellis steps), stored in chunks of U words
+//    (U = 4 for bits 4/8, 2 for bits 6, 1 otherwise) interleaved across the 32
+//    lanes: chunk j of lane l at tile + (j*32 + l)*U. A warp's load of one chunk
+//    is one contiguous 128*U-byte segment.
 //  * repack_frag: the reference's own load-time permutation into its mma.sync
 //    "frag" order (src/repack.cu:10-18), kept bit-identical for the C ABI, written
 //    with 16-byte moves (one thread per chunk of 4 words) instead of one per word.
@@ -15,39 +17,40 @@
 
 namespace yskn {
 
-__global__ void __launch_bounds__(256) pack_kernel(const uint4* __restrict__ src, int layout, int phys, int phys_pad,
-                                                   int seqs, int bits, uint4* __restrict__ dst, int64_t total) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+__global__ void __launch_bounds__(256) pack_kernel(const uint32_t* __restrict__ src, int layout, int phys, int seqs,
+                                                   int bits, int U, uint32_t* __restrict__ dst, int64_t total) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // (row block, sequence, lane)
   if (i >= total) return;
   const int lane = (int)(i & 31);
-  const int64_t t = i >> 5;
-  const int c = (int)(t % bits);
-  const int64_t rest = t / bits;
-  const int groups = phys_pad >> 5;
-  const int rg = (int)(rest % groups);
-  const int64_t seq = rest / groups;
-  const int row = rg * 32 + lane;
-  uint4 v = make_uint4(0u, 0u, 0u, 0u);
-  if (row < phys) {
-    int64_t s;
-    if (layout == YSKN_LAYOUT_WARP) {
-      const int64_t q = seq * phys + row;
-      s = ((q >> 5) * bits + c) * 32 + (q & 31);
-    } else {
-      s = ((int64_t)row * seqs + seq) * bits + c;
+  const int64_t tile = i >> 5;
+  const int64_t seq = tile % seqs, rb = tile / seqs;
+  const int n = lane >> 2, q = lane & 3;
+  const int64_t row = rb * 8 + n;
+  uint32_t* t = dst + tile * (int64_t)bits * 32;
+  for (int j = 0; j < bits; ++j) {
+    uint32_t v = 0;
+    if (row < phys) {
+      const int64_t w = (int64_t)q * bits + j;  // word of the sequence
+      int64_t s;
+      if (layout == YSKN_LAYOUT_WARP) {
+        const int64_t qq = seq * phys + row;
+        s = (((qq >> 5) * bits + (w >> 2)) * 32 + (qq & 31)) * 4 + (w & 3);
+      } else {
+        s = (row * seqs + seq) * (4 * (int64_t)bits) + w;
+      }
+      v = __ldg(src + s);
     }
-    v = __ldg(src + s);
+    t[((j / U) * 32 + lane) * U + (j % U)] = v;
   }
-  dst[i] = v;
 }
 
-int launch_pack(const uint32_t* words, int layout, int phys, int cols, int bits, uint4* out, cudaStream_t st) {
-  const int phys_pad = (int)ceil_div(phys, 32) * 32;
+int launch_pack(const uint32_t* words, int layout, int phys, int cols, int bits, uint32_t* out, cudaStream_t st) {
+  const int64_t pad8 = ceil_div(phys, 8) * 8;
   const int seqs = cols / 256;
-  const int64_t total = (int64_t)seqs * (phys_pad / 32) * bits * 32;
+  const int U = bits % 4 == 0 ? 4 : (bits % 2 == 0 ? 2 : 1);
+  const int64_t total = pad8 / 8 * seqs * 32;
   if (total == 0) return YSKN_OK;
-  pack_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, st>>>(reinterpret_cast<const uint4*>(words), layout, phys,
-                                                              phys_pad, seqs, bits, out, total);
+  pack_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, st>>>(words, layout, phys, seqs, bits, U, out, total);
   return cuda_fail(cudaGetLastError(), "pack_kernel");
 }
 
