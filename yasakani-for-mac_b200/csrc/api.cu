@@ -42,12 +42,21 @@ struct DeviceScratch {
 static DeviceScratch g_scratch[64];
 static std::mutex g_scratch_mutex;
 
-static int ensure_scratch(int row_blocks) {
+static int ensure_scratch(int row_blocks, int64_t gemm_bytes) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return fail(YSKN_EINVAL, "device index out of range");
   std::lock_guard<std::mutex> lock(g_scratch_mutex);
   DeviceScratch& d = g_scratch[dev];
+  if (gemm_bytes > d.s.gemm_w_bytes) {
+    void* w = nullptr;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMalloc(&w, (size_t)gemm_bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "gemm workspace");
+    if (d.s.gemm_w) cudaFree(d.s.gemm_w);
+    d.s.gemm_w = reinterpret_cast<int8_t*>(w);
+    d.s.gemm_w_bytes = gemm_bytes;
+  }
   const int64_t want_counters = std::max<int64_t>(3 * (int64_t)row_blocks, 4096);
   const int64_t want_warps = gemv_max_warps();
   if (d.block && d.s.n_counters >= want_counters && d.s.max_warps >= want_warps) return YSKN_OK;
@@ -262,7 +271,7 @@ YSKN_B200_API yskn_b200_matrix* yskn_b200_matrix_create(const uint32_t* d_codes,
       return fail(YSKN_EINVAL, "non-finite weight row scales"), nullptr;
   }
 
-  if (ensure_scratch((int)ceil_div(physical_rows, 8))) return nullptr;
+  if (ensure_scratch((int)ceil_div(physical_rows, 8), ceil_div(physical_rows, 8) * 8 * (int64_t)cols)) return nullptr;
   std::unique_ptr<yskn_b200_matrix> m(new yskn_b200_matrix);
   const int64_t packed = yskn_b200_pack_bytes(physical_rows, cols, bits);
   const size_t off_tau = 8192, off_sin = off_tau + ceil_div(4 * (int64_t)physical_rows, 256) * 256;
@@ -343,6 +352,21 @@ static int check_group(const yskn_b200_matrix* const* mats, int n_mats) {
   return YSKN_OK;
 }
 
+// Skinny inputs stream the codes through the decode GEMV; from GEMM_MIN_M rows
+// the weights are expanded once and multiplied on the tensor cores. Inputs of
+// >= 512 groups stay on the GEMV, whose ordered variant checks every i64 add.
+static int run_sums(const MatrixDev* devs, int n_mats, const int8_t* act, const int32_t* scales, int M,
+                    int64_t* const* out, const int* rows, const GemvScratch& sc, cudaStream_t st) {
+  if (M >= GEMM_MIN_M && devs[0].cols / 512 < 512) {
+    for (int i = 0; i < n_mats; ++i) {
+      if (gemm_workspace_bytes(devs[i]) > sc.gemm_w_bytes) return fail(YSKN_EINVAL, "gemm workspace too small");
+      if (int rc = launch_gemm(devs[i], act, scales, M, out[i], rows[i], sc.gemm_w, st)) return rc;
+    }
+    return YSKN_OK;
+  }
+  return launch_gemv(devs, n_mats, act, scales, M, out, rows, sc, st);
+}
+
 static int finish_checked(int cols, void* stream) {
   // Overflow is only possible with at least 512 groups: |dot| < 2^23, |A| <= 2^31.
   if (cols / 512 < 512) return YSKN_OK;
@@ -363,7 +387,7 @@ YSKN_B200_API int yskn_b200_weighted_sums(const yskn_b200_matrix* const* mats, i
   }
   const GemvScratch* sc = current_scratch();
   if (!sc) return fail(YSKN_EINVAL, "weighted_sums: no matrix was created on this device");
-  if (int rc = launch_gemv(devs, n_mats, d_act, d_scales, M, d_out, rows, *sc, as_stream(stream))) return rc;
+  if (int rc = run_sums(devs, n_mats, d_act, d_scales, M, d_out, rows, *sc, as_stream(stream))) return rc;
   return finish_checked(mats[0]->dev.cols, stream);
 }
 
@@ -378,7 +402,7 @@ YSKN_B200_API int yskn_b200_weighted_sums_prefix(const yskn_b200_matrix* mat, co
   int rows = n_rows;
   const GemvScratch* sc = current_scratch();
   if (!sc) return fail(YSKN_EINVAL, "weighted_sums: no matrix was created on this device");
-  if (int rc = launch_gemv(&mat->dev, 1, d_act, d_scales, M, &d_out, &rows, *sc, as_stream(stream))) return rc;
+  if (int rc = run_sums(&mat->dev, 1, d_act, d_scales, M, &d_out, &rows, *sc, as_stream(stream))) return rc;
   return finish_checked(mat->dev.cols, stream);
 }
 
@@ -456,7 +480,7 @@ YSKN_B200_API int yskn_b200_linear(const yskn_b200_matrix* const* mats, int n_ma
   }
   const GemvScratch* sc = current_scratch();
   if (!sc) return fail(YSKN_EINVAL, "linear: no matrix was created on this device");
-  if (int rc = launch_gemv(devs, n_mats, act, scales, M, ws, rows, *sc, st)) return rc;
+  if (int rc = run_sums(devs, n_mats, act, scales, M, ws, rows, *sc, st)) return rc;
   for (int i = 0; i < n_mats; ++i) {
     const MatrixDev& d = mats[i]->dev;
     if (int rc = launch_restore(ws[i], d.phys, rq, d_inv_rms, d.tau, d.s_out, M, d.phys, d.rows, 0, d_y[i], st))

@@ -48,10 +48,18 @@ struct GemvScratch {
   unsigned* counters;   // [n_counters], zeroed at allocation, reset by the kernel
   int64_t n_counters;
   int64_t max_warps;
+  int8_t* gemm_w;        // dense int8 weights of one matrix for the GEMM path
+  int64_t gemm_w_bytes;
 };
 
 constexpr int GEMV_WARPS = 16;  // warps per persistent GEMV CTA (one CTA per SM)
 int gemv_max_warps();
+
+// Activation rows from which the tcgen05 GEMM (gemm.cu) replaces the GEMV.
+constexpr int GEMM_MIN_M = 64;
+int64_t gemm_workspace_bytes(const MatrixDev& m);  // dense int8 copy of the weights
+int launch_gemm(const MatrixDev& m, const int8_t* act, const int32_t* scales, int M, int64_t* out, int out_rows,
+                int8_t* W, cudaStream_t st);
 
 // Launchers (one per .cu file).
 int launch_gemv(const MatrixDev* mats, int n_mats, const int8_t* act, const int32_t* scales, int M, int64_t* const* out,
