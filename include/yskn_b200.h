@@ -131,6 +131,21 @@ YSKN_B200_API int yskn_b200_restore(int64_t* d_ws, const float* d_row_quantum, c
                                     const yskn_b200_matrix* mat, int M, int rotate_out, int n_rows, int clear_ws,
                                     float* d_y, void* stream);
 
+/* No counterpart in the reference. Same contract and results as
+ * yskn_b200_weighted_sums, for callers that must not have the library allocate
+ * device memory (a serving process that gave nearly all HBM to its own pool at
+ * start-up, or a latency-critical loop in which cudaMalloc/cudaFree could
+ * synchronise the device). It always runs the decode GEMV and keeps its
+ * reduction scratch in a static device array of 5,373,952 bytes, which every GPU
+ * that loads the library holds until exit. Limits (else YSKN_EINVAL): M <= 64,
+ * at most 262,144 physical rows over the call's matrices, cols < 262,144.
+ * All calls on a device share that array: calls that overlap on the GPU race, so
+ * issue them in order on one stream. The first call on each device looks up the
+ * array's device address; make that first call before any stream capture. */
+YSKN_B200_API int yskn_b200_weighted_sums_noalloc(const yskn_b200_matrix* const* mats, int n_mats,
+                                                  const int8_t* d_act, const int32_t* d_scales, int M,
+                                                  int64_t* const* d_out, void* stream);
+
 /* Whole operator for up to 3 matrices sharing one input: quantise x with the first
  * matrix's input signs, weighted sums, restore (with each matrix's output rotation
  * if it has one). Replaces CompressedLinear::project (compressed_linear.rs:254-285)

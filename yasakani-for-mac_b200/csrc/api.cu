@@ -152,6 +152,10 @@ struct yskn_b200_matrix {
   bool has_rot = false;
 };
 
+namespace yskn {
+const MatrixDev* matrix_dev(const yskn_b200_matrix* m) { return m ? &m->dev : nullptr; }
+}  // namespace yskn
+
 static cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

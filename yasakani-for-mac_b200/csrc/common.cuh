@@ -61,6 +61,9 @@ int64_t gemm_workspace_bytes(const MatrixDev& m);  // dense int8 copy of the wei
 int launch_gemm(const MatrixDev& m, const int8_t* act, const int32_t* scales, int M, int64_t* out, int out_rows,
                 int8_t* W, cudaStream_t st);
 
+// The device view of a matrix handle (nullptr for a null handle).
+const MatrixDev* matrix_dev(const yskn_b200_matrix* m);
+
 // Launchers (one per .cu file).
 int launch_gemv(const MatrixDev* mats, int n_mats, const int8_t* act, const int32_t* scales, int M, int64_t* const* out,
                 const int* out_rows, const GemvScratch& scratch, cudaStream_t st);

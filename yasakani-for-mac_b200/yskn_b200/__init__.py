@@ -37,6 +37,7 @@ _SIGNATURES = {
     "yskn_b200_matrix_signs_out": (_vp, [_vp]),
     "yskn_b200_weighted_sums": (_i, [_vp, _i, _vp, _vp, _i, _vp, _vp]),
     "yskn_b200_weighted_sums_prefix": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp]),
+    "yskn_b200_weighted_sums_noalloc": (_i, [_vp, _i, _vp, _vp, _i, _vp, _vp]),
     "yskn_b200_quantize": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp]),
     "yskn_b200_restore": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
     "yskn_b200_linear_work_bytes": (_i64, [_vp, _i, _i]),
@@ -150,6 +151,15 @@ def weighted_sums(mats, act, scales, outs, stream=None):
     outp = (C.c_void_p * len(outs))(*[o.data_ptr() for o in outs])
     check(lib().yskn_b200_weighted_sums(_handles(mats), len(mats), _ptr(act), _ptr(scales), M, outp, _stream(stream)),
           "weighted_sums")
+
+
+def weighted_sums_noalloc(mats, act, scales, outs, stream=None):
+    """yskn_b200_weighted_sums_noalloc: the same sums with the library allocating nothing
+    (scratch in a static device array; M <= 64; calls on one device must not overlap)."""
+    M = act.shape[0]
+    outp = (C.c_void_p * len(outs))(*[o.data_ptr() for o in outs])
+    check(lib().yskn_b200_weighted_sums_noalloc(_handles(mats), len(mats), _ptr(act), _ptr(scales), M, outp,
+                                                _stream(stream)), "weighted_sums_noalloc")
 
 
 def weighted_sums_prefix(mat, act, scales, n_rows, out, stream=None):
