@@ -155,6 +155,31 @@ YSKN_B200_API int64_t yskn_b200_linear_work_bytes(const yskn_b200_matrix* const*
 YSKN_B200_API int yskn_b200_linear(const yskn_b200_matrix* const* mats, int n_mats, const float* d_x, int M,
                                    const float* d_inv_rms, void* d_work, float* const* d_y, void* stream);
 
+/* Quantised-KV decode attention over packed 4-bit trellis rows, with the split
+ * combination, inverse cache rotation and output gate. Replaces launch_q35_atx_pk
+ * (src/q35_atxpk.cu:702-741) followed by q35_combine_kernel (src/q35_kernels.cu:
+ * 1279-1399); scalar semantics Attention::output_head_with (crates/yskn-ref/src/
+ * attention.rs:486-518) with the prefix schedule of attention.rs:207-232.
+ *   d_q, d_gate: bf16 [M][n_query_heads][256] (queries cache-rotated; gate may be NULL,
+ *     then the output is the rounded inverse-rotated head).
+ *   d_k_rows, d_v_rows: u32 [n_kv_heads][capacity][8*kb], MSB-first kb-bit fields
+ *     (kv_codec.rs:447-458); d_k_scales, d_v_scales: f32 [n_kv_heads][capacity].
+ *   d_k_codebook, d_v_codebook: bf16 [n_kv_heads][256], bfloat(reconstruction(state));
+ *   d_v_mean: f32 [n_kv_heads][256] or NULL.
+ * Query row m sees cache rows [0, length - M + m]; the last is its own row. Query head
+ * j reads KV head j / (n_query_heads / n_kv_heads). n_splits 0 = the reference
+ * schedule (31 splits below 4096 rows, else 42), else 1..64 fixed. kb must be 4.
+ * d_attended: optional f32 [M][n_query_heads][256] (before the inverse rotation).
+ * d_out: bf16 [M][n_query_heads][256]. d_work: yskn_b200_kv4_attention_work_bytes(). */
+YSKN_B200_API int64_t yskn_b200_kv4_attention_work_bytes(int M, int n_query_heads, int length, int n_splits);
+YSKN_B200_API int yskn_b200_kv4_attention(const uint16_t* d_q, const uint16_t* d_gate, const uint32_t* d_k_rows,
+                                          const float* d_k_scales, const uint32_t* d_v_rows,
+                                          const float* d_v_scales, const uint16_t* d_k_codebook,
+                                          const uint16_t* d_v_codebook, const float* d_v_mean, int M,
+                                          int n_query_heads, int n_kv_heads, int length, int capacity, int kb,
+                                          int n_splits, void* d_work, float* d_attended, uint16_t* d_out,
+                                          void* stream);
+
 #ifdef __cplusplus
 }
 #endif

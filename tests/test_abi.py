@@ -60,3 +60,20 @@ def test_shape_errors_are_returned_not_trapped():
                                       si.ctypes.data, None)
         assert not h
         assert yskn_b200.last_error()
+
+
+def test_kv_attention_argument_errors_are_returned():
+    import yskn_b200
+    L = yskn_b200.lib()
+    call = lambda M, nq, nk, length, cap, kb, splits: L.yskn_b200_kv4_attention(  # noqa: E731
+        *([None] * 9), M, nq, nk, length, cap, kb, splits, None, None, None, None)
+    assert call(1, 24, 4, 10, 10, 5, 0) == yskn_b200.EINVAL  # kb 5 rows are not supported by this kernel
+    assert call(1, 24, 5, 10, 10, 4, 0) == yskn_b200.EINVAL  # heads not a multiple
+    assert call(1, 36, 4, 10, 10, 4, 0) == yskn_b200.EINVAL  # more than 8 query heads per KV head
+    assert call(1, 24, 4, 11, 10, 4, 0) == yskn_b200.EINVAL  # length beyond capacity
+    assert call(4, 24, 4, 3, 10, 4, 0) == yskn_b200.EINVAL  # more query rows than cache rows
+    assert call(1, 24, 4, 10, 10, 4, 65) == yskn_b200.EINVAL
+    assert call(1, 24, 4, 10, 10, 4, 0) == yskn_b200.EINVAL  # null buffers
+    assert L.yskn_b200_kv4_attention_work_bytes(1, 24, 2048, 0) == 24 * 31 * 258 * 4
+    assert L.yskn_b200_kv4_attention_work_bytes(8, 24, 4100, 0) == 8 * 24 * 42 * 258 * 4
+    assert L.yskn_b200_kv4_attention_work_bytes(1, 24, 100, 65) == -1

@@ -493,4 +493,57 @@ YSKN_B200_API int yskn_b200_linear(const yskn_b200_matrix* const* mats, int n_ma
   return finish_checked(Kc, stream);
 }
 
+static int kv_check(int M, int n_qh, int n_kvh, int length, int capacity, int kb, int n_splits) {
+  if (M < 1 || n_qh < 1 || n_kvh < 1 || n_qh % n_kvh != 0 || n_qh / n_kvh > KV_MAX_GROUP)
+    return fail(YSKN_EINVAL, "kv4 attention: query heads must be a multiple (at most 8x) of the KV heads");
+  if (length < M || capacity < length) return fail(YSKN_EINVAL, "kv4 attention: need M <= length <= capacity");
+  if (kb != 4) return fail(YSKN_EINVAL, "kv4 attention: only kb = 4 packed rows are supported");
+  if (n_splits < 0 || n_splits > KV_MAX_SPLITS) return fail(YSKN_EINVAL, "kv4 attention: n_splits outside [0, 64]");
+  return YSKN_OK;
+}
+
+YSKN_B200_API int64_t yskn_b200_kv4_attention_work_bytes(int M, int n_query_heads, int length, int n_splits) {
+  if (M < 1 || n_query_heads < 1 || length < M || n_splits < 0 || n_splits > KV_MAX_SPLITS) return -1;
+  KvArgs a{};
+  a.M = M;
+  a.length = length;
+  a.n_splits = n_splits;
+  return 4 * kv_partials_floats(M, n_query_heads, kv_max_splits(a));
+}
+
+YSKN_B200_API int yskn_b200_kv4_attention(const uint16_t* d_q, const uint16_t* d_gate, const uint32_t* d_k_rows,
+                                          const float* d_k_scales, const uint32_t* d_v_rows, const float* d_v_scales,
+                                          const uint16_t* d_k_codebook, const uint16_t* d_v_codebook,
+                                          const float* d_v_mean, int M, int n_query_heads, int n_kv_heads, int length,
+                                          int capacity, int kb, int n_splits, void* d_work, float* d_attended,
+                                          uint16_t* d_out, void* stream) {
+  if (int rc = kv_check(M, n_query_heads, n_kv_heads, length, capacity, kb, n_splits)) return rc;
+  if (!d_q || !d_k_rows || !d_k_scales || !d_v_rows || !d_v_scales || !d_k_codebook || !d_v_codebook || !d_work ||
+      !d_out)
+    return fail(YSKN_EINVAL, "kv4 attention: null argument");
+  if (!aligned16(d_k_rows) || !aligned16(d_v_rows) || !aligned16(d_work))
+    return fail(YSKN_EINVAL, "kv4 attention: rows and work area must be 16-byte aligned");
+  KvArgs a{};
+  a.q = d_q;
+  a.gate = d_gate;
+  a.kw = d_k_rows;
+  a.ks = d_k_scales;
+  a.vw = d_v_rows;
+  a.vs = d_v_scales;
+  a.kbase = d_k_codebook;
+  a.vbase = d_v_codebook;
+  a.vmean = d_v_mean;
+  a.partials = reinterpret_cast<float*>(d_work);
+  a.attended = d_attended;
+  a.out = d_out;
+  a.M = M;
+  a.n_qh = n_query_heads;
+  a.n_kvh = n_kv_heads;
+  a.length = length;
+  a.capacity = capacity;
+  a.kb = kb;
+  a.n_splits = n_splits;
+  return launch_kv4_attention(a, as_stream(stream));
+}
+
 }  // extern "C"

@@ -74,6 +74,29 @@ int launch_restore(int64_t* ws, int ws_ld, const float* row_quantum, const float
 int launch_pack(const uint32_t* words, int layout, int phys, int cols, int bits, uint32_t* out, cudaStream_t st);
 int launch_repack_frag(const uint32_t* w, uint32_t* f, int rows, int seqs, int wps, cudaStream_t st);
 
+// Quantised-KV decode attention (kvattn.cu). Query row m of M sees cache rows
+// [0, length - M + m], the last of which is its own (the self term).
+struct KvArgs {
+  const uint16_t* q;      // bf16 [M][n_qh][256], cache-rotated
+  const uint32_t* kw;     // [n_kvh][capacity][8*kb] packed key rows
+  const float* ks;        // [n_kvh][capacity]
+  const uint32_t* vw;     // [n_kvh][capacity][8*kb] packed value rows
+  const float* vs;        // [n_kvh][capacity]
+  const uint16_t* kbase;  // bf16 [n_kvh][256] codebooks
+  const uint16_t* vbase;
+  const float* vmean;     // [n_kvh][256] or nullptr
+  const uint16_t* gate;   // bf16 [M][n_qh][256] or nullptr
+  float* partials;        // kv_partials_floats(...) floats
+  float* attended;        // f32 [M][n_qh][256] before the inverse rotation, or nullptr
+  uint16_t* out;          // bf16 [M][n_qh][256]
+  int M, n_qh, n_kvh, length, capacity, kb, n_splits;  // n_splits 0: 31 below 4096 rows, else 42
+};
+constexpr int KV_MAX_SPLITS = 64;
+constexpr int KV_MAX_GROUP = 8;  // query heads per KV head
+int kv_max_splits(const KvArgs& a);
+int64_t kv_partials_floats(int M, int n_qh, int max_splits);
+int launch_kv4_attention(const KvArgs& a, cudaStream_t st);
+
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 }  // namespace yskn

@@ -42,6 +42,8 @@ _SIGNATURES = {
     "yskn_b200_restore": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
     "yskn_b200_linear_work_bytes": (_i64, [_vp, _i, _i]),
     "yskn_b200_linear": (_i, [_vp, _i, _vp, _i, _vp, _vp, _vp, _vp]),
+    "yskn_b200_kv4_attention_work_bytes": (_i64, [_i, _i, _i, _i]),
+    "yskn_b200_kv4_attention": (_i, [_vp] * 9 + [_i] * 7 + [_vp] * 4),
 }
 
 _lib = None
@@ -199,3 +201,19 @@ def repack_warp_to_frag(words, frag, rows, seqs, wps, stream=None):
 def pack(words, layout, physical_rows, cols, bits, out, stream=None):
     check(lib().yskn_b200_pack(_ptr(words), LAYOUTS.get(layout, layout), physical_rows, cols, bits, _ptr(out),
                                _stream(stream)), "pack")
+
+
+def kv4_attention_work_bytes(M, n_query_heads, length, n_splits=0):
+    return lib().yskn_b200_kv4_attention_work_bytes(M, n_query_heads, length, n_splits)
+
+
+def kv4_attention(q, k_rows, k_scales, v_rows, v_scales, k_codebook, v_codebook, length, work, out, gate=None,
+                  v_mean=None, attended=None, n_splits=0, kb=4, stream=None):
+    """q, gate, out: bf16 [M][n_qh][256] (passed as int16/bfloat16 tensors); k_rows/v_rows:
+    int32 [n_kvh][capacity][8*kb]; scales f32 [n_kvh][capacity]; codebooks bf16 [n_kvh][256]."""
+    M, n_qh = q.shape[0], q.shape[1]
+    n_kvh, capacity = k_rows.shape[0], k_rows.shape[1]
+    check(lib().yskn_b200_kv4_attention(_ptr(q), _ptr(gate), _ptr(k_rows), _ptr(k_scales), _ptr(v_rows),
+                                        _ptr(v_scales), _ptr(k_codebook), _ptr(v_codebook), _ptr(v_mean), M, n_qh,
+                                        n_kvh, length, capacity, kb, n_splits, _ptr(work), _ptr(attended),
+                                        _ptr(out), _stream(stream)), "kv4_attention")
