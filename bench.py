@@ -37,6 +37,9 @@ LAYER = [("q_proj", 12288, 5120), ("k_proj", 1024, 5120), ("v_proj", 1024, 5120)
          ("gate_proj", 17408, 5120), ("up_proj", 17408, 5120), ("down_proj", 5120, 17408)]
 CALLS = [["q_proj", "k_proj", "v_proj"], ["o_proj"], ["in_proj_qkv", "in_proj_z"], ["out_proj"],
          ["gate_proj", "up_proj"], ["down_proj"]]
+# DRAM bytes (read + write) of the six weighted-sums launches of one step, from one ncu
+# capture of this workload (profiles/gemv_kernel_layer_bits8.md); None where not captured.
+GEMV_TRAFFIC = {(8, 1): 244_913_920}
 METRIC = "compressed GEMV HBM TB/s (one hybrid layer's linear set, batch-1 decode)"
 UNIT = "TB/s"
 
@@ -344,7 +347,7 @@ def run_b200(args, rank, world, local_rank):
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "i8", "data": "synthetic", "config": config(args),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None,
+                         "frac": achieved / peak, "traffic": GEMV_TRAFFIC.get((args.bits, M)),
                          "kernel": "gemv_kernel (weighted sums; the 6 launches of one step, each timed alone)",
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
             "cpu_baseline": cpu,
