@@ -180,6 +180,36 @@ def test_linear_27b_shape_matches_oracle(cuda, bits):
         assert yskn_b200.status() == 0
 
 
+@pytest.mark.parametrize("M,cols", [(1, 2048), (3, 2048), (16, 2048), (17, 2048), (8, 17408)])
+def test_linear_fused_and_staged_paths(cuda, M, cols):
+    """Three matrices sharing one input, two with an output rotation and one without
+    (rows < physical rows), with 1/rms, bit-exact. M <= 16 with the activations in
+    shared memory runs the one-launch fused operator; M = 17 and (8, 17408) run the
+    staged quantise / sums / restore launches. Twice in a row, so the per-block
+    counters of the fused restore are seen to reset."""
+    import torch
+    import yskn_b200
+    specs = [(1024, 1024, True), (512, 512, True), (300, 304, False)]
+    si = O.signs("mulberry32_7919_13", 7, 0, cols)
+    mats, keep, refs = [], [], []
+    x = fixtures.normal(900 + M, M * cols).reshape(M, cols)
+    inv_rms = (1.0 + 0.01 * np.arange(M)).astype(np.float32)
+    for i, (rows, phys, rot) in enumerate(specs):
+        words, lut16, sc16 = fixtures.model_matrix(rows, cols, 8, 500 + i, physical_rows=phys)
+        so = O.signs("mulberry32_7919_13", 7, cols + 4096 * i, phys) if rot else None
+        dw = _dev(words.view(np.int32))
+        mats.append(yskn_b200.Matrix(dw, "warp", rows, phys, cols, 8, lut16, sc16, si, so))
+        keep.append(dw)
+        refs.append(O.linear(words, "warp", phys, cols, 8, lut16, sc16, x, si, so, inv_rms, rows))
+    work = torch.empty(yskn_b200.linear_work_bytes(mats, M), dtype=torch.uint8, device="cuda")
+    for _ in range(2):
+        ys = [torch.full((M, r), float("nan"), dtype=torch.float32, device="cuda") for r, _, _ in specs]
+        yskn_b200.linear(mats, _dev(x), work, ys, inv_rms=_dev(inv_rms))
+        for y, ref in zip(ys, refs):
+            assert np.array_equal(y.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+        assert yskn_b200.status() == 0
+
+
 def test_overflow_is_an_error_and_the_library_recovers(cuda):
     """crates/yskn-engine/tests/linear.rs:277-308."""
     import torch

@@ -57,7 +57,8 @@ static int ensure_scratch(int row_blocks, int64_t gemm_bytes) {
     d.s.gemm_w = reinterpret_cast<int8_t*>(w);
     d.s.gemm_w_bytes = gemm_bytes;
   }
-  const int64_t want_counters = std::max<int64_t>(3 * (int64_t)row_blocks, 4096);
+  // Row-block counters of up to 3 matrices per call, plus one per 512-row block for the fused restore.
+  const int64_t want_counters = std::max<int64_t>(4 * (int64_t)row_blocks, 4096);
   const int64_t want_warps = gemv_max_warps();
   if (d.block && d.s.n_counters >= want_counters && d.s.max_warps >= want_warps) return YSKN_OK;
   const int64_t n_counters = std::max(want_counters, d.s.n_counters);
@@ -472,7 +473,6 @@ YSKN_B200_API int yskn_b200_linear(const yskn_b200_matrix* const* mats, int n_ma
   float* rq = reinterpret_cast<float*>(base + w.rq);
   const int Kc = mats[0]->dev.cols;
   cudaStream_t st = as_stream(stream);
-  if (int rc = launch_quantize(d_x, mats[0]->dev.s_in, M, Kc, act, alpha, scales, rq, st)) return rc;
   MatrixDev devs[3];
   int rows[3];
   int64_t* ws[3];
@@ -484,6 +484,11 @@ YSKN_B200_API int yskn_b200_linear(const yskn_b200_matrix* const* mats, int n_ma
   }
   const GemvScratch* sc = current_scratch();
   if (!sc) return fail(YSKN_EINVAL, "linear: no matrix was created on this device");
+  if (fused_linear_fits(M, Kc)) {  // decode: one launch for the whole operator
+    if (int rc = launch_linear_fused(devs, n_mats, d_x, M, d_inv_rms, ws, d_y, *sc, st)) return rc;
+    return finish_checked(Kc, stream);
+  }
+  if (int rc = launch_quantize(d_x, mats[0]->dev.s_in, M, Kc, act, alpha, scales, rq, st)) return rc;
   if (int rc = run_sums(devs, n_mats, act, scales, M, ws, rows, *sc, st)) return rc;
   for (int i = 0; i < n_mats; ++i) {
     const MatrixDev& d = mats[i]->dev;

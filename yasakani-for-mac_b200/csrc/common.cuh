@@ -67,6 +67,11 @@ const MatrixDev* matrix_dev(const yskn_b200_matrix* m);
 // Launchers (one per .cu file).
 int launch_gemv(const MatrixDev* mats, int n_mats, const int8_t* act, const int32_t* scales, int M, int64_t* const* out,
                 const int* out_rows, const GemvScratch& scratch, cudaStream_t st);
+// The whole decode operator in one launch (quantise, sums, restore): M <= 16 rows
+// whose activations fit in shared memory next to the table, fewer than 512 groups.
+bool fused_linear_fits(int M, int Kc);
+int launch_linear_fused(const MatrixDev* mats, int n_mats, const float* x, int M, const float* inv_rms,
+                        int64_t* const* ws, float* const* y, const GemvScratch& scratch, cudaStream_t st);
 int launch_quantize(const float* x, const int8_t* signs, int M, int Kc, int8_t* act, float* alpha, int32_t* scales,
                     float* row_quantum, cudaStream_t st);
 int launch_restore(int64_t* ws, int ws_ld, const float* row_quantum, const float* inv_rms, const float* tau,

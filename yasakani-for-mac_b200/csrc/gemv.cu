@@ -39,7 +39,7 @@
 #include <algorithm>
 #include <mutex>
 
-#include "common.cuh"
+#include "quant.cuh"
 
 namespace yskn {
 
@@ -59,6 +59,12 @@ struct GemvSeg {
   int cta_begin;       // first CTA of this segment
   int n_ctas;
   int base, rem;       // balanced unit ranges of the segment's warps
+  // Fused operator only: restore into y instead of returning int64 sums.
+  const float* tau;
+  const int8_t* s_out;     // output rotation signs (sums go to `out` first), or nullptr
+  float* y;                // f32 [mv][y_rows]
+  int y_rows;
+  unsigned* blk_counters;  // one per 512-row block (rotated restore), zero between launches
 };
 
 struct GemvParams {
@@ -73,6 +79,10 @@ struct GemvParams {
   int checked;
   long long* partials;  // [2 * warps][32 lanes][4] i64
   unsigned* err;
+  // Fused operator only: f32 input rows, input signs, optional 1/rms per row.
+  const float* x;
+  const int8_t* s_in;
+  const float* inv_rms;
 };
 
 template <int BITS>
@@ -200,7 +210,13 @@ struct Ranges {
 
 // ACT_SMEM: activations and scales staged once per CTA in shared memory after
 // the table (rows padded by 16 bytes so the 8 token rows fall in different banks).
-template <int BITS, bool M1, bool ACT_SMEM>
+// FUSED (implies ACT_SMEM): the whole operator. Every CTA quantises the f32 input
+// rows itself while it builds the table (the same device functions as the
+// standalone quantiser, so the same bits), and results leave as restored f32:
+// rows without an output rotation are restored where they are stored; with a
+// rotation the int64 sums go to `out` and the warp that completes the last 8-row
+// block of a 512-row block (a counter per 512-row block) restores and rotates it.
+template <int BITS, bool M1, bool ACT_SMEM, bool FUSED>
 __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(16) uint8_t s_lut[];
   // Which matrix this CTA serves.
@@ -211,6 +227,8 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   const int G = p.G, Kc = p.Kc, act_ld = Kc + 16;
   int8_t* s_act = reinterpret_cast<int8_t*>(s_lut + LUT_COPY_BYTES + LUT_RAW_BYTES);
   int32_t* s_scale = reinterpret_cast<int32_t*>(s_lut + LUT_COPY_BYTES + LUT_RAW_BYTES + (size_t)p.mv * act_ld);
+  float* s_alpha = reinterpret_cast<float*>(s_scale + p.mv * G);  // FUSED: group scales
+  float* s_rq = s_alpha + p.mv * G;                                // FUSED: row quanta
 
   // 16 copies of the int8-pair table: slot s (32 bytes) holds entry s 16 times.
   // The raw 8 KiB table is staged once (one 16-byte load per thread), then each
@@ -220,7 +238,16 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   {
     static_assert(GEMV_WARPS * 32 == 512, "the fill assumes 512 threads");
     reinterpret_cast<uint4*>(s_raw)[threadIdx.x] = __ldg(reinterpret_cast<const uint4*>(S.lut) + threadIdx.x);
-    if (ACT_SMEM) {
+    if (FUSED) {
+      bool bad = false;
+      for (int item = warp; item < p.mv * G; item += GEMV_WARPS) {
+        const int m = item / G, g = item - m * G;
+        const float a = quantize_group512(p.x + (size_t)m * Kc + g * 512, p.s_in + g * 512,
+                                          s_act + (size_t)m * act_ld + g * 512, lane, bad);
+        if (lane == 0) s_alpha[item] = a;
+      }
+      if (blockIdx.x == 0 && __any_sync(0xffffffffu, bad) && lane == 0) raise_device_error(p.err, DERR_NONFINITE);
+    } else if (ACT_SMEM) {
       // Batches of 8 independent 16-byte loads per thread before their stores.
       const int vec = Kc / 16, total = p.mv * vec;
       for (int base = 0; base < total; base += 8 * GEMV_WARPS * 32) {
@@ -246,6 +273,15 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
     const uint32_t h = s_raw[k >> 1];
     const uint32_t v = h | (h << 16);
     reinterpret_cast<uint4*>(s_lut)[k] = make_uint4(v, v, v, v);
+  }
+  if (FUSED) {  // the rows' common integer grids (compressed_linear.rs:113-128)
+    for (int item = threadIdx.x; item < p.mv * G; item += blockDim.x) {
+      const int m = item / G;
+      float mx = 0.0f;
+      for (int g = 0; g < G; ++g) mx = fmaxf(mx, s_alpha[m * G + g]);
+      s_scale[item] = integer_group_scale(s_alpha[item], row_grid_multiplier(mx));
+      if (item == m * G) s_rq[m] = row_quantum_of(mx);
+    }
   }
   __syncthreads();
 
@@ -279,6 +315,46 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   int rb = u / G, g = u % G;
   long long acc[4] = {0, 0, 0, 0};
   bool overflow = false;
+  bool bad = false;  // FUSED: non-finite restored values
+
+  // Final sums of rows row0, row0 + 1 for tokens n, n + 8 (the C fragment).
+  auto emit = [&](const long long (&v)[4], int row0) {
+    if (!FUSED || S.s_out) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int tok = n + (i >> 1) * 8, row = row0 + (i & 1);
+        if (tok < p.mv && row < S.out_rows) S.out[(size_t)tok * S.out_ld + row] = v[i];
+      }
+    }
+    if constexpr (FUSED) {
+      if (!S.s_out) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int tok = n + (i >> 1) * 8, row = row0 + (i & 1);
+          if (tok < p.mv && row < S.y_rows) {
+            const float t = restore_value(v[i], s_rq[tok], p.inv_rms ? p.inv_rms + tok : nullptr, __ldg(S.tau + row));
+            bad |= !finite32(t) || (p.inv_rms && !finite32(p.inv_rms[tok]));
+            S.y[(size_t)tok * S.y_rows + row] = t;
+          }
+        }
+      } else {
+        // This 8-row block is final; the last of the 64 in its 512-row block restores the block.
+        __threadfence();
+        __syncwarp();
+        const int blk = rb >> 6;
+        unsigned prev = 0;
+        if (lane == 0) prev = atomicAdd(S.blk_counters + blk, 1u);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        if (prev == 63u) {
+          __threadfence();
+          for (int tok = 0; tok < p.mv; ++tok)
+            restore_block512(S.out + (size_t)tok * S.out_ld, s_rq[tok], p.inv_rms ? p.inv_rms + tok : nullptr, S.tau,
+                             S.s_out, blk * 512, S.y_rows, S.y + (size_t)tok * S.y_rows, lane, bad);
+          if (lane == 0) S.blk_counters[blk] = 0u;
+        }
+      }
+    }
+  };
   // Units are consecutive in memory: (rb, g) -> (rb, g+1) -> (rb+1, 0) is a
   // stride of two tiles, so the walk needs no division.
   const uint32_t* ptr = S.codes + ((size_t)rb * p.S + 2 * g) * TILE_WORDS;
@@ -323,11 +399,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
       const int first = rb * G, last = first + G - 1;
       const bool sole = p.checked || (my_begin <= first && u_end > last);
       if (sole) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int tok = n + (i >> 1) * 8, row = row0 + (i & 1);
-          if (tok < p.mv && row < S.out_rows) S.out[(size_t)tok * S.out_ld + row] = acc[i];
-        }
+        emit(acc, row0);
       } else {
         // Split row block: publish this warp's partial; the last of the
         // contributing warps (consecutive, all non-empty) adds them up.
@@ -352,12 +424,8 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
 #pragma unroll
             for (int i = 0; i < 4; ++i) sum[i] += __ldcg(src + i);
           }
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int tok = n + (i >> 1) * 8, row = row0 + (i & 1);
-            if (tok < p.mv && row < S.out_rows) S.out[(size_t)tok * S.out_ld + row] = sum[i];
-          }
           if (lane == 0) S.counters[rb] = 0u;
+          emit(sum, row0);
         }
       }
 #pragma unroll
@@ -372,6 +440,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
     if (step(ub, ua)) break;
   }
   if (p.checked && __any_sync(0xffffffffu, overflow) && lane == 0) raise_device_error(p.err, DERR_OVERFLOW);
+  if (FUSED && __any_sync(0xffffffffu, bad) && lane == 0) raise_device_error(p.err, DERR_NONFINITE);
   (void)nw;
 }
 
@@ -390,35 +459,54 @@ int gemv_max_warps() { return (sm_count() + 8) * GEMV_WARPS; }
 
 constexpr int SMEM_LIMIT = 232448;  // opt-in shared memory per CTA on B200
 
-static size_t act_smem_bytes(int mv, int Kc) { return (size_t)mv * (Kc + 16) + 4 * (size_t)mv * (Kc / 512); }
+static size_t act_smem_bytes(int mv, int Kc, bool fused) {
+  const size_t G = Kc / 512;
+  return (size_t)mv * (Kc + 16) + 4 * (size_t)mv * G + (fused ? 4 * (size_t)mv * G + 64 : 0);
+}
 static size_t table_smem_bytes() { return LUT_COPY_BYTES + LUT_RAW_BYTES; }
 
-template <int BITS, bool M1, bool ACT_SMEM>
+template <int BITS, bool M1, bool ACT_SMEM, bool FUSED>
 static int launch_one(const GemvParams& p, int grid, cudaStream_t st) {
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(gemv_kernel<BITS, M1, ACT_SMEM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    SMEM_LIMIT);
+    attr_err = cudaFuncSetAttribute(gemv_kernel<BITS, M1, ACT_SMEM, FUSED>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT);
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "gemv_kernel attributes");
-  const size_t smem = table_smem_bytes() + (ACT_SMEM ? act_smem_bytes(p.mv, p.Kc) : 0);
-  gemv_kernel<BITS, M1, ACT_SMEM><<<grid, GEMV_WARPS * 32, smem, st>>>(p);
+  const size_t smem = table_smem_bytes() + (ACT_SMEM ? act_smem_bytes(p.mv, p.Kc, FUSED) : 0);
+  gemv_kernel<BITS, M1, ACT_SMEM, FUSED><<<grid, GEMV_WARPS * 32, smem, st>>>(p);
   return cuda_fail(cudaGetLastError(), "gemv_kernel");
 }
 
 template <int BITS>
-static int launch_bits(const GemvParams& p, int grid, cudaStream_t st) {
-  const bool fits = table_smem_bytes() + act_smem_bytes(p.mv, p.Kc) <= (size_t)SMEM_LIMIT;
-  if (p.mv == 1) return fits ? launch_one<BITS, true, true>(p, grid, st) : launch_one<BITS, true, false>(p, grid, st);
-  return fits ? launch_one<BITS, false, true>(p, grid, st) : launch_one<BITS, false, false>(p, grid, st);
+static int launch_bits(const GemvParams& p, int grid, bool fused, cudaStream_t st) {
+  if (fused)
+    return p.mv == 1 ? launch_one<BITS, true, true, true>(p, grid, st) : launch_one<BITS, false, true, true>(p, grid, st);
+  const bool fits = table_smem_bytes() + act_smem_bytes(p.mv, p.Kc, false) <= (size_t)SMEM_LIMIT;
+  if (p.mv == 1)
+    return fits ? launch_one<BITS, true, true, false>(p, grid, st) : launch_one<BITS, true, false, false>(p, grid, st);
+  return fits ? launch_one<BITS, false, true, false>(p, grid, st) : launch_one<BITS, false, false, false>(p, grid, st);
 }
 
-int launch_gemv(const MatrixDev* mats, int n_mats, const int8_t* act, const int32_t* scales, int M, int64_t* const* out,
-                const int* out_rows, const GemvScratch& scratch, cudaStream_t st) {
-  const int Kc = mats[0].cols, G = Kc / 512, bits = mats[0].bits;
+static int launch_bits_any(int bits, const GemvParams& p, int grid, bool fused, cudaStream_t st) {
+  switch (bits) {
+    case 4: return launch_bits<4>(p, grid, fused, st);
+    case 5: return launch_bits<5>(p, grid, fused, st);
+    case 6: return launch_bits<6>(p, grid, fused, st);
+    case 7: return launch_bits<7>(p, grid, fused, st);
+    default: return launch_bits<8>(p, grid, fused, st);
+  }
+}
+
+// Segments, CTA split and scratch for one call. The CTAs (one per SM) are split
+// between the matrices in proportion to their units by largest remainders, so the
+// grid never exceeds the SM count (a CTA beyond it would run as a second wave).
+static int build_params(const MatrixDev* mats, int n_mats, const int* out_rows, const GemvScratch& scratch,
+                        bool fused, GemvParams& p, int& grid) {
+  const int Kc = mats[0].cols, G = Kc / 512;
   const int sms = sm_count();
-  GemvParams p{};
+  p = GemvParams{};
   p.n_seg = n_mats;
   p.G = G;
   p.S = Kc / 256;
@@ -426,11 +514,43 @@ int launch_gemv(const MatrixDev* mats, int n_mats, const int8_t* act, const int3
   p.checked = G >= 512 ? 1 : 0;
   p.partials = scratch.partials;
   p.err = device_error_word();
-  // Split the CTAs between the matrices in proportion to their units.
   int64_t total = 0;
   for (int i = 0; i < n_mats; ++i) total += (int64_t)(mats[i].phys_pad8 / 8) * G;
   if (total >= (int64_t)1 << 31) return fail(YSKN_EINVAL, "gemv: matrix too large for one call");
-  int grid = 0;
+  int64_t want[GEMV_MAX_SEG];
+  if (p.checked) {
+    for (int i = 0; i < n_mats; ++i) want[i] = ceil_div(mats[i].phys_pad8 / 8, GEMV_WARPS);  // a warp per row block
+  } else {
+    const int budget = std::max(sms, n_mats);
+    double frac[GEMV_MAX_SEG];
+    int64_t used = 0;
+    for (int i = 0; i < n_mats; ++i) {
+      const int64_t units = (int64_t)(mats[i].phys_pad8 / 8) * G;
+      const double exact = (double)budget * units / total;
+      want[i] = std::max<int64_t>(1, (int64_t)exact);
+      frac[i] = exact - (double)(int64_t)exact;
+      used += want[i];
+    }
+    while (used < budget) {  // hand the remaining CTAs to the largest remainders
+      int best = 0;
+      for (int i = 1; i < n_mats; ++i)
+        if (frac[i] > frac[best]) best = i;
+      ++want[best];
+      frac[best] = -1.0;
+      ++used;
+    }
+    while (used > budget) {  // only when a tiny segment was lifted to one CTA
+      int big = 0;
+      for (int i = 1; i < n_mats; ++i)
+        if (want[i] > want[big]) big = i;
+      --want[big];
+      --used;
+    }
+    for (int i = 0; i < n_mats; ++i)  // no more CTAs than unit runs of 16 warps
+      want[i] = std::max<int64_t>(1, std::min<int64_t>(want[i], ceil_div((int64_t)(mats[i].phys_pad8 / 8) * G,
+                                                                          GEMV_WARPS)));
+  }
+  grid = 0;
   unsigned* cnt = scratch.counters;
   for (int i = 0; i < n_mats; ++i) {
     GemvSeg& s = p.seg[i];
@@ -442,36 +562,66 @@ int launch_gemv(const MatrixDev* mats, int n_mats, const int8_t* act, const int3
     s.out_ld = out_rows[i];
     s.counters = cnt;
     cnt += s.row_blocks;
-    int64_t want = std::max<int64_t>(1, (int64_t)((double)sms * s.units / total + 0.5));
-    want = std::max<int64_t>(1, std::min<int64_t>(want, ceil_div(s.units, GEMV_WARPS)));
-    if (p.checked) want = ceil_div(s.row_blocks, GEMV_WARPS);  // one warp per row block, no partials
+    if (fused && mats[i].s_out) {
+      s.blk_counters = cnt;
+      cnt += s.row_blocks / 64;
+    }
     s.cta_begin = grid;
-    s.n_ctas = (int)want;
-    const int64_t nw = want * GEMV_WARPS;
+    s.n_ctas = (int)want[i];
+    const int64_t nw = want[i] * GEMV_WARPS;
     s.base = (int)(s.units / nw);
     s.rem = (int)(s.units % nw);
-    grid += (int)want;
+    grid += (int)want[i];
   }
   if ((int64_t)(cnt - scratch.counters) > scratch.n_counters ||
       (!p.checked && (int64_t)grid * GEMV_WARPS > scratch.max_warps))
     return fail(YSKN_EINVAL, "gemv: scratch too small for this call");
+  return YSKN_OK;
+}
+
+int launch_gemv(const MatrixDev* mats, int n_mats, const int8_t* act, const int32_t* scales, int M, int64_t* const* out,
+                const int* out_rows, const GemvScratch& scratch, cudaStream_t st) {
+  const int Kc = mats[0].cols, G = Kc / 512;
+  GemvParams p;
+  int grid = 0;
+  if (int rc = build_params(mats, n_mats, out_rows, scratch, false, p, grid)) return rc;
   for (int m0 = 0; m0 < M; m0 += 16) {
     const int mv = std::min(16, M - m0);
     p.act = act + (int64_t)m0 * Kc;
     p.scales = scales + (int64_t)m0 * G;
     p.mv = mv;
     for (int i = 0; i < n_mats; ++i) p.seg[i].out = out[i] + (int64_t)m0 * out_rows[i];
-    int rc;
-    switch (bits) {
-      case 4: rc = launch_bits<4>(p, grid, st); break;
-      case 5: rc = launch_bits<5>(p, grid, st); break;
-      case 6: rc = launch_bits<6>(p, grid, st); break;
-      case 7: rc = launch_bits<7>(p, grid, st); break;
-      default: rc = launch_bits<8>(p, grid, st); break;
-    }
-    if (rc) return rc;
+    if (int rc = launch_bits_any(mats[0].bits, p, grid, false, st)) return rc;
   }
   return YSKN_OK;
+}
+
+bool fused_linear_fits(int M, int Kc) {
+  return M >= 1 && M <= 16 && Kc / 512 < 512 &&
+         table_smem_bytes() + act_smem_bytes(M, Kc, true) <= (size_t)SMEM_LIMIT;
+}
+
+int launch_linear_fused(const MatrixDev* mats, int n_mats, const float* x, int M, const float* inv_rms,
+                        int64_t* const* ws, float* const* y, const GemvScratch& scratch, cudaStream_t st) {
+  if (!fused_linear_fits(M, mats[0].cols)) return fail(YSKN_EINVAL, "fused linear: shape out of range");
+  int out_rows[GEMV_MAX_SEG];
+  for (int i = 0; i < n_mats; ++i) out_rows[i] = mats[i].phys;
+  GemvParams p;
+  int grid = 0;
+  if (int rc = build_params(mats, n_mats, out_rows, scratch, true, p, grid)) return rc;
+  p.x = x;
+  p.s_in = mats[0].s_in;
+  p.inv_rms = inv_rms;
+  p.mv = M;
+  for (int i = 0; i < n_mats; ++i) {
+    GemvSeg& s = p.seg[i];
+    s.out = ws[i];
+    s.tau = mats[i].tau;
+    s.s_out = mats[i].s_out;
+    s.y = y[i];
+    s.y_rows = mats[i].rows;
+  }
+  return launch_bits_any(mats[0].bits, p, grid, true, st);
 }
 
 }  // namespace yskn

@@ -1,0 +1,142 @@
+// Device functions of the operator prologue (activation quantiser) and epilogue
+// (restore + output rotation), shared by the standalone kernels (quant.cu) and the
+// fused decode operator (gemv.cu), so both produce the same bits.
+//
+// Bit-exact restatements of the reference's scalar order (docs/spec/
+// 02_COMPRESSED_LINEAR.md:84-101,129-241; crates/yskn-ref/src/compressed_linear.rs:
+// 14-29,57-135,288-370). Every binary32 operation is an explicit round-to-nearest
+// intrinsic, so no multiply-add contraction can occur (the reference build relies on
+// --fmad=false, CMakeLists.txt:47-51).
+//
+// One warp transforms one 512-element block: lane l holds elements 16l..16l+15. The
+// Hadamard butterflies run in ascending stride order as the spec requires: strides
+// 1..8 inside a lane, 16..256 across lanes (shfl_xor with lane bit stride/16). Each
+// element's value after every stage is the same binary32 value the scalar loop
+// produces, so the parallel transform is bit-identical.
+#pragma once
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+
+namespace yskn {
+
+__device__ __forceinline__ void hadamard512_warp(float (&v)[16], int lane) {
+#pragma unroll
+  for (int stride = 1; stride < 16; stride <<= 1) {
+#pragma unroll
+    for (int base = 0; base < 16; base += 2 * stride) {
+#pragma unroll
+      for (int o = 0; o < stride; ++o) {
+        const float lower = v[base + o], upper = v[base + o + stride];
+        v[base + o] = __fadd_rn(lower, upper);
+        v[base + o + stride] = __fsub_rn(lower, upper);
+      }
+    }
+  }
+#pragma unroll
+  for (int mask = 1; mask < 32; mask <<= 1) {
+    const bool upper_half = (lane & mask) != 0;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const float other = __shfl_xor_sync(0xffffffffu, v[e], mask);
+      v[e] = upper_half ? __fsub_rn(other, v[e]) : __fadd_rn(v[e], other);
+    }
+  }
+}
+
+__device__ __forceinline__ bool finite32(float x) { return (__float_as_uint(x) & 0x7f800000u) != 0x7f800000u; }
+
+// One 512-column group of one activation row (compressed_linear.rs:57-112): x*s_in,
+// H512, half(v * 1/sqrt(512)), alpha = max|v|/127, q = clamp(rne(v/alpha), +-127).
+// xg, sg: the group's 512 inputs and input signs; the lane's 16 int8 go to dst
+// (16-byte aligned). Returns alpha on every lane; `bad` collects non-finite values.
+__device__ __forceinline__ float quantize_group512(const float* __restrict__ xg, const int8_t* __restrict__ sg,
+                                                   int8_t* dst, int lane, bool& bad) {
+  float v[16];
+  const float4* xp = reinterpret_cast<const float4*>(xg + lane * 16);
+  const int4 sp = __ldg(reinterpret_cast<const int4*>(sg + lane * 16));
+  const int8_t* sb = reinterpret_cast<const int8_t*>(&sp);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 f = __ldg(xp + q);
+    v[4 * q + 0] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+  }
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    bad |= !finite32(v[e]);
+    v[e] = __fmul_rn(v[e], (float)sb[e]);
+  }
+  hadamard512_warp(v, lane);
+  float mx = 0.0f;
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    v[e] = __half2float(__float2half_rn(__fmul_rn(v[e], kHadamardNorm)));
+    bad |= !finite32(v[e]);
+    mx = fmaxf(mx, fabsf(v[e]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const float scale = __fdiv_rn(mx, 127.0f);
+  uint32_t packed[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      int r = scale > 0.0f ? __float2int_rn(__fdiv_rn(v[4 * q + b], scale)) : 0;
+      r = max(-127, min(127, r));
+      w |= (uint32_t)(r & 0xff) << (8 * b);
+    }
+    packed[q] = w;
+  }
+  *reinterpret_cast<uint4*>(dst + lane * 16) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+  return scale;
+}
+
+// The row's common 2^24 integer grid (compressed_linear.rs:113-128) from its group
+// scales: multiplier 2^24 / max alpha, and row_quantum = max alpha * 2^-24.
+__device__ __forceinline__ float row_grid_multiplier(float max_alpha) {
+  return max_alpha > 0.0f ? __fdiv_rn(16777216.0f, max_alpha) : 0.0f;
+}
+__device__ __forceinline__ int32_t integer_group_scale(float alpha, float mult) {
+  return __float2int_rn(__fmul_rn(alpha, mult));
+}
+__device__ __forceinline__ float row_quantum_of(float max_alpha) {
+  return __fmul_rn(max_alpha, 5.9604644775390625e-08f /* 2^-24 */);
+}
+
+// f32(ws) * row_quantum (* inv_rms) * tau (compressed_linear.rs:288-312).
+__device__ __forceinline__ float restore_value(long long ws, float rq, const float* inv_rms_m, float tau) {
+  float t = __fmul_rn(__ll2float_rn(ws), rq);
+  if (inv_rms_m) t = __fmul_rn(t, *inv_rms_m);
+  return __fmul_rn(t, tau);
+}
+
+// One 512-row block of one token (compressed_linear.rs:313-348): restore, H512,
+// * 1/sqrt(512), * s_out; rows >= n_rows are not stored. ws is read through L2
+// (other SMs may have written it in the same launch).
+__device__ __forceinline__ void restore_block512(const int64_t* wsr, float rq, const float* inv_rms_m,
+                                                 const float* __restrict__ tau, const int8_t* __restrict__ s_out,
+                                                 int r0, int n_rows, float* __restrict__ yr, int lane, bool& bad) {
+  float v[16];
+  const int rl = r0 + lane * 16;
+  if (inv_rms_m) bad |= !finite32(*inv_rms_m);
+#pragma unroll
+  for (int e = 0; e < 16; e += 2) {
+    const longlong2 w = __ldcg(reinterpret_cast<const longlong2*>(wsr + rl + e));
+    v[e] = restore_value(w.x, rq, inv_rms_m, __ldg(tau + rl + e));
+    v[e + 1] = restore_value(w.y, rq, inv_rms_m, __ldg(tau + rl + e + 1));
+    bad |= !finite32(v[e]) | !finite32(v[e + 1]);
+  }
+  hadamard512_warp(v, lane);
+  const int4 sp = __ldg(reinterpret_cast<const int4*>(s_out + rl));
+  const int8_t* sb = reinterpret_cast<const int8_t*>(&sp);
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    const float t = __fmul_rn(__fmul_rn(v[e], kHadamardNorm), (float)sb[e]);
+    bad |= !finite32(t);
+    if (rl + e < n_rows) yr[rl + e] = t;
+  }
+}
+
+}  // namespace yskn
