@@ -180,6 +180,30 @@ YSKN_B200_API int yskn_b200_kv4_attention(const uint16_t* d_q, const uint16_t* d
                                           int n_splits, void* d_work, float* d_attended, uint16_t* d_out,
                                           void* stream);
 
+/* Quantised-KV row encoder for packed (trellis) rows: replaces launch_tb_fast ->
+ * tbf_vit_kernel / tbf2_vit_kernel + tbf_sel_kernel (src/kvq_fast.cuh:150-249,
+ * src/kvq_vit2.cuh:217); scalar spec encode_packed (crates/yskn-ref/src/kv_codec.rs:
+ * 408-441) for groups that are packable (mode 0, no guard, no basis; kv_profile.rs:
+ * 251-286). Bit-identical words and scales.
+ *   d_rows: f32 [n_rows][256] cache-rotated rows; d_row_group: i32 [n_rows] profile
+ *     group of each row (layer, head, side); d_tables: i16 [n_groups][256] table codes
+ *     of each group's trellis table; d_gains: f32 [n_groups] that table's gain;
+ *   d_means: f32 [n_groups][256] decoded group means, or NULL; d_has_mean: u8 [n_groups]
+ *     (NULL: every group has a mean when d_means is given);
+ *   d_mults: f32 [n_mult] the profile's scale multipliers (1..16); kb: 4 or 5 (the
+ *     profile's packed bits); vit2: the profile is vit2-eligible (kv_profile.rs:276-286).
+ *   d_dest: i64 [n_rows] destination row of each encoded row in d_words / d_scales
+ *     (for example head * capacity + position), or NULL for row i.
+ *   d_words: u32 [*][8*kb] MSB-first fields; d_scales: f32 [*].
+ * A row whose arithmetic overflows i32 or turns non-finite (the reference's Err) is not
+ * written and raises YSKN_ENONFINITE at the next yskn_b200_status(). One launch, no
+ * scratch: one CTA per row runs the chains of up to four multipliers at once. */
+YSKN_B200_API int yskn_b200_kv_encode(const float* d_rows, const int32_t* d_row_group, int n_rows,
+                                      const int16_t* d_tables, const float* d_gains, const float* d_means,
+                                      const uint8_t* d_has_mean, const float* d_mults, int n_mult, int kb,
+                                      int vit2, const int64_t* d_dest, uint32_t* d_words, float* d_scales,
+                                      void* stream);
+
 #ifdef __cplusplus
 }
 #endif

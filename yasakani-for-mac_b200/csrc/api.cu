@@ -551,4 +551,31 @@ YSKN_B200_API int yskn_b200_kv4_attention(const uint16_t* d_q, const uint16_t* d
   return launch_kv4_attention(a, as_stream(stream));
 }
 
+YSKN_B200_API int yskn_b200_kv_encode(const float* d_rows, const int32_t* d_row_group, int n_rows,
+                                      const int16_t* d_tables, const float* d_gains, const float* d_means,
+                                      const uint8_t* d_has_mean, const float* d_mults, int n_mult, int kb, int vit2,
+                                      const int64_t* d_dest, uint32_t* d_words, float* d_scales, void* stream) {
+  if (n_rows < 1 || n_rows > 65535) return fail(YSKN_EINVAL, "kv encode: n_rows outside [1, 65535]");
+  if (n_mult < 1 || n_mult > 16) return fail(YSKN_EINVAL, "kv encode: 1 to 16 scale multipliers");
+  if (kb != 4 && kb != 5) return fail(YSKN_EINVAL, "kv encode: packed rows have 4 or 5 bits per channel");
+  if (!d_rows || !d_row_group || !d_tables || !d_gains || !d_mults || !d_words || !d_scales)
+    return fail(YSKN_EINVAL, "kv encode: null argument");
+  KvEncArgs a{};
+  a.rows = d_rows;
+  a.row_group = d_row_group;
+  a.tables = d_tables;
+  a.gains = d_gains;
+  a.means = d_means;
+  a.has_mean = d_has_mean;
+  a.mults = d_mults;
+  a.dest = d_dest;
+  a.words = d_words;
+  a.scales = d_scales;
+  a.n_rows = n_rows;
+  a.n_mult = n_mult;
+  a.kb = kb;
+  a.vit2 = vit2 ? 1 : 0;
+  return launch_kv_encode(a, as_stream(stream));
+}
+
 }  // extern "C"

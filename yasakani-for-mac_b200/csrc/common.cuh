@@ -102,6 +102,22 @@ int kv_max_splits(const KvArgs& a);
 int64_t kv_partials_floats(int M, int n_qh, int max_splits);
 int launch_kv4_attention(const KvArgs& a, cudaStream_t st);
 
+// Quantised-KV row encoder for packed rows (kvenc.cu).
+struct KvEncArgs {
+  const float* rows;         // f32 [n_rows][256] (cache-rotated)
+  const int32_t* row_group;  // [n_rows] profile group of each row
+  const int16_t* tables;     // [n_groups][256] trellis table codes
+  const float* gains;        // [n_groups]
+  const float* means;        // [n_groups][256] or nullptr
+  const uint8_t* has_mean;   // [n_groups] or nullptr
+  const float* mults;        // [n_mult] profile scale multipliers
+  const int64_t* dest;       // [n_rows] destination row, or nullptr (row i)
+  uint32_t* words;           // [*][8*kb]
+  float* scales;             // [*]
+  int n_rows, n_mult, kb, vit2;
+};
+int launch_kv_encode(const KvEncArgs& a, cudaStream_t st);
+
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 }  // namespace yskn

@@ -44,6 +44,7 @@ _SIGNATURES = {
     "yskn_b200_linear": (_i, [_vp, _i, _vp, _i, _vp, _vp, _vp, _vp]),
     "yskn_b200_kv4_attention_work_bytes": (_i64, [_i, _i, _i, _i]),
     "yskn_b200_kv4_attention": (_i, [_vp] * 9 + [_i] * 7 + [_vp] * 4),
+    "yskn_b200_kv_encode": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp]),
 }
 
 _lib = None
@@ -217,3 +218,12 @@ def kv4_attention(q, k_rows, k_scales, v_rows, v_scales, k_codebook, v_codebook,
                                         _ptr(v_scales), _ptr(k_codebook), _ptr(v_codebook), _ptr(v_mean), M, n_qh,
                                         n_kvh, length, capacity, kb, n_splits, _ptr(work), _ptr(attended),
                                         _ptr(out), _stream(stream)), "kv4_attention")
+
+
+def kv_encode(rows, row_group, tables, gains, mults, kb, vit2, words, scales, means=None, has_mean=None, dest=None,
+              stream=None):
+    """rows f32 [n][256]; row_group int32 [n]; tables int16 [groups][256]; gains f32 [groups];
+    mults f32 [n_mult]; words int32 [*][8*kb]; scales f32 [*]; dest int64 [n] or None."""
+    check(lib().yskn_b200_kv_encode(_ptr(rows), _ptr(row_group), rows.shape[0], _ptr(tables), _ptr(gains),
+                                    _ptr(means), _ptr(has_mean), _ptr(mults), mults.shape[0], kb, int(vit2),
+                                    _ptr(dest), _ptr(words), _ptr(scales), _stream(stream)), "kv_encode")
