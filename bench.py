@@ -13,6 +13,13 @@ per call at M=1), captured in one CUDA graph. The metric is HBM throughput of th
 algorithmic bytes per step / step time. Codes per step (243.8 MB at bits=8) exceed
 the 126 MB L2, so no L2 flush is needed between steps.
 
+With --gpus N > 1 (torchrun, one rank per GPU) the same layer step runs tensor-
+parallel (yskn_b200/tp.py): q/k/v, qkv/z and gate/up column-parallel over whole
+512-row blocks (k/v replicated at 4 and 8 GPUs), o/out/down row-parallel over
+512-column groups with an NCCL all-reduce MAX of the row maxima and an exact int64
+all-reduce SUM each; the value is the whole layer's bytes over the max-over-ranks
+step time (strong scaling).
+
 `--impl reference` times the CPU path instead: the C restatement (oracle/) of the
 reference's CPU engine (crates/yskn-engine kernel + pool, crates/yskn-ref quantiser
 and restore), on all host threads, rank 0 only.
@@ -35,6 +42,7 @@ import numpy as np  # noqa: E402
 LAYER = [("q_proj", 12288, 5120), ("k_proj", 1024, 5120), ("v_proj", 1024, 5120), ("o_proj", 5120, 6144),
          ("in_proj_qkv", 10240, 5120), ("in_proj_z", 6144, 5120), ("out_proj", 5120, 6144),
          ("gate_proj", 17408, 5120), ("up_proj", 17408, 5120), ("down_proj", 5120, 17408)]
+ROW_PARALLEL = {"o_proj", "out_proj", "down_proj"}
 CALLS = [["q_proj", "k_proj", "v_proj"], ["o_proj"], ["in_proj_qkv", "in_proj_z"], ["out_proj"],
          ["gate_proj", "up_proj"], ["down_proj"]]
 # DRAM bytes (read + write) of the six weighted-sums launches of one step, from one ncu
@@ -76,10 +84,9 @@ def algorithmic_bytes(bits, M):
     return total
 
 
-def gemv_bytes(name, bits, M):
+def gemv_bytes(rows, cols, bits, M):
     """Algorithmic bytes of one weighted-sums launch: codes + int8 table + int8
     activations + int32 group scales + int64 sums."""
-    rows, cols = LAYER_ROWS[name], LAYER_COLS[name]
     return rows * cols * bits // 16 + 8192 + M * cols + 4 * M * (cols // 512) + 8 * M * rows
 
 
@@ -197,7 +204,8 @@ def config(args):
             "bits": args.bits, "bits_per_weight": args.bits / 2, "M": 1,
             "codes_mb_per_step": sum(r * c * args.bits // 16 for _, r, c in LAYER) / 1e6,
             "l2": "inputs larger than L2: every step streams all codes (>126 MB); no flush",
-            "parallelism": "replicas" if args.gpus > 1 else "single"}
+            "parallelism": "tp%d (column-parallel q/k/v, qkv/z, gate/up; row-parallel o, out, down)" % args.gpus
+            if args.gpus > 1 else "single"}
 
 
 def run_b200(args, rank, world, local_rank):
@@ -205,24 +213,61 @@ def run_b200(args, rank, world, local_rank):
     import yskn_b200 as Y
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    W = make_weights(args.bits, 1000 + 101 * rank)
-    mats, keep = {}, []
+    from yskn_b200 import tp
+    W = make_weights(args.bits)
+    # N > 1: tensor parallelism over whole 512-blocks (yskn_b200/tp.py). Column-parallel
+    # projections keep whole 512-row blocks per rank (replicated when there are fewer
+    # blocks than ranks: k/v at 4 and 8 GPUs); o/out/down are row-parallel.
+    mats, rowpar = {}, {}
     for name, w in W.items():
         dw = torch.from_numpy(w["words"].view(np.int32)).to(dev)
-        mats[name] = Y.Matrix(dw, "warp", w["rows"], w["rows"], w["cols"], args.bits, w["lut16"], w["sc16"],
-                              w["s_in"], w["s_out"])
+        args_m = (dw, "warp", w["rows"], w["rows"], w["cols"], args.bits, w["lut16"], w["sc16"], w["s_in"],
+                  w["s_out"])
+        if world > 1 and name in ROW_PARALLEL:
+            rowpar[name] = tp.RowParallelLinear(*args_m)
+            mats[name] = rowpar[name].mat
+        else:
+            shard = None
+            if world > 1:
+                ranges = tp.split_blocks(w["rows"], world)
+                r0, r1 = ranges[rank] if all(a < b for a, b in ranges) else (0, w["rows"])
+                shard = (r0, r1, 0, w["cols"])
+            mats[name] = Y.Matrix(*args_m, shard=shard)
         del dw
     M = 1
-    xs_host = make_inputs(M)
-    xs = [torch.from_numpy(x).to(dev) for x in xs_host]
+    xs_full = make_inputs(M)
+    # Row-parallel calls take this rank's column slice of their input.
+    xs_host = [np.ascontiguousarray(x[:, rowpar[c[0]].col_begin:rowpar[c[0]].col_end]) if c[0] in rowpar else x
+               for x, c in zip(xs_full, CALLS)]
+    # A step's inputs (and its outputs) are views of one buffer, 256-byte aligned, so the
+    # end-to-end step moves each direction with a single copy.
+    def packed(shapes, **kw):
+        offs, o = [], 0
+        for s in shapes:
+            offs.append(o)
+            o += -(-int(np.prod(s)) // 64) * 64
+        buf = torch.empty(o, dtype=torch.float32, **kw)
+        return buf, [buf[a:a + int(np.prod(s))].view(*s) for a, s in zip(offs, shapes)]
+
+    x_all, xs = packed([x.shape for x in xs_host], device=dev)
+    for v, x in zip(xs, xs_host):
+        v.copy_(torch.from_numpy(x))
+    out_shapes = [(M, mats[n].rows) for c in CALLS for n in c]
+    y_all, y_flat = packed(out_shapes, device=dev)
+    ys, k = [], 0
+    for c in CALLS:
+        ys.append(y_flat[k:k + len(c)])
+        k += len(c)
     group = [[mats[n] for n in c] for c in CALLS]
     works = [torch.empty(Y.linear_work_bytes(g, M), dtype=torch.uint8, device=dev) for g in group]
-    ys = [[torch.empty((M, LAYER_ROWS[n]), dtype=torch.float32, device=dev) for n in c] for c in CALLS]
     stream = torch.cuda.Stream(dev)
 
     def step():
-        for g, x, wk, y in zip(group, xs, works, ys):
-            Y.linear(g, x, wk, y, stream=stream)
+        for c, g, x, wk, y in zip(CALLS, group, xs, works, ys):
+            if c[0] in rowpar:
+                rowpar[c[0]](x, y[0], stream=stream)
+            else:
+                Y.linear(g, x, wk, y, stream=stream)
 
     with torch.cuda.stream(stream):
         step()
@@ -257,7 +302,7 @@ def run_b200(args, rank, world, local_rank):
         # Dominant kernel: time the weighted-sums launches alone, same matrices, same order.
         acts = [torch.empty((M, x.shape[1]), dtype=torch.int8, device=dev) for x in xs]
         scs = [torch.empty((M, x.shape[1] // 512), dtype=torch.int32, device=dev) for x in xs]
-        wss = [[torch.empty((M, LAYER_ROWS[n]), dtype=torch.int64, device=dev) for n in c] for c in CALLS]
+        wss = [[torch.empty((M, mats[n].physical_rows), dtype=torch.int64, device=dev) for n in c] for c in CALLS]
         for g, x, a, s in zip(group, xs, acts, scs):
             al = torch.empty((M, x.shape[1] // 512), dtype=torch.float32, device=dev)
             rq = torch.empty(M, dtype=torch.float32, device=dev)
@@ -286,15 +331,15 @@ def run_b200(args, rank, world, local_rank):
         # End to end through the public API, every step: pinned host input in,
         # the six operator calls, host output back; captured as one graph per
         # step the way a decode loop runs it (as the reference engine does).
-        xh = [torch.from_numpy(x).pin_memory() for x in xs_host]
-        yh = [[torch.empty((M, LAYER_ROWS[n]), dtype=torch.float32).pin_memory() for n in c] for c in CALLS]
+        xh_all, xh = packed([x.shape for x in xs_host], pin_memory=True)
+        for v, x in zip(xh, xs_host):
+            v.copy_(torch.from_numpy(x))
+        yh_all, _ = packed(out_shapes, pin_memory=True)
         e2e_graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(e2e_graph, stream=stream):
-            for g, x, xd, wk, y, yhh in zip(group, xh, xs, works, ys, yh):
-                xd.copy_(x, non_blocking=True)
-                Y.linear(g, xd, wk, y, stream=stream)
-                for a, b in zip(yhh, y):
-                    a.copy_(b, non_blocking=True)
+            x_all.copy_(xh_all, non_blocking=True)
+            step()
+            yh_all.copy_(y_all, non_blocking=True)
         e2e_steps = max(10, min(args.steps, 500))
         barrier()
         e2 = torch.cuda.Event(enable_timing=True)
@@ -309,15 +354,25 @@ def run_b200(args, rank, world, local_rank):
         barrier()
         e2e_ms = e2.elapsed_time(e3)
     Y.check(Y.status(stream), "status")
+    torch.cuda.synchronize()
+    del graph, graphs, e2e_graph  # graphs holding NCCL calls go before the process group
     t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     ms, e2e_ms = t.tolist()
+    # This rank's algorithmic bytes of its own weighted-sums launches, and its copies.
+    gemv_local = sum(gemv_bytes(mats[n].physical_rows, mats[n].cols, args.bits, M) for c in CALLS for n in c)
+    h2d_local = 4 * x_all.numel()  # the copies as issued (inputs + alignment padding)
+    d2h_local = 4 * y_all.numel()
+    tot = torch.tensor([h2d_local, d2h_local], dtype=torch.int64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(tot)
+    h2d, d2h = tot.tolist()
     if rank != 0:
         return
     step_bytes = algorithmic_bytes(args.bits, M)
-    value = world * step_bytes * args.steps / (ms * 1e-3) / 1e12
-    e2e_value = world * step_bytes * e2e_steps / (e2e_ms * 1e-3) / 1e12
+    value = step_bytes * args.steps / (ms * 1e-3) / 1e12  # one layer step for the whole job (strong scaling)
+    e2e_value = step_bytes * e2e_steps / (e2e_ms * 1e-3) / 1e12
     with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) \
             else open(os.devnull) as f:
         try:
@@ -325,10 +380,8 @@ def run_b200(args, rank, world, local_rank):
         except ValueError:
             peaks = {}
     peak = peaks.get("hbm_gbs", 6650.0)
-    gemv_total_bytes = sum(gemv_bytes(n, args.bits, M) for c in CALLS for n in c)
+    gemv_total_bytes = gemv_local
     achieved = gemv_total_bytes / (sum(gemv_ms) * 1e-3) / 1e9
-    h2d = sum(4 * M * LAYER_COLS[c[0]] for c in CALLS)
-    d2h = sum(4 * M * LAYER_ROWS[n] for c in CALLS for n in c)
     # CPU baseline (rank 0, N=1 only): the oracle port on a bounded sample.
     cpu = None
     if world == 1 and not args.skip_cpu:
@@ -344,16 +397,21 @@ def run_b200(args, rank, world, local_rank):
         cpu = {"value": nbytes / dt / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
                "sample": "%d full layer-set steps (quantise + threaded int64 sums + restore), %.1f s" % (n, dt)}
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak",
             "vs_baseline": None, "dtype": "i8", "data": "synthetic", "config": config(args),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": GEMV_TRAFFIC.get((args.bits, M)),
-                         "kernel": "gemv_kernel (weighted sums; the 6 launches of one step, each timed alone)",
+                         "frac": achieved / peak,
+                         "traffic": GEMV_TRAFFIC.get((args.bits, M)) if world == 1 else None,
+                         "kernel": "gemv_kernel (weighted sums; the 6 launches of one step on rank 0, each timed alone)",
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             # One fused launch (quantise + sums + restore) per operator call at M=1.
-            "gpu_launches": args.steps * len(CALLS),
+            # Own kernels per step: one fused launch per column-parallel call; quantise,
+            # rescale, weighted sums and restore per row-parallel call (plus torch's
+            # row-max reduction and NCCL's kernels, not counted).
+            "gpu_launches": args.steps * (len(CALLS) + 3 * len(rowpar)),
             "clocks": sampler.summary(),
             "step_bytes": step_bytes, "gemv_us_per_call": [round(1e3 * x, 2) for x in gemv_ms]}
     print(json.dumps(line), flush=True)

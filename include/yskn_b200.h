@@ -88,6 +88,20 @@ YSKN_B200_API yskn_b200_matrix* yskn_b200_matrix_create(const uint32_t* d_codes,
                                                         int physical_rows, int cols, int bits,
                                                         const uint16_t* lut16_host, const uint16_t* scale16_host,
                                                         const int8_t* signs_in_host, const int8_t* signs_out_host);
+/* Tensor-parallel shard of the same tensor (the arguments describe the whole tensor as
+ * above): physical rows [row_begin, row_end) (row_begin % 8 == 0; whole 512-row blocks
+ * when there is an output rotation) and columns [col_begin, col_end) (whole 512-column
+ * groups). Column-parallel projections split rows, row-parallel ones split columns; the
+ * shard's sums equal the whole tensor's sums restricted to those rows / columns. No
+ * counterpart function in the reference, whose engine runs on one GPU; the split
+ * follows the 512-blocks of docs/FORMAT.md. */
+YSKN_B200_API yskn_b200_matrix* yskn_b200_matrix_create_shard(const uint32_t* d_codes, int layout, int rows,
+                                                              int physical_rows, int cols, int bits,
+                                                              const uint16_t* lut16_host,
+                                                              const uint16_t* scale16_host,
+                                                              const int8_t* signs_in_host,
+                                                              const int8_t* signs_out_host, int row_begin,
+                                                              int row_end, int col_begin, int col_end);
 YSKN_B200_API void yskn_b200_matrix_destroy(yskn_b200_matrix* m);
 /* rows, physical_rows, cols, bits, has_output_rotation, packed bytes. */
 YSKN_B200_API int yskn_b200_matrix_info(const yskn_b200_matrix* m, int64_t* out6);
@@ -120,6 +134,16 @@ YSKN_B200_API int yskn_b200_weighted_sums_prefix(const yskn_b200_matrix* mat, co
  * device error word (read with yskn_b200_status). */
 YSKN_B200_API int yskn_b200_quantize(const float* d_x, const int8_t* d_signs, int M, int Kc, int8_t* d_act,
                                      float* d_alpha, int32_t* d_scales, float* d_row_quantum, void* stream);
+
+/* The integer grid of each activation row from a given maximum of its group scales
+ * (compressed_linear.rs:113-128): d_scales[m][g] = rne(alpha * (2^24 / row_max[m])),
+ * d_row_quantum[m] = row_max[m] * 2^-24. Tensor parallelism (row-parallel projections):
+ * each rank quantises its own 512-column groups with yskn_b200_quantize, the ranks take
+ * the maximum of their row maxima (an all-reduce MAX of M floats), and this call puts
+ * every rank on the whole row's grid, so the int64 partial sums add up (all-reduce
+ * SUM) to exactly the one-GPU sums. No counterpart in the single-GPU reference. */
+YSKN_B200_API int yskn_b200_rescale(const float* d_alpha, const float* d_row_max, int M, int groups,
+                                    int32_t* d_scales, float* d_row_quantum, void* stream);
 
 /* Restore + output rotation (replaces src/a8_prologue.cuh:10-15 xsum_combine and the
  * restore part of src/q35_kernels.cu:1402-1474; compressed_linear.rs:288-370):

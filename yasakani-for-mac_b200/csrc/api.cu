@@ -235,15 +235,27 @@ YSKN_B200_API int yskn_b200_pack(const uint32_t* d_words, int layout, int physic
                      as_stream(stream));
 }
 
-YSKN_B200_API yskn_b200_matrix* yskn_b200_matrix_create(const uint32_t* d_codes, int layout, int rows,
-                                                        int physical_rows, int cols, int bits,
-                                                        const uint16_t* lut16_host, const uint16_t* scale16_host,
-                                                        const int8_t* signs_in_host, const int8_t* signs_out_host) {
-  if (check_shape(layout, physical_rows, cols, bits)) return nullptr;
-  if (rows <= 0 || rows > physical_rows) return fail(YSKN_EINVAL, "rows must be in 1..physical_rows"), nullptr;
-  if (!d_codes || !aligned16(d_codes) || !lut16_host || !scale16_host || !signs_in_host)
+// A matrix handle for physical rows [row0, row1) and columns [col0, col1) of a source
+// tensor of src_rows x src_phys x src_cols (the whole tensor, or one tensor-parallel
+// shard). The lookup table is per tensor, so every shard quantises it identically.
+static yskn_b200_matrix* create_matrix(const uint32_t* d_codes, int layout, int src_rows, int src_phys, int src_cols,
+                                       int bits, const uint16_t* lut16_host, const uint16_t* scale16_src,
+                                       const int8_t* signs_in_src, const int8_t* signs_out_src, int row0, int row1,
+                                       int col0, int col1) {
+  if (check_shape(layout, src_phys, src_cols, bits)) return nullptr;
+  if (src_rows <= 0 || src_rows > src_phys) return fail(YSKN_EINVAL, "rows must be in 1..physical_rows"), nullptr;
+  if (!d_codes || !aligned16(d_codes) || !lut16_host || !scale16_src || !signs_in_src)
     return fail(YSKN_EINVAL, "matrix_create: missing or misaligned input"), nullptr;
-  if (signs_out_host && physical_rows % 512)
+  if (row0 < 0 || row1 > src_phys || row0 >= row1 || row0 % 8 || col0 < 0 || col1 > src_cols || col0 >= col1 ||
+      col0 % 512 || col1 % 512 || row0 >= src_rows)
+    return fail(YSKN_EINVAL, "shard: rows [row0, row1) need row0 % 8 == 0 and real rows; columns whole 512-groups"),
+           nullptr;
+  const int physical_rows = row1 - row0, cols = col1 - col0;
+  const int rows = std::min(src_rows, row1) - row0;
+  const uint16_t* scale16_host = scale16_src + row0;
+  const int8_t* signs_in_host = signs_in_src + col0;
+  const int8_t* signs_out_host = signs_out_src ? signs_out_src + row0 : nullptr;
+  if (signs_out_host && (physical_rows % 512 || row0 % 512))
     return fail(YSKN_EINVAL, "an output rotation needs whole 512-row blocks"), nullptr;
   for (int i = 0; i < cols; ++i)
     if (signs_in_host[i] != 1 && signs_in_host[i] != -1) return fail(YSKN_EINVAL, "signs must be -1 or +1"), nullptr;
@@ -295,8 +307,8 @@ YSKN_B200_API yskn_b200_matrix* yskn_b200_matrix_create(const uint32_t* d_codes,
   if (e == cudaSuccess) e = cudaMemcpy(small + off_sin, signs_in_host, cols, cudaMemcpyHostToDevice);
   if (e == cudaSuccess && signs_out_host)
     e = cudaMemcpy(small + off_sout, signs_out_host, physical_rows, cudaMemcpyHostToDevice);
-  int rc = e == cudaSuccess ? launch_pack(d_codes, layout, physical_rows, cols, bits,
-                                          reinterpret_cast<uint32_t*>(m->codes), nullptr)
+  int rc = e == cudaSuccess ? launch_pack_range(d_codes, layout, src_phys, src_cols, row0, col0, physical_rows, cols,
+                                                bits, reinterpret_cast<uint32_t*>(m->codes), nullptr)
                             : cuda_fail(e, "matrix_create: copy");
   if (rc == YSKN_OK) rc = cuda_fail(cudaDeviceSynchronize(), "matrix_create: pack");
   if (rc != YSKN_OK) {
@@ -318,6 +330,32 @@ YSKN_B200_API yskn_b200_matrix* yskn_b200_matrix_create(const uint32_t* d_codes,
   d.cols = cols;
   d.bits = bits;
   return m.release();
+}
+
+YSKN_B200_API yskn_b200_matrix* yskn_b200_matrix_create(const uint32_t* d_codes, int layout, int rows,
+                                                        int physical_rows, int cols, int bits,
+                                                        const uint16_t* lut16_host, const uint16_t* scale16_host,
+                                                        const int8_t* signs_in_host, const int8_t* signs_out_host) {
+  return create_matrix(d_codes, layout, rows, physical_rows, cols, bits, lut16_host, scale16_host, signs_in_host,
+                       signs_out_host, 0, physical_rows, 0, cols);
+}
+
+YSKN_B200_API yskn_b200_matrix* yskn_b200_matrix_create_shard(const uint32_t* d_codes, int layout, int rows,
+                                                              int physical_rows, int cols, int bits,
+                                                              const uint16_t* lut16_host,
+                                                              const uint16_t* scale16_host,
+                                                              const int8_t* signs_in_host,
+                                                              const int8_t* signs_out_host, int row_begin, int row_end,
+                                                              int col_begin, int col_end) {
+  return create_matrix(d_codes, layout, rows, physical_rows, cols, bits, lut16_host, scale16_host, signs_in_host,
+                       signs_out_host, row_begin, row_end, col_begin, col_end);
+}
+
+YSKN_B200_API int yskn_b200_rescale(const float* d_alpha, const float* d_row_max, int M, int groups,
+                                    int32_t* d_scales, float* d_row_quantum, void* stream) {
+  if (M < 1 || groups < 1 || !d_alpha || !d_row_max || !d_scales || !d_row_quantum)
+    return fail(YSKN_EINVAL, "rescale: bad arguments");
+  return launch_rescale(d_alpha, d_row_max, M, groups, d_scales, d_row_quantum, as_stream(stream));
 }
 
 YSKN_B200_API void yskn_b200_matrix_destroy(yskn_b200_matrix* m) {

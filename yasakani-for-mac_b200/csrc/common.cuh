@@ -77,6 +77,12 @@ int launch_quantize(const float* x, const int8_t* signs, int M, int Kc, int8_t* 
 int launch_restore(int64_t* ws, int ws_ld, const float* row_quantum, const float* inv_rms, const float* tau,
                    const int8_t* s_out, int M, int phys, int n_rows, int clear_ws, float* y, cudaStream_t st);
 int launch_pack(const uint32_t* words, int layout, int phys, int cols, int bits, uint32_t* out, cudaStream_t st);
+int launch_pack_range(const uint32_t* words, int layout, int src_phys, int src_cols, int row0, int col0, int phys,
+                      int cols, int bits, uint32_t* out, cudaStream_t st);
+// Integer grid of each activation row from a given row maximum of the group scales
+// (tensor parallelism: the maximum over all ranks' groups).
+int launch_rescale(const float* alpha, const float* row_max, int M, int G, int32_t* scales, float* row_quantum,
+                   cudaStream_t st);
 int launch_repack_frag(const uint32_t* w, uint32_t* f, int rows, int seqs, int wps, cudaStream_t st);
 
 // Quantised-KV decode attention (kvattn.cu). Query row m of M sees cache rows

@@ -17,8 +17,13 @@
 
 namespace yskn {
 
-__global__ void __launch_bounds__(256) pack_kernel(const uint32_t* __restrict__ src, int layout, int phys, int seqs,
-                                                   int bits, int U, uint32_t* __restrict__ dst, int64_t total) {
+// The packed matrix may be a shard of the source tensor: physical rows
+// [row0, row0 + phys) and sequences [seq0, seq0 + seqs) of a source with src_phys
+// rows and src_seqs sequences (the addressing of docs/FORMAT.md:139-151 uses the
+// source's geometry).
+__global__ void __launch_bounds__(256) pack_kernel(const uint32_t* __restrict__ src, int layout, int src_phys,
+                                                   int src_seqs, int row0, int seq0, int phys, int seqs, int bits,
+                                                   int U, uint32_t* __restrict__ dst, int64_t total) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // (row block, sequence, lane)
   if (i >= total) return;
   const int lane = (int)(i & 31);
@@ -31,12 +36,13 @@ __global__ void __launch_bounds__(256) pack_kernel(const uint32_t* __restrict__ 
     uint32_t v = 0;
     if (row < phys) {
       const int64_t w = (int64_t)q * bits + j;  // word of the sequence
+      const int64_t sr = row0 + row, ss = seq0 + seq;
       int64_t s;
       if (layout == YSKN_LAYOUT_WARP) {
-        const int64_t qq = seq * phys + row;
+        const int64_t qq = ss * src_phys + sr;
         s = (((qq >> 5) * bits + (w >> 2)) * 32 + (qq & 31)) * 4 + (w & 3);
       } else {
-        s = (row * seqs + seq) * (4 * (int64_t)bits) + w;
+        s = (sr * src_seqs + ss) * (4 * (int64_t)bits) + w;
       }
       v = __ldg(src + s);
     }
@@ -44,14 +50,20 @@ __global__ void __launch_bounds__(256) pack_kernel(const uint32_t* __restrict__ 
   }
 }
 
-int launch_pack(const uint32_t* words, int layout, int phys, int cols, int bits, uint32_t* out, cudaStream_t st) {
+int launch_pack_range(const uint32_t* words, int layout, int src_phys, int src_cols, int row0, int col0, int phys,
+                      int cols, int bits, uint32_t* out, cudaStream_t st) {
   const int64_t pad8 = ceil_div(phys, 8) * 8;
   const int seqs = cols / 256;
   const int U = bits % 4 == 0 ? 4 : (bits % 2 == 0 ? 2 : 1);
   const int64_t total = pad8 / 8 * seqs * 32;
   if (total == 0) return YSKN_OK;
-  pack_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, st>>>(words, layout, phys, seqs, bits, U, out, total);
+  pack_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, st>>>(words, layout, src_phys, src_cols / 256, row0,
+                                                              col0 / 256, phys, seqs, bits, U, out, total);
   return cuda_fail(cudaGetLastError(), "pack_kernel");
+}
+
+int launch_pack(const uint32_t* words, int layout, int phys, int cols, int bits, uint32_t* out, cudaStream_t st) {
+  return launch_pack_range(words, layout, phys, cols, 0, 0, phys, cols, bits, out, st);
 }
 
 // One thread per 16-byte chunk of the warp-layout source: chunk k belongs to

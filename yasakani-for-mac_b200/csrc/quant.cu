@@ -41,6 +41,27 @@ int launch_quantize(const float* x, const int8_t* signs, int M, int Kc, int8_t* 
   return cuda_fail(cudaGetLastError(), "quantize_kernel");
 }
 
+// The integer grid from a given row maximum (compressed_linear.rs:113-128): under
+// tensor parallelism the maximum over every rank's groups, so all ranks form the
+// integers of the whole row.
+__global__ void __launch_bounds__(256) rescale_kernel(const float* __restrict__ alpha,
+                                                      const float* __restrict__ row_max, int M, int G,
+                                                      int32_t* __restrict__ scales, float* __restrict__ row_quantum) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)M * G) return;
+  const int m = (int)(i / G);
+  const float mx = row_max[m];
+  scales[i] = integer_group_scale(alpha[i], row_grid_multiplier(mx));
+  if (i == (int64_t)m * G) row_quantum[m] = row_quantum_of(mx);
+}
+
+int launch_rescale(const float* alpha, const float* row_max, int M, int G, int32_t* scales, float* row_quantum,
+                   cudaStream_t st) {
+  const int64_t n = (int64_t)M * G;
+  rescale_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(alpha, row_max, M, G, scales, row_quantum);
+  return cuda_fail(cudaGetLastError(), "rescale_kernel");
+}
+
 // Restore with output rotation: one warp per (row m, 512-row block).
 __global__ void __launch_bounds__(256) restore_rot_kernel(int64_t* __restrict__ ws, int ws_ld,
                                                           const float* __restrict__ row_quantum,

@@ -29,6 +29,7 @@ _SIGNATURES = {
     "yskn_b200_pack_bytes": (_i64, [_i, _i, _i]),
     "yskn_b200_pack": (_i, [_vp, _i, _i, _i, _i, _vp, _vp]),
     "yskn_b200_matrix_create": (_vp, [_vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
+    "yskn_b200_matrix_create_shard": (_vp, [_vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i]),
     "yskn_b200_matrix_destroy": (None, [_vp]),
     "yskn_b200_matrix_info": (_i, [_vp, _vp]),
     "yskn_b200_matrix_lut8": (_vp, [_vp]),
@@ -39,6 +40,7 @@ _SIGNATURES = {
     "yskn_b200_weighted_sums_prefix": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp]),
     "yskn_b200_weighted_sums_noalloc": (_i, [_vp, _i, _vp, _vp, _i, _vp, _vp]),
     "yskn_b200_quantize": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp]),
+    "yskn_b200_rescale": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp]),
     "yskn_b200_restore": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
     "yskn_b200_linear_work_bytes": (_i64, [_vp, _i, _i]),
     "yskn_b200_linear": (_i, [_vp, _i, _vp, _i, _vp, _vp, _vp, _vp]),
@@ -107,19 +109,29 @@ def signs(rule, seed, offset, n):
 class Matrix:
     """One compressed matrix on the device (yskn_b200_matrix_create)."""
 
-    def __init__(self, d_codes, layout, rows, physical_rows, cols, bits, lut16, scale16, signs_in, signs_out=None):
+    def __init__(self, d_codes, layout, rows, physical_rows, cols, bits, lut16, scale16, signs_in, signs_out=None,
+                 shard=None):
+        """shard: (row_begin, row_end, col_begin, col_end) of the whole tensor described by
+        the other arguments (yskn_b200_matrix_create_shard), or None for the whole tensor."""
         import numpy as np
         lut16 = np.ascontiguousarray(lut16, np.uint16)
         scale16 = np.ascontiguousarray(scale16, np.uint16)
         signs_in = np.ascontiguousarray(signs_in, np.int8)
         so = None if signs_out is None else np.ascontiguousarray(signs_out, np.int8)
-        h = lib().yskn_b200_matrix_create(_ptr(d_codes), LAYOUTS.get(layout, layout), rows, physical_rows, cols, bits,
-                                          lut16.ctypes.data, scale16.ctypes.data, signs_in.ctypes.data,
-                                          None if so is None else so.ctypes.data)
+        args = (_ptr(d_codes), LAYOUTS.get(layout, layout), rows, physical_rows, cols, bits, lut16.ctypes.data,
+                scale16.ctypes.data, signs_in.ctypes.data, None if so is None else so.ctypes.data)
+        if shard is None:
+            h = lib().yskn_b200_matrix_create(*args)
+            shard = (0, physical_rows, 0, cols)
+        else:
+            h = lib().yskn_b200_matrix_create_shard(*args, *shard)
         if not h:
             raise YsknError(EINVAL, "matrix_create: " + last_error())
         self.handle = C.c_void_p(h)
-        self.rows, self.physical_rows, self.cols, self.bits = rows, physical_rows, cols, bits
+        r0, r1, c0, c1 = shard
+        self.shard = tuple(shard)
+        self.rows, self.physical_rows = min(rows, r1) - r0, r1 - r0
+        self.cols, self.bits = c1 - c0, bits
         self.has_rotation = so is not None
 
     def info(self):
@@ -174,6 +186,13 @@ def quantize(x, signs_dev_ptr, act, alpha, scales, row_quantum, stream=None):
     M, K = x.shape
     check(lib().yskn_b200_quantize(_ptr(x), signs_dev_ptr, M, K, _ptr(act), _ptr(alpha), _ptr(scales),
                                    _ptr(row_quantum), _stream(stream)), "quantize")
+
+
+def rescale(alpha, row_max, scales, row_quantum, stream=None):
+    """yskn_b200_rescale: the rows' integer grids from given row maxima of the group scales."""
+    M, G = alpha.shape
+    check(lib().yskn_b200_rescale(_ptr(alpha), _ptr(row_max), M, G, _ptr(scales), _ptr(row_quantum),
+                                  _stream(stream)), "rescale")
 
 
 def restore(ws, row_quantum, inv_rms, mat, rotate_out, n_rows, clear_ws, y, stream=None):
