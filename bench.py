@@ -53,20 +53,20 @@ UNIT = "TB/s"
 
 
 def make_weights(bits, seed0=1000):
-    import fixtures
-    import oracle as O
+    import yskn_b200 as Y
+    from yskn_b200 import synthetic
     out = {}
     for i, (name, rows, cols) in enumerate(LAYER):
-        words, lut16, sc16 = fixtures.model_matrix(rows, cols, bits, seed0 + 17 * i)
+        words, lut16, sc16 = synthetic.model_matrix(rows, cols, bits, seed0 + 17 * i)
         out[name] = dict(rows=rows, cols=cols, words=words, lut16=lut16, sc16=sc16,
-                         s_in=O.signs("mulberry32_7919_13", 7, 0, cols),
-                         s_out=O.signs("mulberry32_7919_13", 7, cols, rows))
+                         s_in=Y.signs("mulberry32_7919_13", 7, 0, cols),
+                         s_out=Y.signs("mulberry32_7919_13", 7, cols, rows))
     return out
 
 
 def make_inputs(M):
-    import fixtures
-    return [fixtures.normal(500 + j, M * LAYER_COLS[c[0]]).reshape(M, LAYER_COLS[c[0]]) for j, c in enumerate(CALLS)]
+    from yskn_b200 import synthetic
+    return [synthetic.normal(500 + j, M * LAYER_COLS[c[0]]).reshape(M, LAYER_COLS[c[0]]) for j, c in enumerate(CALLS)]
 
 
 LAYER_COLS = {n: c for n, _, c in LAYER}
@@ -417,6 +417,229 @@ def run_b200(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------- KV attention
+# --workload kv4: config 4 of the path (24 query / 4 KV heads, head dim 256, packed
+# 4-bit rows, one decode token). One step = the attention of the model's 16 attention
+# layers (every fourth of 64), each layer with its own cache of `--ctx` rows, so the
+# step streams 16 x 1056 x ctx bytes of cache (> L2 from ctx 8192; smaller contexts
+# rotate over as many cache copies as exceed L2).
+KV_QH, KV_KVH, KV_LAYERS = 24, 4, 16
+KV_METRIC = "KV4 decode attention cache GB/s (24 q / 4 KV heads, 16 attention layers, one token)"
+
+
+def kv_layer_bytes(ctx, M):
+    """Algorithmic bytes of one layer: packed rows + row scales of both sides, both
+    codebooks, value means, bf16 queries and gates in, bf16 outputs."""
+    return KV_KVH * 2 * ctx * (128 + 4) + 2 * KV_KVH * 512 + KV_KVH * 1024 + 3 * M * KV_QH * 512
+
+
+def kv_config(args, copies):
+    return {"workload": "KV4 decode attention (config 4): 24 query / 4 KV heads, head dim 256, packed 4-bit "
+                        "trellis rows, M=1, %d attention layers per step" % KV_LAYERS,
+            "ctx": args.ctx, "splits": "one wave over the SMs" if args.kv_splits < 0 else args.kv_splits,
+            "cache_mb_per_step": KV_LAYERS * 1056 * args.ctx / 1e6, "distinct_caches": copies,
+            "l2": "the step's caches exceed L2 (126 MB); no flush",
+            "parallelism": "KV heads over %d GPUs" % args.gpus if args.gpus > 1 else "single"}
+
+
+def kv_host_inputs(ctx, layer):
+    from yskn_b200 import synthetic
+    kw, ks, vw, vs = synthetic.kv_cache(KV_KVH, ctx, 9000 + 13 * layer)
+    book = np.tile(synthetic.kv_codebook_bf16(), (KV_KVH, 1))
+    vmean = (synthetic.normal(7000 + layer, KV_KVH * 256) * np.float32(0.05)).reshape(KV_KVH, 256)
+    bf = lambda x: ((x.view(np.uint32).astype(np.uint64) + 0x7FFF + ((x.view(np.uint32) >> 16) & 1)) >> 16)  # noqa
+    q = bf(synthetic.normal(7100 + layer, KV_QH * 256)).astype(np.uint16).reshape(1, KV_QH, 256)
+    gate = bf(synthetic.normal(7200 + layer, KV_QH * 256)).astype(np.uint16).reshape(1, KV_QH, 256)
+    return kw, ks, vw, vs, book, vmean, q, gate
+
+
+def cpu_kv_sample(args, seconds=10.0):
+    """The oracle's attention (oracle/kv_oracle.c) on the host: whole query heads of one
+    layer, as many as fit in `seconds`, each KV head's rows decoded once for its six
+    query heads. Returns (GB/s of cache rows, query heads done, seconds)."""
+    import kv
+    kw, ks, vw, vs, book, vmean, q, _ = kv_host_inputs(args.ctx, 0)
+    t0 = time.perf_counter()
+    done, nbytes = 0, 0
+    dec = {}
+    while time.perf_counter() - t0 < seconds or done == 0:
+        j = done % KV_QH
+        h = j // (KV_QH // KV_KVH)
+        if h not in dec:
+            dec[h] = (kv.decode_packed_rows(kw[h], 4, book[h]), kv.decode_packed_rows(vw[h], 4, book[h]))
+        qf = (q[0, j].astype(np.uint32) << 16).view(np.float32)
+        kv.attend_head(qf, dec[h][0], ks[h], dec[h][1], vs[h], vmean[h], args.ctx, 31 if args.ctx < 4096 else 42)
+        nbytes += 2 * args.ctx * 132 * (1.0 / (KV_QH // KV_KVH))  # a KV head's rows serve 6 query heads
+        done += 1
+    dt = time.perf_counter() - t0
+    return nbytes / dt / 1e9, done, dt
+
+
+def run_kv(args, rank, world, local_rank):
+    import torch
+    import yskn_b200 as Y
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    M = 1
+    copies = max(KV_LAYERS, int(np.ceil(400e6 / (1056 * args.ctx))))  # cache copies: together > L2
+    heads = [h for h in range(KV_KVH) if h % world == rank]  # KV heads of this rank (N > 1)
+    nh = len(heads)
+    layers = []
+    for layer in range(copies):
+        kw, ks, vw, vs, book, vmean, q, gate = kv_host_inputs(args.ctx, layer)
+        qsel = np.concatenate([q[:, h * 6:(h + 1) * 6] for h in heads], axis=1) if nh else q[:, :0]
+        gsel = np.concatenate([gate[:, h * 6:(h + 1) * 6] for h in heads], axis=1) if nh else gate[:, :0]
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
+        layers.append(dict(kw=t(kw[heads].view(np.int32)), ks=t(ks[heads]), vw=t(vw[heads].view(np.int32)),
+                           vs=t(vs[heads]), kb=t(book[heads].view(np.int16)), vb=t(book[heads].view(np.int16)),
+                           vm=t(vmean[heads]), q=t(qsel.view(np.int16)), gate=t(gsel.view(np.int16)),
+                           out=torch.empty((M, 6 * nh, 256), dtype=torch.int16, device=dev),
+                           work=torch.empty(max(16, Y.kv4_attention_work_bytes(M, max(1, 6 * nh), args.ctx,
+                                                                               args.kv_splits)),
+                                            dtype=torch.uint8, device=dev)))
+    stream = torch.cuda.Stream(dev)
+    steps_per_graph = max(1, copies // KV_LAYERS)
+
+    def step(layer_set):
+        if not nh:
+            return
+        for L in layer_set:
+            Y.kv4_attention(L["q"], L["kw"], L["ks"], L["vw"], L["vs"], L["kb"], L["vb"], args.ctx, L["work"],
+                            L["out"], gate=L["gate"], v_mean=L["vm"], n_splits=args.kv_splits, stream=stream)
+
+    # One graph = `steps_per_graph` steps of 16 layers over distinct caches.
+    with torch.cuda.stream(stream):
+        step(layers)
+    torch.cuda.synchronize()
+    Y.check(Y.status(stream), "status")
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step(layers[:steps_per_graph * KV_LAYERS])
+    replays = max(1, -(-args.steps // steps_per_graph))
+    steps = replays * steps_per_graph
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            graph.replay()
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    ids = [v.strip() for v in visible.split(",") if v.strip()]
+    sampler = ClockSampler(ids[local_rank] if local_rank < len(ids) else str(local_rank))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with sampler:
+        barrier()
+        e0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(replays):
+                graph.replay()
+        e1.record(stream)
+        barrier()
+        ms = e0.elapsed_time(e1)
+        # End to end, every step: that step's 16 layers' queries and gates in from pinned
+        # host memory (one copy), the attention, the gated outputs back (one copy); the
+        # graph runs `steps_per_graph` such steps over the distinct caches.
+        used = layers[:steps_per_graph * KV_LAYERS]
+        per_step = []
+        for s0 in range(0, len(used), KV_LAYERS):
+            group = used[s0:s0 + KV_LAYERS]
+            qg = torch.cat([torch.cat([L["q"].reshape(-1), L["gate"].reshape(-1)]) for L in group])
+            outs = torch.cat([L["out"].reshape(-1) for L in group])
+            o = 0
+            for L in group:
+                n = L["q"].numel()
+                L["q"], L["gate"] = qg[o:o + n].view_as(L["q"]), qg[o + n:o + 2 * n].view_as(L["gate"])
+                o += 2 * n
+            o = 0
+            for L in group:
+                n = L["out"].numel()
+                L["out"] = outs[o:o + n].view_as(L["out"])
+                o += n
+            per_step.append((group, qg, qg.cpu().pin_memory(), outs, torch.empty_like(outs, device="cpu").pin_memory()))
+        e2e_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(e2e_graph, stream=stream):
+            for group, qg, qg_host, outs, out_host in per_step:
+                qg.copy_(qg_host, non_blocking=True)
+                step(group)
+                out_host.copy_(outs, non_blocking=True)
+        e2e_replays = max(1, -(-max(10, min(args.steps, 200)) // steps_per_graph))
+        barrier()
+        e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e2e_graph.replay()
+            stream.synchronize()
+            e2.record(stream)
+            for _ in range(e2e_replays):
+                e2e_graph.replay()
+            e3.record(stream)
+        barrier()
+        e2e_ms = e2.elapsed_time(e3)
+    Y.check(Y.status(stream), "status")
+    torch.cuda.synchronize()
+    del graph, e2e_graph
+    h2d, d2h = 2 * per_step[0][1].numel(), 2 * per_step[0][3].numel()
+    t = torch.tensor([ms / steps, e2e_ms / (e2e_replays * steps_per_graph), h2d, d2h], dtype=torch.float64,
+                     device=dev)
+    if world > 1:
+        mx = t[:2].clone()
+        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
+        tot = t[2:].clone()
+        torch.distributed.all_reduce(tot)
+        t = torch.cat([mx, tot])
+    ms_step, e2e_ms_step, h2d, d2h = t.tolist()
+    if rank != 0:
+        return
+    step_bytes = KV_LAYERS * kv_layer_bytes(args.ctx, M)
+    value = step_bytes / (ms_step * 1e-3) / 1e9
+    peaks = {}
+    if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")):
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    peak = peaks.get("hbm_gbs", 6650.0)
+    cpu = None
+    if world == 1 and not args.skip_cpu:
+        v, done, dt = cpu_kv_sample(args)
+        cpu = {"value": v, "unit": "GB/s", "cores": 1, "kind": "port",
+               "sample": "%d query heads of one layer at ctx %d (oracle attention, 1 thread), %.1f s" %
+                         (done, args.ctx, dt)}
+    line = {"metric": KV_METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": kv_config(args, copies),
+            "roofline": {"bound": "hbm", "achieved": value, "peak": peak, "unit": "GB/s", "frac": value / peak,
+                         "traffic": None,
+                         "kernel": "kv4_split_kernel + kv4_combine_kernel (the step's 32 launches, device time)",
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": step_bytes / (e2e_ms_step * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": steps * 2 * KV_LAYERS,
+            "clocks": sampler.summary(), "step_bytes": step_bytes}
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_kv(args, rank, world):
+    if rank != 0:
+        return
+    budget = max(5.0, min(60.0, 90.0 / max(1, args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        cpu_kv_sample(args, 1.0)
+    vals = [cpu_kv_sample(args, budget) for _ in range(max(1, min(args.steps, 3)))]
+    value = float(np.median([v for v, _, _ in vals]))
+    done = sum(d for _, d, _ in vals)
+    sample = "%d query heads of one layer at ctx %d over %d samples (oracle attention, 1 thread)" % (
+        done, args.ctx, len(vals))
+    line = {"impl": "reference", "metric": KV_METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": kv_config(args, KV_LAYERS),
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": 1, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -425,12 +648,15 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--bits", type=int, default=8, choices=[6, 8])
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--workload", default="linear", choices=["linear", "kv4"])
+    ap.add_argument("--ctx", type=int, default=32768, help="kv4: cache rows per layer")
+    ap.add_argument("--kv-splits", type=int, default=-1, help="kv4: 0 reference schedule, -1 one wave over the SMs")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        run_reference(args, rank, world)
+        (run_reference_kv if args.workload == "kv4" else run_reference)(args, rank, world)
         return
     if world > 1:
         import datetime
@@ -439,7 +665,7 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local_rank))
     try:
-        run_b200(args, rank, world, local_rank)
+        (run_kv if args.workload == "kv4" else run_b200)(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch

@@ -192,7 +192,13 @@ YSKN_B200_API int yskn_b200_linear(const yskn_b200_matrix* const* mats, int n_ma
  *   d_v_mean: f32 [n_kv_heads][256] or NULL.
  * Query row m sees cache rows [0, length - M + m]; the last is its own row. Query head
  * j reads KV head j / (n_query_heads / n_kv_heads). n_splits 0 = the reference
- * schedule (31 splits below 4096 rows, else 42), else 1..64 fixed. kb must be 4.
+ * schedule (31 splits below 4096 rows, else 42); 1..64 fixed; -1 = as many splits as
+ * fill one wave of the device's SMs (results differ from other split counts only by
+ * float rounding). kb must be 4. All device pointers 16-byte aligned. One launch: the
+ * last CTA of each (query row, KV head) combines the splits, counting arrivals in a
+ * static device array of 4096 counters that the launch leaves at zero; so M *
+ * n_kv_heads <= 4096, and calls on one device must not overlap (issue them in order
+ * on one stream, as a decode loop does).
  * d_attended: optional f32 [M][n_query_heads][256] (before the inverse rotation).
  * d_out: bf16 [M][n_query_heads][256]. d_work: yskn_b200_kv4_attention_work_bytes(). */
 YSKN_B200_API int64_t yskn_b200_kv4_attention_work_bytes(int M, int n_query_heads, int length, int n_splits);

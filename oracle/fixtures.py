@@ -7,31 +7,13 @@
 * `synthetic()` restates the single-matrix fixture of the reference's kernel tests,
   crates/yskn-engine/tests/fixture/mod.rs:47-114 (seed 0x31875bde0219faff; table
   values (r % 2049)/1024 - 1; row scales (row - P/2)/128).
-* `model_matrix()` makes 27B-shape matrices for the benchmark: uniformly random
-  code words (every bit string is a valid code, docs/FORMAT.md:137-138), an
-  N(0,1)-shaped value table and row scales near 0.02.
+* `model_matrix()` / `normal()` (the benchmark's 27B-shape matrices and activations)
+  are the package's own generators (yskn_b200/synthetic.py), re-exported here.
 """
 import numpy as np
 
 from container import write_container
-
-GOLDEN = np.uint64(0x9E3779B97F4A7C15)
-M1 = np.uint64(0xBF58476D1CE4E5B9)
-M2 = np.uint64(0x94D049BB133111EB)
-
-
-def _mix(z):
-    with np.errstate(over="ignore"):
-        z = (z ^ (z >> np.uint64(30))) * M1
-        z = (z ^ (z >> np.uint64(27))) * M2
-        return z ^ (z >> np.uint64(31))
-
-
-def stream64(seed, n, first=1):
-    """Outputs first..first+n-1 of the splitmix64 sequence started at `seed`."""
-    k = np.arange(first, first + n, dtype=np.uint64)
-    with np.errstate(over="ignore"):
-        return _mix(np.uint64(seed) + k * GOLDEN)
+from yskn_b200.synthetic import GOLDEN, model_matrix, normal, stream64  # noqa: F401
 
 
 def uniform(seed, n, lo, hi):
@@ -121,31 +103,3 @@ def synthetic(bits, layout, rows, physical_rows, cols, output_rotation, stream_o
                       "rule": "mulberry32_7919_13"} if output_rotation else None)}
     model = {"source": "synthetic integration test; no model weights"}
     return write_container(model, [t], [], blobs, data_offset, 1)
-
-
-def model_matrix(rows, cols, bits, seed, physical_rows=None):
-    """Raw arrays for one 27B-shape matrix: warp-layout code words, fp16 table, fp16 row scales.
-
-    Codes: uniformly random bits. Table: N(0,1) values (deterministic Box-Muller on
-    splitmix uniforms). Row scales: 0.02 * (1 + U(-0.1, 0.1)), so that scale * table
-    has a standard deviation near 0.02.
-    """
-    phys = physical_rows or rows
-    n_words = phys * (cols // 256) * 4 * bits
-    words = (stream64(seed, n_words) & np.uint64(0xFFFFFFFF)).astype(np.uint32)
-    u1 = (stream64(seed + 1, 4096) >> np.uint64(11)).astype(np.float64) / 2.0 ** 53
-    u2 = (stream64(seed + 2, 4096) >> np.uint64(11)).astype(np.float64) / 2.0 ** 53
-    r = np.sqrt(-2.0 * np.log(np.maximum(u1, 1e-300)))
-    table = np.concatenate([r * np.cos(2 * np.pi * u2), r * np.sin(2 * np.pi * u2)]).astype(np.float32)
-    u3 = (stream64(seed + 3, phys) >> np.uint64(11)).astype(np.float64) / 2.0 ** 53
-    scales = (0.02 * (1.0 + 0.2 * (u3 - 0.5))).astype(np.float32)
-    return words, _f16_bits(table), _f16_bits(scales)
-
-
-def normal(seed, n):
-    """Deterministic N(0,1) float32 samples (Box-Muller on splitmix uniforms)."""
-    half = (n + 1) // 2
-    u1 = (stream64(seed, half) >> np.uint64(11)).astype(np.float64) / 2.0 ** 53
-    u2 = (stream64(seed ^ 0x5555, half) >> np.uint64(11)).astype(np.float64) / 2.0 ** 53
-    r = np.sqrt(-2.0 * np.log(np.maximum(u1, 1e-300)))
-    return np.concatenate([r * np.cos(2 * np.pi * u2), r * np.sin(2 * np.pi * u2)])[:n].astype(np.float32)

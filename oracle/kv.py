@@ -28,6 +28,7 @@ def _lib():
         L.orc_kv_packed_state.argtypes = [vp, i, i]
         L.orc_kv_cache_sign.restype = C.c_float
         L.orc_kv_inverse_rotate.argtypes = [vp]
+        L.orc_kv_decode_rows.argtypes = [vp, C.c_int64, i, vp, vp]
         _sig = True
     return L
 
@@ -274,9 +275,12 @@ def packed_states(words, bits):
 
 
 def decode_packed_rows(words, bits, codebook_bf16):
-    """decode_packed (kv_codec.rs:485-495) as floats: codebook[packed_state]."""
-    table = (np.asarray(codebook_bf16, np.uint16).astype(np.uint32) << 16).view(np.float32)
-    return table[packed_states(words, bits)]
+    """decode_packed (kv_codec.rs:485-495) as floats: codebook[packed_state] (C loop)."""
+    words = np.ascontiguousarray(np.asarray(words, np.uint32).reshape(-1, 8 * bits))
+    book = np.ascontiguousarray(codebook_bf16, np.uint16)
+    out = np.empty((words.shape[0], 256), np.float32)
+    _lib().orc_kv_decode_rows(O._p(words), C.c_int64(words.shape[0]), bits, O._p(book), O._p(out))
+    return out
 
 
 def prefix_schedule(length):

@@ -463,3 +463,20 @@ void orc_kv_inverse_rotate(float* v) {
       }
   for (int c = 0; c < 256; ++c) v[c] = (v[c] * 0.0625f) * orc_kv_cache_sign(c);
 }
+
+/* decode_packed (kv_codec.rs:485-495) for n_rows rows as floats: book[packed_state]. The
+ * running fold (acc << bits | field) & 0xff, reset at each 64-channel chain, keeps exactly
+ * the last eight stream bits, which is packed_state's window (kv_codec.rs:467-475). */
+void orc_kv_decode_rows(const uint32_t* words, int64_t n_rows, int bits, const uint16_t* book_bf16, float* out) {
+  const int W = 8 * bits;
+  for (int64_t r = 0; r < n_rows; ++r) {
+    const uint32_t* w = words + r * W;
+    int acc = 0;
+    for (int c = 0; c < 256; ++c) {
+      if (c % 64 == 0) acc = 0;
+      acc = ((acc << bits) | field_of(w, bits, c)) & 0xff;
+      const uint32_t u = (uint32_t)book_bf16[acc] << 16;
+      memcpy(out + r * 256 + c, &u, 4);
+    }
+  }
+}

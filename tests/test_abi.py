@@ -74,6 +74,6 @@ def test_kv_attention_argument_errors_are_returned():
     assert call(4, 24, 4, 3, 10, 4, 0) == yskn_b200.EINVAL  # more query rows than cache rows
     assert call(1, 24, 4, 10, 10, 4, 65) == yskn_b200.EINVAL
     assert call(1, 24, 4, 10, 10, 4, 0) == yskn_b200.EINVAL  # null buffers
-    assert L.yskn_b200_kv4_attention_work_bytes(1, 24, 2048, 0) == 24 * 31 * 258 * 4
-    assert L.yskn_b200_kv4_attention_work_bytes(8, 24, 4100, 0) == 8 * 24 * 42 * 258 * 4
+    assert L.yskn_b200_kv4_attention_work_bytes(1, 24, 2048, 0) == 24 * 31 * 260 * 4
+    assert L.yskn_b200_kv4_attention_work_bytes(8, 24, 4100, 0) == 8 * 24 * 42 * 260 * 4
     assert L.yskn_b200_kv4_attention_work_bytes(1, 24, 100, 65) == -1

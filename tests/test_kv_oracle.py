@@ -69,6 +69,15 @@ def test_packed_states_match_c(bits):
             assert st[r, c] == L.orc_kv_packed_state(w.ctypes.data, bits, c)
 
 
+@pytest.mark.parametrize("bits", [4, 5])
+def test_row_decoder_matches_packed_state(bits):
+    rng = np.random.default_rng(10 + bits)
+    words = rng.integers(0, 2**32, size=(5, 8 * bits), dtype=np.uint64).astype(np.uint32)
+    book = rng.integers(0, 2**16, size=256, dtype=np.uint64).astype(np.uint16) & np.uint16(0x7F7F)
+    table = (book.astype(np.uint32) << 16).view(np.float32)
+    assert np.array_equal(kv.decode_packed_rows(words, bits, book), table[kv.packed_states(words, bits)])
+
+
 def test_encoded_bases_decode_back():
     p = kv.parse_profile(kv.synthetic_profile(1, 1, 4))
     table = kv.base_table_bf16(p, 0)

@@ -541,12 +541,13 @@ static int kv_check(int M, int n_qh, int n_kvh, int length, int capacity, int kb
     return fail(YSKN_EINVAL, "kv4 attention: query heads must be a multiple (at most 8x) of the KV heads");
   if (length < M || capacity < length) return fail(YSKN_EINVAL, "kv4 attention: need M <= length <= capacity");
   if (kb != 4) return fail(YSKN_EINVAL, "kv4 attention: only kb = 4 packed rows are supported");
-  if (n_splits < 0 || n_splits > KV_MAX_SPLITS) return fail(YSKN_EINVAL, "kv4 attention: n_splits outside [0, 64]");
+  if (n_splits < -1 || n_splits > KV_MAX_SPLITS) return fail(YSKN_EINVAL, "kv4 attention: n_splits outside [-1, 64]");
   return YSKN_OK;
 }
 
 YSKN_B200_API int64_t yskn_b200_kv4_attention_work_bytes(int M, int n_query_heads, int length, int n_splits) {
-  if (M < 1 || n_query_heads < 1 || length < M || n_splits < 0 || n_splits > KV_MAX_SPLITS) return -1;
+  if (M < 1 || n_query_heads < 1 || length < M || n_splits < -1 || n_splits > KV_MAX_SPLITS) return -1;
+  if (n_splits < 0) return 4 * kv_partials_floats(M, n_query_heads, KV_MAX_SPLITS);  // depends on the device
   KvArgs a{};
   a.M = M;
   a.length = length;
@@ -564,8 +565,9 @@ YSKN_B200_API int yskn_b200_kv4_attention(const uint16_t* d_q, const uint16_t* d
   if (!d_q || !d_k_rows || !d_k_scales || !d_v_rows || !d_v_scales || !d_k_codebook || !d_v_codebook || !d_work ||
       !d_out)
     return fail(YSKN_EINVAL, "kv4 attention: null argument");
-  if (!aligned16(d_k_rows) || !aligned16(d_v_rows) || !aligned16(d_work))
-    return fail(YSKN_EINVAL, "kv4 attention: rows and work area must be 16-byte aligned");
+  if (!aligned16(d_k_rows) || !aligned16(d_v_rows) || !aligned16(d_work) || !aligned16(d_q) || !aligned16(d_out) ||
+      (d_attended && !aligned16(d_attended)))
+    return fail(YSKN_EINVAL, "kv4 attention: queries, rows, outputs and work area must be 16-byte aligned");
   KvArgs a{};
   a.q = d_q;
   a.gate = d_gate;

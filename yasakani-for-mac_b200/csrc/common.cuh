@@ -103,7 +103,8 @@ struct KvArgs {
   int M, n_qh, n_kvh, length, capacity, kb, n_splits;  // n_splits 0: 31 below 4096 rows, else 42
 };
 constexpr int KV_MAX_SPLITS = 64;
-constexpr int KV_MAX_GROUP = 8;  // query heads per KV head
+constexpr int KV_MAX_GROUP = 8;        // query heads per KV head
+constexpr int KV_MAX_ARRIVALS = 4096;  // (query row, KV head) pairs per launch
 int kv_max_splits(const KvArgs& a);
 int64_t kv_partials_floats(int M, int n_qh, int max_splits);
 int launch_kv4_attention(const KvArgs& a, cudaStream_t st);
