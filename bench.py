@@ -640,6 +640,160 @@ def run_reference_kv(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------ GEMM
+# --workload gemm: config 3 of the path: the operator y = W x for M = --gemm-m tokens
+# (4096: prefill, 8: speculative verify) on one 17408 x 5120 bits=8 matrix; M >= 64 runs
+# the tcgen05 GEMM (predecode + kind::i8 MMA), smaller M the decode GEMV.
+GEMM_N, GEMM_K = 17408, 5120
+I8_PEAK_TOPS = 4375.8  # profiles/tcgen05_i8_peak.md (own kind::i8 measurement on this pool)
+
+
+def gemm_config(args):
+    return {"workload": "prefill / verify operator (config 3): y = W x, W 17408 x 5120 bits=8 (4 b/w), M=%d" %
+                        args.gemm_m, "M": args.gemm_m, "N": GEMM_N, "K": GEMM_K, "bits": 8,
+            "path": "tcgen05 kind::i8 GEMM" if args.gemm_m >= 64 else "decode GEMV",
+            "l2": "codes 44.6 MB + predecoded int8 89 MB + activations per step (> L2 at M=4096); "
+                  "the M=8 step streams the 44.6 MB of codes",
+            "parallelism": "single"}
+
+
+def run_gemm(args, rank, world, local_rank):
+    import torch
+    import yskn_b200 as Y
+    from yskn_b200 import synthetic
+    if world > 1:
+        raise SystemExit("--workload gemm runs on one GPU")
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    M, N, K = args.gemm_m, GEMM_N, GEMM_K
+    words, lut16, sc16 = synthetic.model_matrix(N, K, 8, 4242)
+    si = Y.signs("mulberry32_7919_13", 7, 0, K)
+    so = Y.signs("mulberry32_7919_13", 7, K, N)
+    dw = torch.from_numpy(words.view(np.int32)).to(dev)
+    mat = Y.Matrix(dw, "warp", N, N, K, 8, lut16, sc16, si, so)
+    del dw
+    x_host = torch.from_numpy(synthetic.normal(77, M * K).reshape(M, K)).pin_memory()
+    x = x_host.to(dev)
+    y = torch.empty((M, N), dtype=torch.float32, device=dev)
+    y_host = torch.empty((M, N), dtype=torch.float32).pin_memory()
+    work = torch.empty(Y.linear_work_bytes([mat], M), dtype=torch.uint8, device=dev)
+    act = torch.empty((M, K), dtype=torch.int8, device=dev)
+    alpha = torch.empty((M, K // 512), dtype=torch.float32, device=dev)
+    scales = torch.empty((M, K // 512), dtype=torch.int32, device=dev)
+    rq = torch.empty(M, dtype=torch.float32, device=dev)
+    ws = torch.empty((M, N), dtype=torch.int64, device=dev)
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        Y.linear([mat], x, work, [y], stream=stream)
+        Y.quantize(x, mat.signs_in_ptr, act, alpha, scales, rq, stream=stream)
+        Y.weighted_sums([mat], act, scales, [ws], stream=stream)
+    torch.cuda.synchronize()
+    Y.check(Y.status(stream), "status")
+
+    def timed(fn, reps):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            fn()
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, args.warmup)):
+                g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+        del g
+        return e0.elapsed_time(e1) / reps
+
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    ids = [v.strip() for v in visible.split(",") if v.strip()]
+    sampler = ClockSampler(ids[local_rank] if local_rank < len(ids) else str(local_rank))
+    with sampler:
+        ms = timed(lambda: Y.linear([mat], x, work, [y], stream=stream), args.steps)
+        sums_ms = timed(lambda: Y.weighted_sums([mat], act, scales, [ws], stream=stream), args.steps)
+
+        def e2e():
+            x.copy_(x_host, non_blocking=True)
+            Y.linear([mat], x, work, [y], stream=stream)
+            y_host.copy_(y, non_blocking=True)
+        e2e_ms = timed(e2e, max(5, min(args.steps, 50)))
+    Y.check(Y.status(stream), "status")
+    ops = 2.0 * M * N * K
+    value = ops / (ms * 1e-3) / 1e12
+    achieved = ops / (sums_ms * 1e-3) / 1e12
+    cpu = None
+    if not args.skip_cpu:
+        import oracle as O
+        lut8, _ = O.quantize_weight_table(lut16, sc16)
+        act8, _, A, _ = O.quantize_activation(x_host.numpy()[:min(M, 64)], si)
+        threads = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        rows_done = 0
+        while time.perf_counter() - t0 < 10.0 or rows_done == 0:
+            O.fast_weighted_sums(words, "warp", N, K, 8, lut8, act8, A, rows=2048, threads=threads)
+            rows_done += 2048
+        dt = time.perf_counter() - t0
+        cpu = {"value": 2.0 * act8.shape[0] * rows_done * K / dt / 1e12, "unit": "TOPS", "cores": threads,
+               "kind": "port", "sample": "%d tokens x %d weight rows x 5120 (threaded int64 sums), %.1f s" %
+                                        (act8.shape[0], rows_done, dt)}
+    tensor = M >= 64
+    line = {"metric": "compressed linear TOPS (config 3, M=%d)" % M, "value": value, "unit": "TOPS", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "i8", "data": "synthetic", "config": gemm_config(args),
+            "roofline": ({"bound": "tensor", "achieved": achieved, "peak": I8_PEAK_TOPS, "unit": "TOPS",
+                          "frac": achieved / I8_PEAK_TOPS, "traffic": None,
+                          "kernel": "predecode_kernel + gemm_kernel (weighted sums), device time",
+                          "peak_source": "own tcgen05 kind::i8 measurement, profiles/tcgen05_i8_peak.md"}
+                         if tensor else
+                         {"bound": "hbm", "achieved": (N * K / 2 + 8192 + M * K + 8 * M * N) / (sums_ms * 1e-3) / 1e9,
+                          "peak": 6505.9, "unit": "GB/s", "traffic": None, "kernel": "gemv_kernel (weighted sums)",
+                          "frac": (N * K / 2 + 8192 + M * K + 8 * M * N) / (sums_ms * 1e-3) / 1e9 / 6505.9,
+                          "peak_source": "MEASURED_PEAKS.json hbm_gbs"}),
+            "cpu_baseline": cpu,
+            "e2e": {"value": ops / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS", "h2d_bytes_per_step": 4 * M * K,
+                    "d2h_bytes_per_step": 4 * M * N},
+            "gpu_launches": args.steps * (4 if tensor else 1), "clocks": sampler.summary(),
+            "weighted_sums_ms": sums_ms}
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_gemm(args, rank, world):
+    """The reference's CPU path (the oracle's C restatement of the threaded engine kernel)
+    on a bounded sample of the config-3 operator, on all host threads."""
+    if rank != 0:
+        return
+    import oracle as O
+    from yskn_b200 import synthetic
+    words, lut16, sc16 = synthetic.model_matrix(GEMM_N, GEMM_K, 8, 4242)
+    si = O.signs("mulberry32_7919_13", 7, 0, GEMM_K)
+    lut8, _ = O.quantize_weight_table(lut16, sc16)
+    m = min(args.gemm_m, 64)
+    act8, _, A, _ = O.quantize_activation(synthetic.normal(77, m * GEMM_K).reshape(m, GEMM_K), si)
+    threads = os.cpu_count() or 1
+    budget = max(2.0, min(30.0, 90.0 / max(1, args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        O.fast_weighted_sums(words, "warp", GEMM_N, GEMM_K, 8, lut8, act8, A, rows=512, threads=threads)
+    vals = []
+    for _ in range(max(1, min(args.steps, 3))):
+        t0, rows = time.perf_counter(), 0
+        while time.perf_counter() - t0 < budget or rows == 0:
+            O.fast_weighted_sums(words, "warp", GEMM_N, GEMM_K, 8, lut8, act8, A, rows=2048, threads=threads)
+            rows += 2048
+        vals.append(2.0 * m * rows * GEMM_K / (time.perf_counter() - t0) / 1e12)
+    value = float(np.median(vals))
+    line = {"impl": "reference", "metric": "compressed linear TOPS (config 3, M=%d)" % args.gemm_m, "value": value,
+            "unit": "TOPS", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "i8", "data": "synthetic",
+            "config": gemm_config(args),
+            "cpu_baseline": {"value": value, "unit": "TOPS", "cores": threads, "kind": "port",
+                             "sample": "%d tokens x 2048-row blocks of the 17408 x 5120 matrix, %d samples of "
+                                       "%.0f s (threaded int64 sums)" % (m, len(vals), budget)},
+            "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -648,7 +802,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--bits", type=int, default=8, choices=[6, 8])
     ap.add_argument("--skip-cpu", action="store_true")
-    ap.add_argument("--workload", default="linear", choices=["linear", "kv4"])
+    ap.add_argument("--workload", default="linear", choices=["linear", "kv4", "gemm"])
+    ap.add_argument("--gemm-m", type=int, default=4096, help="gemm: activation rows (4096 prefill, 8 verify)")
     ap.add_argument("--ctx", type=int, default=32768, help="kv4: cache rows per layer")
     ap.add_argument("--kv-splits", type=int, default=-1, help="kv4: 0 reference schedule, -1 one wave over the SMs")
     args = ap.parse_args()
@@ -656,7 +811,7 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        (run_reference_kv if args.workload == "kv4" else run_reference)(args, rank, world)
+        {"kv4": run_reference_kv, "gemm": run_reference_gemm}.get(args.workload, run_reference)(args, rank, world)
         return
     if world > 1:
         import datetime
@@ -665,7 +820,7 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local_rank))
     try:
-        (run_kv if args.workload == "kv4" else run_b200)(args, rank, world, local_rank)
+        {"kv4": run_kv, "gemm": run_gemm}.get(args.workload, run_b200)(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch

@@ -230,6 +230,27 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   float* s_alpha = reinterpret_cast<float*>(s_scale + p.mv * G);  // FUSED: group scales
   float* s_rq = s_alpha + p.mv * G;                                // FUSED: row quanta
 
+  // This warp's units; its first unit's codes are requested before the table is built,
+  // so their HBM latency overlaps the table fill (and, fused, the quantiser).
+  const int w_id = (blockIdx.x - S.cta_begin) * GEMV_WARPS + warp;
+  const Ranges R{S.base, S.rem};
+  int u, u_end;
+  if (p.checked) {
+    // One warp per whole row block, groups in ascending order: every i64 add is
+    // checked in the reference's order (compressed_linear.rs:229-248).
+    u = w_id < S.row_blocks ? w_id * G : 0;
+    u_end = w_id < S.row_blocks ? u + G : 0;
+  } else {
+    u = R.begin(w_id);
+    u_end = R.begin(w_id + 1);
+  }
+  constexpr int TILE_WORDS = BITS * 32;
+  // Units are consecutive in memory: (rb, g) -> (rb, g+1) -> (rb+1, 0) is a
+  // stride of two tiles, so the walk needs no division.
+  const uint32_t* ptr = S.codes + ((size_t)(u / G) * p.S + 2 * (u % G)) * TILE_WORDS;
+  Unit<BITS> ua, ub;
+  if (u < u_end) load_unit<BITS>(ua, ptr, lane);
+
   // 16 copies of the int8-pair table: slot s (32 bytes) holds entry s 16 times.
   // The raw 8 KiB table is staged once (one 16-byte load per thread), then each
   // thread writes 16-byte chunks k = tid + 512*i, so a warp's stores cover 512
@@ -286,19 +307,6 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   __syncthreads();
 
   const int nw = S.n_ctas * GEMV_WARPS;
-  const int w_id = (blockIdx.x - S.cta_begin) * GEMV_WARPS + warp;
-  const Ranges R{S.base, S.rem};
-  int u, u_end;
-  if (p.checked) {
-    // One warp per whole row block, groups in ascending order: every i64 add is
-    // checked in the reference's order (compressed_linear.rs:229-248).
-    if (w_id >= S.row_blocks) return;
-    u = w_id * G;
-    u_end = u + G;
-  } else {
-    u = R.begin(w_id);
-    u_end = R.begin(w_id + 1);
-  }
   if (u >= u_end) return;
   const int my_begin = u;
 
@@ -310,7 +318,6 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   const int8_t* act1 = ACT_SMEM ? s_act + tok1 * act_ld : p.act + (size_t)tok1 * Kc;
   const int32_t* sc0 = ACT_SMEM ? s_scale + tok0 * G : p.scales + (size_t)tok0 * G;
   const int32_t* sc1 = ACT_SMEM ? s_scale + tok1 * G : p.scales + (size_t)tok1 * G;
-  constexpr int TILE_WORDS = BITS * 32;
 
   int rb = u / G, g = u % G;
   long long acc[4] = {0, 0, 0, 0};
@@ -355,12 +362,6 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
       }
     }
   };
-  // Units are consecutive in memory: (rb, g) -> (rb, g+1) -> (rb+1, 0) is a
-  // stride of two tiles, so the walk needs no division.
-  const uint32_t* ptr = S.codes + ((size_t)rb * p.S + 2 * g) * TILE_WORDS;
-  Unit<BITS> ua, ub;
-  load_unit<BITS>(ua, ptr, lane);
-
   // One unit: prefetch the next one into `nxt`, compute `cur`; true when done.
   // The loop below alternates the two buffers, so no registers are copied.
   auto step = [&](Unit<BITS>& cur, Unit<BITS>& nxt) -> bool {
