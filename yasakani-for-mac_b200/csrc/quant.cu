@@ -78,10 +78,10 @@ __global__ void __launch_bounds__(256) restore_rot_kernel(int64_t* __restrict__ 
   int64_t* wsr = ws + (int64_t)m * ws_ld;
   restore_block512(wsr, row_quantum[m], inv_rms ? inv_rms + m : nullptr, tau, s_out, b * 512, n_rows,
                    y + (int64_t)m * n_rows, lane, bad);
-  if (clear_ws) {
+  if (clear_ws) {  // the rows this lane read (restore_block512's lane mapping)
 #pragma unroll
-    for (int e = 0; e < 16; e += 2)
-      *reinterpret_cast<longlong2*>(wsr + b * 512 + lane * 16 + e) = make_longlong2(0, 0);
+    for (int k = 0; k < 8; ++k)
+      *reinterpret_cast<longlong2*>(wsr + b * 512 + 64 * k + 2 * lane) = make_longlong2(0, 0);
   }
   if (__any_sync(0xffffffffu, bad) && lane == 0) raise_device_error(err, DERR_NONFINITE);
 }

@@ -113,29 +113,68 @@ __device__ __forceinline__ float restore_value(long long ws, float rq, const flo
 }
 
 // One 512-row block of one token (compressed_linear.rs:313-348): restore, H512,
-// * 1/sqrt(512), * s_out; rows >= n_rows are not stored. ws is read through L2
-// (other SMs may have written it in the same launch).
+// * 1/sqrt(512), * s_out; rows >= n_rows are not stored. Lane l holds rows
+// 64k + 2l + b (k = 0..7, b = 0..1), so each of the warp's loads and stores is one
+// contiguous access (512 B of int64, 256 B of f32), and the butterflies still run in
+// ascending stride order: stride 1 in the lane (b), 2..32 across lanes (lane bits),
+// 64..256 in the lane (k). ws is read through L2 (other SMs may have written it in
+// the same launch).
 __device__ __forceinline__ void restore_block512(const int64_t* wsr, float rq, const float* inv_rms_m,
                                                  const float* __restrict__ tau, const int8_t* __restrict__ s_out,
                                                  int r0, int n_rows, float* __restrict__ yr, int lane, bool& bad) {
   float v[16];
-  const int rl = r0 + lane * 16;
   if (inv_rms_m) bad |= !finite32(*inv_rms_m);
 #pragma unroll
-  for (int e = 0; e < 16; e += 2) {
-    const longlong2 w = __ldcg(reinterpret_cast<const longlong2*>(wsr + rl + e));
-    v[e] = restore_value(w.x, rq, inv_rms_m, __ldg(tau + rl + e));
-    v[e + 1] = restore_value(w.y, rq, inv_rms_m, __ldg(tau + rl + e + 1));
-    bad |= !finite32(v[e]) | !finite32(v[e + 1]);
+  for (int k = 0; k < 8; ++k) {
+    const int r = r0 + 64 * k + 2 * lane;
+    const longlong2 w = __ldcg(reinterpret_cast<const longlong2*>(wsr + r));
+    const float2 t = __ldg(reinterpret_cast<const float2*>(tau + r));
+    v[2 * k] = restore_value(w.x, rq, inv_rms_m, t.x);
+    v[2 * k + 1] = restore_value(w.y, rq, inv_rms_m, t.y);
+    bad |= !finite32(v[2 * k]) | !finite32(v[2 * k + 1]);
   }
-  hadamard512_warp(v, lane);
-  const int4 sp = __ldg(reinterpret_cast<const int4*>(s_out + rl));
-  const int8_t* sb = reinterpret_cast<const int8_t*>(&sp);
 #pragma unroll
-  for (int e = 0; e < 16; ++e) {
-    const float t = __fmul_rn(__fmul_rn(v[e], kHadamardNorm), (float)sb[e]);
-    bad |= !finite32(t);
-    if (rl + e < n_rows) yr[rl + e] = t;
+  for (int k = 0; k < 8; ++k) {  // stride 1
+    const float lower = v[2 * k], upper = v[2 * k + 1];
+    v[2 * k] = __fadd_rn(lower, upper);
+    v[2 * k + 1] = __fsub_rn(lower, upper);
+  }
+#pragma unroll
+  for (int mask = 1; mask < 32; mask <<= 1) {  // strides 2..32
+    const bool upper_half = (lane & mask) != 0;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const float other = __shfl_xor_sync(0xffffffffu, v[e], mask);
+      v[e] = upper_half ? __fsub_rn(other, v[e]) : __fadd_rn(v[e], other);
+    }
+  }
+#pragma unroll
+  for (int kb = 1; kb < 8; kb <<= 1) {  // strides 64, 128, 256
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (k & kb) continue;
+#pragma unroll
+      for (int b = 0; b < 2; ++b) {
+        const float lower = v[2 * k + b], upper = v[2 * (k + kb) + b];
+        v[2 * k + b] = __fadd_rn(lower, upper);
+        v[2 * (k + kb) + b] = __fsub_rn(lower, upper);
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int r = r0 + 64 * k + 2 * lane;
+    const char2 sg = *reinterpret_cast<const char2*>(s_out + r);
+    const float t0 = __fmul_rn(__fmul_rn(v[2 * k], kHadamardNorm), (float)sg.x);
+    const float t1 = __fmul_rn(__fmul_rn(v[2 * k + 1], kHadamardNorm), (float)sg.y);
+    bad |= !finite32(t0) | !finite32(t1);
+    float* dst = yr + r;
+    if (r + 1 < n_rows && (reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
+      *reinterpret_cast<float2*>(dst) = make_float2(t0, t1);
+    } else {
+      if (r < n_rows) dst[0] = t0;
+      if (r + 1 < n_rows) dst[1] = t1;
+    }
   }
 }
 
