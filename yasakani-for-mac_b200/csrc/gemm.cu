@@ -12,15 +12,18 @@
 //     in a workspace, once per call (decoding inside the MMA loop would cost
 //     shared-memory bandwidth the tensor cores need; this is the reference's own
 //     choice for >= 256 rows, q35_g6.cu:35-69).
-//  2. gemm_kernel: one CTA per 128 x 128 output tile (128 activation rows x 128
-//     weight rows). Warp 0 streams 128-byte K chunks of both operands with TMA
-//     (128B swizzle, 4-stage mbarrier ring); one thread of warp 1 issues
+//  2. gemm_kernel: persistent, one CTA per SM looping over 128 x 128 output tiles
+//     (128 activation rows x 128 weight rows) in a grouped raster. Warp 0 streams
+//     128-byte K chunks of both operands with TMA (128B swizzle, 4-stage mbarrier
+//     ring, counted across tiles); one thread of warp 1 issues
 //     tcgen05.mma.cta_group::1.kind::i8 (M=128, N=128, K=32) into TMEM; warps
 //     2..9 drain each 512-column group's int32 tile with tcgen05.ld, multiply it
-//     by the activation row's integer group scale and accumulate i64 in registers.
-//     TMEM is double buffered (2 x 128 columns), so the drain of group g overlaps
-//     the MMAs of group g+1. Activation rows are the MMA's M dimension, so each
-//     epilogue thread owns one activation row and one scale per group.
+//     by the activation row's integer group scale and accumulate i64 in registers,
+//     then write the tile through a shared staging buffer. TMEM holds four group
+//     accumulators (all 512 columns), so the MMAs run up to four groups ahead of
+//     the drain, also across a tile's output write. Activation rows are the MMA's M
+//     dimension, so each epilogue thread owns one activation row and one scale per
+//     group.
 //  Every mbarrier wait is bounded: on timeout the CTA raises YSKN_ETIMEDOUT in
 //  the device error word, stops issuing work, waits (bounded) for its own copies
 //  and frees its TMEM before returning.
@@ -39,7 +42,10 @@ constexpr int GM_BK = 128;    // bytes of K per stage (one 128-byte swizzle row)
 constexpr int GM_STAGES = 4;
 constexpr int GM_THREADS = 320;  // 10 warps
 constexpr int GM_STAGE_BYTES = (GM_BM + GM_BN) * GM_BK;
-constexpr int GM_SMEM = GM_STAGES * GM_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int GM_TMEM_BUFS = 4;  // group accumulators of 128 columns: the whole TMEM
+constexpr int GM_OUT_LD = 64 + 2;  // int64 per staged output row (16 bytes of padding)
+constexpr int GM_OUT_BYTES = GM_BM * GM_OUT_LD * 8;
+constexpr int GM_SMEM = GM_STAGES * GM_STAGE_BYTES + GM_OUT_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr long long GM_WAIT_LIMIT = 4000000000ll;  // clock cycles (~2 s) before a wait gives up
 
 // ------------------------------------------------------------------ PTX helpers
@@ -181,36 +187,37 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;                                 // [stage][128 rows][128 B]
   uint8_t* sB = smem + GM_STAGES * GM_BM * GM_BK;     // [stage][128 rows][128 B]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + GM_STAGES * GM_STAGE_BYTES);
-  uint64_t* full = bars;                      // [GM_STAGES] TMA landed
-  uint64_t* empty = bars + GM_STAGES;         // [GM_STAGES] MMAs done reading
-  uint64_t* tmem_full = bars + 2 * GM_STAGES; // [2] group accumulator ready
-  uint64_t* tmem_empty = tmem_full + 2;       // [2] group accumulator drained
-  uint64_t* drained = tmem_empty + 2;         // all MMAs of this CTA complete
+  long long* stage_out = reinterpret_cast<long long*>(smem + GM_STAGES * GM_STAGE_BYTES);  // [128][GM_OUT_LD]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + GM_STAGES * GM_STAGE_BYTES + GM_OUT_BYTES);
+  uint64_t* full = bars;                           // [GM_STAGES] TMA landed
+  uint64_t* empty = bars + GM_STAGES;              // [GM_STAGES] MMAs done reading
+  uint64_t* tmem_full = bars + 2 * GM_STAGES;      // [GM_TMEM_BUFS] group accumulator ready
+  uint64_t* tmem_empty = tmem_full + GM_TMEM_BUFS; // [GM_TMEM_BUFS] group accumulator drained
+  uint64_t* drained = tmem_empty + GM_TMEM_BUFS;   // all MMAs of this CTA complete
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drained + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Grouped tile order: consecutive CTAs sweep GM_GROUP activation tiles for
-  // each weight tile, so one wave's operands (~16 MB) stay in the 126 MB L2 and
-  // each weight tile is read from HBM about once per GM_GROUP activation tiles.
-  int m_tile, n_tile;
-  {
-    const int t = blockIdx.x, per_group = GM_GROUP * p.n_tiles;
+  const int n_total = p.m_tiles * p.n_tiles;
+  // Grouped tile order: consecutive tiles sweep GM_GROUP activation tiles for each
+  // weight tile, so the tiles in flight across the SMs (~16 MB of operands) stay in
+  // the 126 MB L2 and each weight tile is read from HBM about once per GM_GROUP
+  // activation tiles. CTA c takes tiles c, c + grid, c + 2*grid, ...
+  auto coords = [&](int t, int& m0, int& n0) {
+    const int per_group = GM_GROUP * p.n_tiles;
     const int first_m = (t / per_group) * GM_GROUP;
     const int gsize = min(p.m_tiles - first_m, GM_GROUP);
-    m_tile = first_m + (t % per_group) % gsize;
-    n_tile = (t % per_group) / gsize;
-  }
-  const int m0 = m_tile * GM_BM, n0 = n_tile * GM_BN;
-  const int G = p.G, KB = G * 4;  // 128-byte chunks
+    m0 = (first_m + (t % per_group) % gsize) * GM_BM;
+    n0 = ((t % per_group) / gsize) * GM_BN;
+  };
+  const int G = p.G, KB = G * 4;  // 128-byte chunks per tile
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < GM_STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < GM_TMEM_BUFS; ++b) {
       mbar_init(&tmem_full[b], 1);
       mbar_init(&tmem_empty[b], 8);
     }
@@ -221,7 +228,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(256));
+                 "r"(GM_TMEM_BUFS * GM_BN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -230,50 +237,58 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ---- TMA producer
+    // ---- TMA producer: K chunks of every tile of this CTA through the stage ring
     if (lane == 0) {
-      int issued = 0;
-      for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % GM_STAGES, u = kb / GM_STAGES;
-        if (u > 0 && !mbar_wait(&empty[s], (u - 1) & 1, abort_flag)) break;
-        mbar_expect_tx(&full[s], GM_STAGE_BYTES);
-        tma_load_2d(sA + s * GM_BM * GM_BK, &map_act, &full[s], kb * GM_BK, m0);
-        tma_load_2d(sB + s * GM_BN * GM_BK, &map_w, &full[s], kb * GM_BK, n0);
-        ++issued;
+      int c = 0;  // chunks issued by this CTA
+      for (int t = blockIdx.x; t < n_total && !*abort_flag; t += gridDim.x) {
+        int m0, n0;
+        coords(t, m0, n0);
+        for (int kb = 0; kb < KB; ++kb, ++c) {
+          const int s = c % GM_STAGES, u = c / GM_STAGES;
+          if (u > 0 && !mbar_wait(&empty[s], (u - 1) & 1, abort_flag)) break;
+          mbar_expect_tx(&full[s], GM_STAGE_BYTES);
+          tma_load_2d(sA + s * GM_BM * GM_BK, &map_act, &full[s], kb * GM_BK, m0);
+          tma_load_2d(sB + s * GM_BN * GM_BK, &map_w, &full[s], kb * GM_BK, n0);
+        }
       }
       if (*abort_flag) {
         // Let the copies this thread started land before the CTA leaves.
-        for (int kb = std::max(0, issued - GM_STAGES); kb < issued; ++kb) {
+        for (int k = std::max(0, c - GM_STAGES); k < c; ++k) {
           const long long t0 = clock64();
-          while (!mbar_try_wait(&full[kb % GM_STAGES], (kb / GM_STAGES) & 1) && clock64() - t0 < GM_WAIT_LIMIT) {
+          while (!mbar_try_wait(&full[k % GM_STAGES], (k / GM_STAGES) & 1) && clock64() - t0 < GM_WAIT_LIMIT) {
           }
         }
       }
     }
   } else if (warp == 1) {
-    // ---- MMA issuer (one thread)
+    // ---- MMA issuer (one thread): groups of every tile into the TMEM ring
     if (lane == 0) {
-      for (int g = 0; g < G && !*abort_flag; ++g) {
-        const int b = g & 1, u = g >> 1;
-        if (u > 0 && !mbar_wait(&tmem_empty[b], (u - 1) & 1, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t d = tmem + b * GM_BN;
-        bool ok = true;
-        for (int c = 0; c < 4; ++c) {
-          const int kb = g * 4 + c, s = kb % GM_STAGES;
-          if (!mbar_wait(&full[s], (kb / GM_STAGES) & 1, abort_flag)) {
+      int c = 0, q = 0;  // chunks consumed, groups issued
+      bool ok = true;
+      for (int t = blockIdx.x; t < n_total && ok; t += gridDim.x) {
+        for (int g = 0; g < G && ok; ++g, ++q) {
+          const int b = q % GM_TMEM_BUFS, v = q / GM_TMEM_BUFS;
+          if (v > 0 && !mbar_wait(&tmem_empty[b], (v - 1) & 1, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sA + s * GM_BM * GM_BK), b0 = smem_u32(sB + s * GM_BN * GM_BK);
+          const uint32_t d = tmem + b * GM_BN;
+          for (int cc = 0; cc < 4; ++cc, ++c) {
+            const int s = c % GM_STAGES;
+            if (!mbar_wait(&full[s], (c / GM_STAGES) & 1, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a0 = smem_u32(sA + s * GM_BM * GM_BK), b0 = smem_u32(sB + s * GM_BN * GM_BK);
 #pragma unroll
-          for (int k = 0; k < GM_BK / 32; ++k)
-            umma_i8(d, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), (c > 0 || k > 0) ? 1u : 0u);
-          umma_commit(&empty[s]);  // frees the stage when these MMAs have read it
+            for (int k = 0; k < GM_BK / 32; ++k)
+              umma_i8(d, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), (cc > 0 || k > 0) ? 1u : 0u);
+            umma_commit(&empty[s]);  // frees the stage when these MMAs have read it
+          }
+          if (ok) umma_commit(&tmem_full[b]);
         }
-        if (!ok) break;
-        umma_commit(&tmem_full[b]);
       }
       // Every MMA this thread issued has completed before TMEM can be freed.
       umma_commit(drained);
@@ -283,63 +298,70 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     }
   } else {
     // ---- Epilogue: warps 2..9. TMEM lanes 32*(warp%4).. ; column half (warp-2)/4.
+    // Every epilogue warp runs the same tiles and the same named barriers whether or
+    // not the CTA aborted (then it skips the waits and the stores).
     const int quarter = warp & 3, half = (warp - 2) >> 2;
-    const int row = m0 + quarter * 32 + lane;  // activation row of this thread
-    const int32_t* sc = p.scales + (size_t)min(row, p.M - 1) * G;
-    long long acc[64];
+    int q = 0;  // groups drained
+    for (int t = blockIdx.x; t < n_total; t += gridDim.x) {
+      int m0, n0;
+      coords(t, m0, n0);
+      const int row = m0 + quarter * 32 + lane;  // activation row of this thread
+      const int32_t* sc = p.scales + (size_t)min(row, p.M - 1) * G;
+      long long acc[64];
 #pragma unroll
-    for (int j = 0; j < 64; ++j) acc[j] = 0;
-    int s_next = __ldg(sc);  // the row's scale of the next group, loaded one group ahead
-    for (int g = 0; g < G; ++g) {
-      const int b = g & 1, u = g >> 1;
-      const long long s = s_next;
-      if (g + 1 < G) s_next = __ldg(sc + g + 1);
-      if (!mbar_wait(&tmem_full[b], u & 1, abort_flag)) break;
-      tc_fence_after();
-      const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + b * GM_BN + half * 64;
+      for (int j = 0; j < 64; ++j) acc[j] = 0;
+      int s_next = __ldg(sc);  // the row's scale of the next group, loaded one group ahead
+      for (int g = 0; g < G; ++g, ++q) {
+        const int b = q % GM_TMEM_BUFS, v = q / GM_TMEM_BUFS;
+        const long long s = s_next;
+        if (g + 1 < G) s_next = __ldg(sc + g + 1);
+        if (!mbar_wait(&tmem_full[b], v & 1, abort_flag)) continue;
+        tc_fence_after();
+        const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + b * GM_BN + half * 64;
 #pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t r[32];
+          tmem_ld32(taddr + h * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[h * 32 + j] += s * (long long)(int)r[j];
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tmem_empty[b]);
+      }
+      // Output tile through the staging buffer: one 64-column half at a time, rows
+      // padded by 16 bytes; then each warp writes whole 512-byte row segments (direct
+      // per-row stores from registers measured 24 % slower). The MMA issuer meanwhile
+      // runs the next tile's groups into the other TMEM buffers.
+      const bool live = !*abort_flag;
       for (int h = 0; h < 2; ++h) {
-        uint32_t r[32];
-        tmem_ld32(taddr + h * 32, r);
-        tmem_ld_wait();
+        if (half == h) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) acc[h * 32 + j] += s * (long long)(int)r[j];
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tmem_empty[b]);
-    }
-    // Output tile through shared memory (the pipeline buffers are idle once the
-    // last group is drained): one 64-column half at a time, rows padded by 16
-    // bytes; then each warp writes whole 512-byte row segments.
-    const bool live = !*abort_flag;
-    long long* stage = reinterpret_cast<long long*>(smem);
-    constexpr int LD = 64 + 2;  // int64 per staged row
-    for (int h = 0; h < 2; ++h) {
-      if (half == h) {
-#pragma unroll
-        for (int j = 0; j < 64; j += 2)
-          *reinterpret_cast<longlong2*>(stage + (quarter * 32 + lane) * LD + j) = make_longlong2(acc[j], acc[j + 1]);
-      }
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      if (live) {
-        const int et = threadIdx.x - 64;  // 0..255
-        const int c0 = n0 + h * 64;
-        for (int idx = et; idx < GM_BM * 32; idx += 256) {
-          const int r = idx >> 5, ch = idx & 31;
-          const int orow = m0 + r, col = c0 + 2 * ch;
-          if (orow >= p.M) continue;
-          const longlong2 v = *reinterpret_cast<const longlong2*>(stage + r * LD + 2 * ch);
-          int64_t* dst = p.out + (size_t)orow * p.out_ld + col;
-          if (col + 1 < p.out_rows && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
-            *reinterpret_cast<longlong2*>(dst) = v;
-          } else {
-            if (col < p.out_rows) dst[0] = v.x;
-            if (col + 1 < p.out_rows) dst[1] = v.y;
+          for (int j = 0; j < 64; j += 2)
+            *reinterpret_cast<longlong2*>(stage_out + (quarter * 32 + lane) * GM_OUT_LD + j) =
+                make_longlong2(acc[j], acc[j + 1]);
+        }
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        if (live) {
+          const int et = threadIdx.x - 64;  // 0..255
+          const int c0 = n0 + h * 64;
+          for (int idx = et; idx < GM_BM * 32; idx += 256) {
+            const int r = idx >> 5, ch = idx & 31;
+            const int orow = m0 + r, col = c0 + 2 * ch;
+            if (orow >= p.M) continue;
+            const longlong2 val = *reinterpret_cast<const longlong2*>(stage_out + r * GM_OUT_LD + 2 * ch);
+            int64_t* dst = p.out + (size_t)orow * p.out_ld + col;
+            if (col + 1 < p.out_rows && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+              *reinterpret_cast<longlong2*>(dst) = val;
+            } else {
+              if (col < p.out_rows) dst[0] = val.x;
+              if (col + 1 < p.out_rows) dst[1] = val.y;
+            }
           }
         }
+        asm volatile("bar.sync 1, 256;" ::: "memory");
       }
-      asm volatile("bar.sync 1, 256;" ::: "memory");
     }
   }
   tc_fence_before();
@@ -347,7 +369,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   if (threadIdx.x == 0 && *abort_flag) raise_device_error(p.err, DERR_TIMEOUT);
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(GM_TMEM_BUFS * GM_BN));
   }
 }
 
@@ -421,7 +443,11 @@ int launch_gemm(const MatrixDev& m, const int8_t* act, const int32_t* scales, in
   p.err = device_error_word();
   p.n_tiles = (int)ceil_div(out_rows, GM_BN);
   p.m_tiles = (int)ceil_div(M, GM_BM);
-  gemm_kernel<<<p.n_tiles * p.m_tiles, GM_THREADS, GM_SMEM, st>>>(map_act, map_w, p);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = (int)std::min<int64_t>((int64_t)p.n_tiles * p.m_tiles, sms);  // persistent: one CTA per SM
+  gemm_kernel<<<grid, GM_THREADS, GM_SMEM, st>>>(map_act, map_w, p);
   return cuda_fail(cudaGetLastError(), "gemm_kernel");
 }
 
