@@ -42,12 +42,28 @@ struct DeviceScratch {
 static DeviceScratch g_scratch[64];
 static std::mutex g_scratch_mutex;
 
-static int ensure_scratch(int row_blocks, int64_t gemm_bytes) {
+// rot_rows: physical rows of a matrix with an output rotation (0 without), whose
+// fused decode operator adds its int64 sums into scratch.fused_sums.
+static int ensure_scratch(int row_blocks, int64_t gemm_bytes, int64_t rot_rows) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return fail(YSKN_EINVAL, "device index out of range");
   std::lock_guard<std::mutex> lock(g_scratch_mutex);
   DeviceScratch& d = g_scratch[dev];
+  const int64_t want_sums = 3 * 16 * rot_rows;
+  if (want_sums > d.s.fused_sums_len) {
+    void* s = nullptr;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMalloc(&s, (size_t)want_sums * sizeof(long long));
+    if (e == cudaSuccess) e = cudaMemset(s, 0, (size_t)want_sums * sizeof(long long));
+    if (e != cudaSuccess) {
+      if (s) cudaFree(s);
+      return cuda_fail(e, "fused sums scratch");
+    }
+    if (d.s.fused_sums) cudaFree(d.s.fused_sums);
+    d.s.fused_sums = reinterpret_cast<long long*>(s);
+    d.s.fused_sums_len = want_sums;
+  }
   if (gemm_bytes > d.s.gemm_w_bytes) {
     void* w = nullptr;
     cudaError_t e = cudaDeviceSynchronize();
@@ -148,7 +164,7 @@ using namespace yskn;
 struct yskn_b200_matrix {
   MatrixDev dev{};
   void* codes = nullptr;
-  void* small = nullptr;  // lut8 | tau | s_in | s_out in one allocation
+  void* small = nullptr;  // lut8 | tau | s_in | s_out | lutx in one allocation
   int64_t packed_bytes = 0;
   bool has_rot = false;
 };
@@ -288,12 +304,19 @@ static yskn_b200_matrix* create_matrix(const uint32_t* d_codes, int layout, int 
       return fail(YSKN_EINVAL, "non-finite weight row scales"), nullptr;
   }
 
-  if (ensure_scratch((int)ceil_div(physical_rows, 8), ceil_div(physical_rows, 8) * 8 * (int64_t)cols)) return nullptr;
+  if (ensure_scratch((int)ceil_div(physical_rows, 8), ceil_div(physical_rows, 8) * 8 * (int64_t)cols,
+                     signs_out_host ? physical_rows : 0))
+    return nullptr;
   std::unique_ptr<yskn_b200_matrix> m(new yskn_b200_matrix);
   const int64_t packed = yskn_b200_pack_bytes(physical_rows, cols, bits);
   const size_t off_tau = 8192, off_sin = off_tau + ceil_div(4 * (int64_t)physical_rows, 256) * 256;
   const size_t off_sout = off_sin + ceil_div(cols, 256) * 256;
-  const size_t small_bytes = off_sout + ceil_div(physical_rows, 256) * 256;
+  const size_t off_lutx = off_sout + ceil_div(physical_rows, 256) * 256;
+  const size_t small_bytes = off_lutx + 4096 * 32;
+  // The GEMV's shared-memory image of the table (gemv.cu): slot s = 16 copies of entry s.
+  std::vector<uint16_t> lutx(4096 * 16);
+  for (int s = 0; s < 4096; ++s)
+    for (int c = 0; c < 16; ++c) lutx[16 * s + c] = (uint16_t)((uint8_t)lut8[2 * s] | ((uint8_t)lut8[2 * s + 1] << 8));
   cudaError_t e = cudaMalloc(&m->codes, (size_t)packed);
   if (e == cudaSuccess) e = cudaMalloc(&m->small, small_bytes);
   if (e != cudaSuccess) {
@@ -303,6 +326,7 @@ static yskn_b200_matrix* create_matrix(const uint32_t* d_codes, int layout, int 
   }
   char* small = reinterpret_cast<char*>(m->small);
   e = cudaMemcpy(small, lut8.data(), 8192, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(small + off_lutx, lutx.data(), 4096 * 32, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemcpy(small + off_tau, tau.data(), 4 * (size_t)physical_rows, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemcpy(small + off_sin, signs_in_host, cols, cudaMemcpyHostToDevice);
   if (e == cudaSuccess && signs_out_host)
@@ -321,6 +345,7 @@ static yskn_b200_matrix* create_matrix(const uint32_t* d_codes, int layout, int 
   MatrixDev& d = m->dev;
   d.codes = reinterpret_cast<const uint32_t*>(m->codes);
   d.lut8 = reinterpret_cast<const uint16_t*>(small);
+  d.lutx = reinterpret_cast<const uint8_t*>(small + off_lutx);
   d.tau = reinterpret_cast<const float*>(small + off_tau);
   d.s_in = reinterpret_cast<const int8_t*>(small + off_sin);
   d.s_out = m->has_rot ? reinterpret_cast<const int8_t*>(small + off_sout) : nullptr;
@@ -523,7 +548,7 @@ YSKN_B200_API int yskn_b200_linear(const yskn_b200_matrix* const* mats, int n_ma
   const GemvScratch* sc = current_scratch();
   if (!sc) return fail(YSKN_EINVAL, "linear: no matrix was created on this device");
   if (fused_linear_fits(M, Kc)) {  // decode: one launch for the whole operator
-    if (int rc = launch_linear_fused(devs, n_mats, d_x, M, d_inv_rms, ws, d_y, *sc, st)) return rc;
+    if (int rc = launch_linear_fused(devs, n_mats, d_x, M, d_inv_rms, d_y, *sc, st)) return rc;
     return finish_checked(Kc, stream);
   }
   if (int rc = launch_quantize(d_x, mats[0]->dev.s_in, M, Kc, act, alpha, scales, rq, st)) return rc;

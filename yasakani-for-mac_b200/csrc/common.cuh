@@ -35,6 +35,7 @@ constexpr float kHadamardNorm = 0.044194173824159216f;
 struct MatrixDev {
   const uint32_t* codes;  // B200 streaming layout (see pack.cu)
   const uint16_t* lut8;   // 4096 entries: int8 pair (component 0 low byte, component 1 high byte)
+  const uint8_t* lutx;    // the GEMV's shared-memory image of lut8: 4096 slots of 32 bytes, entry s 16 times in slot s
   const float* tau;       // effective row scale, f32[physical_rows]
   const int8_t* s_in;     // i8[cols]
   const int8_t* s_out;    // i8[physical_rows] or nullptr
@@ -42,12 +43,16 @@ struct MatrixDev {
 };
 
 // Scratch of the decode GEMV's split-row-block reduction (gemv.cu): per-warp i64
-// partials and one arrival counter per 8-row block (zero between launches).
+// partials and one arrival counter per 8-row block (zero between launches); for the
+// fused operator's rotated rows, int64 sums that every contributing warp adds into
+// (zero between launches: the warp that restores a 512-row block clears it).
 struct GemvScratch {
   long long* partials;  // [2 * max_warps][32][4]
   unsigned* counters;   // [n_counters], zeroed at allocation, reset by the kernel
   int64_t n_counters;
   int64_t max_warps;
+  long long* fused_sums;   // [fused_sums_len], zeroed at allocation, cleared by the kernel
+  int64_t fused_sums_len;  // >= 16 tokens x the physical rows of any 3 rotated matrices
   int8_t* gemm_w;        // dense int8 weights of one matrix for the GEMM path
   int64_t gemm_w_bytes;
 };
@@ -71,7 +76,7 @@ int launch_gemv(const MatrixDev* mats, int n_mats, const int8_t* act, const int3
 // whose activations fit in shared memory next to the table, fewer than 512 groups.
 bool fused_linear_fits(int M, int Kc);
 int launch_linear_fused(const MatrixDev* mats, int n_mats, const float* x, int M, const float* inv_rms,
-                        int64_t* const* ws, float* const* y, const GemvScratch& scratch, cudaStream_t st);
+                        float* const* y, const GemvScratch& scratch, cudaStream_t st);
 int launch_quantize(const float* x, const int8_t* signs, int M, int Kc, int8_t* act, float* alpha, int32_t* scales,
                     float* row_quantum, cudaStream_t st);
 int launch_restore(int64_t* ws, int ws_ld, const float* row_quantum, const float* inv_rms, const float* tau,

@@ -39,17 +39,19 @@
 #include <algorithm>
 #include <mutex>
 
+#include "async.cuh"
 #include "quant.cuh"
 
 namespace yskn {
 
 constexpr int GEMV_MAX_SEG = 3;
 constexpr int LUT_COPY_BYTES = 128 * 1024;  // 16 copies x 4096 entries x 2 bytes
-constexpr int LUT_RAW_BYTES = 8192;         // the table as stored, staged for the expansion
+constexpr int LUT_BAR_BYTES = 16;           // the table copy's mbarrier, after the table
+constexpr long long TABLE_WAIT_LIMIT = 2000000000ll;  // clock cycles (~1 s) before the table wait gives up
 
 struct GemvSeg {
   const uint32_t* codes;
-  const uint16_t* lut;
+  const uint8_t* lutx;  // shared-memory image of the table (MatrixDev::lutx)
   int64_t* out;
   unsigned* counters;  // one per row block, zero between launches
   int64_t units;       // row blocks * G
@@ -197,6 +199,19 @@ __device__ __forceinline__ void sequence_mma(const uint32_t (&w)[BITS], int lane
   }
 }
 
+// Arrival of a warp on a GPU-scope counter: the fence (acq_rel, lighter than the
+// sequentially consistent __threadfence) releases every lane's earlier writes, then one
+// lane adds n. Returns the counter's previous value on every lane. The warp that sees
+// the final count runs gpu_acquire() before it reads what the others wrote.
+__device__ __forceinline__ unsigned warp_arrive(unsigned* counter, unsigned n, int lane) {
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+  __syncwarp();
+  unsigned prev = 0;
+  if (lane == 0) prev = atomicAdd(counter, n);
+  return __shfl_sync(0xffffffffu, prev, 0);
+}
+__device__ __forceinline__ void gpu_acquire() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
 // Balanced contiguous ranges: warp w of a segment owns units
 // [w*base + min(w, rem), (w+1)*base + min(w+1, rem)), base = units / warps.
 struct Ranges {
@@ -225,8 +240,9 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   const GemvSeg& S = p.seg[si];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int G = p.G, Kc = p.Kc, act_ld = Kc + 16;
-  int8_t* s_act = reinterpret_cast<int8_t*>(s_lut + LUT_COPY_BYTES + LUT_RAW_BYTES);
-  int32_t* s_scale = reinterpret_cast<int32_t*>(s_lut + LUT_COPY_BYTES + LUT_RAW_BYTES + (size_t)p.mv * act_ld);
+  uint64_t* s_bar = reinterpret_cast<uint64_t*>(s_lut + LUT_COPY_BYTES);
+  int8_t* s_act = reinterpret_cast<int8_t*>(s_lut + LUT_COPY_BYTES + LUT_BAR_BYTES);
+  int32_t* s_scale = reinterpret_cast<int32_t*>(s_lut + LUT_COPY_BYTES + LUT_BAR_BYTES + (size_t)p.mv * act_ld);
   float* s_alpha = reinterpret_cast<float*>(s_scale + p.mv * G);  // FUSED: group scales
   float* s_rq = s_alpha + p.mv * G;                                // FUSED: row quanta
 
@@ -251,20 +267,33 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   Unit<BITS> ua, ub;
   if (u < u_end) load_unit<BITS>(ua, ptr, lane);
 
-  // 16 copies of the int8-pair table: slot s (32 bytes) holds entry s 16 times.
-  // The raw 8 KiB table is staged once (one 16-byte load per thread), then each
-  // thread writes 16-byte chunks k = tid + 512*i, so a warp's stores cover 512
-  // consecutive bytes (no bank conflicts) and every load is issued up front.
-  uint16_t* s_raw = reinterpret_cast<uint16_t*>(s_lut + LUT_COPY_BYTES);
+  // 16 copies of the int8-pair table: slot s (32 bytes) holds entry s 16 times. The
+  // matrix keeps this image prebuilt (MatrixDev::lutx); one thread starts bulk
+  // asynchronous copies of it at once, and they land while the warps quantise the
+  // input (fused) or stage the activations.
+  if (threadIdx.x == 0) {
+    mbar_init(s_bar, 1);
+    mbar_init_fence();
+    mbar_expect_tx(s_bar, LUT_COPY_BYTES);
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      bulk_copy_g2s(s_lut + c * (LUT_COPY_BYTES / 4), S.lutx + c * (LUT_COPY_BYTES / 4), LUT_COPY_BYTES / 4, s_bar);
+  }
   {
-    static_assert(GEMV_WARPS * 32 == 512, "the fill assumes 512 threads");
-    reinterpret_cast<uint4*>(s_raw)[threadIdx.x] = __ldg(reinterpret_cast<const uint4*>(S.lut) + threadIdx.x);
     if (FUSED) {
+      // A warp's groups in turn, each one's inputs requested before the previous is quantised.
       bool bad = false;
-      for (int item = warp; item < p.mv * G; item += GEMV_WARPS) {
+      const int items = p.mv * G;
+      Group512In nxt;
+      if (warp < items) load_group512(p.x + (size_t)(warp / G) * Kc + (warp % G) * 512, p.s_in + (warp % G) * 512,
+                                      lane, nxt);
+      for (int item = warp; item < items; item += GEMV_WARPS) {
         const int m = item / G, g = item - m * G;
-        const float a = quantize_group512(p.x + (size_t)m * Kc + g * 512, p.s_in + g * 512,
-                                          s_act + (size_t)m * act_ld + g * 512, lane, bad);
+        const Group512In cur = nxt;
+        const int after = item + GEMV_WARPS;
+        if (after < items)
+          load_group512(p.x + (size_t)(after / G) * Kc + (after % G) * 512, p.s_in + (after % G) * 512, lane, nxt);
+        const float a = quantize_loaded512(cur, s_act + (size_t)m * act_ld + g * 512, lane, bad);
         if (lane == 0) s_alpha[item] = a;
       }
       if (blockIdx.x == 0 && __any_sync(0xffffffffu, bad) && lane == 0) raise_device_error(p.err, DERR_NONFINITE);
@@ -287,14 +316,10 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
       for (int idx = threadIdx.x; idx < p.mv * G; idx += blockDim.x) s_scale[idx] = __ldg(p.scales + idx);
     }
   }
-  __syncthreads();
-#pragma unroll 4
-  for (int i = 0; i < LUT_COPY_BYTES / 16 / 512; ++i) {
-    const int k = threadIdx.x + 512 * i;  // 16-byte chunk k = half (k & 1) of slot k >> 1
-    const uint32_t h = s_raw[k >> 1];
-    const uint32_t v = h | (h << 16);
-    reinterpret_cast<uint4*>(s_lut)[k] = make_uint4(v, v, v, v);
-  }
+  __syncthreads();  // the barrier is initialised; fused: the group scales are in place
+  // Every thread waits (bounded) for the table. A timeout is reported and the CTA still
+  // runs its units, so the arrival counters and the zero-kept sums stay consistent.
+  if (!mbar_wait_bounded(s_bar, 0, TABLE_WAIT_LIMIT) && threadIdx.x == 0) raise_device_error(p.err, DERR_TIMEOUT);
   if (FUSED) {  // the rows' common integer grids (compressed_linear.rs:113-128)
     for (int item = threadIdx.x; item < p.mv * G; item += blockDim.x) {
       const int m = item / G;
@@ -322,43 +347,23 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   int rb = u / G, g = u % G;
   long long acc[4] = {0, 0, 0, 0};
   bool overflow = false;
-  bool bad = false;  // FUSED: non-finite restored values
+  bool bad = false;       // FUSED: non-finite restored values
+  unsigned pend = 0;      // FUSED, rotated rows: groups added to the current 512-row block, not yet counted
 
-  // Final sums of rows row0, row0 + 1 for tokens n, n + 8 (the C fragment).
+  // Final sums of rows row0, row0 + 1 for tokens n, n + 8 (the C fragment): stored
+  // as int64, or (fused operator, rows without an output rotation) restored to f32.
   auto emit = [&](const long long (&v)[4], int row0) {
-    if (!FUSED || S.s_out) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int tok = n + (i >> 1) * 8, row = row0 + (i & 1);
-        if (tok < p.mv && row < S.out_rows) S.out[(size_t)tok * S.out_ld + row] = v[i];
-      }
-    }
-    if constexpr (FUSED) {
-      if (!S.s_out) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int tok = n + (i >> 1) * 8, row = row0 + (i & 1);
-          if (tok < p.mv && row < S.y_rows) {
-            const float t = restore_value(v[i], s_rq[tok], p.inv_rms ? p.inv_rms + tok : nullptr, __ldg(S.tau + row));
-            bad |= !finite32(t) || (p.inv_rms && !finite32(p.inv_rms[tok]));
-            S.y[(size_t)tok * S.y_rows + row] = t;
-          }
+    for (int i = 0; i < 4; ++i) {
+      const int tok = n + (i >> 1) * 8, row = row0 + (i & 1);
+      if constexpr (FUSED) {
+        if (tok < p.mv && row < S.y_rows) {
+          const float t = restore_value(v[i], s_rq[tok], p.inv_rms ? p.inv_rms + tok : nullptr, __ldg(S.tau + row));
+          bad |= !finite32(t) || (p.inv_rms && !finite32(p.inv_rms[tok]));
+          S.y[(size_t)tok * S.y_rows + row] = t;
         }
       } else {
-        // This 8-row block is final; the last of the 64 in its 512-row block restores the block.
-        __threadfence();
-        __syncwarp();
-        const int blk = rb >> 6;
-        unsigned prev = 0;
-        if (lane == 0) prev = atomicAdd(S.blk_counters + blk, 1u);
-        prev = __shfl_sync(0xffffffffu, prev, 0);
-        if (prev == 63u) {
-          __threadfence();
-          for (int tok = 0; tok < p.mv; ++tok)
-            restore_block512(S.out + (size_t)tok * S.out_ld, s_rq[tok], p.inv_rms ? p.inv_rms + tok : nullptr, S.tau,
-                             S.s_out, blk * 512, S.y_rows, S.y + (size_t)tok * S.y_rows, lane, bad);
-          if (lane == 0) S.blk_counters[blk] = 0u;
-        }
+        if (tok < p.mv && row < S.out_rows) S.out[(size_t)tok * S.out_ld + row] = v[i];
       }
     }
   };
@@ -399,7 +404,37 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
       const int row0 = rb * 8 + 2 * q;
       const int first = rb * G, last = first + G - 1;
       const bool sole = p.checked || (my_begin <= first && u_end > last);
-      if (sole) {
+      if (FUSED && S.s_out) {
+        // Rotated rows: every contributor adds its partial into the zeroed sums (integer
+        // adds commute, so any order gives the same bits) and counts the groups it added
+        // per 512-row block; the warp that brings a block to 64 x G groups restores it,
+        // then clears the sums and the counter for the next launch.
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int tok = n + (i >> 1) * 8;
+          if (tok < p.mv)
+            atomicAdd(reinterpret_cast<unsigned long long*>(S.out + (size_t)tok * S.out_ld + row0 + (i & 1)),
+                      (unsigned long long)acc[i]);
+        }
+        pend += (unsigned)(u - max(my_begin, first));
+        if (!has_next || (rbn >> 6) != (rb >> 6)) {
+          const int blk = rb >> 6;
+          const unsigned prev = warp_arrive(S.blk_counters + blk, pend, lane);
+          if (prev + pend == 64u * (unsigned)G) {
+            gpu_acquire();
+            for (int tok = 0; tok < p.mv; ++tok) {
+              int64_t* wsr = S.out + (size_t)tok * S.out_ld;
+              restore_block512(wsr, s_rq[tok], p.inv_rms ? p.inv_rms + tok : nullptr, S.tau, S.s_out, blk * 512,
+                               S.y_rows, S.y + (size_t)tok * S.y_rows, lane, bad);
+#pragma unroll
+              for (int k = 0; k < 8; ++k)  // the rows this lane read (restore_block512's lane mapping)
+                __stcg(reinterpret_cast<longlong2*>(wsr + blk * 512 + 64 * k + 2 * lane), make_longlong2(0, 0));
+            }
+            if (lane == 0) S.blk_counters[blk] = 0u;
+          }
+          pend = 0;
+        }
+      } else if (sole) {
         emit(acc, row0);
       } else {
         // Split row block: publish this warp's partial; the last of the
@@ -409,14 +444,10 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         long long* mine = p.partials + ((size_t)(gw * 2 + slot_kind) * 32 + lane) * 4;
 #pragma unroll
         for (int i = 0; i < 4; ++i) __stcg(mine + i, acc[i]);
-        __threadfence();
-        __syncwarp();
         const int wf = R.owner(first), wl = R.owner(last);
-        unsigned prev = 0;
-        if (lane == 0) prev = atomicAdd(S.counters + rb, 1u);
-        prev = __shfl_sync(0xffffffffu, prev, 0);
+        const unsigned prev = warp_arrive(S.counters + rb, 1u, lane);
         if (prev == (unsigned)(wl - wf)) {
-          __threadfence();
+          gpu_acquire();
           long long sum[4] = {0, 0, 0, 0};
           for (int cw = wf; cw <= wl; ++cw) {
             const int kind = R.begin(cw) >= first ? 0 : 1;
@@ -464,7 +495,7 @@ static size_t act_smem_bytes(int mv, int Kc, bool fused) {
   const size_t G = Kc / 512;
   return (size_t)mv * (Kc + 16) + 4 * (size_t)mv * G + (fused ? 4 * (size_t)mv * G + 64 : 0);
 }
-static size_t table_smem_bytes() { return LUT_COPY_BYTES + LUT_RAW_BYTES; }
+static size_t table_smem_bytes() { return LUT_COPY_BYTES + LUT_BAR_BYTES; }
 
 template <int BITS, bool M1, bool ACT_SMEM, bool FUSED>
 static int launch_one(const GemvParams& p, int grid, cudaStream_t st) {
@@ -556,7 +587,7 @@ static int build_params(const MatrixDev* mats, int n_mats, const int* out_rows, 
   for (int i = 0; i < n_mats; ++i) {
     GemvSeg& s = p.seg[i];
     s.codes = mats[i].codes;
-    s.lut = mats[i].lut8;
+    s.lutx = mats[i].lutx;
     s.row_blocks = mats[i].phys_pad8 / 8;
     s.units = (int64_t)s.row_blocks * G;
     s.out_rows = out_rows[i];
@@ -603,7 +634,7 @@ bool fused_linear_fits(int M, int Kc) {
 }
 
 int launch_linear_fused(const MatrixDev* mats, int n_mats, const float* x, int M, const float* inv_rms,
-                        int64_t* const* ws, float* const* y, const GemvScratch& scratch, cudaStream_t st) {
+                        float* const* y, const GemvScratch& scratch, cudaStream_t st) {
   if (!fused_linear_fits(M, mats[0].cols)) return fail(YSKN_EINVAL, "fused linear: shape out of range");
   int out_rows[GEMV_MAX_SEG];
   for (int i = 0; i < n_mats; ++i) out_rows[i] = mats[i].phys;
@@ -614,9 +645,15 @@ int launch_linear_fused(const MatrixDev* mats, int n_mats, const float* x, int M
   p.s_in = mats[0].s_in;
   p.inv_rms = inv_rms;
   p.mv = M;
+  int64_t sums_used = 0;  // rotated rows add into the zero-kept scratch sums
   for (int i = 0; i < n_mats; ++i) {
     GemvSeg& s = p.seg[i];
-    s.out = ws[i];
+    s.out = nullptr;
+    if (mats[i].s_out) {
+      s.out = reinterpret_cast<int64_t*>(scratch.fused_sums) + sums_used;
+      sums_used += (int64_t)M * mats[i].phys;
+      if (sums_used > scratch.fused_sums_len) return fail(YSKN_EINVAL, "fused linear: sums scratch too small");
+    }
     s.tau = mats[i].tau;
     s.s_out = mats[i].s_out;
     s.y = y[i];

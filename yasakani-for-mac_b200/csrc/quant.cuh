@@ -46,19 +46,29 @@ __device__ __forceinline__ void hadamard512_warp(float (&v)[16], int lane) {
 
 __device__ __forceinline__ bool finite32(float x) { return (__float_as_uint(x) & 0x7f800000u) != 0x7f800000u; }
 
+// The lane's share of one 512-column group: inputs 16*lane .. 16*lane+15 and their signs.
+struct Group512In {
+  float4 x[4];
+  int4 s;
+};
+__device__ __forceinline__ void load_group512(const float* __restrict__ xg, const int8_t* __restrict__ sg, int lane,
+                                              Group512In& in) {
+  const float4* xp = reinterpret_cast<const float4*>(xg + lane * 16);
+  in.s = __ldg(reinterpret_cast<const int4*>(sg + lane * 16));
+#pragma unroll
+  for (int q = 0; q < 4; ++q) in.x[q] = __ldg(xp + q);
+}
+
 // One 512-column group of one activation row (compressed_linear.rs:57-112): x*s_in,
 // H512, half(v * 1/sqrt(512)), alpha = max|v|/127, q = clamp(rne(v/alpha), +-127).
-// xg, sg: the group's 512 inputs and input signs; the lane's 16 int8 go to dst
+// in: the lane's inputs and signs (load_group512); the lane's 16 int8 go to dst
 // (16-byte aligned). Returns alpha on every lane; `bad` collects non-finite values.
-__device__ __forceinline__ float quantize_group512(const float* __restrict__ xg, const int8_t* __restrict__ sg,
-                                                   int8_t* dst, int lane, bool& bad) {
+__device__ __forceinline__ float quantize_loaded512(const Group512In& in, int8_t* dst, int lane, bool& bad) {
   float v[16];
-  const float4* xp = reinterpret_cast<const float4*>(xg + lane * 16);
-  const int4 sp = __ldg(reinterpret_cast<const int4*>(sg + lane * 16));
-  const int8_t* sb = reinterpret_cast<const int8_t*>(&sp);
+  const int8_t* sb = reinterpret_cast<const int8_t*>(&in.s);
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    const float4 f = __ldg(xp + q);
+    const float4 f = in.x[q];
     v[4 * q + 0] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
   }
 #pragma unroll
@@ -92,6 +102,13 @@ __device__ __forceinline__ float quantize_group512(const float* __restrict__ xg,
   *reinterpret_cast<uint4*>(dst + lane * 16) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
   return scale;
 }
+// xg, sg: the group's 512 inputs and input signs.
+__device__ __forceinline__ float quantize_group512(const float* __restrict__ xg, const int8_t* __restrict__ sg,
+                                                   int8_t* dst, int lane, bool& bad) {
+  Group512In in;
+  load_group512(xg, sg, lane, in);
+  return quantize_loaded512(in, dst, lane, bad);
+}
 
 // The row's common 2^24 integer grid (compressed_linear.rs:113-128) from its group
 // scales: multiplier 2^24 / max alpha, and row_quantum = max alpha * 2^-24.
@@ -123,12 +140,14 @@ __device__ __forceinline__ void restore_block512(const int64_t* wsr, float rq, c
                                                  const float* __restrict__ tau, const int8_t* __restrict__ s_out,
                                                  int r0, int n_rows, float* __restrict__ yr, int lane, bool& bad) {
   float v[16];
+  char2 sg[8];  // output signs, requested with the sums so their latency overlaps
   if (inv_rms_m) bad |= !finite32(*inv_rms_m);
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     const int r = r0 + 64 * k + 2 * lane;
     const longlong2 w = __ldcg(reinterpret_cast<const longlong2*>(wsr + r));
     const float2 t = __ldg(reinterpret_cast<const float2*>(tau + r));
+    sg[k] = __ldg(reinterpret_cast<const char2*>(s_out + r));
     v[2 * k] = restore_value(w.x, rq, inv_rms_m, t.x);
     v[2 * k + 1] = restore_value(w.y, rq, inv_rms_m, t.y);
     bad |= !finite32(v[2 * k]) | !finite32(v[2 * k + 1]);
@@ -164,9 +183,8 @@ __device__ __forceinline__ void restore_block512(const int64_t* wsr, float rq, c
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     const int r = r0 + 64 * k + 2 * lane;
-    const char2 sg = *reinterpret_cast<const char2*>(s_out + r);
-    const float t0 = __fmul_rn(__fmul_rn(v[2 * k], kHadamardNorm), (float)sg.x);
-    const float t1 = __fmul_rn(__fmul_rn(v[2 * k + 1], kHadamardNorm), (float)sg.y);
+    const float t0 = __fmul_rn(__fmul_rn(v[2 * k], kHadamardNorm), (float)sg[k].x);
+    const float t1 = __fmul_rn(__fmul_rn(v[2 * k + 1], kHadamardNorm), (float)sg[k].y);
     bad |= !finite32(t0) | !finite32(t1);
     float* dst = yr + r;
     if (r + 1 < n_rows && (reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
