@@ -36,6 +36,14 @@
 //   writes its i64 partial to scratch, and the last one to arrive (a counter per
 //   row block) adds the partials and stores the result, then resets the counter.
 //   The output is written exactly once, so it needs no zeroing.
+// * Fused operator, rows with an output rotation: contributors add their partials
+//   into int64 sums kept zero in library scratch (64-bit integer reductions, exact
+//   in any order) and count the groups they added per 512-row block; the warp that
+//   completes a block restores and rotates it, then clears the sums and the count.
+//   One arrival per warp and block replaces the per-row-block hand-over.
+// * Prologue: the input groups are requested first, then the first unit's codes,
+//   then the 128 KiB table image (one bulk asynchronous copy), so the quantiser's
+//   input latency, the code fetch and the table copy overlap.
 #include <algorithm>
 #include <mutex>
 
@@ -246,6 +254,13 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   float* s_alpha = reinterpret_cast<float*>(s_scale + p.mv * G);  // FUSED: group scales
   float* s_rq = s_alpha + p.mv * G;                                // FUSED: row quanta
 
+  // Fused: the first input group of this warp is requested first of all, ahead of the
+  // code and table traffic below, since the quantiser's latency starts with it.
+  const int items = FUSED ? p.mv * G : 0;
+  Group512In nxt;
+  if (FUSED && warp < items)
+    load_group512(p.x + (size_t)(warp / G) * Kc + (warp % G) * 512, p.s_in + (warp % G) * 512, lane, nxt);
+
   // This warp's units; its first unit's codes are requested before the table is built,
   // so their HBM latency overlaps the table fill (and, fused, the quantiser).
   const int w_id = (blockIdx.x - S.cta_begin) * GEMV_WARPS + warp;
@@ -270,7 +285,8 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   // 16 copies of the int8-pair table: slot s (32 bytes) holds entry s 16 times. The
   // matrix keeps this image prebuilt (MatrixDev::lutx); one thread starts bulk
   // asynchronous copies of it at once, and they land while the warps quantise the
-  // input (fused) or stage the activations.
+  // input (fused) or stage the activations. (Expanding the stored 8 KiB table in
+  // shared memory instead costs every SM about 0.5 us more, measured.)
   if (threadIdx.x == 0) {
     mbar_init(s_bar, 1);
     mbar_init_fence();
@@ -283,10 +299,6 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
     if (FUSED) {
       // A warp's groups in turn, each one's inputs requested before the previous is quantised.
       bool bad = false;
-      const int items = p.mv * G;
-      Group512In nxt;
-      if (warp < items) load_group512(p.x + (size_t)(warp / G) * Kc + (warp % G) * 512, p.s_in + (warp % G) * 512,
-                                      lane, nxt);
       for (int item = warp; item < items; item += GEMV_WARPS) {
         const int m = item / G, g = item - m * G;
         const Group512In cur = nxt;
@@ -319,7 +331,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   __syncthreads();  // the barrier is initialised; fused: the group scales are in place
   // Every thread waits (bounded) for the table. A timeout is reported and the CTA still
   // runs its units, so the arrival counters and the zero-kept sums stay consistent.
-  if (!mbar_wait_bounded(s_bar, 0, TABLE_WAIT_LIMIT) && threadIdx.x == 0) raise_device_error(p.err, DERR_TIMEOUT);
+  if (!mbar_wait_bounded(s_bar, 0, TABLE_WAIT_LIMIT) && lane == 0) raise_device_error(p.err, DERR_TIMEOUT);
   if (FUSED) {  // the rows' common integer grids (compressed_linear.rs:113-128)
     for (int item = threadIdx.x; item < p.mv * G; item += blockDim.x) {
       const int m = item / G;

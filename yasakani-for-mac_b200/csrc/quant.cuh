@@ -59,22 +59,40 @@ __device__ __forceinline__ void load_group512(const float* __restrict__ xg, cons
   for (int q = 0; q < 4; ++q) in.x[q] = __ldg(xp + q);
 }
 
+// rne(fl(v / scale)) as an int, where scale > 0 and |v / scale| <= 128: the quotient
+// is estimated as y = v * rcp (rcp = 1/scale correctly rounded), within 1.5 * 2^-23
+// relative of the correctly rounded quotient, i.e. within 2.3e-5 of it. Unless y lies
+// within 2^-14 of a half-integer, both round to the same integer, read off
+// y + 1.5 * 2^23 (exact round-to-nearest-even into the low mantissa bits). Otherwise,
+// and for non-finite values, the exact division decides.
+__device__ __forceinline__ int quotient_rne(float v, float scale, float rcp) {
+  const float y = __fmul_rn(v, rcp);
+  const float t = __fadd_rn(y, 12582912.0f);                 // 1.5 * 2^23
+  const float d = __fsub_rn(y, __fsub_rn(t, 12582912.0f));  // y - rne(y), exact
+  if (fabsf(d) < 0.49993896484375f) return (int)(__float_as_uint(t) - 0x4B400000u);  // 0.5 - 2^-14
+  return __float2int_rn(__fdiv_rn(v, scale));
+}
+
 // One 512-column group of one activation row (compressed_linear.rs:57-112): x*s_in,
 // H512, half(v * 1/sqrt(512)), alpha = max|v|/127, q = clamp(rne(v/alpha), +-127).
 // in: the lane's inputs and signs (load_group512); the lane's 16 int8 go to dst
 // (16-byte aligned). Returns alpha on every lane; `bad` collects non-finite values.
 __device__ __forceinline__ float quantize_loaded512(const Group512In& in, int8_t* dst, int lane, bool& bad) {
   float v[16];
-  const int8_t* sb = reinterpret_cast<const int8_t*>(&in.s);
+  const uint32_t* sw = reinterpret_cast<const uint32_t*>(&in.s);
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     const float4 f = in.x[q];
     v[4 * q + 0] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
   }
+  // x * s for s = +1/-1 is x with its sign bit flipped when s < 0 (bit 7 of the sign
+  // byte). For a NaN x the product would be the canonical NaN instead, but every value
+  // then passes through an add of the first butterfly, which makes any NaN canonical.
 #pragma unroll
   for (int e = 0; e < 16; ++e) {
     bad |= !finite32(v[e]);
-    v[e] = __fmul_rn(v[e], (float)sb[e]);
+    const uint32_t flip = (sw[e >> 2] << (24 - 8 * (e & 3))) & 0x80000000u;
+    v[e] = __uint_as_float(__float_as_uint(v[e]) ^ flip);
   }
   hadamard512_warp(v, lane);
   float mx = 0.0f;
@@ -87,13 +105,14 @@ __device__ __forceinline__ float quantize_loaded512(const Group512In& in, int8_t
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   const float scale = __fdiv_rn(mx, 127.0f);
+  const float rcp = __frcp_rn(scale);
   uint32_t packed[4];
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     uint32_t w = 0;
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
-      int r = scale > 0.0f ? __float2int_rn(__fdiv_rn(v[4 * q + b], scale)) : 0;
+      int r = scale > 0.0f ? quotient_rne(v[4 * q + b], scale, rcp) : 0;
       r = max(-127, min(127, r));
       w |= (uint32_t)(r & 0xff) << (8 * b);
     }
