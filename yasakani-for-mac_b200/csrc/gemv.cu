@@ -62,13 +62,13 @@ struct GemvSeg {
   const uint8_t* lutx;  // shared-memory image of the table (MatrixDev::lutx)
   int64_t* out;
   unsigned* counters;  // one per row block, zero between launches
-  int64_t units;       // row blocks * G
+  int64_t tiles;       // row blocks * 2G
   int row_blocks;
   int out_rows;        // rows written (<= physical rows)
   int out_ld;
   int cta_begin;       // first CTA of this segment
   int n_ctas;
-  int base, rem;       // balanced unit ranges of the segment's warps
+  int base, rem;       // balanced tile ranges of the segment's warps
   // Fused operator only: restore into y instead of returning int64 sums.
   const float* tau;
   const int8_t* s_out;     // output rotation signs (sums go to `out` first), or nullptr
@@ -81,7 +81,6 @@ struct GemvParams {
   GemvSeg seg[GEMV_MAX_SEG];
   int n_seg;
   int G;
-  int S;  // sequences per row (cols / 256)
   int Kc;
   const int8_t* act;
   const int32_t* scales;
@@ -220,14 +219,14 @@ __device__ __forceinline__ unsigned warp_arrive(unsigned* counter, unsigned n, i
 }
 __device__ __forceinline__ void gpu_acquire() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
-// Balanced contiguous ranges: warp w of a segment owns units
-// [w*base + min(w, rem), (w+1)*base + min(w+1, rem)), base = units / warps.
+// Balanced contiguous ranges: warp w of a segment owns tiles
+// [w*base + min(w, rem), (w+1)*base + min(w+1, rem)), base = tiles / warps.
 struct Ranges {
   int base, rem;
   __device__ __forceinline__ int begin(int w) const { return w * base + min(w, rem); }
-  __device__ __forceinline__ int owner(int u) const {
+  __device__ __forceinline__ int owner(int t) const {
     const int cut = rem * (base + 1);
-    return u < cut ? u / (base + 1) : rem + (u - cut) / base;
+    return t < cut ? t / (base + 1) : rem + (t - cut) / base;
   }
 };
 
@@ -261,24 +260,29 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   if (FUSED && warp < items)
     load_group512(p.x + (size_t)(warp / G) * Kc + (warp % G) * 512, p.s_in + (warp % G) * 512, lane, nxt);
 
-  // This warp's units; its first unit's codes are requested before the table is built,
-  // so their HBM latency overlaps the table fill (and, fused, the quantiser).
+  // This warp's tiles [t_begin, t_end) (tile t = sequence t % 2G of row block t / 2G),
+  // walked as units u = (row block, group) = tiles 2u, 2u+1; only the first and the
+  // last unit can be half units. Its first unit's codes are requested before the table
+  // is built, so their HBM latency overlaps the table copy (and, fused, the quantiser).
   const int w_id = (blockIdx.x - S.cta_begin) * GEMV_WARPS + warp;
   const Ranges R{S.base, S.rem};
-  int u, u_end;
+  const int T2 = 2 * G;  // tiles per row block
+  int t_begin, t_end;
   if (p.checked) {
     // One warp per whole row block, groups in ascending order: every i64 add is
     // checked in the reference's order (compressed_linear.rs:229-248).
-    u = w_id < S.row_blocks ? w_id * G : 0;
-    u_end = w_id < S.row_blocks ? u + G : 0;
+    t_begin = w_id < S.row_blocks ? w_id * T2 : 0;
+    t_end = w_id < S.row_blocks ? t_begin + T2 : 0;
   } else {
-    u = R.begin(w_id);
-    u_end = R.begin(w_id + 1);
+    t_begin = R.begin(w_id);
+    t_end = R.begin(w_id + 1);
   }
+  int u = t_begin >> 1;
+  const int u_end = (t_end + 1) >> 1;
   constexpr int TILE_WORDS = BITS * 32;
-  // Units are consecutive in memory: (rb, g) -> (rb, g+1) -> (rb+1, 0) is a
-  // stride of two tiles, so the walk needs no division.
-  const uint32_t* ptr = S.codes + ((size_t)(u / G) * p.S + 2 * (u % G)) * TILE_WORDS;
+  // The tiles of a row block are consecutive in memory, so units are a stride of two
+  // tiles apart and the walk needs no division.
+  const uint32_t* ptr = S.codes + (size_t)u * 2 * TILE_WORDS;
   Unit<BITS> ua, ub;
   if (u < u_end) load_unit<BITS>(ua, ptr, lane);
 
@@ -343,9 +347,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   }
   __syncthreads();
 
-  const int nw = S.n_ctas * GEMV_WARPS;
-  if (u >= u_end) return;
-  const int my_begin = u;
+  if (t_begin >= t_end) return;
 
   const uint32_t copy_off = (uint32_t)(lane >> 1) << 1;
   const int q = lane & 3, n = lane >> 2;
@@ -360,7 +362,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   long long acc[4] = {0, 0, 0, 0};
   bool overflow = false;
   bool bad = false;       // FUSED: non-finite restored values
-  unsigned pend = 0;      // FUSED, rotated rows: groups added to the current 512-row block, not yet counted
+  unsigned pend = 0;      // FUSED, rotated rows: tiles added to the current 512-row block, not yet counted
 
   // Final sums of rows row0, row0 + 1 for tokens n, n + 8 (the C fragment): stored
   // as int64, or (fused operator, rows without an output rotation) restored to f32.
@@ -394,8 +396,10 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
     const int col = g * 512 + q * 64;
     const uint4* a0p = reinterpret_cast<const uint4*>(act0 + col);
     const uint4* a1p = reinterpret_cast<const uint4*>(act1 + col);
-    sequence_mma<BITS, M1>(cur.w[0], lane, s_lut, copy_off, a0p, a1p, c);
-    sequence_mma<BITS, M1>(cur.w[1], lane, s_lut, copy_off, a0p + 16, a1p + 16, c);
+    // A half unit at either end of the range holds one tile (the integer dot of a half
+    // group, scaled by the group's scale, adds up exactly with the other half's).
+    if (2 * u >= t_begin) sequence_mma<BITS, M1>(cur.w[0], lane, s_lut, copy_off, a0p, a1p, c);
+    if (2 * u + 1 < t_end) sequence_mma<BITS, M1>(cur.w[1], lane, s_lut, copy_off, a0p + 16, a1p + 16, c);
     const long long s0 = sc0[g], s1 = sc1[g];
     const long long t[4] = {s0 * c[0], s0 * c[1], s1 * c[2], s1 * c[3]};
     if (p.checked) {
@@ -414,12 +418,12 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
     if (!has_next || rbn != rb) {
       // Rows 2q, 2q+1 of the block for tokens n and n+8 (the C fragment).
       const int row0 = rb * 8 + 2 * q;
-      const int first = rb * G, last = first + G - 1;
-      const bool sole = p.checked || (my_begin <= first && u_end > last);
+      const int first = rb * T2, last = first + T2 - 1;  // the row block's tiles
+      const bool sole = p.checked || (t_begin <= first && t_end > last);
       if (FUSED && S.s_out) {
         // Rotated rows: every contributor adds its partial into the zeroed sums (integer
-        // adds commute, so any order gives the same bits) and counts the groups it added
-        // per 512-row block; the warp that brings a block to 64 x G groups restores it,
+        // adds commute, so any order gives the same bits) and counts the tiles it added
+        // per 512-row block; the warp that brings a block to 64 x 2G tiles restores it,
         // then clears the sums and the counter for the next launch.
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -428,11 +432,11 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
             atomicAdd(reinterpret_cast<unsigned long long*>(S.out + (size_t)tok * S.out_ld + row0 + (i & 1)),
                       (unsigned long long)acc[i]);
         }
-        pend += (unsigned)(u - max(my_begin, first));
+        pend += (unsigned)(min(2 * u, t_end) - max(t_begin, first));
         if (!has_next || (rbn >> 6) != (rb >> 6)) {
           const int blk = rb >> 6;
           const unsigned prev = warp_arrive(S.blk_counters + blk, pend, lane);
-          if (prev + pend == 64u * (unsigned)G) {
+          if (prev + pend == 64u * (unsigned)T2) {
             gpu_acquire();
             for (int tok = 0; tok < p.mv; ++tok) {
               int64_t* wsr = S.out + (size_t)tok * S.out_ld;
@@ -452,7 +456,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         // Split row block: publish this warp's partial; the last of the
         // contributing warps (consecutive, all non-empty) adds them up.
         const int gw = blockIdx.x * GEMV_WARPS + warp;  // global warp id: scratch slot owner
-        const int slot_kind = my_begin >= first ? 0 : 1;
+        const int slot_kind = t_begin >= first ? 0 : 1;
         long long* mine = p.partials + ((size_t)(gw * 2 + slot_kind) * 32 + lane) * 4;
 #pragma unroll
         for (int i = 0; i < 4; ++i) __stcg(mine + i, acc[i]);
@@ -485,7 +489,6 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   }
   if (p.checked && __any_sync(0xffffffffu, overflow) && lane == 0) raise_device_error(p.err, DERR_OVERFLOW);
   if (FUSED && __any_sync(0xffffffffu, bad) && lane == 0) raise_device_error(p.err, DERR_NONFINITE);
-  (void)nw;
 }
 
 static int sm_count() {
@@ -553,13 +556,12 @@ static int build_params(const MatrixDev* mats, int n_mats, const int* out_rows, 
   p = GemvParams{};
   p.n_seg = n_mats;
   p.G = G;
-  p.S = Kc / 256;
   p.Kc = Kc;
   p.checked = G >= 512 ? 1 : 0;
   p.partials = scratch.partials;
   p.err = device_error_word();
-  int64_t total = 0;
-  for (int i = 0; i < n_mats; ++i) total += (int64_t)(mats[i].phys_pad8 / 8) * G;
+  int64_t total = 0;  // tiles of the call
+  for (int i = 0; i < n_mats; ++i) total += (int64_t)(mats[i].phys_pad8 / 8) * 2 * G;
   if (total >= (int64_t)1 << 31) return fail(YSKN_EINVAL, "gemv: matrix too large for one call");
   int64_t want[GEMV_MAX_SEG];
   if (p.checked) {
@@ -569,8 +571,8 @@ static int build_params(const MatrixDev* mats, int n_mats, const int* out_rows, 
     double frac[GEMV_MAX_SEG];
     int64_t used = 0;
     for (int i = 0; i < n_mats; ++i) {
-      const int64_t units = (int64_t)(mats[i].phys_pad8 / 8) * G;
-      const double exact = (double)budget * units / total;
+      const int64_t tiles = (int64_t)(mats[i].phys_pad8 / 8) * 2 * G;
+      const double exact = (double)budget * tiles / total;
       want[i] = std::max<int64_t>(1, (int64_t)exact);
       frac[i] = exact - (double)(int64_t)exact;
       used += want[i];
@@ -590,8 +592,8 @@ static int build_params(const MatrixDev* mats, int n_mats, const int* out_rows, 
       --want[big];
       --used;
     }
-    for (int i = 0; i < n_mats; ++i)  // no more CTAs than unit runs of 16 warps
-      want[i] = std::max<int64_t>(1, std::min<int64_t>(want[i], ceil_div((int64_t)(mats[i].phys_pad8 / 8) * G,
+    for (int i = 0; i < n_mats; ++i)  // no more CTAs than tile runs of 16 warps
+      want[i] = std::max<int64_t>(1, std::min<int64_t>(want[i], ceil_div((int64_t)(mats[i].phys_pad8 / 8) * 2 * G,
                                                                           GEMV_WARPS)));
   }
   grid = 0;
@@ -601,7 +603,7 @@ static int build_params(const MatrixDev* mats, int n_mats, const int* out_rows, 
     s.codes = mats[i].codes;
     s.lutx = mats[i].lutx;
     s.row_blocks = mats[i].phys_pad8 / 8;
-    s.units = (int64_t)s.row_blocks * G;
+    s.tiles = (int64_t)s.row_blocks * 2 * G;
     s.out_rows = out_rows[i];
     s.out_ld = out_rows[i];
     s.counters = cnt;
@@ -613,8 +615,8 @@ static int build_params(const MatrixDev* mats, int n_mats, const int* out_rows, 
     s.cta_begin = grid;
     s.n_ctas = (int)want[i];
     const int64_t nw = want[i] * GEMV_WARPS;
-    s.base = (int)(s.units / nw);
-    s.rem = (int)(s.units % nw);
+    s.base = (int)(s.tiles / nw);
+    s.rem = (int)(s.tiles % nw);
     grid += (int)want[i];
   }
   if ((int64_t)(cnt - scratch.counters) > scratch.n_counters ||
