@@ -45,9 +45,9 @@ LAYER = [("q_proj", 12288, 5120), ("k_proj", 1024, 5120), ("v_proj", 1024, 5120)
 ROW_PARALLEL = {"o_proj", "out_proj", "down_proj"}
 CALLS = [["q_proj", "k_proj", "v_proj"], ["o_proj"], ["in_proj_qkv", "in_proj_z"], ["out_proj"],
          ["gate_proj", "up_proj"], ["down_proj"]]
-# DRAM bytes (read + write) of the six weighted-sums launches of one step, from one ncu
-# capture of this workload (profiles/gemv_kernel_layer_bits8.md); None where not captured.
-GEMV_TRAFFIC = {(8, 1): 244_913_920}
+# DRAM bytes (read + write) of the six fused gemv_kernel launches of one step, from one
+# ncu capture of this workload (profiles/gemv_kernel_layer_bits8.md); None where not captured.
+GEMV_TRAFFIC = {(8, 1): 248_152_576}
 METRIC = "compressed GEMV HBM TB/s (one hybrid layer's linear set, batch-1 decode)"
 UNIT = "TB/s"
 
@@ -299,24 +299,33 @@ def run_b200(args, rank, world, local_rank):
         e1.record(stream)
         barrier()
         ms = e0.elapsed_time(e1)
-        # Dominant kernel: time the weighted-sums launches alone, same matrices, same order.
-        acts = [torch.empty((M, x.shape[1]), dtype=torch.int8, device=dev) for x in xs]
-        scs = [torch.empty((M, x.shape[1] // 512), dtype=torch.int32, device=dev) for x in xs]
-        wss = [[torch.empty((M, mats[n].physical_rows), dtype=torch.int64, device=dev) for n in c] for c in CALLS]
-        for g, x, a, s in zip(group, xs, acts, scs):
-            al = torch.empty((M, x.shape[1] // 512), dtype=torch.float32, device=dev)
-            rq = torch.empty(M, dtype=torch.float32, device=dev)
-            Y.quantize(x, g[0].signs_in_ptr, a, al, s, rq, stream=stream)
-        # Each weighted-sums call captured alone in a graph with events on the
-        # launching stream, replayed in step order (device time, no host gaps).
+        # Per call: each launch captured alone in a graph with events on the launching
+        # stream, replayed in step order (device time, no host gaps; each figure holds
+        # one graph launch's latency). One GPU: the step's own launches, the fused
+        # operator (gemv_kernel quantises, sums and restores); tensor parallel: the
+        # weighted-sums launches of the same matrices, which set the roofline there.
         reps = max(20, min(200, args.steps))
         gemv_ms = [0.0] * len(CALLS)
         graphs = []
-        for g, a, s, o in zip(group, acts, scs, wss):
-            gg = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(gg, stream=stream):
-                Y.weighted_sums(g, a, s, o, stream=stream)
-            graphs.append(gg)
+        if world == 1:
+            for c, g, x, wk, y in zip(CALLS, group, xs, works, ys):
+                gg = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gg, stream=stream):
+                    Y.linear(g, x, wk, y, stream=stream)
+                graphs.append(gg)
+        else:
+            acts = [torch.empty((M, x.shape[1]), dtype=torch.int8, device=dev) for x in xs]
+            scs = [torch.empty((M, x.shape[1] // 512), dtype=torch.int32, device=dev) for x in xs]
+            wss = [[torch.empty((M, mats[n].physical_rows), dtype=torch.int64, device=dev) for n in c] for c in CALLS]
+            for g, x, a, s in zip(group, xs, acts, scs):
+                al = torch.empty((M, x.shape[1] // 512), dtype=torch.float32, device=dev)
+                rq = torch.empty(M, dtype=torch.float32, device=dev)
+                Y.quantize(x, g[0].signs_in_ptr, a, al, s, rq, stream=stream)
+            for g, a, s, o in zip(group, acts, scs, wss):
+                gg = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gg, stream=stream):
+                    Y.weighted_sums(g, a, s, o, stream=stream)
+                graphs.append(gg)
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in CALLS]
         with torch.cuda.stream(stream):
             for r in range(reps + 3):
@@ -360,8 +369,11 @@ def run_b200(args, rank, world, local_rank):
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     ms, e2e_ms = t.tolist()
-    # This rank's algorithmic bytes of its own weighted-sums launches, and its copies.
-    gemv_local = sum(gemv_bytes(mats[n].physical_rows, mats[n].cols, args.bits, M) for c in CALLS for n in c)
+    # This rank's algorithmic bytes of the timed launches, and its copies.
+    if world == 1:
+        gemv_local = algorithmic_bytes(args.bits, M)
+    else:
+        gemv_local = sum(gemv_bytes(mats[n].physical_rows, mats[n].cols, args.bits, M) for c in CALLS for n in c)
     h2d_local = 4 * x_all.numel()  # the copies as issued (inputs + alignment padding)
     d2h_local = 4 * y_all.numel()
     tot = torch.tensor([h2d_local, d2h_local], dtype=torch.int64, device=dev)
@@ -380,8 +392,13 @@ def run_b200(args, rank, world, local_rank):
         except ValueError:
             peaks = {}
     peak = peaks.get("hbm_gbs", 6650.0)
-    gemv_total_bytes = gemv_local
-    achieved = gemv_total_bytes / (sum(gemv_ms) * 1e-3) / 1e9
+    if world == 1:
+        # One GPU: the timed region is the dominant kernel's launches back to back (six
+        # fused gemv_kernel launches per step, nothing else), so its average launch
+        # duration is the timed region's device time / launches (inter-launch gaps in).
+        achieved = gemv_local * args.steps / (ms * 1e-3) / 1e9
+    else:
+        achieved = gemv_local / (sum(gemv_ms) * 1e-3) / 1e9
     # CPU baseline (rank 0, N=1 only): the oracle port on a bounded sample.
     cpu = None
     if world == 1 and not args.skip_cpu:
@@ -403,7 +420,9 @@ def run_b200(args, rank, world, local_rank):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
                          "traffic": GEMV_TRAFFIC.get((args.bits, M)) if world == 1 else None,
-                         "kernel": "gemv_kernel (weighted sums; the 6 launches of one step on rank 0, each timed alone)",
+                         "kernel": ("gemv_kernel (fused operator: quantise + weighted sums + restore; the 6 launches "
+                                    "of each step, timed over the timed region)") if world == 1 else
+                                   "gemv_kernel (weighted sums; the 6 launches of one step on rank 0, each timed alone)",
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
@@ -413,7 +432,7 @@ def run_b200(args, rank, world, local_rank):
             # row-max reduction and NCCL's kernels, not counted).
             "gpu_launches": args.steps * (len(CALLS) + 3 * len(rowpar)),
             "clocks": sampler.summary(),
-            "step_bytes": step_bytes, "gemv_us_per_call": [round(1e3 * x, 2) for x in gemv_ms]}
+            "step_bytes": step_bytes, "us_per_call_alone": [round(1e3 * x, 2) for x in gemv_ms]}
     print(json.dumps(line), flush=True)
 
 

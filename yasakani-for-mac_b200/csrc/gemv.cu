@@ -41,9 +41,10 @@
 //   in any order) and count the groups they added per 512-row block; the warp that
 //   completes a block restores and rotates it, then clears the sums and the count.
 //   One arrival per warp and block replaces the per-row-block hand-over.
-// * Prologue: the input groups are requested first, then the first unit's codes,
-//   then the 128 KiB table image (one bulk asynchronous copy), so the quantiser's
-//   input latency, the code fetch and the table copy overlap.
+// * Prologue: the first unit's codes and the 128 KiB table image (one bulk
+//   asynchronous copy) are requested before the kernel waits for its predecessor on
+//   the stream (programmatic dependent launch), then the input groups: the code
+//   fetch and the table copy overlap the previous kernel's tail and the quantiser.
 #include <algorithm>
 #include <mutex>
 
@@ -253,12 +254,11 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   float* s_alpha = reinterpret_cast<float*>(s_scale + p.mv * G);  // FUSED: group scales
   float* s_rq = s_alpha + p.mv * G;                                // FUSED: row quanta
 
-  // Fused: the first input group of this warp is requested first of all, ahead of the
-  // code and table traffic below, since the quantiser's latency starts with it.
+  // Programmatic dependent launch: the next kernel on the stream may be scheduled as
+  // SMs free up; it waits (griddepcontrol.wait) before it reads anything this grid writes.
+  asm volatile("griddepcontrol.launch_dependents;");
   const int items = FUSED ? p.mv * G : 0;
   Group512In nxt;
-  if (FUSED && warp < items)
-    load_group512(p.x + (size_t)(warp / G) * Kc + (warp % G) * 512, p.s_in + (warp % G) * 512, lane, nxt);
 
   // This warp's tiles [t_begin, t_end) (tile t = sequence t % 2G of row block t / 2G),
   // walked as units u = (row block, group) = tiles 2u, 2u+1; only the first and the
@@ -299,6 +299,13 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
     for (int c = 0; c < 4; ++c)
       bulk_copy_g2s(s_lut + c * (LUT_COPY_BYTES / 4), S.lutx + c * (LUT_COPY_BYTES / 4), LUT_COPY_BYTES / 4, s_bar);
   }
+  // Everything above reads only the matrix (codes, table), which no kernel writes. The
+  // inputs, the scales and every scratch word may belong to the previous kernel on the
+  // stream until it completes: wait for it here (a no-op without a programmatic launch).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // Fused: each warp's first input group is requested first, ahead of the staging below.
+  if (FUSED && warp < items)
+    load_group512(p.x + (size_t)(warp / G) * Kc + (warp % G) * 512, p.s_in + (warp % G) * 512, lane, nxt);
   {
     if (FUSED) {
       // A warp's groups in turn, each one's inputs requested before the previous is quantised.
@@ -522,8 +529,20 @@ static int launch_one(const GemvParams& p, int grid, cudaStream_t st) {
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "gemv_kernel attributes");
   const size_t smem = table_smem_bytes() + (ACT_SMEM ? act_smem_bytes(p.mv, p.Kc, FUSED) : 0);
-  gemv_kernel<BITS, M1, ACT_SMEM, FUSED><<<grid, GEMV_WARPS * 32, smem, st>>>(p);
-  return cuda_fail(cudaGetLastError(), "gemv_kernel");
+  // Launched as a programmatic dependent of the previous kernel on the stream: the CTAs
+  // may start on SMs that kernel has left and fetch their table and first codes while it
+  // finishes (the kernel waits for it before touching its inputs or the scratch).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(GEMV_WARPS * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_fail(cudaLaunchKernelEx(&cfg, gemv_kernel<BITS, M1, ACT_SMEM, FUSED>, p), "gemv_kernel");
 }
 
 template <int BITS>
