@@ -217,14 +217,18 @@ def run_b200(args, rank, world, local_rank):
     W = make_weights(args.bits)
     # N > 1: tensor parallelism over whole 512-blocks (yskn_b200/tp.py). Column-parallel
     # projections keep whole 512-row blocks per rank (replicated when there are fewer
-    # blocks than ranks: k/v at 4 and 8 GPUs); o/out/down are row-parallel.
+    # blocks than ranks: k/v at 4 and 8 GPUs); o/out/down are row-parallel, one launch
+    # per rank and call with their exchange over NVLink (yskn_b200_linear_rowpar).
     mats, rowpar = {}, {}
+    exchange = None
+    if world > 1:
+        exchange = tp.make_exchange(max(r for n, r, _ in LAYER if n in ROW_PARALLEL))
     for name, w in W.items():
         dw = torch.from_numpy(w["words"].view(np.int32)).to(dev)
         args_m = (dw, "warp", w["rows"], w["rows"], w["cols"], args.bits, w["lut16"], w["sc16"], w["s_in"],
                   w["s_out"])
         if world > 1 and name in ROW_PARALLEL:
-            rowpar[name] = tp.RowParallelLinear(*args_m)
+            rowpar[name] = tp.RowParallelLinear(*args_m, exchange=exchange)
             mats[name] = rowpar[name].mat
         else:
             shard = None
@@ -299,33 +303,20 @@ def run_b200(args, rank, world, local_rank):
         e1.record(stream)
         barrier()
         ms = e0.elapsed_time(e1)
-        # Per call: each launch captured alone in a graph with events on the launching
-        # stream, replayed in step order (device time, no host gaps; each figure holds
-        # one graph launch's latency). One GPU: the step's own launches, the fused
-        # operator (gemv_kernel quantises, sums and restores); tensor parallel: the
-        # weighted-sums launches of the same matrices, which set the roofline there.
+        # Per call (informative): each of the step's launches captured alone in a graph
+        # with events on the launching stream, replayed in step order (device time, no
+        # host gaps; each figure holds one graph launch's latency).
         reps = max(20, min(200, args.steps))
         gemv_ms = [0.0] * len(CALLS)
         graphs = []
-        if world == 1:
-            for c, g, x, wk, y in zip(CALLS, group, xs, works, ys):
-                gg = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(gg, stream=stream):
+        for c, g, x, wk, y in zip(CALLS, group, xs, works, ys):
+            gg = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gg, stream=stream):
+                if c[0] in rowpar:
+                    rowpar[c[0]](x, y[0], stream=stream)
+                else:
                     Y.linear(g, x, wk, y, stream=stream)
-                graphs.append(gg)
-        else:
-            acts = [torch.empty((M, x.shape[1]), dtype=torch.int8, device=dev) for x in xs]
-            scs = [torch.empty((M, x.shape[1] // 512), dtype=torch.int32, device=dev) for x in xs]
-            wss = [[torch.empty((M, mats[n].physical_rows), dtype=torch.int64, device=dev) for n in c] for c in CALLS]
-            for g, x, a, s in zip(group, xs, acts, scs):
-                al = torch.empty((M, x.shape[1] // 512), dtype=torch.float32, device=dev)
-                rq = torch.empty(M, dtype=torch.float32, device=dev)
-                Y.quantize(x, g[0].signs_in_ptr, a, al, s, rq, stream=stream)
-            for g, a, s, o in zip(group, acts, scs, wss):
-                gg = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(gg, stream=stream):
-                    Y.weighted_sums(g, a, s, o, stream=stream)
-                graphs.append(gg)
+            graphs.append(gg)
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in CALLS]
         with torch.cuda.stream(stream):
             for r in range(reps + 3):
@@ -365,15 +356,26 @@ def run_b200(args, rank, world, local_rank):
     Y.check(Y.status(stream), "status")
     torch.cuda.synchronize()
     del graph, graphs, e2e_graph  # graphs holding NCCL calls go before the process group
+    if exchange is not None:  # unmapped only once no rank has kernels in flight
+        torch.distributed.barrier()
+        exchange.close()
     t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     ms, e2e_ms = t.tolist()
-    # This rank's algorithmic bytes of the timed launches, and its copies.
+    # This rank's algorithmic bytes per step (its shards: codes, table, row scales, signs,
+    # f32 input slice, f32 outputs), and its copies.
     if world == 1:
         gemv_local = algorithmic_bytes(args.bits, M)
     else:
-        gemv_local = sum(gemv_bytes(mats[n].physical_rows, mats[n].cols, args.bits, M) for c in CALLS for n in c)
+        gemv_local = 0
+        for c in CALLS:
+            kc = mats[c[0]].cols
+            gemv_local += 4 * M * kc + kc
+            for n in c:
+                m = mats[n]
+                out_rows = LAYER_ROWS[n] if n in rowpar else m.rows
+                gemv_local += m.physical_rows * kc * args.bits // 16 + 8192 + 5 * m.physical_rows + 4 * M * out_rows
     h2d_local = 4 * x_all.numel()  # the copies as issued (inputs + alignment padding)
     d2h_local = 4 * y_all.numel()
     tot = torch.tensor([h2d_local, d2h_local], dtype=torch.int64, device=dev)
@@ -392,13 +394,11 @@ def run_b200(args, rank, world, local_rank):
         except ValueError:
             peaks = {}
     peak = peaks.get("hbm_gbs", 6650.0)
-    if world == 1:
-        # One GPU: the timed region is the dominant kernel's launches back to back (six
-        # fused gemv_kernel launches per step, nothing else), so its average launch
-        # duration is the timed region's device time / launches (inter-launch gaps in).
-        achieved = gemv_local * args.steps / (ms * 1e-3) / 1e9
-    else:
-        achieved = gemv_local / (sum(gemv_ms) * 1e-3) / 1e9
+    # The timed region is the dominant kernel's launches back to back (six fused
+    # gemv_kernel launches per step and rank, nothing else: the row-parallel exchange
+    # runs inside them), so its average launch duration is the timed region's device
+    # time / launches (inter-launch gaps in); per GPU, against one GPU's HBM peak.
+    achieved = gemv_local * args.steps / (ms * 1e-3) / 1e9
     # CPU baseline (rank 0, N=1 only): the oracle port on a bounded sample.
     cpu = None
     if world == 1 and not args.skip_cpu:
@@ -420,17 +420,16 @@ def run_b200(args, rank, world, local_rank):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
                          "traffic": GEMV_TRAFFIC.get((args.bits, M)) if world == 1 else None,
-                         "kernel": ("gemv_kernel (fused operator: quantise + weighted sums + restore; the 6 launches "
-                                    "of each step, timed over the timed region)") if world == 1 else
-                                   "gemv_kernel (weighted sums; the 6 launches of one step on rank 0, each timed alone)",
+                         "kernel": "gemv_kernel (fused operator: quantise + weighted sums + restore; the 6 launches "
+                                   "of each step, timed over the timed region)" + (
+                                       "; rank 0's shards, row-parallel calls exchanging over NVLink in-kernel"
+                                       if world > 1 else ""),
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            # One fused launch (quantise + sums + restore) per operator call at M=1.
-            # Own kernels per step: one fused launch per column-parallel call; quantise,
-            # rescale, weighted sums and restore per row-parallel call (plus torch's
-            # row-max reduction and NCCL's kernels, not counted).
-            "gpu_launches": args.steps * (len(CALLS) + 3 * len(rowpar)),
+            # One fused launch (quantise + sums + restore) per operator call at M=1, on
+            # every rank (row-parallel calls included: their exchange is in the kernel).
+            "gpu_launches": args.steps * len(CALLS),
             "clocks": sampler.summary(),
             "step_bytes": step_bytes, "us_per_call_alone": [round(1e3 * x, 2) for x in gemv_ms]}
     print(json.dumps(line), flush=True)

@@ -46,6 +46,9 @@ extern "C" {
 #define YSKN_SIGNS_MULBERRY32 1
 
 typedef struct yskn_b200_matrix yskn_b200_matrix;
+typedef struct yskn_b200_tp yskn_b200_tp;
+
+#define YSKN_B200_TP_HANDLE_BYTES 64 /* one rank's exchange-area handle (a CUDA IPC handle) */
 
 /* Thread-local message of the last failure (src/c_api.cpp:11-14 `yskn_last_error`). */
 YSKN_B200_API const char* yskn_b200_last_error(void);
@@ -144,6 +147,26 @@ YSKN_B200_API int yskn_b200_quantize(const float* d_x, const int8_t* d_signs, in
  * SUM) to exactly the one-GPU sums. No counterpart in the single-GPU reference. */
 YSKN_B200_API int yskn_b200_rescale(const float* d_alpha, const float* d_row_max, int M, int groups,
                                     int32_t* d_scales, float* d_row_quantum, void* stream);
+
+/* Tensor-parallel row-parallel operator in one launch per rank (no counterpart in the
+ * single-GPU reference; replaces quantize + all-reduce MAX + rescale + weighted_sums +
+ * all-reduce SUM + restore). Each rank (one process per GPU) creates an exchange area
+ * sized for its largest row-parallel matrix and gets a YSKN_B200_TP_HANDLE_BYTES handle;
+ * the ranks swap handles (any host channel), then connect, which maps the peers' areas
+ * over NVLink. yskn_b200_linear_rowpar then computes, on every rank, the whole output
+ * of the matrix from this rank's 512-column groups: row maxima and int64 sums of
+ * finished 512-row blocks go to the peers' areas with plain stores and flag words
+ * (bounded waits: a peer that never arrives gives YSKN_ETIMEDOUT from
+ * yskn_b200_status), and y is bit-identical to one GPU's yskn_b200_linear.
+ * Every rank issues the same calls in the same order on one stream per device; calls on
+ * one exchange area never overlap. mat: a shard of whole 512-column groups (all rows),
+ * with an output rotation, at most max_physical_rows rows; M = 1..16; d_x_local: this
+ * rank's columns of the input (f32 [M][cols of the shard]); d_y: f32 [M][rows]. */
+YSKN_B200_API yskn_b200_tp* yskn_b200_tp_create(int world, int rank, int max_physical_rows, void* ipc_handle_out);
+YSKN_B200_API int yskn_b200_tp_connect(yskn_b200_tp* tp, const void* handles /* world x 64 bytes, rank order */);
+YSKN_B200_API void yskn_b200_tp_destroy(yskn_b200_tp* tp);
+YSKN_B200_API int yskn_b200_linear_rowpar(yskn_b200_tp* tp, const yskn_b200_matrix* mat, const float* d_x_local, int M,
+                                          const float* d_inv_rms, float* d_y, void* stream);
 
 /* Restore + output rotation (replaces src/a8_prologue.cuh:10-15 xsum_combine and the
  * restore part of src/q35_kernels.cu:1402-1474; compressed_linear.rs:288-370):

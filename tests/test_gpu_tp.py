@@ -110,3 +110,105 @@ def test_tp_two_gpus_bit_identical(cuda):
     for _, y, yc in results:
         assert np.array_equal(y.view(np.uint32), ref.view(np.uint32))
         assert np.array_equal(yc.view(np.uint32), ref.view(np.uint32))
+
+
+def _rowpar_worker(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+    import yskn_b200
+    from yskn_b200 import tp
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world)
+    try:
+        out = {}
+        ex = tp.make_exchange(2048)
+        mats = {}
+        for name, (rows, cols, seed) in _ROWPAR_SHAPES.items():
+            words, lut16, sc16 = fixtures.model_matrix(rows, cols, 8, seed)
+            si = O.signs("mulberry32_7919_13", 7, 0, cols)
+            so = O.signs("mulberry32_7919_13", 7, cols, rows)
+            mats[name] = tp.RowParallelLinear(_dev(words.view(np.int32)), "warp", rows, rows, cols, 8, lut16, sc16,
+                                              si, so, exchange=ex)
+        # Interleaved calls, three rounds: the exchange cycles through its epochs and both slots.
+        for rnd in range(3):
+            for name, (rows, cols, seed) in _ROWPAR_SHAPES.items():
+                M = 1 + (rnd + len(name)) % 3
+                x = fixtures.normal(seed + 100 * rnd, M * cols).reshape(M, cols)
+                rp = mats[name]
+                y = torch.empty((M, rows), dtype=torch.float32, device="cuda")
+                rp(_dev(x[:, rp.col_begin:rp.col_end]), y)
+                out[(name, rnd)] = y.cpu().numpy()
+        # The same calls captured in a CUDA graph and replayed twice.
+        st = torch.cuda.Stream()
+        xs, ys = {}, {}
+        for name, (rows, cols, seed) in _ROWPAR_SHAPES.items():
+            x = fixtures.normal(seed + 999, cols).reshape(1, cols)
+            rp = mats[name]
+            xs[name] = _dev(x[:, rp.col_begin:rp.col_end])
+            ys[name] = torch.empty((1, rows), dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            for name in _ROWPAR_SHAPES:
+                mats[name](xs[name], ys[name], stream=st)
+        for rep in range(2):
+            for y in ys.values():
+                y.zero_()
+            torch.cuda.synchronize()
+            g.replay()
+            torch.cuda.synchronize()
+            for name in _ROWPAR_SHAPES:
+                out[(name, "graph%d" % rep)] = ys[name].cpu().numpy()
+        del g
+        assert yskn_b200.status() == 0
+        torch.cuda.synchronize()
+        dist.barrier()  # no rank has kernels in flight before the areas are unmapped
+        ex.close()
+        q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+_ROWPAR_SHAPES = {"o": (1024, 3072, 21), "down": (2048, 4096, 23)}
+
+
+def test_tp_rowpar_one_launch_two_gpus_bit_identical(cuda):
+    """yskn_b200_linear_rowpar on 2 GPUs (row maxima and int64 block sums exchanged over
+    NVLink inside the kernel) gives the one-GPU operator's bits, for interleaved
+    matrices, M = 1..3, repeated rounds and CUDA-graph replays."""
+    import torch
+    import torch.multiprocessing as mp
+    import yskn_b200
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ref = {}
+    for name, (rows, cols, seed) in _ROWPAR_SHAPES.items():
+        words, lut16, sc16 = fixtures.model_matrix(rows, cols, 8, seed)
+        si = O.signs("mulberry32_7919_13", 7, 0, cols)
+        so = O.signs("mulberry32_7919_13", 7, cols, rows)
+        m = yskn_b200.Matrix(_dev(words.view(np.int32)), "warp", rows, rows, cols, 8, lut16, sc16, si, so)
+        cases = [(rnd, 1 + (rnd + len(name)) % 3, seed + 100 * rnd) for rnd in range(3)]
+        cases += [("graph0", 1, seed + 999), ("graph1", 1, seed + 999)]
+        for key, M, xseed in cases:
+            x = fixtures.normal(xseed, M * cols).reshape(M, cols)
+            work = torch.empty(yskn_b200.linear_work_bytes([m], M), dtype=torch.uint8, device="cuda")
+            y = torch.empty((M, rows), dtype=torch.float32, device="cuda")
+            yskn_b200.linear([m], _dev(x), work, [y])
+            ref[(name, key)] = y.cpu().numpy()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rowpar_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for _, out in results:
+        assert set(out) == set(ref)
+        for k, y in out.items():
+            assert np.array_equal(y.view(np.uint32), ref[k].view(np.uint32)), k

@@ -143,3 +143,61 @@ def test_tp_world2_matches_one_process(tmp_path):
     for r in range(2):
         assert np.array_equal(np.load(tmp_path / ("row_%d.npy" % r)).view(np.uint32), ref.view(np.uint32))
         assert np.array_equal(np.load(tmp_path / ("col_%d.npy" % r)).view(np.uint32), ref2.view(np.uint32))
+
+
+class _FakeExchange:
+    """Stand-in for yskn_b200.TpExchange: a recognisable handle per rank; connect records
+    what it was given."""
+
+    def __init__(self, world, rank, rows):
+        self.world, self.rank, self.rows = world, rank, rows
+        self.ipc_handle = bytes([rank + 1]) * 64
+        self.handles = None
+
+    def connect(self, handles):
+        self.handles = list(handles)
+
+
+class _ExchangeOps(_OracleOps):
+    TpExchange = _FakeExchange
+    rowpar_calls = []
+
+    @staticmethod
+    def linear_rowpar(exchange, mat, x_local, y, inv_rms=None, stream=None):
+        _ExchangeOps.rowpar_calls.append((exchange.rank, tuple(x_local.shape)))
+        y.fill_(1.0)
+
+
+def _exchange_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ex = tp.make_exchange(5000, ops=_ExchangeOps)
+        # every rank holds every rank's handle, in rank order; the area is whole 512-blocks
+        assert ex.handles == [bytes([r + 1]) * 64 for r in range(world)]
+        assert (ex.world, ex.rank, ex.rows) == (world, rank, 5120)
+        w, l16, s16, si, so = _tensor(1024, 2048, 3, True)
+        rp = tp.RowParallelLinear(w, "row", 1024, 1024, 2048, 8, l16, s16, si, so, ops=_ExchangeOps, exchange=ex)
+        x = fixtures.normal(41, 17 * 2048).reshape(17, 2048)
+        xl = torch.from_numpy(np.ascontiguousarray(x[:, rp.col_begin:rp.col_end]))
+        y = torch.zeros((2, 1024), dtype=torch.float32)
+        rp(xl[:2], y)  # M <= 16 with a rotation: the one-launch operator
+        assert _ExchangeOps.rowpar_calls == [(rank, (2, 1024))] and float(y.min()) == 1.0
+        y17 = torch.empty((17, 1024), dtype=torch.float32)
+        rp(xl, y17)  # M = 17: the NCCL path, which matches one process
+        ref = O.linear(w, "row", 1024, 2048, 8, l16, s16, x, si, so, None)
+        assert np.array_equal(y17.numpy().view(np.uint32), ref.view(np.uint32))
+        assert len(_ExchangeOps.rowpar_calls) == 1
+        np.save(os.path.join(out_dir, "ok_%d.npy" % rank), np.ones(1))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_tp_exchange_plumbing_world2(tmp_path):
+    """make_exchange swaps the ranks' handles through the process group and connects
+    each rank with all of them in rank order; RowParallelLinear takes the one-launch
+    operator for M <= 16 and the NCCL path beyond."""
+    mp.spawn(_exchange_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    for r in range(2):
+        assert (tmp_path / ("ok_%d.npy" % r)).exists()

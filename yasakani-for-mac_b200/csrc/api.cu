@@ -173,6 +173,15 @@ namespace yskn {
 const MatrixDev* matrix_dev(const yskn_b200_matrix* m) { return m ? &m->dev : nullptr; }
 }  // namespace yskn
 
+// One rank's side of the row-parallel exchange: its own area (cudaMalloc, shared by
+// CUDA IPC) and the peers' areas mapped into this process.
+struct yskn_b200_tp {
+  TpView view{};
+  void* local = nullptr;
+  bool mapped[TP_MAX_WORLD] = {};
+  bool connected = false;
+};
+
 static cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -381,6 +390,62 @@ YSKN_B200_API int yskn_b200_rescale(const float* d_alpha, const float* d_row_max
   if (M < 1 || groups < 1 || !d_alpha || !d_row_max || !d_scales || !d_row_quantum)
     return fail(YSKN_EINVAL, "rescale: bad arguments");
   return launch_rescale(d_alpha, d_row_max, M, groups, d_scales, d_row_quantum, as_stream(stream));
+}
+
+YSKN_B200_API yskn_b200_tp* yskn_b200_tp_create(int world, int rank, int max_physical_rows, void* ipc_handle_out) {
+  if (world < 2 || world > TP_MAX_WORLD || rank < 0 || rank >= world || max_physical_rows < 512 ||
+      max_physical_rows % 512 || !ipc_handle_out)
+    return fail(YSKN_EINVAL, "tp_create: need 2 <= world <= 8, 0 <= rank < world, rows a multiple of 512"), nullptr;
+  std::unique_ptr<yskn_b200_tp> t(new yskn_b200_tp);
+  t->view = tp_layout(world, rank, max_physical_rows / 512);
+  cudaError_t e = cudaMalloc(&t->local, t->view.bytes);
+  if (e == cudaSuccess) e = cudaMemset(t->local, 0, t->view.bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, t->local);
+  if (e != cudaSuccess) {
+    if (t->local) cudaFree(t->local);
+    return cuda_fail(e, "tp_create"), nullptr;
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == YSKN_B200_TP_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(ipc_handle_out, &h, sizeof h);
+  t->view.base[rank] = reinterpret_cast<char*>(t->local);
+  return t.release();
+}
+
+YSKN_B200_API int yskn_b200_tp_connect(yskn_b200_tp* t, const void* handles) {
+  if (!t || !handles || t->connected) return fail(YSKN_EINVAL, "tp_connect: bad arguments");
+  const auto* h = reinterpret_cast<const unsigned char*>(handles);
+  for (int q = 0; q < t->view.world; ++q) {
+    if (q == t->view.rank) continue;
+    cudaIpcMemHandle_t hq;
+    std::memcpy(&hq, h + (size_t)q * YSKN_B200_TP_HANDLE_BYTES, sizeof hq);
+    void* ptr = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&ptr, hq, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e, "tp_connect: mapping a peer's exchange area");
+    t->view.base[q] = reinterpret_cast<char*>(ptr);
+    t->mapped[q] = true;
+  }
+  t->connected = true;
+  return YSKN_OK;
+}
+
+YSKN_B200_API void yskn_b200_tp_destroy(yskn_b200_tp* t) {
+  if (!t) return;
+  cudaDeviceSynchronize();
+  for (int q = 0; q < t->view.world; ++q)
+    if (t->mapped[q]) cudaIpcCloseMemHandle(t->view.base[q]);
+  if (t->local) cudaFree(t->local);
+  delete t;
+}
+
+YSKN_B200_API int yskn_b200_linear_rowpar(yskn_b200_tp* t, const yskn_b200_matrix* mat, const float* d_x_local, int M,
+                                          const float* d_inv_rms, float* d_y, void* stream) {
+  if (!t || !t->connected || !mat || !d_x_local || !d_y || !aligned16(d_x_local))
+    return fail(YSKN_EINVAL, "linear_rowpar: bad arguments (connected exchange, matrix, aligned input, output)");
+  const GemvScratch* sc = current_scratch();
+  if (!sc) return fail(YSKN_EINVAL, "linear_rowpar: no matrix was created on this device");
+  return launch_linear_rowpar(mat->dev, t->view, d_x_local, M, d_inv_rms, d_y, *sc, as_stream(stream));
 }
 
 YSKN_B200_API void yskn_b200_matrix_destroy(yskn_b200_matrix* m) {

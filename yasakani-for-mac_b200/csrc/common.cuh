@@ -60,6 +60,36 @@ struct GemvScratch {
 constexpr int GEMV_WARPS = 16;  // warps per persistent GEMV CTA (one CTA per SM)
 int gemv_max_warps();
 
+// Exchange areas of the tensor-parallel row-parallel operator (gemv.cu). Every rank
+// allocates one area with this layout (zeroed); base[q] is rank q's area as mapped in
+// this process (peer memory through CUDA IPC over NVLink; base[rank] is local).
+// Every exchanged 32-bit datum travels as one 64-bit word (datum | launch epoch << 32),
+// a single-copy-atomic access: the receiver polls the words themselves until they
+// carry its epoch, so no fences are needed. Double-buffered by launch parity.
+constexpr int TP_MAX_WORLD = 8;
+constexpr int TP_MAX_M = 16;
+struct TpView {
+  char* base[TP_MAX_WORLD];
+  int world, rank;
+  int max_blocks;                   // 512-row blocks of the largest matrix
+  size_t off_counter;               // u64: launches x CTAs on this rank (the epoch source)
+  size_t off_maxbox;                // u64 [2][world][TP_MAX_M]: row maxima (f32 bits) by source rank
+  size_t off_recv;                  // u64 x2 [2][world][TP_MAX_M][max_blocks * 512]: int64 block sums by source
+  size_t bytes;
+};
+inline TpView tp_layout(int world, int rank, int max_blocks) {
+  auto up = [](size_t v) { return (v + 255) / 256 * 256; };
+  TpView v{};
+  v.world = world;
+  v.rank = rank;
+  v.max_blocks = max_blocks;
+  v.off_counter = 0;
+  v.off_maxbox = 256;
+  v.off_recv = v.off_maxbox + up(2 * (size_t)world * TP_MAX_M * 8);
+  v.bytes = v.off_recv + up(2 * (size_t)world * TP_MAX_M * max_blocks * 512 * 16);
+  return v;
+}
+
 // Activation rows from which the tcgen05 GEMM (gemm.cu) replaces the GEMV.
 constexpr int GEMM_MIN_M = 64;
 int64_t gemm_workspace_bytes(const MatrixDev& m);  // dense int8 copy of the weights
@@ -77,6 +107,11 @@ int launch_gemv(const MatrixDev* mats, int n_mats, const int8_t* act, const int3
 bool fused_linear_fits(int M, int Kc);
 int launch_linear_fused(const MatrixDev* mats, int n_mats, const float* x, int M, const float* inv_rms,
                         float* const* y, const GemvScratch& scratch, cudaStream_t st);
+// The row-parallel operator of one rank in one launch: this rank's 512-column groups
+// of a matrix with an output rotation, the row maxima and the int64 block sums
+// exchanged with the peers through `tp`, the whole output restored on every rank.
+int launch_linear_rowpar(const MatrixDev& mat, const TpView& tp, const float* x_local, int M, const float* inv_rms,
+                         float* y, const GemvScratch& scratch, cudaStream_t st);
 int launch_quantize(const float* x, const int8_t* signs, int M, int Kc, int8_t* act, float* alpha, int32_t* scales,
                     float* row_quantum, cudaStream_t st);
 int launch_restore(int64_t* ws, int ws_ld, const float* row_quantum, const float* inv_rms, const float* tau,

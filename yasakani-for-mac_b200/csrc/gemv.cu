@@ -93,6 +93,8 @@ struct GemvParams {
   const float* x;
   const int8_t* s_in;
   const float* inv_rms;
+  // Row-parallel tensor-parallel operator (tp.world > 1): exchange areas of all ranks.
+  TpView tp;
 };
 
 template <int BITS>
@@ -220,6 +222,53 @@ __device__ __forceinline__ unsigned warp_arrive(unsigned* counter, unsigned n, i
 }
 __device__ __forceinline__ void gpu_acquire() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
+// Cross-GPU exchange of the row-parallel operator. Each 32-bit datum goes to a peer's
+// area as one 64-bit word (datum | epoch << 32) with a plain (volatile) store over
+// NVLink; an aligned 64-bit access is single-copy atomic, so a receiver that reads a
+// word carrying its epoch has the datum too, without fences. Receivers poll their own
+// area for at most TP_WAIT_LIMIT clock cycles (then the device error word gets
+// DERR_TIMEOUT and the call's output is not valid).
+constexpr long long TP_WAIT_LIMIT = 2000000000ll;  // ~1 s
+__device__ __forceinline__ uint64_t ll_word(uint32_t datum, uint32_t epoch) {
+  return (uint64_t)datum | ((uint64_t)epoch << 32);
+}
+__device__ __forceinline__ void st_ll(uint64_t* p, uint64_t w) {
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ void st_ll2(uint64_t* p, uint64_t w0, uint64_t w1) {  // two words, each atomic
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(w0), "l"(w1) : "memory");
+}
+__device__ __forceinline__ ulonglong2 ld_ll2(const uint64_t* p) {
+  ulonglong2 v;
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t ld_ll(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// The int64 sum of two epoch-tagged words (low half first), polling until both carry
+// `epoch`; `ok` turns false on a timeout.
+__device__ __forceinline__ long long recv_sum(const uint64_t* p, uint32_t epoch, bool& ok) {
+  ulonglong2 v = ld_ll2(p);
+  if ((uint32_t)(v.x >> 32) != epoch || (uint32_t)(v.y >> 32) != epoch) {
+    const long long t0 = clock64();
+    do {
+      if (clock64() - t0 > TP_WAIT_LIMIT) {
+        ok = false;
+        break;
+      }
+      v = ld_ll2(p);
+    } while ((uint32_t)(v.x >> 32) != epoch || (uint32_t)(v.y >> 32) != epoch);
+  }
+  return (long long)(((uint64_t)(uint32_t)v.y << 32) | (uint32_t)v.x);
+}
+template <typename T>
+__device__ __forceinline__ T* tp_at(const TpView& tp, int q, size_t off) {
+  return reinterpret_cast<T*>(tp.base[q] + off);
+}
+
 // Balanced contiguous ranges: warp w of a segment owns tiles
 // [w*base + min(w, rem), (w+1)*base + min(w+1, rem)), base = tiles / warps.
 struct Ranges {
@@ -343,11 +392,58 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   // Every thread waits (bounded) for the table. A timeout is reported and the CTA still
   // runs its units, so the arrival counters and the zero-kept sums stay consistent.
   if (!mbar_wait_bounded(s_bar, 0, TABLE_WAIT_LIMIT) && lane == 0) raise_device_error(p.err, DERR_TIMEOUT);
+  // Row-parallel tensor parallelism: this launch's epoch (every CTA of every launch on
+  // this rank adds one to the rank's counter, and every such launch has one CTA per SM)
+  // and the slot parity that double-buffers the exchange.
+  __shared__ unsigned s_epoch;
+  __shared__ float s_rowmax[TP_MAX_M];
+  const bool tp = FUSED && p.tp.world > 1;
+  if (tp && threadIdx.x == 0) {
+    const unsigned long long prev = atomicAdd(tp_at<unsigned long long>(p.tp, p.tp.rank, p.tp.off_counter), 1ull);
+    s_epoch = (unsigned)(prev / gridDim.x) + 1u;
+  }
   if (FUSED) {  // the rows' common integer grids (compressed_linear.rs:113-128)
+    if (threadIdx.x < p.mv) {
+      float mx = 0.0f;
+      for (int g = 0; g < G; ++g) mx = fmaxf(mx, s_alpha[threadIdx.x * G + g]);
+      s_rowmax[threadIdx.x] = mx;
+    }
+    if (tp) {
+      // The grid of a row is set by its largest group scale over all ranks' groups:
+      // CTA 0 of every rank sends its row maxima to every rank (epoch-tagged words),
+      // every CTA polls them in its own area and takes the max.
+      __syncthreads();
+      const unsigned epoch = s_epoch, par = epoch & 1u;
+      const int W = p.tp.world, me = p.tp.rank;
+      if (blockIdx.x == 0 && threadIdx.x < p.mv)
+        for (int q = 0; q < W; ++q)
+          st_ll(tp_at<uint64_t>(p.tp, q, p.tp.off_maxbox) + (par * W + me) * TP_MAX_M + threadIdx.x,
+                ll_word(__float_as_uint(s_rowmax[threadIdx.x]), epoch));
+      if (threadIdx.x < 32 && lane < p.mv) {
+        const uint64_t* box = tp_at<uint64_t>(p.tp, me, p.tp.off_maxbox) + (size_t)par * W * TP_MAX_M;
+        bool ok = true;
+        float mx = 0.0f;
+        for (int src = 0; src < W; ++src) {
+          const uint64_t* w = box + src * TP_MAX_M + lane;
+          uint64_t v = ld_ll(w);
+          const long long t0 = clock64();
+          while ((uint32_t)(v >> 32) != epoch) {
+            if (clock64() - t0 > TP_WAIT_LIMIT) {
+              ok = false;
+              break;
+            }
+            v = ld_ll(w);
+          }
+          mx = fmaxf(mx, __uint_as_float((uint32_t)v));
+        }
+        if (!ok) raise_device_error(p.err, DERR_TIMEOUT);
+        s_rowmax[lane] = mx;
+      }
+    }
+    __syncthreads();
     for (int item = threadIdx.x; item < p.mv * G; item += blockDim.x) {
       const int m = item / G;
-      float mx = 0.0f;
-      for (int g = 0; g < G; ++g) mx = fmaxf(mx, s_alpha[m * G + g]);
+      const float mx = s_rowmax[m];
       s_scale[item] = integer_group_scale(s_alpha[item], row_grid_multiplier(mx));
       if (item == m * G) s_rq[m] = row_quantum_of(mx);
     }
@@ -370,6 +466,10 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   bool overflow = false;
   bool bad = false;       // FUSED: non-finite restored values
   unsigned pend = 0;      // FUSED, rotated rows: tiles added to the current 512-row block, not yet counted
+  // Row-parallel: 512-row blocks this warp completed on this rank and sent to the
+  // peers (bit i: block blk_lo + i); it restores them after its last unit.
+  const int blk_lo = (t_begin / T2) >> 6;
+  unsigned done_mask = 0;
 
   // Final sums of rows row0, row0 + 1 for tokens n, n + 8 (the C fragment): stored
   // as int64, or (fused operator, rows without an output rotation) restored to f32.
@@ -385,6 +485,44 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         }
       } else {
         if (tok < p.mv && row < S.out_rows) S.out[(size_t)tok * S.out_ld + row] = v[i];
+      }
+    }
+  };
+  // Rotated rows (fused): restore + H512 of a complete 512-row block of sums, then clear
+  // the sums and the block's counter for the next launch.
+  auto restore_block = [&](int blk) {
+    for (int tok = 0; tok < p.mv; ++tok) {
+      int64_t* wsr = S.out + (size_t)tok * S.out_ld;
+      restore_block512(wsr, s_rq[tok], p.inv_rms ? p.inv_rms + tok : nullptr, S.tau, S.s_out, blk * 512, S.y_rows,
+                       S.y + (size_t)tok * S.y_rows, lane, bad);
+#pragma unroll
+      for (int k = 0; k < 8; ++k)  // the rows this lane read (restore_block512's lane mapping)
+        __stcg(reinterpret_cast<longlong2*>(wsr + blk * 512 + 64 * k + 2 * lane), make_longlong2(0, 0));
+    }
+    if (lane == 0) S.blk_counters[blk] = 0u;
+  };
+  // Row-parallel: this rank's int64 sums of block blk into the receive slot of every
+  // peer, each sum as two epoch-tagged words (plain stores over NVLink, no fence).
+  // Slot word (2 per sum) of row r, token tok, source src: recv + ((par*W + src)*16 + tok) * 2*rows + 2r.
+  auto send_block = [&](int blk) {
+    const unsigned epoch = s_epoch, par = epoch & 1u;
+    const int W = p.tp.world, me = p.tp.rank;
+    const size_t slot = (size_t)p.tp.max_blocks * 512 * 2;
+    for (int tok = 0; tok < p.mv; ++tok) {
+      const int64_t* src = S.out + (size_t)tok * S.out_ld + blk * 512;
+      longlong2 v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = __ldcg(reinterpret_cast<const longlong2*>(src + 64 * k + 2 * lane));
+      for (int qd = 0; qd < W; ++qd) {
+        if (qd == me) continue;
+        uint64_t* dst = tp_at<uint64_t>(p.tp, qd, p.tp.off_recv) + (((size_t)par * W + me) * TP_MAX_M + tok) * slot +
+                        (size_t)blk * 1024;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int r = 64 * k + 2 * lane;  // rows r, r + 1 of the block (restore_block512's lane mapping)
+          st_ll2(dst + 2 * r, ll_word((uint32_t)v[k].x, epoch), ll_word((uint32_t)((uint64_t)v[k].x >> 32), epoch));
+          st_ll2(dst + 2 * r + 2, ll_word((uint32_t)v[k].y, epoch), ll_word((uint32_t)((uint64_t)v[k].y >> 32), epoch));
+        }
       }
     }
   };
@@ -445,15 +583,15 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
           const unsigned prev = warp_arrive(S.blk_counters + blk, pend, lane);
           if (prev + pend == 64u * (unsigned)T2) {
             gpu_acquire();
-            for (int tok = 0; tok < p.mv; ++tok) {
-              int64_t* wsr = S.out + (size_t)tok * S.out_ld;
-              restore_block512(wsr, s_rq[tok], p.inv_rms ? p.inv_rms + tok : nullptr, S.tau, S.s_out, blk * 512,
-                               S.y_rows, S.y + (size_t)tok * S.y_rows, lane, bad);
-#pragma unroll
-              for (int k = 0; k < 8; ++k)  // the rows this lane read (restore_block512's lane mapping)
-                __stcg(reinterpret_cast<longlong2*>(wsr + blk * 512 + 64 * k + 2 * lane), make_longlong2(0, 0));
+            if (tp) {
+              // This rank's sums of the block go to every peer; the block is restored
+              // (with theirs added) after this warp's last unit, so no warp ever waits
+              // for a peer while it still holds work that a peer may wait for.
+              send_block(blk);
+              done_mask |= 1u << (blk - blk_lo);
+            } else {
+              restore_block(blk);
             }
-            if (lane == 0) S.blk_counters[blk] = 0u;
           }
           pend = 0;
         }
@@ -494,6 +632,37 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
     if (step(ua, ub)) break;
     if (step(ub, ua)) break;
   }
+  if (tp) {
+    // Every peer's sums of the blocks this warp completed: wait for them (their warps
+    // send as soon as each block completes there, without waiting on anything), add
+    // them to this rank's, restore the whole block.
+    const unsigned epoch = s_epoch, par = epoch & 1u;
+    const int W = p.tp.world, me = p.tp.rank;
+    const size_t slot = (size_t)p.tp.max_blocks * 512 * 2;
+    const uint64_t* recv = tp_at<uint64_t>(p.tp, me, p.tp.off_recv);
+    while (done_mask) {
+      const int blk = blk_lo + __ffs(done_mask) - 1;
+      done_mask &= done_mask - 1;
+      bool ok = true;
+      for (int tok = 0; tok < p.mv; ++tok) {
+        int64_t* mine = S.out + (size_t)tok * S.out_ld + blk * 512;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int r = 64 * k + 2 * lane;
+          longlong2 s = __ldcg(reinterpret_cast<const longlong2*>(mine + r));
+          for (int src = 0; src < W; ++src) {
+            if (src == me) continue;
+            const uint64_t* w = recv + (((size_t)par * W + src) * TP_MAX_M + tok) * slot + (size_t)blk * 1024 + 2 * r;
+            s.x += recv_sum(w, epoch, ok);
+            s.y += recv_sum(w + 2, epoch, ok);
+          }
+          __stcg(reinterpret_cast<longlong2*>(mine + r), s);
+        }
+      }
+      if (__any_sync(0xffffffffu, !ok) && lane == 0) raise_device_error(p.err, DERR_TIMEOUT);
+      restore_block(blk);
+    }
+  }
   if (p.checked && __any_sync(0xffffffffu, overflow) && lane == 0) raise_device_error(p.err, DERR_OVERFLOW);
   if (FUSED && __any_sync(0xffffffffu, bad) && lane == 0) raise_device_error(p.err, DERR_NONFINITE);
 }
@@ -511,7 +680,9 @@ static int sm_count() {
 
 int gemv_max_warps() { return (sm_count() + 8) * GEMV_WARPS; }
 
-constexpr int SMEM_LIMIT = 232448;  // opt-in shared memory per CTA on B200
+// Dynamic shared memory per CTA: B200's opt-in 232448 bytes less room for the kernel's
+// few static shared words (launch epoch, row maxima).
+constexpr int SMEM_LIMIT = 232448 - 1024;
 
 static size_t act_smem_bytes(int mv, int Kc, bool fused) {
   const size_t G = Kc / 512;
@@ -568,8 +739,10 @@ static int launch_bits_any(int bits, const GemvParams& p, int grid, bool fused, 
 // Segments, CTA split and scratch for one call. The CTAs (one per SM) are split
 // between the matrices in proportion to their units by largest remainders, so the
 // grid never exceeds the SM count (a CTA beyond it would run as a second wave).
+// full_grid (one matrix): exactly one CTA per SM, whatever the work (the row-parallel
+// operator's launch epoch counts CTAs).
 static int build_params(const MatrixDev* mats, int n_mats, const int* out_rows, const GemvScratch& scratch,
-                        bool fused, GemvParams& p, int& grid) {
+                        bool fused, GemvParams& p, int& grid, bool full_grid = false) {
   const int Kc = mats[0].cols, G = Kc / 512;
   const int sms = sm_count();
   p = GemvParams{};
@@ -614,6 +787,7 @@ static int build_params(const MatrixDev* mats, int n_mats, const int* out_rows, 
     for (int i = 0; i < n_mats; ++i)  // no more CTAs than tile runs of 16 warps
       want[i] = std::max<int64_t>(1, std::min<int64_t>(want[i], ceil_div((int64_t)(mats[i].phys_pad8 / 8) * 2 * G,
                                                                           GEMV_WARPS)));
+    if (full_grid && n_mats == 1) want[0] = sms;
   }
   grid = 0;
   unsigned* cnt = scratch.counters;
@@ -693,6 +867,35 @@ int launch_linear_fused(const MatrixDev* mats, int n_mats, const float* x, int M
     s.y_rows = mats[i].rows;
   }
   return launch_bits_any(mats[0].bits, p, grid, true, st);
+}
+
+int launch_linear_rowpar(const MatrixDev& mat, const TpView& tp, const float* x_local, int M, const float* inv_rms,
+                         float* y, const GemvScratch& scratch, cudaStream_t st) {
+  if (!fused_linear_fits(M, mat.cols) || M > TP_MAX_M)
+    return fail(YSKN_EINVAL, "row-parallel linear: M must be 1..16 with the input in shared memory");
+  if (!mat.s_out) return fail(YSKN_EINVAL, "row-parallel linear: the matrix needs an output rotation");
+  if (mat.phys / 512 > tp.max_blocks) return fail(YSKN_EINVAL, "row-parallel linear: matrix taller than the exchange");
+  const int out_rows = mat.phys;
+  GemvParams p;
+  int grid = 0;
+  if (int rc = build_params(&mat, 1, &out_rows, scratch, true, p, grid, true)) return rc;
+  if (grid != sm_count()) return fail(YSKN_EINVAL, "row-parallel linear: needs one CTA per SM");
+  // A warp restores the blocks it completed after its last unit (a 32-bit mask of them).
+  const int64_t span = p.seg[0].base + 1, per_blk = 64 * 2 * (int64_t)p.G;
+  if (span / per_blk + 2 > 32) return fail(YSKN_EINVAL, "row-parallel linear: too many rows per warp");
+  p.x = x_local;
+  p.s_in = mat.s_in;
+  p.inv_rms = inv_rms;
+  p.mv = M;
+  p.tp = tp;
+  GemvSeg& s = p.seg[0];
+  s.out = reinterpret_cast<int64_t*>(scratch.fused_sums);
+  if ((int64_t)M * mat.phys > scratch.fused_sums_len) return fail(YSKN_EINVAL, "row-parallel linear: sums scratch");
+  s.tau = mat.tau;
+  s.s_out = mat.s_out;
+  s.y = y;
+  s.y_rows = mat.rows;
+  return launch_bits_any(mat.bits, p, grid, true, st);
 }
 
 }  // namespace yskn

@@ -41,6 +41,10 @@ _SIGNATURES = {
     "yskn_b200_weighted_sums_noalloc": (_i, [_vp, _i, _vp, _vp, _i, _vp, _vp]),
     "yskn_b200_quantize": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp]),
     "yskn_b200_rescale": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp]),
+    "yskn_b200_tp_create": (_vp, [_i, _i, _i, _vp]),
+    "yskn_b200_tp_connect": (_i, [_vp, _vp]),
+    "yskn_b200_tp_destroy": (None, [_vp]),
+    "yskn_b200_linear_rowpar": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp]),
     "yskn_b200_restore": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
     "yskn_b200_linear_work_bytes": (_i64, [_vp, _i, _i]),
     "yskn_b200_linear": (_i, [_vp, _i, _vp, _i, _vp, _vp, _vp, _vp]),
@@ -193,6 +197,49 @@ def rescale(alpha, row_max, scales, row_quantum, stream=None):
     M, G = alpha.shape
     check(lib().yskn_b200_rescale(_ptr(alpha), _ptr(row_max), M, G, _ptr(scales), _ptr(row_quantum),
                                   _stream(stream)), "rescale")
+
+
+TP_HANDLE_BYTES = 64
+
+
+class TpExchange:
+    """This rank's side of the row-parallel exchange (yskn_b200_tp_create / _connect):
+    create, swap the handles between ranks (`connect(handles)` takes all of them in rank
+    order), then pass it to linear_rowpar."""
+
+    def __init__(self, world, rank, max_physical_rows):
+        self._handle_buf = C.create_string_buffer(TP_HANDLE_BYTES)
+        self.handle = lib().yskn_b200_tp_create(world, rank, max_physical_rows, self._handle_buf)
+        if not self.handle:
+            raise YsknError(-1, "tp_create: " + last_error())
+        self.world, self.rank = world, rank
+
+    @property
+    def ipc_handle(self):
+        return self._handle_buf.raw
+
+    def connect(self, handles):
+        blob = b"".join(handles)
+        if len(blob) != TP_HANDLE_BYTES * self.world:
+            raise ValueError("one %d-byte handle per rank expected" % TP_HANDLE_BYTES)
+        check(lib().yskn_b200_tp_connect(self.handle, blob), "tp_connect")
+
+    def close(self):
+        if self.handle:
+            lib().yskn_b200_tp_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def linear_rowpar(exchange, mat, x_local, y, inv_rms=None, stream=None):
+    """yskn_b200_linear_rowpar: the whole output of a row-parallel shard, on every rank."""
+    check(lib().yskn_b200_linear_rowpar(exchange.handle, mat.handle, _ptr(x_local), x_local.shape[0], _ptr(inv_rms),
+                                        _ptr(y), _stream(stream)), "linear_rowpar")
 
 
 def restore(ws, row_quantum, inv_rms, mat, rotate_out, n_rows, clear_ws, y, stream=None):

@@ -72,13 +72,35 @@ class ColumnParallelLinear:
         return y
 
 
+def make_exchange(max_physical_rows, group=None, ops=None):
+    """This rank's exchange area of the one-launch row-parallel operator
+    (yskn_b200_linear_rowpar), connected to every peer's: the CUDA IPC handles travel
+    once through the process group (all_gather_object), the data then moves GPU to GPU
+    over NVLink without NCCL. Sized for matrices of up to max_physical_rows rows."""
+    ops = ops or _cuda_ops
+    rank, world = _rank_world(group)
+    rows = -(-max_physical_rows // 512) * 512
+    ex = ops.TpExchange(world, rank, rows)
+    handles = [None] * world
+    dist.all_gather_object(handles, ex.ipc_handle, group=group)
+    ex.connect(handles)
+    dist.barrier(group=group)  # every rank mapped before anyone sends
+    return ex
+
+
 class RowParallelLinear:
-    """Columns [col_begin, col_end) of a tensor on this rank (whole 512-column groups)."""
+    """Columns [col_begin, col_end) of a tensor on this rank (whole 512-column groups).
+
+    With `exchange` (make_exchange) a call with M <= 16 rows on a matrix with an output
+    rotation is one launch per rank (yskn_b200_linear_rowpar: the row maxima and the
+    int64 block sums travel over NVLink inside the kernel); otherwise the NCCL path
+    below (quantise, all-reduce MAX, rescale, sums, all-reduce SUM, restore)."""
 
     def __init__(self, d_codes, layout, rows, physical_rows, cols, bits, lut16, scale16, signs_in, signs_out=None,
-                 group=None, ops=None):
+                 group=None, ops=None, exchange=None):
         self.ops = ops or _cuda_ops
         self.group = group
+        self.exchange = exchange
         rank, world = _rank_world(group)
         self.ranges = split_blocks(cols, world)
         self.col_begin, self.col_end = self.ranges[rank]
@@ -105,8 +127,11 @@ class RowParallelLinear:
         """x_local: f32 [M][col_end - col_begin] (this rank's slice of the input);
         y: f32 [M][rows], the whole output, identical on every rank."""
         M = x_local.shape[0]
-        b = self._buffers(M, x_local.device)
         ops = self.ops
+        if self.exchange is not None and M <= 16 and self.mat.has_rotation:
+            ops.linear_rowpar(self.exchange, self.mat, x_local, y, inv_rms=inv_rms, stream=stream)
+            return y
+        b = self._buffers(M, x_local.device)
         ops.quantize(x_local, self.mat.signs_in_ptr, b["act"], b["alpha"], b["scales"], b["rq"], stream=stream)
         row_max = b["alpha"].amax(dim=1)
         dist.all_reduce(row_max, op=dist.ReduceOp.MAX, group=self.group)
