@@ -180,13 +180,15 @@ def test_linear_27b_shape_matches_oracle(cuda, bits):
         assert yskn_b200.status() == 0
 
 
-@pytest.mark.parametrize("M,cols", [(1, 2048), (3, 2048), (16, 2048), (17, 2048), (8, 17408)])
+@pytest.mark.parametrize("M,cols", [(1, 2048), (3, 2048), (16, 2048), (17, 2048), (8, 17408), (64, 2048),
+                                    (130, 1024)])
 def test_linear_fused_and_staged_paths(cuda, M, cols):
     """Three matrices sharing one input, two with an output rotation and one without
     (rows < physical rows), with 1/rms, bit-exact. M <= 16 with the activations in
     shared memory runs the one-launch fused operator; M = 17 and (8, 17408) run the
-    staged quantise / sums / restore launches. Twice in a row, so the per-block
-    counters of the fused restore are seen to reset."""
+    staged quantise / sums / restore launches; M >= 64 puts the tcgen05 GEMM between
+    the quantiser and the restore. Twice in a row, so the per-block counters of the
+    fused restore are seen to reset."""
     import torch
     import yskn_b200
     specs = [(1024, 1024, True), (512, 512, True), (300, 304, False)]
