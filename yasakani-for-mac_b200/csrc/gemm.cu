@@ -14,7 +14,7 @@
 //     choice for >= 256 rows, q35_g6.cu:35-69).
 //  2. gemm_kernel: persistent, one CTA per SM looping over 128 x 128 output tiles
 //     (128 activation rows x 128 weight rows) in a grouped raster. Warp 0 streams
-//     128-byte K chunks of both operands with TMA (128B swizzle, 4-stage mbarrier
+//     128-byte K chunks of both operands with TMA (128B swizzle, 5-stage mbarrier
 //     ring, counted across tiles); one thread of warp 1 issues
 //     tcgen05.mma.cta_group::1.kind::i8 (M=128, N=128, K=32) into TMEM; warps
 //     2..9 drain each 512-column group's int32 tile with tcgen05.ld, multiply it
@@ -40,11 +40,11 @@ namespace yskn {
 constexpr int GM_BM = 128;    // activation rows per tile (MMA M)
 constexpr int GM_BN = 128;    // weight rows per tile (MMA N)
 constexpr int GM_BK = 128;    // bytes of K per stage (one 128-byte swizzle row)
-constexpr int GM_STAGES = 4;
+constexpr int GM_STAGES = 5;
 constexpr int GM_THREADS = 320;  // 10 warps
 constexpr int GM_STAGE_BYTES = (GM_BM + GM_BN) * GM_BK;
 constexpr int GM_TMEM_BUFS = 4;  // group accumulators of 128 columns: the whole TMEM
-constexpr int GM_OUT_LD = 64 + 2;  // int64 per staged output row (16 bytes of padding)
+constexpr int GM_OUT_LD = 32 + 2;  // int64 per staged output row (16 bytes of padding)
 constexpr int GM_OUT_BYTES = GM_BM * GM_OUT_LD * 8;
 constexpr int GM_SMEM = GM_STAGES * GM_STAGE_BYTES + GM_OUT_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr long long GM_WAIT_LIMIT = 4000000000ll;  // clock cycles (~2 s) before a wait gives up
@@ -312,24 +312,26 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&tmem_empty[b]);
       }
-      // Output tile through the staging buffer: one 64-column half at a time, rows
-      // padded by 16 bytes; then each warp writes whole 512-byte row segments (direct
-      // per-row stores from registers measured 24 % slower). The MMA issuer meanwhile
-      // runs the next tile's groups into the other TMEM buffers.
+      // Output tile through the staging buffer: one 32-column quarter at a time (a small
+      // buffer leaves shared memory to the operand ring), rows padded by 16 bytes; then
+      // the warps write whole 256-byte row segments (direct per-row stores from
+      // registers measured 24 % slower). The MMA issuer meanwhile runs the next tile's
+      // groups into the other TMEM buffers.
       const bool live = !*abort_flag;
-      for (int h = 0; h < 2; ++h) {
-        if (half == h) {
 #pragma unroll
-          for (int j = 0; j < 64; j += 2)
+      for (int h = 0; h < 4; ++h) {
+        if (half == (h >> 1)) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 2)
             *reinterpret_cast<longlong2*>(stage_out + (quarter * 32 + lane) * GM_OUT_LD + j) =
-                make_longlong2(acc[j], acc[j + 1]);
+                make_longlong2(acc[(h & 1) * 32 + j], acc[(h & 1) * 32 + j + 1]);
         }
         asm volatile("bar.sync 1, 256;" ::: "memory");
         if (live) {
           const int et = threadIdx.x - 64;  // 0..255
-          const int c0 = n0 + h * 64;
-          for (int idx = et; idx < GM_BM * 32; idx += 256) {
-            const int r = idx >> 5, ch = idx & 31;
+          const int c0 = n0 + h * 32;
+          for (int idx = et; idx < GM_BM * 16; idx += 256) {
+            const int r = idx >> 4, ch = idx & 15;
             const int orow = m0 + r, col = c0 + 2 * ch;
             if (orow >= p.M) continue;
             const longlong2 val = *reinterpret_cast<const longlong2*>(stage_out + r * GM_OUT_LD + 2 * ch);
