@@ -656,8 +656,8 @@ YSKN_B200_API int yskn_b200_kv4_attention(const uint16_t* d_q, const uint16_t* d
       !d_out)
     return fail(YSKN_EINVAL, "kv4 attention: null argument");
   if (!aligned16(d_k_rows) || !aligned16(d_v_rows) || !aligned16(d_work) || !aligned16(d_q) || !aligned16(d_out) ||
-      (d_attended && !aligned16(d_attended)))
-    return fail(YSKN_EINVAL, "kv4 attention: queries, rows, outputs and work area must be 16-byte aligned");
+      (d_attended && !aligned16(d_attended)) || (d_gate && !aligned16(d_gate)))
+    return fail(YSKN_EINVAL, "kv4 attention: queries, gate, rows, outputs and work area must be 16-byte aligned");
   KvArgs a{};
   a.q = d_q;
   a.gate = d_gate;

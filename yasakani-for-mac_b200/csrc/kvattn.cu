@@ -39,11 +39,14 @@
 // so a warp's 32 lookups are one shared-memory wavefront; the address is one shift
 // (a funnel shift for a word's first state) and one LOP3.
 // Then the warps' (max, den, O) are merged, the self row added (FP32 weight, as the
-// spec keeps it separate) and den * mean; the CTA writes its split partial. The last
-// CTA of a (query row, KV head) to finish (an arrival counter in a static device
-// array, reset by that CTA) combines the splits of its G heads (padded to a power of
-// two, native expf), divides, applies the inverse H256 cache rotation with the hash
-// signs, rounds to BF16 and multiplies by the BF16 sigmoid of the gate.
+// spec keeps it separate) and den * mean; the CTA writes its split partial. The splits
+// of a (query row, KV head) are combined (padded to a power of two, native expf),
+// divided, inverse-rotated (H256 with the hash signs), rounded to BF16 and multiplied by
+// the BF16 sigmoid of the gate: when the grid is one wave of CTAs, by the last G CTAs to
+// arrive (an arrival counter in a static device array), one query head each with the
+// whole CTA, the earlier ones waiting (bounded) for the last arrival; otherwise by the
+// last CTA, one warp per head. The combiners count themselves in after the arrivals and
+// the last of them resets the counter.
 // Sums are FP32 in this kernel's own order: parity with the scalar spec is within a
 // tolerance (the reference's own kernels also use an unspecified MMA order, ATT-01).
 #include <cuda_bf16.h>
@@ -81,7 +84,10 @@ struct KvParams {
   float* attended;        // [M][n_qh][256] or nullptr
   uint16_t* out;          // [M][n_qh][256] bf16
   int M, n_qh, n_kvh, G, length, capacity, n_splits, max_splits;
+  int one_wave;  // every CTA of the grid fits on the SMs at once
+  unsigned* err;
 };
+constexpr long long KV_WAIT_LIMIT = 2000000000ll;  // clock cycles (~1 s) before a combiner's wait gives up
 
 // Splits of query row m (reference schedule unless fixed by the caller).
 __host__ __device__ __forceinline__ int kv_row_length(int length, int M, int m) { return length - M + 1 + m; }
@@ -103,6 +109,8 @@ struct KvSmem {
   uint4 selfrow[2][8];   // the self row's K and V words
   float selfscale[4];    // its K and V scales
   float comb[KV_WARPS][KV_MAX_SPLITS];  // per combining warp: the splits' weights
+  float vmean[256];                      // the value mean (zeros without one), staged at set-up
+  uint16_t qrow[KV_MAX_GROUP][256];      // the G query rows (bf16), staged at set-up for the self score
   int last;
 };
 
@@ -165,36 +173,122 @@ __device__ __forceinline__ float kv_cache_sign(int channel) {  // attention.rs:9
 // 04_ATTENTION.md:428-453: pad to a power of two, native expf, divide), the inverse
 // cache rotation, BF16 and the gate, by one warp: lane l owns channels 8l..8l+7, so
 // the H256 strides 1..4 stay in the lane and 8..128 are lane shuffles (ascending).
-// comb: this warp's 64 floats of scratch.
-__device__ void combine_head_warp(const KvParams& p, float* comb, size_t row, int n_splits, int lane) {
-  const float* P = p.partials + row * p.max_splits * KV_PART;
+// One warp: the splits' weights comb[s] = exp(max_s - max) (zero for the padding) and
+// the total den, lane-parallel over s = lane + 32 i, then a butterfly sum.
+__device__ __forceinline__ float kv_split_weights(const float* P, int n_splits, float* comb, int lane) {
+  float ms[2], ds[2];  // split s = lane + 32 i (at most 64 splits): its max and den, loaded once
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int s = lane + 32 * i;
+    const float2 md = s < n_splits ? __ldcg(reinterpret_cast<const float2*>(P + (size_t)s * KV_PART))
+                                   : make_float2(-1e30f, 0.0f);
+    ms[i] = md.x;
+    ds[i] = md.y;
+  }
   int padded = 1;
   while (padded < n_splits) padded <<= 1;
-  float mx = -1e30f;
-  for (int s = lane; s < padded; s += 32) mx = fmaxf(mx, s < n_splits ? __ldcg(P + (size_t)s * KV_PART) : -1e30f);
+  float mx = fmaxf(ms[0], ms[1]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  float tot = 0.0f;  // lane-parallel, then a butterfly sum
-  for (int s = lane; s < padded; s += 32) {
-    const float ms = s < n_splits ? __ldcg(P + (size_t)s * KV_PART) : -1e30f;
-    const float f = ms > -1e29f ? expf(ms - mx) : 0.0f;
+  float tot = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int s = lane + 32 * i;
+    if (s >= padded) break;
+    const float f = ms[i] > -1e29f ? expf(ms[i] - mx) : 0.0f;
     comb[s] = f;
-    if (s < n_splits) tot += f * __ldcg(P + (size_t)s * KV_PART + 1);
+    if (s < n_splits) tot += f * ds[i];
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
   __syncwarp();
+  return tot;
+}
+
+__device__ void finish_head(const KvParams& p, float (&v)[8], uint4 gate8, size_t row, int lane);
+
+// comb: this warp's 64 floats of scratch. The gate and the first KV_COMB_BATCH splits'
+// numerators are requested before the split weights are formed, and the splits are
+// then taken in batches of that many with all their loads in flight (the sums still
+// run over the splits in ascending order).
+constexpr int KV_COMB_BATCH = 20;
+__device__ void combine_head_warp(const KvParams& p, float* comb, size_t row, int n_splits, int lane) {
+  const float* P = p.partials + row * p.max_splits * KV_PART;
+  uint4 gate8 = make_uint4(0, 0, 0, 0);
+  if (p.gate) gate8 = __ldg(reinterpret_cast<const uint4*>(p.gate + row * 256 + 8 * lane));
+  float4 nb[KV_COMB_BATCH][2];
+  auto load_batch = [&](int s0) {
+#pragma unroll
+    for (int j = 0; j < KV_COMB_BATCH; ++j)
+      if (s0 + j < n_splits) {
+        const float4* src = reinterpret_cast<const float4*>(P + (size_t)(s0 + j) * KV_PART + KV_NUM + 8 * lane);
+        nb[j][0] = __ldcg(src);
+        nb[j][1] = __ldcg(src + 1);
+      }
+  };
+  load_batch(0);
+  const float tot = kv_split_weights(P, n_splits, comb, lane);
   float v[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 4
-  for (int s = 0; s < n_splits; ++s) {
-    const float f = comb[s];
-    const float4* src = reinterpret_cast<const float4*>(P + (size_t)s * KV_PART + KV_NUM + 8 * lane);
-    const float4 a = __ldcg(src), b = __ldcg(src + 1);
-    v[0] += f * a.x; v[1] += f * a.y; v[2] += f * a.z; v[3] += f * a.w;
-    v[4] += f * b.x; v[5] += f * b.y; v[6] += f * b.z; v[7] += f * b.w;
+  for (int s0 = 0; s0 < n_splits; s0 += KV_COMB_BATCH) {
+#pragma unroll
+    for (int j = 0; j < KV_COMB_BATCH; ++j)
+      if (s0 + j < n_splits) {
+        const float f = comb[s0 + j];
+        const float4 a = nb[j][0], b = nb[j][1];
+        v[0] += f * a.x; v[1] += f * a.y; v[2] += f * a.z; v[3] += f * a.w;
+        v[4] += f * b.x; v[5] += f * b.y; v[6] += f * b.z; v[7] += f * b.w;
+      }
+    load_batch(s0 + KV_COMB_BATCH);
   }
 #pragma unroll
   for (int e = 0; e < 8; ++e) v[e] = v[e] / tot;
+  finish_head(p, v, gate8, row, lane);
+}
+
+// The same combination of one query head by a whole CTA: thread t owns channel t and
+// has all the splits' numerators of its channel in flight at once, warp 0 forms the
+// weights meanwhile; the per-channel sums run over the splits in the same ascending
+// order as above (same bits). Then warp 0 finishes the head from shared memory.
+// stage: 256 floats of shared scratch; comb: 64; tot_s: 1.
+__device__ void combine_head_cta(const KvParams& p, float* comb, float* stage, float* tot_s, size_t row,
+                                 int n_splits) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  const float* P = p.partials + row * p.max_splits * KV_PART;
+  constexpr int CH = 32;  // splits in flight per thread
+  float val[CH];
+  auto load = [&](int s0) {
+#pragma unroll
+    for (int j = 0; j < CH; ++j)
+      if (s0 + j < n_splits) val[j] = __ldcg(P + (size_t)(s0 + j) * KV_PART + KV_NUM + tid);
+  };
+  load(0);
+  uint4 gate8 = make_uint4(0, 0, 0, 0);
+  if (tid < 32 && p.gate) gate8 = __ldg(reinterpret_cast<const uint4*>(p.gate + row * 256 + 8 * lane));
+  if (tid < 32) {
+    const float tot = kv_split_weights(P, n_splits, comb, lane);
+    if (lane == 0) *tot_s = tot;
+  }
+  __syncthreads();
+  float v = 0.0f;
+  for (int s0 = 0; s0 < n_splits; s0 += CH) {
+#pragma unroll
+    for (int j = 0; j < CH; ++j)
+      if (s0 + j < n_splits) v += comb[s0 + j] * val[j];
+    if (s0 + CH < n_splits) load(s0 + CH);
+  }
+  stage[tid] = v / *tot_s;
+  __syncthreads();
+  if (tid < 32) {
+    float w[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) w[e] = stage[8 * lane + e];
+    finish_head(p, w, gate8, row, lane);
+  }
+}
+
+// The divided head (lane l: channels 8l..8l+7): the attended values, the inverse H256
+// cache rotation with the hash signs, BF16, times the BF16 sigmoid of the gate.
+__device__ void finish_head(const KvParams& p, float (&v)[8], uint4 gate8, size_t row, int lane) {
   if (p.attended) {
     float4* dst = reinterpret_cast<float4*>(p.attended + row * 256 + 8 * lane);
     dst[0] = make_float4(v[0], v[1], v[2], v[3]);
@@ -226,7 +320,8 @@ __device__ void combine_head_warp(const KvParams& p, float* comb, size_t row, in
     const float r = __bfloat162float(__float2bfloat16_rn((v[e] * 0.0625f) * kv_cache_sign(ch)));
     float o = r;
     if (p.gate) {
-      const float gv = __uint_as_float((uint32_t)p.gate[row * 256 + ch] << 16);
+      const uint32_t gw = (&gate8.x)[e >> 1];
+      const float gv = __uint_as_float((e & 1) ? (gw & 0xffff0000u) : (gw << 16));
       const float sg = __bfloat162float(__float2bfloat16_rn(1.0f / (1.0f + expf(-gv))));
       o = r * sg;
     }
@@ -300,6 +395,10 @@ __global__ void __launch_bounds__(KV_THREADS, 1) kv4_attention_kernel(const __gr
   uint16_t* raw_k = &S.pt[0][0];
   uint16_t* raw_v = &S.pt[2][0];
   raw_k[tid] = p.kbase[h * 256 + tid];
+  // Staged now for the end of the kernel (the self score and the value mean), so their
+  // global-memory latency is paid during the set-up, not after the key loop.
+  S.vmean[tid] = p.vmean ? __ldg(p.vmean + h * 256 + tid) : 0.0f;
+  for (int hh = 0; hh < G; ++hh) S.qrow[hh][tid] = __ldg(p.q + ((size_t)m * p.n_qh + h * G + hh) * 256 + tid);
   raw_v[tid] = p.vbase[h * 256 + tid];
   const int g = lane >> 2, t = lane & 3;
   const uint32_t lane4 = (uint32_t)lane << 2;
@@ -523,7 +622,7 @@ __global__ void __launch_bounds__(KV_THREADS, 1) kv4_attention_kernel(const __gr
   // Self score of head `warp` in FP32 (the spec's separate self term).
   if (include_self && warp < G) {
     const uint32_t w = selfk[lane], pw = (lane & 7) ? selfk[lane - 1] : 0u;
-    const uint16_t* qr = p.q + ((size_t)m * p.n_qh + h * G + warp) * 256 + 8 * lane;
+    const uint16_t* qr = &S.qrow[warp][8 * lane];
     float a = 0.0f;
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
@@ -543,7 +642,7 @@ __global__ void __launch_bounds__(KV_THREADS, 1) kv4_attention_kernel(const __gr
     vself = __uint_as_float(lds32(lutV + lut_off(w, pw, n, lane4)) << 16);
     vs_self = S.selfscale[1];
   }
-  const float mean = p.vmean ? p.vmean[h * 256 + ch] : 0.0f;
+  const float mean = S.vmean[ch];
   for (int hh = 0; hh < G; ++hh) {
     float M = -1e30f;
 #pragma unroll
@@ -573,16 +672,46 @@ __global__ void __launch_bounds__(KV_THREADS, 1) kv4_attention_kernel(const __gr
     out[KV_NUM + ch] = num;
   }
 
-  // ---- the last CTA of this (query row, KV head) combines the splits
-  __threadfence();
+  // ---- the last CTA of this (query row, KV head) combines the splits. Release: every
+  // thread's partial stores, then the CTA barrier, then one arrival; the last arriver
+  // acquires before it reads the other splits' partials (acq_rel fences, lighter than
+  // the sequentially consistent __threadfence).
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
   __syncthreads();
   unsigned* arrivals = g_kv_arrivals + (size_t)m * p.n_kvh + h;
-  if (tid == 0) S.last = atomicAdd(arrivals, 1u) == (unsigned)(n_splits - 1);
+  if (tid == 0) S.last = (int)atomicAdd(arrivals, 1u);
   __syncthreads();
-  if (!S.last) return;
-  __threadfence();
-  if (warp < G) combine_head_warp(p, S.comb[warp], (size_t)m * p.n_qh + h * G + warp, n_splits, lane);
-  if (tid == 0) *arrivals = 0u;
+  // The last G CTAs to arrive combine one query head each (k = 0: the last one), when
+  // the whole grid is one wave of CTAs (they all run at once, so the others' waits for
+  // the final arrival end); otherwise the last CTA combines all G heads.
+  const int ncomb = p.one_wave ? min(G, n_splits) : 1;  // combiner k takes heads k, k + ncomb, ...
+  const int k = n_splits - 1 - S.last;
+  if (k >= ncomb) return;
+  if (k > 0 && tid == 0) {  // wait (bounded) until every split's partial is in
+    const long long t0 = clock64();
+    unsigned v;
+    do {
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(arrivals) : "memory");
+      if (clock64() - t0 > KV_WAIT_LIMIT) {
+        raise_device_error(p.err, DERR_TIMEOUT);
+        break;
+      }
+    } while (v < (unsigned)n_splits);
+  }
+  __syncthreads();
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+  if (ncomb == 1) {
+    if (warp < G) combine_head_warp(p, S.comb[warp], (size_t)m * p.n_qh + h * G + warp, n_splits, lane);
+  } else {
+    for (int hh = k; hh < G; hh += ncomb) {
+      combine_head_cta(p, S.comb[0], &S.u.merge[0][0][0], &S.wden[0][0], (size_t)m * p.n_qh + h * G + hh, n_splits);
+      __syncthreads();  // the shared scratch is reused by the next head
+    }
+  }
+  // The combiners count themselves in after the arrivals; the last of them resets the
+  // counter for the next launch.
+  __syncthreads();
+  if (tid == 0 && atomicAdd(arrivals, 1u) == (unsigned)(n_splits + ncomb - 1)) *arrivals = 0u;
 }
 
 static int sm_count_kv() {
@@ -627,6 +756,8 @@ int launch_kv4_attention(const KvArgs& a, cudaStream_t st) {
   p.capacity = a.capacity;
   p.n_splits = kv_resolved_splits(a);
   p.max_splits = kv_max_splits(a);
+  p.err = device_error_word();
+  p.one_wave = (int64_t)p.max_splits * a.n_kvh * a.M <= sm_count_kv() ? 1 : 0;
   if ((int64_t)a.M * a.n_kvh > KV_MAX_ARRIVALS) return fail(YSKN_EINVAL, "kv4 attention: M * n_kv_heads > 4096");
   static bool attr[64] = {};
   int dev = 0;
