@@ -377,6 +377,30 @@ __global__ void __launch_bounds__(KV_THREADS, 1) kv4_attention_kernel(const __gr
     }
   };
 
+  // Programmatic dependent launch: the next kernel on the stream may be scheduled as SMs
+  // free up (it waits before it reads anything this grid writes).
+  asm volatile("griddepcontrol.launch_dependents;");
+  // 32 copies of each codebook: one coalesced load of the 256 entries (staged in the
+  // transpose buffers), then consecutive-word stores read back as broadcasts. The
+  // codebooks and the value mean belong to the model, so they are fetched and expanded
+  // before this grid waits for the previous kernel on the stream.
+  uint16_t* raw_k = &S.pt[0][0];
+  uint16_t* raw_v = &S.pt[2][0];
+  raw_k[tid] = p.kbase[h * 256 + tid];
+  raw_v[tid] = p.vbase[h * 256 + tid];
+  S.vmean[tid] = p.vmean ? __ldg(p.vmean + h * 256 + tid) : 0.0f;  // for the end of the kernel
+  __syncthreads();
+#pragma unroll 8
+  for (int i = tid; i < 256 * 32; i += KV_THREADS) {
+    S.lut[0][i] = raw_k[i >> 5];
+    S.lut[1][i] = raw_v[i >> 5];
+  }
+  if (tid < 8) S.run[tid] = -1e30f;
+  // The cache rows (the newest one may come from the encoder just before), the queries
+  // and the gate may be the previous kernel's output: wait for it (a no-op without a
+  // programmatic launch).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
   // First requests: the chunk's first two blocks of this warp (K, V, scales) and the self row.
   int nb = n_tiles > 0 ? blocks_of(0) : 0;
   for (int j = 0; j < min(nb, 2); ++j) {
@@ -389,17 +413,8 @@ __global__ void __launch_bounds__(KV_THREADS, 1) kv4_attention_kernel(const __gr
     else if (lane < 18) cp_async4(&S.selfscale[lane - 16], (lane == 16 ? Ks : Vs) + self, 4);
     cp_commit();
   }
-
-  // 32 copies of each codebook: one coalesced load of the 256 entries (staged in the
-  // transpose buffers), then consecutive-word stores read back as broadcasts.
-  uint16_t* raw_k = &S.pt[0][0];
-  uint16_t* raw_v = &S.pt[2][0];
-  raw_k[tid] = p.kbase[h * 256 + tid];
-  // Staged now for the end of the kernel (the self score and the value mean), so their
-  // global-memory latency is paid during the set-up, not after the key loop.
-  S.vmean[tid] = p.vmean ? __ldg(p.vmean + h * 256 + tid) : 0.0f;
+  // The query rows, staged for the self score at the end of the kernel.
   for (int hh = 0; hh < G; ++hh) S.qrow[hh][tid] = __ldg(p.q + ((size_t)m * p.n_qh + h * G + hh) * 256 + tid);
-  raw_v[tid] = p.vbase[h * 256 + tid];
   const int g = lane >> 2, t = lane & 3;
   const uint32_t lane4 = (uint32_t)lane << 2;
   // B fragments of Q^T: head g (zero beyond G), channels 64t + 4i + {0,1} and {2,3}.
@@ -413,13 +428,6 @@ __global__ void __launch_bounds__(KV_THREADS, 1) kv4_attention_kernel(const __gr
       qb[i][1] = g < G ? v.y : 0u;
     }
   }
-  __syncthreads();
-#pragma unroll 8
-  for (int i = tid; i < 256 * 32; i += KV_THREADS) {
-    S.lut[0][i] = raw_k[i >> 5];
-    S.lut[1][i] = raw_v[i >> 5];
-  }
-  if (tid < 8) S.run[tid] = -1e30f;
   __syncthreads();
   const uint32_t lutK = (uint32_t)__cvta_generic_to_shared(S.lut[0]);
   const uint32_t lutV = (uint32_t)__cvta_generic_to_shared(S.lut[1]);
@@ -769,8 +777,19 @@ int launch_kv4_attention(const KvArgs& a, cudaStream_t st) {
     if (e != cudaSuccess) return cuda_fail(e, "kv4 attributes");
     attr[dev] = true;
   }
-  kv4_attention_kernel<<<dim3(p.max_splits, a.n_kvh, a.M), KV_THREADS, sizeof(KvSmem), st>>>(p);
-  return cuda_fail(cudaGetLastError(), "kv4_attention_kernel");
+  // A programmatic dependent of the previous kernel on the stream: the CTAs may start
+  // on SMs that kernel has left and build their codebooks while it finishes.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.max_splits, a.n_kvh, a.M);
+  cfg.blockDim = dim3(KV_THREADS);
+  cfg.dynamicSmemBytes = sizeof(KvSmem);
+  cfg.stream = st;
+  cudaLaunchAttribute attr_pdl[1];
+  attr_pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr_pdl[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr_pdl;
+  cfg.numAttrs = 1;
+  return cuda_fail(cudaLaunchKernelEx(&cfg, kv4_attention_kernel, p), "kv4_attention_kernel");
 }
 
 }  // namespace yskn
