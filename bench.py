@@ -16,9 +16,10 @@ the 126 MB L2, so no L2 flush is needed between steps.
 With --gpus N > 1 (torchrun, one rank per GPU) the same layer step runs tensor-
 parallel (yskn_b200/tp.py): q/k/v, qkv/z and gate/up column-parallel over whole
 512-row blocks (k/v replicated at 4 and 8 GPUs), o/out/down row-parallel over
-512-column groups with an NCCL all-reduce MAX of the row maxima and an exact int64
-all-reduce SUM each; the value is the whole layer's bytes over the max-over-ranks
-step time (strong scaling).
+512-column groups, each one launch per rank that exchanges the row maxima and the
+exact int64 block sums with the other ranks over NVLink (yskn_b200_linear_rowpar);
+the value is the whole layer's bytes over the max-over-ranks step time (strong
+scaling).
 
 `--impl reference` times the CPU path instead: the C restatement (oracle/) of the
 reference's CPU engine (crates/yskn-engine kernel + pool, crates/yskn-ref quantiser
@@ -47,7 +48,7 @@ CALLS = [["q_proj", "k_proj", "v_proj"], ["o_proj"], ["in_proj_qkv", "in_proj_z"
          ["gate_proj", "up_proj"], ["down_proj"]]
 # DRAM bytes (read + write) of the six fused gemv_kernel launches of one step, from one
 # ncu capture of this workload (profiles/gemv_kernel_layer_bits8.md); None where not captured.
-GEMV_TRAFFIC = {(8, 1): 248_152_576}
+GEMV_TRAFFIC = {(8, 1): 248_069_888}
 METRIC = "compressed GEMV HBM TB/s (one hybrid layer's linear set, batch-1 decode)"
 UNIT = "TB/s"
 
