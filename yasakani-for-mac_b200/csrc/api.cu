@@ -322,10 +322,15 @@ static yskn_b200_matrix* create_matrix(const uint32_t* d_codes, int layout, int 
   const size_t off_sout = off_sin + ceil_div(cols, 256) * 256;
   const size_t off_lutx = off_sout + ceil_div(physical_rows, 256) * 256;
   const size_t small_bytes = off_lutx + 4096 * 32;
-  // The GEMV's shared-memory image of the table (gemv.cu): slot s = 16 copies of entry s.
+  // The GEMV's shared-memory image of the table (MatrixDev::lutx).
   std::vector<uint16_t> lutx(4096 * 16);
-  for (int s = 0; s < 4096; ++s)
-    for (int c = 0; c < 16; ++c) lutx[16 * s + c] = (uint16_t)((uint8_t)lut8[2 * s] | ((uint8_t)lut8[2 * s + 1] << 8));
+  auto pair = [&](uint32_t s) { return (uint16_t)((uint8_t)lut8[2 * s] | ((uint8_t)lut8[2 * s + 1] << 8)); };
+  if (bits == 8) {
+    for (uint32_t e = 0; e < 4096 * 16; ++e) lutx[e] = pair(lutx8_state(2 * e));
+  } else {
+    for (int s = 0; s < 4096; ++s)
+      for (int c = 0; c < 16; ++c) lutx[16 * s + c] = pair(s);
+  }
   cudaError_t e = cudaMalloc(&m->codes, (size_t)packed);
   if (e == cudaSuccess) e = cudaMalloc(&m->small, small_bytes);
   if (e != cudaSuccess) {

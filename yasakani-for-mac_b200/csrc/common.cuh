@@ -32,10 +32,35 @@ int cuda_fail(cudaError_t e, const char* where);
 // 1/sqrt(512) as the binary32 literal 0.044194173824159216f (bits 0x3d3504f3).
 constexpr float kHadamardNorm = 0.044194173824159216f;
 
+// bits = 8: the streaming layout stores every byte c of the code stream with its bits
+// moved, b = file byte: c[0,1] = b[4,5], c[2..5] = b[0..3], c[6,7] = b[6,7]. A 12-bit
+// state is the high nibble of byte i-1 and all of byte i, so in the 16 stored bits of
+// bytes i-1, i the state's bits sit at 0,1 and 6..15 and bits 2..5 (the low nibble of
+// byte i-1) are not part of it. Shifted left by one, those four bits land on the
+// table image's copy field (address bits 3..6): the GEMV forms a lookup address with
+// one shift and one LOP3 while each table copy spans two banks (gemv.cu).
+__host__ __device__ inline uint32_t stream8_store(uint32_t b) {
+  return ((b >> 4) & 0x03030303u) | ((b & 0x0f0f0f0fu) << 2) | (b & 0xc0c0c0c0u);
+}
+__host__ __device__ inline uint32_t stream8_load(uint32_t c) {
+  return ((c & 0x03030303u) << 4) | ((c >> 2) & 0x0f0f0f0fu) | (c & 0xc0c0c0c0u);
+}
+// The state whose entry the bits = 8 table image holds at byte address a (even,
+// < 128 KiB): address bit j is stored bit j-1 of bytes (i-1, i); bits 3..6 pick the copy.
+__host__ __device__ inline uint32_t lutx8_state(uint32_t a) {
+  const uint32_t c_prev = ((a >> 1) & 3u) | (((a >> 7) & 3u) << 6);  // stored byte i-1, bits 2..5 unused
+  const uint32_t c_cur = (a >> 9) & 0xffu;                           // stored byte i
+  const uint32_t b_prev = stream8_load(c_prev), b_cur = stream8_load(c_cur);
+  return (b_prev >> 4) | (b_cur << 4);
+}
+
 struct MatrixDev {
   const uint32_t* codes;  // B200 streaming layout (see pack.cu)
   const uint16_t* lut8;   // 4096 entries: int8 pair (component 0 low byte, component 1 high byte)
-  const uint8_t* lutx;    // the GEMV's shared-memory image of lut8: 4096 slots of 32 bytes, entry s 16 times in slot s
+  // The GEMV's shared-memory image of lut8 (128 KiB, 16 copies). bits = 8: the entry of
+  // lutx8_state(a) at every even byte address a, copy (a >> 3) & 15 in banks 2c, 2c+1;
+  // other bits: 4096 slots of 32 bytes, entry s 16 times in slot s.
+  const uint8_t* lutx;
   const float* tau;       // effective row scale, f32[physical_rows]
   const int8_t* s_in;     // i8[cols]
   const int8_t* s_out;    // i8[physical_rows] or nullptr

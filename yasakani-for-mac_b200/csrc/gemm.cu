@@ -128,7 +128,10 @@ __global__ void __launch_bounds__(256) predecode_kernel(const uint32_t* __restri
     const uint32_t* tile = codes + t * (BITS * 32);
     uint32_t w[BITS];
 #pragma unroll
-    for (int j = 0; j < BITS; ++j) w[j] = __ldg(tile + ((j / U) * 32 + lane) * U + (j % U));
+    for (int j = 0; j < BITS; ++j) {
+      w[j] = __ldg(tile + ((j / U) * 32 + lane) * U + (j % U));
+      if constexpr (BITS == 8) w[j] = stream8_load(w[j]);  // the file's bit order (common.cuh)
+    }
     uint32_t carry = __shfl_up_sync(0xffffffffu, w[BITS - 1], 1);
     if ((lane & 3) == 0) carry = 0u;
     uint32_t out[16];

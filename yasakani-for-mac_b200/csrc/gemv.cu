@@ -15,13 +15,12 @@
 // * Decode: each lane rebuilds its 32 states with constant shifts (the
 //   12-bit window of its first step reaches into the previous quarter: one
 //   shfl_up of the neighbour's last word), and looks the int8 pairs up in
-//   shared memory. The table is stored 16 times (two lanes per copy, four lanes
-//   per group of 4 banks), so a warp-wide lookup costs about 3 shared-memory
-//   wavefronts instead of ~3.6 for one shared copy, and the address is one shift
-//   (a funnel shift only where the 12-bit window straddles two words) plus one
-//   LOP3. B200's integer pipe (16 lanes/clk per SM sub-partition) is as scarce
-//   as shared-memory bandwidth here, so the layout is chosen for fewer integer
-//   ops per lookup rather than fewer bank conflicts.
+//   shared memory. The table is stored 16 times (two lanes per copy); the
+//   address is one shift (a funnel shift only where the 12-bit window straddles
+//   two words) plus one LOP3, because B200's integer pipe (16 lanes/clk per SM
+//   sub-partition) is as scarce as shared-memory bandwidth here. At bits = 8 the
+//   stored bit order lets each copy own two banks (~2 wavefronts per warp-wide
+//   lookup); at other bits four lanes share four banks (~3 wavefronts).
 // * Math: the 8 decoded weights of a lane per 32-column chunk are exactly its
 //   B fragment of mma.sync.m16n8k32.s8 (n = row, k = 8 consecutive columns of its
 //   quarter); the activations (A, 16 token rows) are loaded in the same column
@@ -145,17 +144,25 @@ __device__ __forceinline__ uint32_t window(uint32_t carry, const uint32_t (&w)[B
   return __funnelshift_r(lo, hi, sh);
 }
 
-// Shared-memory byte address of state(step i) in this lane's table copy. The
-// table is 4096 slots of 32 bytes (slot s holds 16 copies of entry s), so the
-// state lands in address bits 5..16 with one shift and one LOP3, and the copy
-// (lane/2) in bits 1..4. Four lanes share the 4 banks {c, c+8, c+16, c+24}
-// picked by the state's two low bits: ~3 wavefronts per 32 random lookups,
-// against ~2 for a layout that needs two shifted fields; on B200 the integer
-// pipe, not shared memory, was the tighter limit of the two-field form.
+// Shared-memory byte address of state(step i) in this lane's table copy, one shift
+// (a funnel shift where the bits straddle two words) and one LOP3 either way.
+// * bits = 8: the stored bytes carry the state's bits at 0,1 and 6..15 of bytes
+//   (i-1, i) (stream8_store, common.cuh); shifted left by one and masked, they fill
+//   address bits 1,2 and 7..16 around the copy (lane/2) in bits 3..6, so copy c sits
+//   in banks 2c and 2c+1 and only the two lanes of a copy can conflict: ~2 shared-
+//   memory wavefronts per 32 random lookups.
+// * other bits: 4096 slots of 32 bytes (slot s holds 16 copies of entry s), the state
+//   in address bits 5..16, the copy in bits 1..4. Four lanes share the 4 banks
+//   {c, c+8, c+16, c+24} picked by the state's two low bits: ~3 wavefronts.
 template <int BITS>
 __device__ __forceinline__ uint32_t lut_addr(uint32_t carry, const uint32_t (&w)[BITS], int i, uint32_t copy_off) {
   const int P = 32 + BITS * (i + 1) - 12;  // first bit of the state in V
+  if constexpr (BITS == 8) return (window<BITS, 1, 17>(carry, w, P - 5) & 0x1ff86u) | copy_off;
   return (window<BITS, 5, 17>(carry, w, P - 5) & 0x1ffe0u) | copy_off;
+}
+template <int BITS>
+__device__ __forceinline__ uint32_t lut_copy_off(int lane) {
+  return BITS == 8 ? (uint32_t)(lane >> 1) << 3 : (uint32_t)(lane >> 1) << 1;
 }
 
 // lo | hi << 16 on the FMA pipe (lo, hi are zero-extended 16-bit entries).
@@ -452,7 +459,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
 
   if (t_begin >= t_end) return;
 
-  const uint32_t copy_off = (uint32_t)(lane >> 1) << 1;
+  const uint32_t copy_off = lut_copy_off<BITS>(lane);
   const int q = lane & 3, n = lane >> 2;
   const int tok0 = n < p.mv ? n : p.mv - 1;
   const int tok1 = n + 8 < p.mv ? n + 8 : p.mv - 1;

@@ -9,7 +9,8 @@
 //    sequence (its 32 trellis steps), stored in chunks of U words
 //    (U = 4 for bits 4/8, 2 for bits 6, 1 otherwise) interleaved across the 32
 //    lanes: chunk j of lane l at tile + (j*32 + l)*U. A warp's load of one chunk
-//    is one contiguous 128*U-byte segment.
+//    is one contiguous 128*U-byte segment. At bits = 8 each byte is stored with its
+//    bits moved (stream8_store, common.cuh) for the GEMV's table addressing.
 //  * repack_frag: the reference's own load-time permutation into its mma.sync
 //    "frag" order (src/repack.cu:10-18), kept bit-identical for the C ABI, written
 //    with 16-byte moves (one thread per chunk of 4 words) instead of one per word.
@@ -45,6 +46,7 @@ __global__ void __launch_bounds__(256) pack_kernel(const uint32_t* __restrict__ 
         s = (sr * src_seqs + ss) * (4 * (int64_t)bits) + w;
       }
       v = __ldg(src + s);
+      if (bits == 8) v = stream8_store(v);  // bit order inside each byte (common.cuh)
     }
     t[((j / U) * 32 + lane) * U + (j % U)] = v;
   }
