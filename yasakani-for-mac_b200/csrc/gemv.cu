@@ -351,27 +351,50 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
     mbar_init(s_bar, 1);
     mbar_init_fence();
     mbar_expect_tx(s_bar, LUT_COPY_BYTES);
+    // Every CTA of the segment copies the same image: each starts at another quarter, so
+    // the CTAs' first requests spread over the L2 slices instead of queueing on the same lines.
 #pragma unroll
-    for (int c = 0; c < 4; ++c)
+    for (int k = 0; k < 4; ++k) {
+      const int c = (k + blockIdx.x) & 3;
       bulk_copy_g2s(s_lut + c * (LUT_COPY_BYTES / 4), S.lutx + c * (LUT_COPY_BYTES / 4), LUT_COPY_BYTES / 4, s_bar);
+    }
+  }
+  if (FUSED && S.s_out) {
+    // The restores at the end of the launch read the row scales and output signs of
+    // whole 512-row blocks; the segment's CTAs bring both into L2 now, a share each.
+    const size_t t_lines = ((size_t)S.y_rows * 4 + 127) / 128, s_lines = ((size_t)S.y_rows + 127) / 128;
+    for (size_t l = (size_t)(blockIdx.x - S.cta_begin) * blockDim.x + threadIdx.x; l < t_lines + s_lines;
+         l += (size_t)S.n_ctas * blockDim.x) {
+      const char* a = l < t_lines ? reinterpret_cast<const char*>(S.tau) + 128 * l
+                                  : reinterpret_cast<const char*>(S.s_out) + 128 * (l - t_lines);
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
+    }
   }
   // Everything above reads only the matrix (codes, table), which no kernel writes. The
   // inputs, the scales and every scratch word may belong to the previous kernel on the
   // stream until it completes: wait for it here (a no-op without a programmatic launch).
   asm volatile("griddepcontrol.wait;" ::: "memory");
   // Fused: each warp's first input group is requested first, ahead of the staging below.
-  if (FUSED && warp < items)
-    load_group512(p.x + (size_t)(warp / G) * Kc + (warp % G) * 512, p.s_in + (warp % G) * 512, lane, nxt);
+  // Warp w quantises items w, w + 16, ... counted from a CTA-dependent start, so the CTAs
+  // do not all read the same input lines at the same moment.
+  const int item_rot = FUSED ? (int)(blockIdx.x % (unsigned)items) : 0;
+  auto item_of = [&](int k) { return k + item_rot < items ? k + item_rot : k + item_rot - items; };
+  if (FUSED && warp < items) {
+    const int it = item_of(warp);
+    load_group512(p.x + (size_t)(it / G) * Kc + (it % G) * 512, p.s_in + (it % G) * 512, lane, nxt);
+  }
   {
     if (FUSED) {
       // A warp's groups in turn, each one's inputs requested before the previous is quantised.
       bool bad = false;
-      for (int item = warp; item < items; item += GEMV_WARPS) {
+      for (int k = warp; k < items; k += GEMV_WARPS) {
+        const int item = item_of(k);
         const int m = item / G, g = item - m * G;
         const Group512In cur = nxt;
-        const int after = item + GEMV_WARPS;
-        if (after < items)
+        if (k + GEMV_WARPS < items) {
+          const int after = item_of(k + GEMV_WARPS);
           load_group512(p.x + (size_t)(after / G) * Kc + (after % G) * 512, p.s_in + (after % G) * 512, lane, nxt);
+        }
         const float a = quantize_loaded512(cur, s_act + (size_t)m * act_ld + g * 512, lane, bad);
         if (lane == 0) s_alpha[item] = a;
       }

@@ -20,6 +20,12 @@
 
 namespace yskn {
 
+// One butterfly across lanes: the lower lane keeps v + other, the upper lane other - v.
+// Both are fma(v, s, other) with s = +1 or -1: v * s is exact, so the single rounding
+// of the fma gives exactly fadd_rn(v, other) or fsub_rn(other, v) (signed zeros, infinities
+// and NaN included), in one instruction instead of an add, a subtract and a select.
+__device__ __forceinline__ float cross_butterfly(float v, float other, float s) { return __fmaf_rn(v, s, other); }
+
 __device__ __forceinline__ void hadamard512_warp(float (&v)[16], int lane) {
 #pragma unroll
   for (int stride = 1; stride < 16; stride <<= 1) {
@@ -35,12 +41,9 @@ __device__ __forceinline__ void hadamard512_warp(float (&v)[16], int lane) {
   }
 #pragma unroll
   for (int mask = 1; mask < 32; mask <<= 1) {
-    const bool upper_half = (lane & mask) != 0;
+    const float s = (lane & mask) ? -1.0f : 1.0f;
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const float other = __shfl_xor_sync(0xffffffffu, v[e], mask);
-      v[e] = upper_half ? __fsub_rn(other, v[e]) : __fadd_rn(v[e], other);
-    }
+    for (int e = 0; e < 16; ++e) v[e] = cross_butterfly(v[e], __shfl_xor_sync(0xffffffffu, v[e], mask), s);
   }
 }
 
@@ -88,9 +91,11 @@ __device__ __forceinline__ float quantize_loaded512(const Group512In& in, int8_t
   // x * s for s = +1/-1 is x with its sign bit flipped when s < 0 (bit 7 of the sign
   // byte). For a NaN x the product would be the canonical NaN instead, but every value
   // then passes through an add of the first butterfly, which makes any NaN canonical.
+  // Inputs are not checked for finiteness here: every output of the transform is a
+  // signed sum of all 512 inputs, so a NaN or infinite input leaves every output NaN or
+  // infinite, and the check after the transform reports it.
 #pragma unroll
   for (int e = 0; e < 16; ++e) {
-    bad |= !finite32(v[e]);
     const uint32_t flip = (sw[e >> 2] << (24 - 8 * (e & 3))) & 0x80000000u;
     v[e] = __uint_as_float(__float_as_uint(v[e]) ^ flip);
   }
@@ -179,12 +184,9 @@ __device__ __forceinline__ void restore_block512(const int64_t* wsr, float rq, c
   }
 #pragma unroll
   for (int mask = 1; mask < 32; mask <<= 1) {  // strides 2..32
-    const bool upper_half = (lane & mask) != 0;
+    const float s = (lane & mask) ? -1.0f : 1.0f;
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const float other = __shfl_xor_sync(0xffffffffu, v[e], mask);
-      v[e] = upper_half ? __fsub_rn(other, v[e]) : __fadd_rn(v[e], other);
-    }
+    for (int e = 0; e < 16; ++e) v[e] = cross_butterfly(v[e], __shfl_xor_sync(0xffffffffu, v[e], mask), s);
   }
 #pragma unroll
   for (int kb = 1; kb < 8; kb <<= 1) {  // strides 64, 128, 256
