@@ -185,19 +185,16 @@ __device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, ui
 // memory or global, same column permutation as the B fragments).
 template <int BITS, bool M1>
 __device__ __forceinline__ void sequence_mma(const uint32_t (&w)[BITS], int lane, const uint8_t* __restrict__ lut,
-                                             uint32_t copy_off, const uint4* a0p, const uint4* a1p, int (&c)[4]) {
+                                             uint32_t copy_off, const uint4* a0p, const uint4* a1p, bool row0,
+                                             bool row1, int (&c)[4]) {
   uint32_t carry = __shfl_up_sync(0xffffffffu, w[BITS - 1], 1);
   if ((lane & 3) == 0) carry = 0u;  // zeros before the start of the sequence (docs/FORMAT.md:121-128)
 #pragma unroll
   for (int tp = 0; tp < 4; ++tp) {
     // Activations of two 32-column chunks, loaded before the 16 lookups that hide their latency.
     uint4 x0 = make_uint4(0, 0, 0, 0), x1 = make_uint4(0, 0, 0, 0);
-    if (M1) {
-      if (lane < 4) x0 = a0p[tp];
-    } else {
-      x0 = a0p[tp];
-      x1 = a1p[tp];
-    }
+    if (row0) x0 = a0p[tp];
+    if (!M1 && row1) x1 = a1p[tp];
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const int t = 2 * tp + half;
@@ -486,6 +483,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   const int q = lane & 3, n = lane >> 2;
   const int tok0 = n < p.mv ? n : p.mv - 1;
   const int tok1 = n + 8 < p.mv ? n + 8 : p.mv - 1;
+  const bool row0 = n < p.mv, row1 = n + 8 < p.mv;
   const int8_t* act0 = ACT_SMEM ? s_act + tok0 * act_ld : p.act + (size_t)tok0 * Kc;
   const int8_t* act1 = ACT_SMEM ? s_act + tok1 * act_ld : p.act + (size_t)tok1 * Kc;
   const int32_t* sc0 = ACT_SMEM ? s_scale + tok0 * G : p.scales + (size_t)tok0 * G;
@@ -573,8 +571,8 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
     const uint4* a1p = reinterpret_cast<const uint4*>(act1 + col);
     // A half unit at either end of the range holds one tile (the integer dot of a half
     // group, scaled by the group's scale, adds up exactly with the other half's).
-    if (2 * u >= t_begin) sequence_mma<BITS, M1>(cur.w[0], lane, s_lut, copy_off, a0p, a1p, c);
-    if (2 * u + 1 < t_end) sequence_mma<BITS, M1>(cur.w[1], lane, s_lut, copy_off, a0p + 16, a1p + 16, c);
+    if (2 * u >= t_begin) sequence_mma<BITS, M1>(cur.w[0], lane, s_lut, copy_off, a0p, a1p, row0, row1, c);
+    if (2 * u + 1 < t_end) sequence_mma<BITS, M1>(cur.w[1], lane, s_lut, copy_off, a0p + 16, a1p + 16, row0, row1, c);
     const long long s0 = sc0[g], s1 = sc1[g];
     const long long t[4] = {s0 * c[0], s0 * c[1], s1 * c[2], s1 * c[3]};
     if (p.checked) {
