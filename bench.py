@@ -48,7 +48,7 @@ CALLS = [["q_proj", "k_proj", "v_proj"], ["o_proj"], ["in_proj_qkv", "in_proj_z"
          ["gate_proj", "up_proj"], ["down_proj"]]
 # DRAM bytes (read + write) of the six fused gemv_kernel launches of one step, from one
 # ncu capture of this workload (profiles/gemv_kernel_layer_bits8.md); None where not captured.
-GEMV_TRAFFIC = {(8, 1): 248_069_888}
+GEMV_TRAFFIC = {(8, 1): 247_838_976}
 METRIC = "compressed GEMV HBM TB/s (one hybrid layer's linear set, batch-1 decode)"
 UNIT = "TB/s"
 
