@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--bits 8|6]
 
-Workload: one hybrid layer's full linear set at batch-1
+Workload (the reference's headline configuration): one hybrid layer's full linear set at batch-1
 decode, hidden 5120 -- attention q/k/v/o, Gated-DeltaNet in_proj_qkv/in_proj_z/
 out_proj, MLP gate/up/down -- on synthetic 27B-shape compressed weights (random
 code words, seeded N(0,1) value table, row scales ~0.02; bits=8 is the format's
