@@ -494,8 +494,9 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   bool overflow = false;
   bool bad = false;       // FUSED: non-finite restored values
   unsigned pend = 0;      // FUSED, rotated rows: tiles added to the current 512-row block, not yet counted
-  // Row-parallel: 512-row blocks this warp completed on this rank and sent to the
-  // peers (bit i: block blk_lo + i); it restores them after its last unit.
+  // 512-row blocks this warp completed (bit i: block blk_lo + i) and restores after its
+  // last unit: row-parallel, the blocks whose sums it sent to the peers; several tokens,
+  // every block it completed (one token: restored at once, inside the loop).
   const int blk_lo = (t_begin / T2) >> 6;
   unsigned done_mask = 0;
 
@@ -518,14 +519,34 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   };
   // Rotated rows (fused): restore + H512 of a complete 512-row block of sums, then clear
   // the sums and the block's counter for the next launch.
+  // Several tokens: restored after the streaming loop (see done_mask), tokens in turn,
+  // each token's sums requested before the previous token is transformed.
   auto restore_block = [&](int blk) {
-    for (int tok = 0; tok < p.mv; ++tok) {
-      int64_t* wsr = S.out + (size_t)tok * S.out_ld;
-      restore_block512(wsr, s_rq[tok], p.inv_rms ? p.inv_rms + tok : nullptr, S.tau, S.s_out, blk * 512, S.y_rows,
-                       S.y + (size_t)tok * S.y_rows, lane, bad);
+    if constexpr (M1) {
+      for (int tok = 0; tok < p.mv; ++tok) {
+        int64_t* wsr = S.out + (size_t)tok * S.out_ld;
+        restore_block512(wsr, s_rq[tok], p.inv_rms ? p.inv_rms + tok : nullptr, S.tau, S.s_out, blk * 512, S.y_rows,
+                         S.y + (size_t)tok * S.y_rows, lane, bad);
 #pragma unroll
-      for (int k = 0; k < 8; ++k)  // the rows this lane read (restore_block512's lane mapping)
-        __stcg(reinterpret_cast<longlong2*>(wsr + blk * 512 + 64 * k + 2 * lane), make_longlong2(0, 0));
+        for (int k = 0; k < 8; ++k)  // the rows this lane read (restore_block512's lane mapping)
+          __stcg(reinterpret_cast<longlong2*>(wsr + blk * 512 + 64 * k + 2 * lane), make_longlong2(0, 0));
+      }
+    } else {
+      Rows512 rr;
+      longlong2 w[8], wn[8];
+      load_sums512(S.out, blk * 512, lane, w);
+      load_rows512(S.tau, S.s_out, blk * 512, lane, rr);
+      for (int tok = 0; tok < p.mv; ++tok) {
+        int64_t* wsr = S.out + (size_t)tok * S.out_ld;
+        if (tok + 1 < p.mv) load_sums512(wsr + S.out_ld, blk * 512, lane, wn);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)  // the rows this lane read, cleared after their reads
+          __stcg(reinterpret_cast<longlong2*>(wsr + blk * 512 + 64 * k + 2 * lane), make_longlong2(0, 0));
+        restore_loaded512(w, rr, s_rq[tok], p.inv_rms ? p.inv_rms + tok : nullptr, blk * 512, S.y_rows,
+                          S.y + (size_t)tok * S.y_rows, lane, bad);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) w[k] = wn[k];
+      }
     }
     if (lane == 0) S.blk_counters[blk] = 0u;
   };
@@ -618,7 +639,10 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
               send_block(blk);
               done_mask |= 1u << (blk - blk_lo);
             } else {
-              restore_block(blk);
+              if constexpr (M1)
+                restore_block(blk);
+              else
+                done_mask |= 1u << (blk - blk_lo);
             }
           }
           pend = 0;
@@ -689,6 +713,15 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
       }
       if (__any_sync(0xffffffffu, !ok) && lane == 0) raise_device_error(p.err, DERR_TIMEOUT);
       restore_block(blk);
+    }
+  }
+  if constexpr (FUSED && !M1) {
+    if (!tp) {
+      while (done_mask) {
+        const int blk = blk_lo + __ffs(done_mask) - 1;
+        done_mask &= done_mask - 1;
+        restore_block(blk);
+      }
     }
   }
   if (p.checked && __any_sync(0xffffffffu, overflow) && lane == 0) raise_device_error(p.err, DERR_OVERFLOW);
@@ -893,6 +926,10 @@ int launch_linear_fused(const MatrixDev* mats, int n_mats, const float* x, int M
     s.s_out = mats[i].s_out;
     s.y = y[i];
     s.y_rows = mats[i].rows;
+    // With several tokens a warp restores the rotated blocks it completed after its last
+    // unit (a 32-bit mask of them).
+    if (M > 1 && mats[i].s_out && (s.base + 1) / (64 * 2 * (int64_t)p.G) + 2 > 32)
+      return fail(YSKN_EINVAL, "fused linear: too many rows per warp");
   }
   return launch_bits_any(mats[0].bits, p, grid, true, st);
 }

@@ -160,6 +160,77 @@ __device__ __forceinline__ float restore_value(long long ws, float rq, const flo
 // ascending stride order: stride 1 in the lane (b), 2..32 across lanes (lane bits),
 // 64..256 in the lane (k). ws is read through L2 (other SMs may have written it in
 // the same launch).
+// The same in separate load and transform steps, for a caller restoring several tokens
+// of a block: it requests the next token's sums before transforming this token's.
+struct Rows512 {  // the block's row scales and output signs, the same for every token
+  float2 tau[8];
+  char2 sg[8];
+};
+__device__ __forceinline__ void load_rows512(const float* __restrict__ tau, const int8_t* __restrict__ s_out, int r0,
+                                             int lane, Rows512& rr) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int r = r0 + 64 * k + 2 * lane;
+    rr.tau[k] = __ldg(reinterpret_cast<const float2*>(tau + r));
+    rr.sg[k] = __ldg(reinterpret_cast<const char2*>(s_out + r));
+  }
+}
+__device__ __forceinline__ void load_sums512(const int64_t* wsr, int r0, int lane, longlong2 (&w)[8]) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) w[k] = __ldcg(reinterpret_cast<const longlong2*>(wsr + r0 + 64 * k + 2 * lane));
+}
+__device__ __forceinline__ void restore_loaded512(const longlong2 (&w)[8], const Rows512& rr, float rq,
+                                                  const float* inv_rms_m, int r0, int n_rows, float* __restrict__ yr,
+                                                  int lane, bool& bad) {
+  float v[16];
+  if (inv_rms_m) bad |= !finite32(*inv_rms_m);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    v[2 * k] = restore_value(w[k].x, rq, inv_rms_m, rr.tau[k].x);
+    v[2 * k + 1] = restore_value(w[k].y, rq, inv_rms_m, rr.tau[k].y);
+    bad |= !finite32(v[2 * k]) | !finite32(v[2 * k + 1]);
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {  // stride 1
+    const float lower = v[2 * k], upper = v[2 * k + 1];
+    v[2 * k] = __fadd_rn(lower, upper);
+    v[2 * k + 1] = __fsub_rn(lower, upper);
+  }
+#pragma unroll
+  for (int mask = 1; mask < 32; mask <<= 1) {  // strides 2..32
+    const float s = (lane & mask) ? -1.0f : 1.0f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) v[e] = cross_butterfly(v[e], __shfl_xor_sync(0xffffffffu, v[e], mask), s);
+  }
+#pragma unroll
+  for (int kb = 1; kb < 8; kb <<= 1) {  // strides 64, 128, 256
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (k & kb) continue;
+#pragma unroll
+      for (int b = 0; b < 2; ++b) {
+        const float lower = v[2 * k + b], upper = v[2 * (k + kb) + b];
+        v[2 * k + b] = __fadd_rn(lower, upper);
+        v[2 * (k + kb) + b] = __fsub_rn(lower, upper);
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int r = r0 + 64 * k + 2 * lane;
+    const float t0 = __fmul_rn(__fmul_rn(v[2 * k], kHadamardNorm), (float)rr.sg[k].x);
+    const float t1 = __fmul_rn(__fmul_rn(v[2 * k + 1], kHadamardNorm), (float)rr.sg[k].y);
+    bad |= !finite32(t0) | !finite32(t1);
+    float* dst = yr + r;
+    if (r + 1 < n_rows && (reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
+      *reinterpret_cast<float2*>(dst) = make_float2(t0, t1);
+    } else {
+      if (r < n_rows) dst[0] = t0;
+      if (r + 1 < n_rows) dst[1] = t1;
+    }
+  }
+}
+
 __device__ __forceinline__ void restore_block512(const int64_t* wsr, float rq, const float* inv_rms_m,
                                                  const float* __restrict__ tau, const int8_t* __restrict__ s_out,
                                                  int r0, int n_rows, float* __restrict__ yr, int lane, bool& bad) {
