@@ -115,6 +115,52 @@ YSKN_B200_API const float* yskn_b200_matrix_tau(const yskn_b200_matrix* m);
 YSKN_B200_API const int8_t* yskn_b200_matrix_signs_in(const yskn_b200_matrix* m);
 YSKN_B200_API const int8_t* yskn_b200_matrix_signs_out(const yskn_b200_matrix* m);
 
+/* ---- .yskn containers (docs/FORMAT.md:33-107) ------------------------------------
+ * yskn_b200_file_open replaces the reference's readers, src/format.hpp:26-61
+ * (Container::open) and crates/yskn-format/src/lib.rs:97-172 (Container::new) with
+ * crates/yskn-format/src/tensor.rs:31-63,83-196,212-236 (descriptors): the file is
+ * memory-mapped read-only and checked as the reference reader checks it (magic,
+ * version, declared lengths, JSON header, every descriptor and data region, unique
+ * names, zero padding). NULL on failure, with the reason in yskn_b200_last_error().
+ * Opening uses no GPU. The handle and the strings it returns stay valid until
+ * yskn_b200_file_close. */
+typedef struct yskn_b200_file yskn_b200_file;
+#define YSKN_ROLE_BODY 0
+#define YSKN_ROLE_HEAD 1
+#define YSKN_ROLE_EMBEDDING 2
+#define YSKN_ROLE_DRAFT 3
+#define YSKN_VECTOR_F16 0
+#define YSKN_VECTOR_BF16 1
+#define YSKN_TENSOR_INFO_FIELDS 17
+YSKN_B200_API yskn_b200_file* yskn_b200_file_open(const char* path);
+YSKN_B200_API void yskn_b200_file_close(yskn_b200_file* f);
+/* The `model` member of the header, as its JSON text. */
+YSKN_B200_API const char* yskn_b200_file_model_json(const yskn_b200_file* f);
+YSKN_B200_API int yskn_b200_file_tensor_count(const yskn_b200_file* f);
+YSKN_B200_API int yskn_b200_file_vector_count(const yskn_b200_file* f);
+/* Index of the tensor or vector named `name` (*is_vector says which), or YSKN_EINVAL. */
+YSKN_B200_API int yskn_b200_file_find(const yskn_b200_file* f, const char* name, int* is_vector);
+YSKN_B200_API const char* yskn_b200_file_tensor_name(const yskn_b200_file* f, int i);
+/* Tensor i's descriptor with the format's defaults applied (tensor.rs:83-196), in this
+ * order: role (YSKN_ROLE_*), rows, cols, physical_rows, bits, layout (YSKN_LAYOUT_*),
+ * stream_off, stream_bytes, lut_off, scale_off, input sign rule (YSKN_SIGNS_*), seed,
+ * offset, has output rotation (0/1), output sign rule (-1 if none), seed, offset. */
+YSKN_B200_API int yskn_b200_file_tensor_info(const yskn_b200_file* f, int i, int64_t* out17);
+YSKN_B200_API const char* yskn_b200_file_vector_name(const yskn_b200_file* f, int i);
+/* Vector i: offset, count, dtype (YSKN_VECTOR_*). */
+YSKN_B200_API int yskn_b200_file_vector_info(const yskn_b200_file* f, int i, int64_t* out3);
+/* Vector i's n values as f32 (f16 converted exactly; bf16 as the upper half of a float),
+ * as crates/yskn-format/src/lib.rs reads them. */
+YSKN_B200_API int yskn_b200_file_vector_read(const yskn_b200_file* f, int i, float* h_out, int64_t n);
+/* Matrix handle of tensor i (replaces src/loader.cpp:19-60 Model::upload_linear): the
+ * code stream goes to the device through a pinned staging buffer, the sign streams are
+ * built from the tensor's rotations, then as yskn_b200_matrix_create[_shard] (the shard
+ * bounds as there). Roles body, head and draft; an embedding is rejected (the reference
+ * decodes it row by row with its 16-bit table). Synchronous; NULL on failure. */
+YSKN_B200_API yskn_b200_matrix* yskn_b200_file_load_matrix(const yskn_b200_file* f, int i);
+YSKN_B200_API yskn_b200_matrix* yskn_b200_file_load_matrix_shard(const yskn_b200_file* f, int i, int row_begin,
+                                                                 int row_end, int col_begin, int col_end);
+
 /* Exact weighted integer sums (the operator core). Replaces
  * crates/yskn-engine/src/model.rs:948-962 `Compute::weighted_sums` (bit-identical to
  * crates/yskn-ref/src/compressed_linear.rs:205-252) and the reference's launch_lnord /

@@ -51,6 +51,19 @@ _SIGNATURES = {
     "yskn_b200_kv4_attention_work_bytes": (_i64, [_i, _i, _i, _i]),
     "yskn_b200_kv4_attention": (_i, [_vp] * 9 + [_i] * 7 + [_vp] * 4),
     "yskn_b200_kv_encode": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp]),
+    "yskn_b200_file_open": (_vp, [C.c_char_p]),
+    "yskn_b200_file_close": (None, [_vp]),
+    "yskn_b200_file_model_json": (C.c_char_p, [_vp]),
+    "yskn_b200_file_tensor_count": (_i, [_vp]),
+    "yskn_b200_file_vector_count": (_i, [_vp]),
+    "yskn_b200_file_find": (_i, [_vp, C.c_char_p, _vp]),
+    "yskn_b200_file_tensor_name": (C.c_char_p, [_vp, _i]),
+    "yskn_b200_file_tensor_info": (_i, [_vp, _i, _vp]),
+    "yskn_b200_file_vector_name": (C.c_char_p, [_vp, _i]),
+    "yskn_b200_file_vector_info": (_i, [_vp, _i, _vp]),
+    "yskn_b200_file_vector_read": (_i, [_vp, _i, _vp, _i64]),
+    "yskn_b200_file_load_matrix": (_vp, [_vp, _i]),
+    "yskn_b200_file_load_matrix_shard": (_vp, [_vp, _i, _i, _i, _i, _i]),
 }
 
 _lib = None
@@ -138,6 +151,18 @@ class Matrix:
         self.cols, self.bits = c1 - c0, bits
         self.has_rotation = so is not None
 
+    @classmethod
+    def _from_handle(cls, h, rows, physical_rows, cols, bits, has_rotation, shard):
+        """A Matrix around a handle the library created (e.g. File.load_matrix)."""
+        m = cls.__new__(cls)
+        m.handle = C.c_void_p(h)
+        r0, r1, c0, c1 = shard
+        m.shard = tuple(shard)
+        m.rows, m.physical_rows = min(rows, r1) - r0, r1 - r0
+        m.cols, m.bits = c1 - c0, bits
+        m.has_rotation = has_rotation
+        return m
+
     def info(self):
         out = (C.c_int64 * 6)()
         check(lib().yskn_b200_matrix_info(self.handle, out), "matrix_info")
@@ -157,6 +182,74 @@ class Matrix:
     @property
     def signs_in_ptr(self):
         return lib().yskn_b200_matrix_signs_in(self.handle)
+
+
+ROLES = ("body", "head", "embedding", "draft")
+_RULE_NAMES = ("splitmix64", "mulberry32_7919_13")  # YSKN_SIGNS_* order
+
+
+class File:
+    """A `.yskn` container opened and checked by the library (yskn_b200_file_open):
+    `model` (the header's model object), `tensors` and `vectors` (name -> descriptor with
+    the format's defaults applied), `vector(name)` (f32 values) and `load_matrix(name)`
+    (a Matrix whose codes, table, scales and signs come from the file)."""
+
+    def __init__(self, path):
+        import json
+        h = lib().yskn_b200_file_open(os.fsencode(path))
+        if not h:
+            raise YsknError(EINVAL, last_error())
+        self.handle = C.c_void_p(h)
+        self.path = path
+        self.model = json.loads(lib().yskn_b200_file_model_json(self.handle).decode("utf-8"))
+        self.tensors, self.vectors = {}, {}
+        info = (C.c_int64 * 17)()
+        for i in range(lib().yskn_b200_file_tensor_count(self.handle)):
+            check(lib().yskn_b200_file_tensor_info(self.handle, i, info), "file_tensor_info")
+            v = list(info)
+            rot = lambda r, seed, off: dict(rule=_RULE_NAMES[r], seed=seed, offset=off)
+            name = lib().yskn_b200_file_tensor_name(self.handle, i).decode("utf-8")
+            self.tensors[name] = dict(
+                index=i, name=name, role=ROLES[v[0]], rows=v[1], cols=v[2], physical_rows=v[3], bits=v[4],
+                layout="warp" if v[5] == LAYOUTS["warp"] else "row", stream_off=v[6], stream_bytes=v[7],
+                lut_off=v[8], scale_off=v[9], rot_in=rot(v[10], v[11], v[12]),
+                rot_out=rot(v[14], v[15], v[16]) if v[13] else None)
+        vinfo = (C.c_int64 * 3)()
+        for i in range(lib().yskn_b200_file_vector_count(self.handle)):
+            check(lib().yskn_b200_file_vector_info(self.handle, i, vinfo), "file_vector_info")
+            name = lib().yskn_b200_file_vector_name(self.handle, i).decode("utf-8")
+            self.vectors[name] = dict(index=i, name=name, off=vinfo[0], n=vinfo[1],
+                                      dtype="bf16" if vinfo[2] == 1 else "f16")
+
+    def vector(self, name):
+        import numpy as np
+        v = self.vectors[name]
+        out = np.empty(v["n"], np.float32)
+        check(lib().yskn_b200_file_vector_read(self.handle, v["index"], out.ctypes.data, v["n"]), "file_vector_read")
+        return out
+
+    def load_matrix(self, name, shard=None):
+        t = self.tensors[name]
+        if shard is None:
+            h = lib().yskn_b200_file_load_matrix(self.handle, t["index"])
+            shard = (0, t["physical_rows"], 0, t["cols"])
+        else:
+            h = lib().yskn_b200_file_load_matrix_shard(self.handle, t["index"], *shard)
+        if not h:
+            raise YsknError(EINVAL, "file_load_matrix: " + last_error())
+        return Matrix._from_handle(h, t["rows"], t["physical_rows"], t["cols"], t["bits"], t["rot_out"] is not None,
+                                   shard)
+
+    def close(self):
+        if self.handle:
+            lib().yskn_b200_file_close(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def _handles(mats):
