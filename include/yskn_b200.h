@@ -161,6 +161,32 @@ YSKN_B200_API yskn_b200_matrix* yskn_b200_file_load_matrix(const yskn_b200_file*
 YSKN_B200_API yskn_b200_matrix* yskn_b200_file_load_matrix_shard(const yskn_b200_file* f, int i, int row_begin,
                                                                  int row_end, int col_begin, int col_end);
 
+/* ---- Coded embedding rows (docs/spec/02_COMPRESSED_LINEAR.md:271-303) -------------
+ * Replaces the reference's coded-embedding path, Engine35 set-up + q35_embed
+ * (src/engine35.cpp:272-299, src/q35_kernels.cu:1501-1574): per token, each table's row
+ * is decoded with its own binary16 table and row scale, the tables are added in order,
+ * then per 512 columns H512, * 1/sqrt(512), * the main table's input signs, one rounding
+ * to bf16. */
+typedef struct yskn_b200_embedding yskn_b200_embedding;
+/* n_parts 1..3 tables (main, then residuals) of rows x cols (cols % 512 == 0), each with
+ *   d_codes[k] its code stream in row layout (docs/FORMAT.md:141-144), device memory;
+ *   bits[k], lut16_host[k] (8192 binary16), scale16_host[k] (rows binary16);
+ * signs_in_host: the main table's cols input signs. Copies everything (synchronous). */
+YSKN_B200_API yskn_b200_embedding* yskn_b200_embedding_create(int n_parts, const uint32_t* const* d_codes,
+                                                             const int* bits, int rows, int cols,
+                                                             const uint16_t* const* lut16_host,
+                                                             const uint16_t* const* scale16_host,
+                                                             const int8_t* signs_in_host);
+YSKN_B200_API void yskn_b200_embedding_destroy(yskn_b200_embedding* e);
+/* d_out: bf16 bits [M][cols] (16-byte aligned) for the int32 token ids d_tokens [M].
+ * A token outside 0..rows-1 gives a zero row and, from yskn_b200_status, YSKN_EINVAL. */
+YSKN_B200_API int yskn_b200_embedding_lookup(const yskn_b200_embedding* e, const int32_t* d_tokens, int M,
+                                             uint16_t* d_out, void* stream);
+/* From a file: tensors main_i and (or -1) res_i, res2_i, checked as the reference engine
+ * checks a coded embedding (src/engine35.cpp:272-299). */
+YSKN_B200_API yskn_b200_embedding* yskn_b200_file_load_embedding(const yskn_b200_file* f, int main_i, int res_i,
+                                                                 int res2_i);
+
 /* Exact weighted integer sums (the operator core). Replaces
  * crates/yskn-engine/src/model.rs:948-962 `Compute::weighted_sums` (bit-identical to
  * crates/yskn-ref/src/compressed_linear.rs:205-252) and the reference's launch_lnord /

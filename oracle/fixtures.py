@@ -65,6 +65,30 @@ def tiny_container():
     return write_container(model, tensors, vectors, blobs, 4096, 64)
 
 
+def embedding_container(rows, cols, parts):
+    """A container of coded embedding tables (role embedding, row layout, no output
+    rotation): parts = [(name, bits, seed, rot_in)], rot_in = (rule, sign_seed, offset).
+    Codes are seeded random words (every bit string is a valid code, docs/FORMAT.md:
+    137-138), tables uniform in [-3, 3] and row scales in [0.01, 0.03], as binary16."""
+    blobs, tensors = [], []
+
+    def blob(b):
+        blobs.append(b)
+        return {"$blob": len(blobs) - 1}
+
+    for name, bits, seed, (rule, sign_seed, offset) in parts:
+        n_words = rows * (cols // 256) * 4 * bits
+        words = (stream64(seed, n_words) & np.uint64(0xFFFFFFFF)).astype("<u4")
+        lut = uniform(seed + 1, 8192, -3.0, 3.0).astype("<f2")
+        scale = uniform(seed + 2, rows, 0.01, 0.03).astype("<f2")
+        tensors.append(dict(name=name, role="embedding", rows=rows, cols=cols, bits=bits, layout="row",
+                            rot_in=dict(kind="H512", m=cols // 512, sign_seed=sign_seed, sign_offset=offset,
+                                        rule=rule),
+                            rot_out=None, stream_off=blob(words.tobytes()), stream_bytes=4 * n_words,
+                            lut_off=blob(lut.tobytes()), scale_off=blob(scale.tobytes())))
+    return write_container(dict(arch="test"), tensors, [], blobs, 4096, 256)
+
+
 TINY_SHA256 = "3f4a48866f6a1751beabc3b9a8d06088672a3db0aa0a4c3f96e1877cb448d393"
 
 

@@ -103,6 +103,36 @@ def hadamard512(v):
     return v
 
 
+def embedding_rows(parts, tokens, signs_in):
+    """docs/spec/02_COMPRESSED_LINEAR.md:271-303 (src/q35_kernels.cu:1501-1574): the
+    bf16 bits [len(tokens), cols] of coded embedding rows. parts: the main table and up
+    to two residual tables, each (words, layout, physical_rows, cols, bits, lut16,
+    scale16); every part is decoded with its own table and row scale, the parts are
+    added in order, then per 512 columns H512 (ascending strides), * 1/sqrt(512) and the
+    main table's input signs, one rounding to bf16. Every float32 operation rounds once
+    (numpy float32 arithmetic, no fused multiply-add)."""
+    signs = np.asarray(signs_in, np.int8).astype(np.float32)
+    cols = signs.size
+    decoded = []
+    for words, layout, phys, pcols, bits, lut16, scale16 in parts:
+        assert pcols == cols
+        st = states(words, layout, phys, cols, bits).reshape(phys, cols // 2)
+        table = np.asarray(lut16, np.uint16).view("<f2").astype(np.float32).reshape(4096, 2)
+        scale = np.asarray(scale16, np.uint16).view("<f2").astype(np.float32)
+        decoded.append((st, table, scale))
+    out = np.empty((len(tokens), cols), np.uint16)
+    for m, t in enumerate(tokens):
+        v = None
+        for st, table, scale in decoded:
+            part = table[st[t]].reshape(cols) * scale[t]
+            v = part if v is None else v + part
+        for b in range(0, cols, 512):
+            h = hadamard512(v[b:b + 512])
+            y = (h * np.float32(0.044194173824159216)) * signs[b:b + 512]
+            out[m, b:b + 512] = [f32_to_bf16(x) for x in y]
+    return out
+
+
 def quantize_activation(x, signs_in):
     """compressed_linear.rs:57-135 for each row of x [M, Kc] -> (act8, alpha, A, row_quantum)."""
     x = np.ascontiguousarray(np.atleast_2d(x), np.float32)

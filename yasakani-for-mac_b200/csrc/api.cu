@@ -134,6 +134,8 @@ static float f16_to_f32(uint16_t bits) {  // crates/yskn-format/src/floats.rs:4-
   return f;
 }
 
+float half_bits_to_float(uint16_t bits) { return f16_to_f32(bits); }
+
 static void sign_stream(int rule, uint64_t seed, uint64_t offset, int64_t n, int8_t* out) {
   for (int64_t i = 0; i < n; ++i) {
     const uint64_t position = offset + (uint64_t)i + 1u;
@@ -201,6 +203,7 @@ YSKN_B200_API int yskn_b200_status(void* stream) {
   if (bits & DERR_TIMEOUT) return fail(YSKN_ETIMEDOUT, "a bounded device wait timed out");
   if (bits & DERR_OVERFLOW) return fail(YSKN_EOVERFLOW, "compressed integer accumulation exceeds i64");
   if (bits & DERR_NONFINITE) return fail(YSKN_ENONFINITE, "non-finite activation or restored value");
+  if (bits & DERR_RANGE) return fail(YSKN_EINVAL, "a token id lies outside the embedding's rows");
   return YSKN_OK;
 }
 

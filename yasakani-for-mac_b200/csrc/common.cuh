@@ -19,6 +19,7 @@ enum : unsigned {
   DERR_NONFINITE = 1u,
   DERR_OVERFLOW = 2u,
   DERR_TIMEOUT = 4u,
+  DERR_RANGE = 8u,  // an index read on the device (a token id) lies outside its table
 };
 // Address of this device's error word (a __device__ variable in api.cu).
 unsigned* device_error_word();
@@ -28,6 +29,8 @@ __device__ __forceinline__ void raise_device_error(unsigned* word, unsigned bits
 // Thread-local error message (src/c_api.cpp:11-14 keeps one per thread as well).
 int fail(int code, const std::string& msg);
 int cuda_fail(cudaError_t e, const char* where);
+// IEEE binary16 bits -> binary32, exact (crates/yskn-format/src/floats.rs:4-19).
+float half_bits_to_float(uint16_t bits);
 
 // 1/sqrt(512) as the binary32 literal 0.044194173824159216f (bits 0x3d3504f3).
 constexpr float kHadamardNorm = 0.044194173824159216f;

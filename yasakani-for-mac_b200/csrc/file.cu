@@ -475,27 +475,6 @@ struct Check {
   }
 };
 
-float f16_bits_to_f32(uint16_t h) {  // IEEE 754 binary16 -> binary32 (exact)
-  const uint32_t sign = (uint32_t)(h >> 15) << 31;
-  const uint32_t exp = (h >> 10) & 0x1f, man = h & 0x3ff;
-  uint32_t bits;
-  if (exp == 0x1f) {
-    bits = sign | 0x7f800000u | (man << 13);
-  } else if (exp) {
-    bits = sign | ((exp + 112) << 23) | (man << 13);
-  } else if (man == 0) {
-    bits = sign;
-  } else {  // subnormal: man * 2^-24, normalised
-    int e = 113;
-    uint32_t m = man;
-    while (!(m & 0x400)) m <<= 1, --e;
-    bits = sign | ((uint32_t)e << 23) | ((m & 0x3ff) << 13);
-  }
-  float f;
-  std::memcpy(&f, &bits, 4);
-  return f;
-}
-
 }  // namespace
 }  // namespace yskn
 
@@ -684,7 +663,7 @@ extern "C" YSKN_B200_API int yskn_b200_file_vector_read(const yskn_b200_file* f,
       const uint32_t bits = (uint32_t)h << 16;
       std::memcpy(h_out + k, &bits, 4);
     } else {
-      h_out[k] = f16_bits_to_f32(h);
+      h_out[k] = half_bits_to_float(h);
     }
   }
   return YSKN_OK;
@@ -783,4 +762,61 @@ extern "C" YSKN_B200_API yskn_b200_matrix* yskn_b200_file_load_matrix_shard(cons
                                                                            int row_begin, int row_end,
                                                                            int col_begin, int col_end) {
   return load_matrix(f, i, true, row_begin, row_end, col_begin, col_end);
+}
+
+// Coded embedding: the main table and up to two residual tables, checked as the
+// reference engine checks them before use (src/engine35.cpp:272-299): role embedding, row
+// layout, no padding rows, no output rotation, the residuals of the main table's shape
+// and input-rotation offset (their own seed and rule are not compared, and the main
+// table's signs are used, as there: docs/spec/02_COMPRESSED_LINEAR.md:305-312), and a
+// second residual only with a first.
+extern "C" YSKN_B200_API yskn_b200_embedding* yskn_b200_file_load_embedding(const yskn_b200_file* f, int main_i,
+                                                                         int res_i, int res2_i) {
+  auto bad = [](const std::string& m) -> yskn_b200_embedding* {
+    fail(YSKN_EINVAL, "file_load_embedding: " + m);
+    return nullptr;
+  };
+  const int n_tensors = f ? (int)f->tensors.size() : 0;
+  if (!f || main_i < 0 || main_i >= n_tensors || res_i >= n_tensors || res2_i >= n_tensors)
+    return bad("bad handle or tensor index");
+  if (res2_i >= 0 && res_i < 0) return bad("a second residual table needs the first");
+  const int idx[3] = {main_i, res_i, res2_i};
+  const TensorDesc& m = f->tensors[main_i];
+  int n = 0;
+  const TensorDesc* parts[3];
+  for (int k = 0; k < 3; ++k) {
+    if (idx[k] < 0) continue;
+    const TensorDesc& t = f->tensors[idx[k]];
+    if (t.role != YSKN_ROLE_EMBEDDING || t.layout != YSKN_LAYOUT_ROW || t.phys != t.rows || t.has_rot_out)
+      return bad(t.name + ": an embedding table must have role embedding, row layout, no padding rows and no "
+                          "output rotation");
+    if (t.rows != m.rows || t.cols != m.cols || t.rot_in.offset != m.rot_in.offset)
+      return bad(t.name + ": a residual table must have the main table's shape and input-rotation offset");
+    if (t.rows > (uint64_t)INT_MAX || t.cols > (uint64_t)INT_MAX) return bad(t.name + ": too large");
+    parts[n++] = &t;
+  }
+  std::vector<std::vector<uint16_t>> lut(n, std::vector<uint16_t>(8192)), scale(n);
+  std::vector<int8_t> s_in((size_t)m.cols);
+  if (yskn_b200_signs(m.rot_in.rule, m.rot_in.seed, m.rot_in.offset, (int64_t)m.cols, s_in.data())) return nullptr;
+  uint32_t* d_codes[3] = {nullptr, nullptr, nullptr};
+  const uint16_t* luts[3];
+  const uint16_t* scales[3];
+  int bits[3];
+  for (int k = 0; k < n; ++k) {
+    const TensorDesc& t = *parts[k];
+    std::memcpy(lut[k].data(), f->map + t.lut_off, 16384);  // no alignment is promised
+    scale[k].resize((size_t)t.rows);
+    std::memcpy(scale[k].data(), f->map + t.scale_off, 2 * (size_t)t.rows);
+    luts[k] = lut[k].data();
+    scales[k] = scale[k].data();
+    bits[k] = (int)t.bits;
+  }
+  yskn_b200_embedding* e = nullptr;
+  int rc = YSKN_OK;
+  for (int k = 0; k < n && rc == YSKN_OK; ++k) rc = upload_codes(f, *parts[k], &d_codes[k]);
+  if (rc == YSKN_OK)
+    e = yskn_b200_embedding_create(n, d_codes, bits, (int)m.rows, (int)m.cols, luts, scales, s_in.data());
+  for (uint32_t* d : d_codes)
+    if (d) cudaFree(d);  // the handle holds its own copies
+  return e;
 }

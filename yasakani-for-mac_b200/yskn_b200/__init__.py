@@ -64,6 +64,10 @@ _SIGNATURES = {
     "yskn_b200_file_vector_read": (_i, [_vp, _i, _vp, _i64]),
     "yskn_b200_file_load_matrix": (_vp, [_vp, _i]),
     "yskn_b200_file_load_matrix_shard": (_vp, [_vp, _i, _i, _i, _i, _i]),
+    "yskn_b200_embedding_create": (_vp, [_i, _vp, _vp, _i, _i, _vp, _vp, _vp]),
+    "yskn_b200_embedding_destroy": (None, [_vp]),
+    "yskn_b200_embedding_lookup": (_i, [_vp, _vp, _i, _vp, _vp]),
+    "yskn_b200_file_load_embedding": (_vp, [_vp, _i, _i, _i]),
 }
 
 _lib = None
@@ -240,9 +244,60 @@ class File:
         return Matrix._from_handle(h, t["rows"], t["physical_rows"], t["cols"], t["bits"], t["rot_out"] is not None,
                                    shard)
 
+    def load_embedding(self, main, res=None, res2=None):
+        """An Embedding from the coded table `main` and up to two residual tables."""
+        idx = [self.tensors[n]["index"] if n is not None else -1 for n in (main, res, res2)]
+        h = lib().yskn_b200_file_load_embedding(self.handle, *idx)
+        if not h:
+            raise YsknError(EINVAL, "file_load_embedding: " + last_error())
+        t = self.tensors[main]
+        return Embedding._from_handle(h, t["rows"], t["cols"])
+
     def close(self):
         if self.handle:
             lib().yskn_b200_file_close(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Embedding:
+    """Coded embedding rows on the device (yskn_b200_embedding_create / _lookup)."""
+
+    def __init__(self, parts, rows, cols, signs_in):
+        """parts: 1..3 tuples (d_codes, bits, lut16, scale16), the main table first; d_codes
+        a device tensor holding the row-layout code stream; signs_in the main table's."""
+        import numpy as np
+        keep = [(np.ascontiguousarray(l, np.uint16), np.ascontiguousarray(s, np.uint16)) for _, _, l, s in parts]
+        n = len(parts)
+        codes = (C.c_void_p * n)(*[_ptr(c) for c, _, _, _ in parts])
+        bits = (C.c_int * n)(*[b for _, b, _, _ in parts])
+        luts = (C.c_void_p * n)(*[l.ctypes.data for l, _ in keep])
+        scales = (C.c_void_p * n)(*[s.ctypes.data for _, s in keep])
+        si = np.ascontiguousarray(signs_in, np.int8)
+        h = lib().yskn_b200_embedding_create(n, codes, bits, rows, cols, luts, scales, si.ctypes.data)
+        if not h:
+            raise YsknError(EINVAL, "embedding_create: " + last_error())
+        self.handle, self.rows, self.cols = C.c_void_p(h), rows, cols
+
+    @classmethod
+    def _from_handle(cls, h, rows, cols):
+        e = cls.__new__(cls)
+        e.handle, e.rows, e.cols = C.c_void_p(h), rows, cols
+        return e
+
+    def lookup(self, tokens, out, stream=None):
+        """bf16 bits [M][cols] into `out` (a 16-bit device tensor) for int32 `tokens` [M]."""
+        check(lib().yskn_b200_embedding_lookup(self.handle, _ptr(tokens), tokens.shape[0], _ptr(out), _stream(stream)),
+              "embedding_lookup")
+
+    def close(self):
+        if self.handle:
+            lib().yskn_b200_embedding_destroy(self.handle)
             self.handle = None
 
     def __del__(self):
