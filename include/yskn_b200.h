@@ -187,6 +187,21 @@ YSKN_B200_API int yskn_b200_embedding_lookup(const yskn_b200_embedding* e, const
 YSKN_B200_API yskn_b200_embedding* yskn_b200_file_load_embedding(const yskn_b200_file* f, int main_i, int res_i,
                                                                  int res2_i);
 
+/* Residual addition and deferred normalisation between projections (replaces the
+ * residual/normalisation part of q35_res_norm_xsm_kernel, src/q35_kernels.cu:1437-1463,
+ * and q35_xsm_r, :81-85; docs/spec/05_RESIDUAL_NORM_MLP.md:53-141). Per row of M:
+ *   d_hidden     bf16 [M][cols], updated in place: bf16(hidden + bf16(projection));
+ *   d_projection f32 [M][cols] (a restored projection output), or NULL for no addition;
+ *   d_norm_weight bf16 [cols]; eps from the model header;
+ *   d_input      f32 [M][cols] = hidden * (1 + weight): the next operator's x (yskn_b200_linear);
+ *   d_inv_rms    f32 [M] = rsqrtf(sum of squares / cols + eps), in the reference's
+ *                reduction order: the next operator's inv_rms;
+ *   d_gate       bf16 [M][cols] copy of d_input, or NULL.
+ * cols a multiple of 512. */
+YSKN_B200_API int yskn_b200_residual_prepare(uint16_t* d_hidden, const float* d_projection,
+                                             const uint16_t* d_norm_weight, int M, int cols, float eps,
+                                             float* d_input, float* d_inv_rms, uint16_t* d_gate, void* stream);
+
 /* Exact weighted integer sums (the operator core). Replaces
  * crates/yskn-engine/src/model.rs:948-962 `Compute::weighted_sums` (bit-identical to
  * crates/yskn-ref/src/compressed_linear.rs:205-252) and the reference's launch_lnord /

@@ -133,6 +133,57 @@ def embedding_rows(parts, tokens, signs_in):
     return out
 
 
+def bf16_bits(x):
+    """Round-to-nearest-even float32 -> bf16 bits, vectorised (finite values; NaN stays NaN)."""
+    u = np.asarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    r = ((u + np.uint64(0x7FFF) + ((u >> np.uint64(16)) & np.uint64(1))) >> np.uint64(16)).astype(np.uint16)
+    nan = np.isnan(np.asarray(x, np.float32))
+    return np.where(nan, np.uint16(0x7FC0), r)
+
+
+def bf16_float(bits):
+    return (np.asarray(bits, np.uint32) << np.uint32(16)).view(np.float32)
+
+
+def block_sum_squares(values):
+    """docs/spec/05_RESIDUAL_NORM_MLP.md:70-101 (src/q35_kernels.cu:1447-1458): 128 partial
+    sums over four elements 128 apart, an XOR reduction with offsets 16..1 in each group
+    of 32, the four group sums added in order from +0."""
+    v = np.asarray(values, np.float32)
+    partial = np.zeros(128, np.float32)
+    for j in range(4):
+        x = v[128 * j:128 * j + 128]
+        partial = partial + x * x
+    result = np.float32(0.0)
+    for g in range(4):
+        lanes = partial[32 * g:32 * g + 32].copy()
+        for off in (16, 8, 4, 2, 1):
+            lanes = lanes + lanes[np.arange(32) ^ off]
+        result = np.float32(result + lanes[0])
+    return result
+
+
+def residual_prepare(hidden_bits, projection, norm_bits, eps):
+    """docs/spec/05_RESIDUAL_NORM_MLP.md:53-141 (src/q35_kernels.cu:1437-1463) for one row:
+    hidden = bf16(hidden + bf16(projection)) (no addition when projection is None), the
+    exact sum of squares, inverse RMS = 1/sqrt(total/cols + eps) (here correctly rounded
+    from double; the reference calls the CUDA rsqrtf, so a device result may differ by
+    that function's error bound), input = hidden * (1 + norm weight) in float32, and the
+    gate copy bf16(input). Returns (hidden_bits, input_f32, inv_rms, gate_bits)."""
+    h = bf16_float(hidden_bits)
+    if projection is not None:
+        h = bf16_float(bf16_bits(h + bf16_float(bf16_bits(projection))))
+    cols = h.size
+    total = np.float32(0.0)
+    for b in range(0, cols, 512):
+        total = np.float32(total + block_sum_squares(h[b:b + 512]))
+    mean = np.float32(np.float32(total / np.float32(cols)) + np.float32(eps))
+    inv_rms = np.float32(1.0 / np.sqrt(np.float64(mean)))
+    gain = np.float32(1.0) + bf16_float(norm_bits)
+    x = h * gain
+    return bf16_bits(h), x, inv_rms, bf16_bits(x)
+
+
 def quantize_activation(x, signs_in):
     """compressed_linear.rs:57-135 for each row of x [M, Kc] -> (act8, alpha, A, row_quantum)."""
     x = np.ascontiguousarray(np.atleast_2d(x), np.float32)

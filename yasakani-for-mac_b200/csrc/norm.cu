@@ -1,0 +1,92 @@
+// Residual addition and deferred RMS normalisation between two projections: the
+// step that turns one projection's restored output into the next projection's input.
+//
+// Reference: the residual + normalisation part of q35_res_norm_xsm_kernel
+// (src/q35_kernels.cu:1437-1463) and q35_xsm_r (src/q35_kernels.cu:81-85); scalar spec
+// docs/spec/05_RESIDUAL_NORM_MLP.md:53-141. Per token row (cols a multiple of 512):
+//   hidden[i] = bf16(hidden[i] + bf16(projection[i]))         (skipped without a projection)
+//   sum of squares of hidden, in the spec's reduction shape, per 512 columns, blocks in order
+//   inverse_rms = rsqrtf(total / cols + eps)
+//   input[i] = hidden[i] * (1 + norm_weight[i])               (binary32, the next operator's x)
+//   gate[i] = bf16(input[i])                                   (optional copy)
+// The next compressed operator quantises `input` and applies inverse_rms in its restore
+// (yskn_b200_linear's inv_rms), so the normalised vector is never formed, as in the
+// reference.
+//
+// B200 design: one 128-thread CTA per row. Thread t owns partial sum t of every 512-column
+// block (elements t, t+128, t+256, t+384), so the spec's reduction — four products
+// added from +0, an XOR butterfly over each group of 32 partials, the four group sums in
+// order — is a per-thread loop, one warp shuffle butterfly and one ordered add; every
+// element is read and written once.
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+
+namespace yskn {
+
+constexpr int NORM_THREADS = 128;
+
+__device__ __forceinline__ float bf16_to_f32(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+__device__ __forceinline__ uint16_t f32_to_bf16(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }
+
+__global__ void __launch_bounds__(NORM_THREADS) residual_prepare_kernel(uint16_t* hidden, const float* projection,
+                                                                        const uint16_t* norm_weight, int cols,
+                                                                        float eps, float* input, float* inv_rms,
+                                                                        uint16_t* gate) {
+  __shared__ float s_group[NORM_THREADS / 32];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const size_t row = blockIdx.x;
+  uint16_t* h = hidden + row * cols;
+  const float* pr = projection ? projection + row * cols : nullptr;
+  float total = 0.0f;  // meaningful in thread 0
+  for (int b = 0; b < cols; b += 512) {
+    float partial = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = b + t + 128 * j;
+      float x = bf16_to_f32(h[i]);
+      if (pr) {
+        x = bf16_to_f32(f32_to_bf16(__fadd_rn(x, bf16_to_f32(f32_to_bf16(pr[i])))));
+        h[i] = f32_to_bf16(x);  // exact: x already has bf16 precision
+      }
+      partial = __fadd_rn(partial, __fmul_rn(x, x));
+      const float in = __fmul_rn(x, __fadd_rn(1.0f, bf16_to_f32(norm_weight[i])));
+      input[row * cols + i] = in;
+      if (gate) gate[row * cols + i] = f32_to_bf16(in);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) partial = __fadd_rn(partial, __shfl_xor_sync(0xffffffffu, partial, off));
+    if (lane == 0) s_group[warp] = partial;
+    __syncthreads();
+    if (t == 0) {
+      float block = 0.0f;
+#pragma unroll
+      for (int g = 0; g < NORM_THREADS / 32; ++g) block = __fadd_rn(block, s_group[g]);
+      total = __fadd_rn(total, block);
+    }
+    __syncthreads();
+  }
+  if (t == 0) inv_rms[row] = rsqrtf(__fadd_rn(__fdiv_rn(total, (float)cols), eps));
+}
+
+}  // namespace yskn
+
+using namespace yskn;
+
+extern "C" YSKN_B200_API int yskn_b200_residual_prepare(uint16_t* d_hidden, const float* d_projection,
+                                                       const uint16_t* d_norm_weight, int M, int cols, float eps,
+                                                       float* d_input, float* d_inv_rms, uint16_t* d_gate,
+                                                       void* stream) {
+  if (!d_hidden || !d_norm_weight || !d_input || !d_inv_rms || M < 1 || cols <= 0 || cols % 512)
+    return fail(YSKN_EINVAL, "residual_prepare: null argument, M < 1, or cols not a multiple of 512");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  for (int m0 = 0; m0 < M; m0 += 65535) {
+    const int n = M - m0 < 65535 ? M - m0 : 65535;
+    const size_t off = (size_t)m0 * cols;
+    residual_prepare_kernel<<<n, NORM_THREADS, 0, st>>>(d_hidden + off, d_projection ? d_projection + off : nullptr,
+                                                         d_norm_weight, cols, eps, d_input + off, d_inv_rms + m0,
+                                                         d_gate ? d_gate + off : nullptr);
+    if (cudaError_t e = cudaGetLastError()) return cuda_fail(e, "residual_prepare_kernel");
+  }
+  return YSKN_OK;
+}

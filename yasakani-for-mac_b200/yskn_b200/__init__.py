@@ -68,6 +68,7 @@ _SIGNATURES = {
     "yskn_b200_embedding_destroy": (None, [_vp]),
     "yskn_b200_embedding_lookup": (_i, [_vp, _vp, _i, _vp, _vp]),
     "yskn_b200_file_load_embedding": (_vp, [_vp, _i, _i, _i]),
+    "yskn_b200_residual_prepare": (_i, [_vp, _vp, _vp, _i, _i, C.c_float, _vp, _vp, _vp, _vp]),
 }
 
 _lib = None
@@ -305,6 +306,14 @@ class Embedding:
             self.close()
         except Exception:
             pass
+
+
+def residual_prepare(hidden, projection, norm_weight, eps, inp, inv_rms, gate=None, stream=None):
+    """hidden (bf16 bits, [M][cols], updated), projection (f32 or None), norm_weight (bf16
+    bits [cols]) -> inp (f32 [M][cols]), inv_rms (f32 [M]), gate (bf16 bits or None)."""
+    check(lib().yskn_b200_residual_prepare(_ptr(hidden), _ptr(projection), _ptr(norm_weight), hidden.shape[0],
+                                           hidden.shape[1], eps, _ptr(inp), _ptr(inv_rms), _ptr(gate),
+                                           _stream(stream)), "residual_prepare")
 
 
 def _handles(mats):
