@@ -202,6 +202,13 @@ YSKN_B200_API int yskn_b200_residual_prepare(uint16_t* d_hidden, const float* d_
                                              const uint16_t* d_norm_weight, int M, int cols, float eps,
                                              float* d_input, float* d_inv_rms, uint16_t* d_gate, void* stream);
 
+/* MLP nonlinear step (replaces src/q35_kernels.cu:1402-1421; docs/spec/
+ * 05_RESIDUAL_NORM_MLP.md:156-176): with g = bf16(gate), u = bf16(up),
+ * d_out = bf16(bf16(g / (1 + expf(-g))) * u) as f32 [M][n], the down projection's input.
+ * d_gate, d_up: the restored f32 outputs of gate_proj and up_proj. */
+YSKN_B200_API int yskn_b200_gated_product(const float* d_gate, const float* d_up, int M, int n, float* d_out,
+                                          void* stream);
+
 /* Exact weighted integer sums (the operator core). Replaces
  * crates/yskn-engine/src/model.rs:948-962 `Compute::weighted_sums` (bit-identical to
  * crates/yskn-ref/src/compressed_linear.rs:205-252) and the reference's launch_lnord /

@@ -184,6 +184,18 @@ def residual_prepare(hidden_bits, projection, norm_bits, eps):
     return bf16_bits(h), x, inv_rms, bf16_bits(x)
 
 
+def gated_product(gate, up):
+    """docs/spec/05_RESIDUAL_NORM_MLP.md:156-176: bf16(bf16(g / (1 + exp(-g))) * u) with
+    g = bf16(gate), u = bf16(up), float32 arithmetic (numpy's float32 exp stands in for
+    CUDA's expf; they can differ in the last bit)."""
+    g = bf16_float(bf16_bits(gate))
+    u = bf16_float(bf16_bits(up))
+    with np.errstate(over="ignore"):  # exp(-g) overflows to +inf for g below about -88, as expf does
+        e = np.exp(-g)
+    silu = bf16_float(bf16_bits(g / (np.float32(1.0) + e)))
+    return bf16_float(bf16_bits(silu * u))
+
+
 def quantize_activation(x, signs_in):
     """compressed_linear.rs:57-135 for each row of x [M, Kc] -> (act8, alpha, A, row_quantum)."""
     x = np.ascontiguousarray(np.atleast_2d(x), np.float32)

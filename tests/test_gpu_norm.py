@@ -75,3 +75,27 @@ def test_prepared_input_feeds_the_next_operator(cuda):
                     inp.cpu().numpy(), si, so, inv_rms=inv.cpu().numpy())
     assert np.array_equal(y.cpu().numpy().view(np.uint32), np.asarray(want, np.float32).view(np.uint32))
     assert yskn_b200.status() == 0
+
+
+def test_gated_product_matches_the_oracle(cuda):
+    """bf16-exact except where CUDA's expf and numpy's float32 exp differ in the last bit
+    and that flips a rounding (the reference's own value of expf is not portable, NORM-01
+    of docs/spec/05_RESIDUAL_NORM_MLP.md): then by one bf16 ulp, on at most 0.1 % of the
+    elements."""
+    import torch
+    import yskn_b200
+    M, n = 3, 17408
+    rng = np.random.default_rng(11)
+    gate = (rng.standard_normal((M, n)) * 3).astype(np.float32)
+    up = rng.standard_normal((M, n)).astype(np.float32)
+    gate[0, :6] = [0.0, -0.0, 30.0, -30.0, 88.0, -100.0]
+    out = torch.empty((M, n), dtype=torch.float32, device="cuda")
+    yskn_b200.gated_product(torch.from_numpy(gate).cuda(), torch.from_numpy(up).cuda(), out)
+    got = out.cpu().numpy()
+    want = O.gated_product(gate, up)
+    assert np.array_equal(got, O.bf16_float(O.bf16_bits(got)))  # every value is a bf16 value
+    diff = got.view(np.int32) != want.view(np.int32)
+    assert diff.mean() <= 1e-3
+    ulps = np.abs((got.view(np.uint32) >> 16).astype(np.int64) - (want.view(np.uint32) >> 16).astype(np.int64))
+    assert ulps.max() <= 1
+    assert yskn_b200.status() == 0

@@ -1,5 +1,6 @@
-// Residual addition and deferred RMS normalisation between two projections: the
-// step that turns one projection's restored output into the next projection's input.
+// The steps between two projections: residual addition with deferred RMS
+// normalisation (what turns one projection's restored output into the next projection's
+// input), and the MLP's gated product (gate and up into down's input).
 //
 // Reference: the residual + normalisation part of q35_res_norm_xsm_kernel
 // (src/q35_kernels.cu:1437-1463) and q35_xsm_r (src/q35_kernels.cu:81-85); scalar spec
@@ -69,9 +70,37 @@ __global__ void __launch_bounds__(NORM_THREADS) residual_prepare_kernel(uint16_t
   if (t == 0) inv_rms[row] = rsqrtf(__fadd_rn(__fdiv_rn(total, (float)cols), eps));
 }
 
+// MLP nonlinear step (src/q35_kernels.cu:1402-1421, 113-116; docs/spec/
+// 05_RESIDUAL_NORM_MLP.md:156-176): with g = bf16(gate), u = bf16(up),
+// out = bf16(bf16(g / (1 + expf(-g))) * u), written as f32 so it is the down projection's
+// x directly. expf is CUDA's, as in the reference. Four elements per thread.
+__global__ void __launch_bounds__(256) gated_product_kernel(const float* gate, const float* up, int64_t n, float* out) {
+  const int64_t i0 = 4 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x);
+  if (i0 >= n) return;
+  const int k_end = n - i0 < 4 ? (int)(n - i0) : 4;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    if (k >= k_end) break;
+    const float g = bf16_to_f32(f32_to_bf16(gate[i0 + k]));
+    const float u = bf16_to_f32(f32_to_bf16(up[i0 + k]));
+    const float silu = bf16_to_f32(f32_to_bf16(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g)))));
+    out[i0 + k] = bf16_to_f32(f32_to_bf16(__fmul_rn(silu, u)));
+  }
+}
+
 }  // namespace yskn
 
 using namespace yskn;
+
+extern "C" YSKN_B200_API int yskn_b200_gated_product(const float* d_gate, const float* d_up, int M, int n,
+                                                    float* d_out, void* stream) {
+  if (!d_gate || !d_up || !d_out || M < 1 || n < 1) return fail(YSKN_EINVAL, "gated_product: bad argument");
+  const int64_t total = (int64_t)M * n;
+  const int64_t threads = (total + 3) / 4;
+  gated_product_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      d_gate, d_up, total, d_out);
+  return cuda_fail(cudaGetLastError(), "gated_product_kernel");
+}
 
 extern "C" YSKN_B200_API int yskn_b200_residual_prepare(uint16_t* d_hidden, const float* d_projection,
                                                        const uint16_t* d_norm_weight, int M, int cols, float eps,

@@ -69,6 +69,7 @@ _SIGNATURES = {
     "yskn_b200_embedding_lookup": (_i, [_vp, _vp, _i, _vp, _vp]),
     "yskn_b200_file_load_embedding": (_vp, [_vp, _i, _i, _i]),
     "yskn_b200_residual_prepare": (_i, [_vp, _vp, _vp, _i, _i, C.c_float, _vp, _vp, _vp, _vp]),
+    "yskn_b200_gated_product": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
 }
 
 _lib = None
@@ -314,6 +315,12 @@ def residual_prepare(hidden, projection, norm_weight, eps, inp, inv_rms, gate=No
     check(lib().yskn_b200_residual_prepare(_ptr(hidden), _ptr(projection), _ptr(norm_weight), hidden.shape[0],
                                            hidden.shape[1], eps, _ptr(inp), _ptr(inv_rms), _ptr(gate),
                                            _stream(stream)), "residual_prepare")
+
+
+def gated_product(gate, up, out, stream=None):
+    """out = bf16(bf16(silu(bf16(gate))) * bf16(up)) as f32, for f32 [M][n] gate and up."""
+    check(lib().yskn_b200_gated_product(_ptr(gate), _ptr(up), gate.shape[0], gate.shape[1], _ptr(out),
+                                        _stream(stream)), "gated_product")
 
 
 def _handles(mats):
