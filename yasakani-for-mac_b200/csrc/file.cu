@@ -26,6 +26,7 @@
 #include <cstring>
 #include <memory>
 #include <string>
+#include <unordered_set>
 #include <utility>
 #include <vector>
 
@@ -549,13 +550,8 @@ extern "C" YSKN_B200_API yskn_b200_file* yskn_b200_file_open(const char* path) {
   const Json* tensors = c.required(root, "tensors");
   if (!tensors) return open_fail(F, c.err);
   if (tensors->kind != Json::Arr) return open_fail(F, "tensors must be an array");
-  std::vector<std::string> names;
-  auto unique = [&](const std::string& n) {
-    for (const auto& x : names)
-      if (x == n) return false;
-    names.push_back(n);
-    return true;
-  };
+  std::unordered_set<std::string> names;
+  auto unique = [&](const std::string& n) { return names.insert(n).second; };
   for (const Json& e : tensors->arr) {
     TensorDesc t{};
     if (!c.tensor(e, F->data_offset, file_bytes, t)) return open_fail(F, c.err);
