@@ -209,6 +209,15 @@ YSKN_B200_API int yskn_b200_residual_prepare(uint16_t* d_hidden, const float* d_
 YSKN_B200_API int yskn_b200_gated_product(const float* d_gate, const float* d_up, int M, int n, float* d_out,
                                           void* stream);
 
+/* Greedy token and top-8 raw logits per row of head logits (replaces the greedy and
+ * top-k kernels, src/misc_kernels.cu:59-88,100-140, src/q35_sample.cu:131-178; docs/spec/
+ * 06_OUTPUT_HEAD_SAMPLER.md:31-64): order (larger logit, smaller id) from (-FLT_MAX,
+ * INT_MAX), so NaN and -inf are never chosen. d_logits f32 [M][n] (yskn_b200_linear of
+ * the head matrix with the row's inverse RMS); d_token int32 [M]; d_top8_logits f32
+ * [M][8] and d_top8_ids int32 [M][8] in that order; any output may be NULL (not all). */
+YSKN_B200_API int yskn_b200_head_select(const float* d_logits, int M, int n, int32_t* d_token, float* d_top8_logits,
+                                        int32_t* d_top8_ids, void* stream);
+
 /* Exact weighted integer sums (the operator core). Replaces
  * crates/yskn-engine/src/model.rs:948-962 `Compute::weighted_sums` (bit-identical to
  * crates/yskn-ref/src/compressed_linear.rs:205-252) and the reference's launch_lnord /

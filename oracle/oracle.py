@@ -196,6 +196,22 @@ def gated_product(gate, up):
     return bf16_float(bf16_bits(silu * u))
 
 
+def head_select(logits, k=8):
+    """docs/spec/06_OUTPUT_HEAD_SAMPLER.md:31-64,240-250: the first k of the order (larger
+    logit, smaller id) among logits that beat the starting point (-FLT_MAX, INT_MAX)
+    (NaN and -inf never do), padded with that starting point. Returns (token, values, ids)."""
+    l = np.asarray(logits, np.float32)
+    ids = np.arange(l.size)
+    ok = ~np.isnan(l) & (l >= np.float32(-3.4028234663852886e38))
+    vals, idx = l[ok], ids[ok]
+    order = np.lexsort((idx, -vals))[:k]
+    top_v = np.full(k, np.float32(-3.4028234663852886e38), np.float32)
+    top_i = np.full(k, 2**31 - 1, np.int64)
+    top_v[:order.size] = vals[order]
+    top_i[:order.size] = idx[order]
+    return int(top_i[0]), top_v, top_i
+
+
 def quantize_activation(x, signs_in):
     """compressed_linear.rs:57-135 for each row of x [M, Kc] -> (act8, alpha, A, row_quantum)."""
     x = np.ascontiguousarray(np.atleast_2d(x), np.float32)

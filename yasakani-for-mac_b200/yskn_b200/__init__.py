@@ -70,6 +70,7 @@ _SIGNATURES = {
     "yskn_b200_file_load_embedding": (_vp, [_vp, _i, _i, _i]),
     "yskn_b200_residual_prepare": (_i, [_vp, _vp, _vp, _i, _i, C.c_float, _vp, _vp, _vp, _vp]),
     "yskn_b200_gated_product": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
+    "yskn_b200_head_select": (_i, [_vp, _i, _i, _vp, _vp, _vp, _vp]),
 }
 
 _lib = None
@@ -321,6 +322,12 @@ def gated_product(gate, up, out, stream=None):
     """out = bf16(bf16(silu(bf16(gate))) * bf16(up)) as f32, for f32 [M][n] gate and up."""
     check(lib().yskn_b200_gated_product(_ptr(gate), _ptr(up), gate.shape[0], gate.shape[1], _ptr(out),
                                         _stream(stream)), "gated_product")
+
+
+def head_select(logits, token=None, top_logits=None, top_ids=None, stream=None):
+    """Greedy token (int32 [M]) and top-8 (f32 / int32 [M][8]) of f32 logits [M][n]."""
+    check(lib().yskn_b200_head_select(_ptr(logits), logits.shape[0], logits.shape[1], _ptr(token), _ptr(top_logits),
+                                      _ptr(top_ids), _stream(stream)), "head_select")
 
 
 def _handles(mats):
