@@ -218,6 +218,21 @@ YSKN_B200_API int yskn_b200_gated_product(const float* d_gate, const float* d_up
 YSKN_B200_API int yskn_b200_head_select(const float* d_logits, int M, int n, int32_t* d_token, float* d_top8_logits,
                                         int32_t* d_top8_ids, void* stream);
 
+/* Attention inputs from the q/k/v projection outputs (replaces the head preparation of
+ * the q35 attention, src/q35_kernels.cu:1013-1059 and :1091-1104, and the cache rotation
+ * src/kvx_codec.cuh:11-48; docs/spec/04_ATTENTION.md:15-106): per row and head, bf16
+ * projections; query and key heads normalised by their RMS times (1 + q_norm / k_norm),
+ * RoPE at d_positions[row] on channels i, i+32 (i < 32); every head through the
+ * 256-element cache rotation. d_q f32 [M][n_qh][512] (query, then gate channels per
+ * head), d_k, d_v f32 [M][n_kvh][256]; out: d_query bf16 [M][n_qh][256] (the attention's
+ * q), d_gate bf16 [M][n_qh][256] (its gate), d_k_rot, d_v_rot f32 [M][n_kvh][256] (the KV
+ * encoder's rows). rsqrtf, cosf and sinf are CUDA's, as in the reference. */
+YSKN_B200_API int yskn_b200_attention_prep(const float* d_q, const float* d_k, const float* d_v,
+                                           const uint16_t* d_q_norm, const uint16_t* d_k_norm,
+                                           const int32_t* d_positions, float eps, int M, int n_qh, int n_kvh,
+                                           uint16_t* d_query, uint16_t* d_gate, float* d_k_rot, float* d_v_rot,
+                                           void* stream);
+
 /* Exact weighted integer sums (the operator core). Replaces
  * crates/yskn-engine/src/model.rs:948-962 `Compute::weighted_sums` (bit-identical to
  * crates/yskn-ref/src/compressed_linear.rs:205-252) and the reference's launch_lnord /

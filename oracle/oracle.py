@@ -212,6 +212,80 @@ def head_select(logits, k=8):
     return int(top_i[0]), top_v, top_i
 
 
+ROPE_FREQ_BITS = [  # docs/spec/04_ATTENTION.md:42-52
+    0x3f800000, 0x3f1ab32b, 0x3ebaf81b, 0x3e61f835, 0x3e088d77, 0x3da50956, 0x3d47763f, 0x3cf11177,
+    0x3c91ad39, 0x3c301052, 0x3bd4ca15, 0x3b80967d, 0x3b1b690d, 0x3abbd3ed, 0x3a6301e2, 0x3a092e02,
+    0x39a5cb60, 0x394860c1, 0x38f22ce2, 0x3892587e, 0x3830df52, 0x37d5c441, 0x37812dab, 0x371c1fc4,
+    0x36bcb0c1, 0x36640cc6, 0x3609cf4a, 0x35a68e4c, 0x35494c57, 0x34f3499d, 0x3493048e, 0x3431af44]
+
+
+def cache_signs():
+    """docs/spec/04_ATTENTION.md:80-88: the sign of each of the 256 cache channels."""
+    x = np.arange(1, 257, dtype=np.uint64)
+    x ^= x >> np.uint64(16)
+    x = (x * np.uint64(0x7FEB352D)) & np.uint64(0xFFFFFFFF)
+    x ^= x >> np.uint64(15)
+    x = (x * np.uint64(0x846CA68B)) & np.uint64(0xFFFFFFFF)
+    x ^= x >> np.uint64(16)
+    return np.where(x & np.uint64(1), np.float32(-1.0), np.float32(1.0)).astype(np.float32)
+
+
+def rotate_cache(x):
+    """docs/spec/04_ATTENTION.md:90-100: signs, H256 with distances 1..128, * 1/16."""
+    a = np.asarray(x, np.float32) * cache_signs()
+    idx = np.arange(256)
+    for d in (1, 2, 4, 8, 16, 32, 64, 128):
+        o = a[idx ^ d]
+        a = np.where((idx & d) != 0, o - a, a + o).astype(np.float32)
+    return a * np.float32(0.0625)
+
+
+def _xor_sum32(v):
+    a = np.asarray(v, np.float32).copy()
+    for off in (16, 8, 4, 2, 1):
+        a = a + a[np.arange(32) ^ off]
+    return a[0]
+
+
+def normalize_head(y, weight_bits, eps):
+    """docs/spec/04_ATTENTION.md:27-37 (the inverse RMS correctly rounded; the reference
+    calls CUDA's rsqrtf, whose bits are not portable)."""
+    y = np.asarray(y, np.float32)
+    total = np.float32(0.0)
+    for g in range(8):
+        total = np.float32(total + _xor_sum32(y[32 * g:32 * g + 32] * y[32 * g:32 * g + 32]))
+    inv = np.float32(1.0 / np.sqrt(np.float64(np.float32(total / np.float32(256.0)) + np.float32(eps))))
+    return bf16_float(bf16_bits((y * inv) * (np.float32(1.0) + bf16_float(weight_bits))))
+
+
+def rope(n, position):
+    """docs/spec/04_ATTENTION.md:54-66 (numpy's float32 cos/sin stand in for CUDA's)."""
+    freq = np.array(ROPE_FREQ_BITS, np.uint32).view(np.float32)
+    arg = np.float32(position) * freq
+    c = bf16_float(bf16_bits(np.cos(arg)))
+    s = bf16_float(bf16_bits(np.sin(arg)))
+    r = np.asarray(n, np.float32).copy()
+    a, b = r[:32].copy(), r[32:64].copy()
+    r[:32] = bf16_float(bf16_bits(bf16_float(bf16_bits(a * c)) + bf16_float(bf16_bits(-b * s))))
+    r[32:64] = bf16_float(bf16_bits(bf16_float(bf16_bits(b * c)) + bf16_float(bf16_bits(a * s))))
+    return r
+
+
+def attention_prep(q, k, v, q_norm_bits, k_norm_bits, position, eps):
+    """One row (docs/spec/04_ATTENTION.md:15-106): q [n_qh][512] (query then gate channels
+    per head), k, v [n_kvh][256] -> (query bf16 bits, gate bf16 bits, k f32, v f32)."""
+    q = np.asarray(q, np.float32)
+    query = np.empty((q.shape[0], 256), np.uint16)
+    gate = bf16_bits(q[:, 256:])
+    for h in range(q.shape[0]):
+        n = rope(normalize_head(bf16_float(bf16_bits(q[h, :256])), q_norm_bits, eps), position)
+        query[h] = bf16_bits(rotate_cache(n))
+    k_out = np.stack([rotate_cache(rope(normalize_head(bf16_float(bf16_bits(x)), k_norm_bits, eps), position))
+                      for x in np.asarray(k, np.float32)])
+    v_out = np.stack([rotate_cache(bf16_float(bf16_bits(x))) for x in np.asarray(v, np.float32)])
+    return query, gate, k_out, v_out
+
+
 def quantize_activation(x, signs_in):
     """compressed_linear.rs:57-135 for each row of x [M, Kc] -> (act8, alpha, A, row_quantum)."""
     x = np.ascontiguousarray(np.atleast_2d(x), np.float32)

@@ -71,6 +71,7 @@ _SIGNATURES = {
     "yskn_b200_residual_prepare": (_i, [_vp, _vp, _vp, _i, _i, C.c_float, _vp, _vp, _vp, _vp]),
     "yskn_b200_gated_product": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
     "yskn_b200_head_select": (_i, [_vp, _i, _i, _vp, _vp, _vp, _vp]),
+    "yskn_b200_attention_prep": (_i, [_vp] * 6 + [C.c_float, _i, _i, _i] + [_vp] * 5),
 }
 
 _lib = None
@@ -328,6 +329,14 @@ def head_select(logits, token=None, top_logits=None, top_ids=None, stream=None):
     """Greedy token (int32 [M]) and top-8 (f32 / int32 [M][8]) of f32 logits [M][n]."""
     check(lib().yskn_b200_head_select(_ptr(logits), logits.shape[0], logits.shape[1], _ptr(token), _ptr(top_logits),
                                       _ptr(top_ids), _stream(stream)), "head_select")
+
+
+def attention_prep(q, k, v, q_norm, k_norm, positions, eps, query, gate, k_rot, v_rot, stream=None):
+    """q f32 [M][n_qh][512], k, v f32 [M][n_kvh][256], norms bf16 bits [256], positions
+    int32 [M] -> query, gate (bf16 bits [M][n_qh][256]), k_rot, v_rot (f32 [M][n_kvh][256])."""
+    check(lib().yskn_b200_attention_prep(_ptr(q), _ptr(k), _ptr(v), _ptr(q_norm), _ptr(k_norm), _ptr(positions), eps,
+                                         q.shape[0], q.shape[1], k.shape[1], _ptr(query), _ptr(gate), _ptr(k_rot),
+                                         _ptr(v_rot), _stream(stream)), "attention_prep")
 
 
 def _handles(mats):
