@@ -233,6 +233,26 @@ YSKN_B200_API int yskn_b200_attention_prep(const float* d_q, const float* d_k, c
                                            uint16_t* d_query, uint16_t* d_gate, float* d_k_rot, float* d_v_rot,
                                            void* stream);
 
+/* Gated DeltaNet decode step (replaces src/q35_kernels.cu:746-820 and :864-980; docs/spec/
+ * 03_GATED_DELTANET.md:33-160), ordinary causal rows. Gates: d_gates f32 [M][96] (48 b, then
+ * 48 a) from the layer's weighted hidden row d_hidden (bf16 [M][hidden], the gate copy of
+ * yskn_b200_residual_prepare), its d_inv_rms [M], and the dense bf16 weights d_wb, d_wa
+ * [48][hidden] (hidden a multiple of 1024). Step: d_qkv f32 [M][10240] and d_z f32 [M][6144]
+ * (the restored in_proj_qkv / in_proj_z outputs), the bf16 conv weights [10240][4], A_log,
+ * dt_bias [48] and norm weight [128]; commits after n_commit rows (0..M; 0 = a provisional
+ * verification pass): d_state f32 [48][128][128] becomes the state after row n_commit - 1 and
+ * d_history bf16 [3][10240] (the newest committed projected rows, oldest first; zero at the
+ * start) takes the committed rows (docs/spec/03_GATED_DELTANET.md:160-186). Writes d_out
+ * f32 [M][6144], the gated output (bf16 values), out_proj's input. expf, rsqrtf and log1pf
+ * are CUDA's, as in the reference. */
+YSKN_B200_API int yskn_b200_gdn_gates(const uint16_t* d_hidden, const float* d_inv_rms, const uint16_t* d_wb,
+                                      const uint16_t* d_wa, int M, int hidden, float* d_gates, void* stream);
+YSKN_B200_API int yskn_b200_gdn_step(const float* d_qkv, const float* d_z, const float* d_gates,
+                                     const uint16_t* d_conv_w, const uint16_t* d_a_log, const uint16_t* d_dt_bias,
+                                     const uint16_t* d_norm_w, float eps, int M, int n_commit, float* d_state,
+                                     uint16_t* d_history,
+                                     float* d_out, void* stream);
+
 /* Exact weighted integer sums (the operator core). Replaces
  * crates/yskn-engine/src/model.rs:948-962 `Compute::weighted_sums` (bit-identical to
  * crates/yskn-ref/src/compressed_linear.rs:205-252) and the reference's launch_lnord /

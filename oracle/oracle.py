@@ -286,6 +286,107 @@ def attention_prep(q, k, v, q_norm_bits, k_norm_bits, position, eps):
     return query, gate, k_out, v_out
 
 
+def _sum4(v):
+    return np.float32(np.float32(np.float32(v[0] + v[1]) + v[2]) + v[3])
+
+
+def _squares128(x):
+    x = np.asarray(x, np.float32)
+    return _sum4([_xor_sum32(x[32 * g:32 * g + 32] * x[32 * g:32 * g + 32]) for g in range(4)])
+
+
+def _silu(x):
+    with np.errstate(over="ignore"):
+        return np.float32(x) / (np.float32(1.0) + np.exp(-np.float32(x)))
+
+
+def gdn_gates(x_bits, inv_rms, wb_bits, wa_bits):
+    """docs/spec/03_GATED_DELTANET.md:57-76 for one row: 96 gates (b, then a)."""
+    x = bf16_float(x_bits)
+    w = np.concatenate([bf16_float(wb_bits), bf16_float(wa_bits)])
+    out = np.empty(w.shape[0], np.float32)
+    p = np.arange(128)
+    for o in range(w.shape[0]):
+        partial = np.zeros(128, np.float32)
+        for chunk in range(x.size // 1024):
+            for e in range(8):
+                i = 8 * p + 1024 * chunk + e
+                partial = partial + w[o, i] * x[i]
+        out[o] = bf16_float(bf16_bits(_sum4([_xor_sum32(partial[32 * g:32 * g + 32]) for g in range(4)]) *
+                                      np.float32(inv_rms)))
+    return out
+
+
+def gdn_step(qkv, z, gates, conv_bits, a_log_bits, dt_bias_bits, norm_bits, eps, state, history_bits,
+             n_commit=None):
+    """docs/spec/03_GATED_DELTANET.md:78-186, ordinary causal rows, numpy float32 with
+    correctly rounded 1/sqrt and numpy's exp/log1p for CUDA's rsqrtf/expf/log1pf. Commits
+    after n_commit rows (default all; 0 = provisional). Returns (out [M][6144], the
+    committed state [48][128][128], the committed history bits [3][10240])."""
+    qkv = np.asarray(qkv, np.float32)
+    M = qkv.shape[0]
+    proj = bf16_float(bf16_bits(qkv))
+    hist = bf16_float(history_bits)
+    cw = bf16_float(conv_bits).reshape(-1, 4)
+    past = lambda r: hist[3 + r] if r < 0 else proj[r]
+    n_commit = M if n_commit is None else n_commit
+    state = np.array(state, np.float32)
+    saved = state.copy()
+    out = np.empty((M, 48 * 128), np.float32)
+    a_log, dt_bias, norm_w = bf16_float(a_log_bits), bf16_float(dt_bias_bits), bf16_float(norm_bits)
+    for row in range(M):
+        a = cw[:, 0] * past(row - 3)
+        a = a + cw[:, 1] * past(row - 2)
+        a = a + cw[:, 2] * past(row - 1)
+        a = a + cw[:, 3] * past(row)
+        conv = bf16_float(bf16_bits(_silu(bf16_float(bf16_bits(a)))))
+        for vh in range(48):
+            kh = vh // 3
+            q = conv[128 * kh:128 * kh + 128]
+            k = conv[2048 + 128 * kh:2048 + 128 * kh + 128]
+            v = conv[4096 + 128 * vh:4096 + 128 * vh + 128]
+            rq = np.float32(1.0 / np.sqrt(np.float64(np.float32(_squares128(q) + np.float32(1e-6)))))
+            rk = np.float32(1.0 / np.sqrt(np.float64(np.float32(_squares128(k) + np.float32(1e-6)))))
+            query = (q * rq) * np.float32(0.08838834764831845)
+            key = k * rk
+            g = np.asarray(gates[row], np.float32)
+            with np.errstate(over="ignore"):
+                beta = bf16_float(bf16_bits(np.float32(1.0) / (np.float32(1.0) + np.exp(-g[vh]))))
+                x = np.float32(g[48 + vh] + dt_bias[vh])
+                sp = x if x > np.float32(20.0) else np.float32(np.log1p(np.exp(x)))
+                decay = np.exp(np.float32(-np.exp(a_log[vh]) * sp))
+            R = state[vh]
+            parts = []
+            for grp in range(4):
+                acc = np.zeros(128, np.float32)
+                for r in range(32):
+                    i = 32 * grp + r
+                    R[i] = R[i] * decay
+                    acc = acc + R[i] * key[i]
+                parts.append(acc)
+            correction = (v - _sum4(parts)) * beta
+            parts = []
+            for grp in range(4):
+                acc = np.zeros(128, np.float32)
+                for r in range(32):
+                    i = 32 * grp + r
+                    R[i] = R[i] + key[i] * correction
+                    acc = acc + R[i] * query[i]
+                parts.append(acc)
+            core = bf16_float(bf16_bits(_sum4(parts)))
+            inv = np.float32(1.0 / np.sqrt(np.float64(np.float32(_squares128(core) / np.float32(128.0)) +
+                                                      np.float32(eps))))
+            normalized = bf16_float(bf16_bits(norm_w * bf16_float(bf16_bits(core * inv))))
+            out[row, 128 * vh:128 * vh + 128] = bf16_float(bf16_bits(normalized *
+                                                                     _silu(z[row, 128 * vh:128 * vh + 128])))
+        if row + 1 == n_commit:
+            saved = state.copy()
+    if n_commit == 0:
+        return out, saved, np.asarray(history_bits, np.uint16).copy()
+    rows = [past(n_commit - 3 + a) for a in range(3)]
+    return out, saved, bf16_bits(np.stack(rows))
+
+
 def quantize_activation(x, signs_in):
     """compressed_linear.rs:57-135 for each row of x [M, Kc] -> (act8, alpha, A, row_quantum)."""
     x = np.ascontiguousarray(np.atleast_2d(x), np.float32)

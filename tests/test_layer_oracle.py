@@ -1,0 +1,53 @@
+"""CPU checks of the layer oracles that have no golden vectors in the reference: the Gated
+DeltaNet step's commit rules (docs/spec/03_GATED_DELTANET.md:160-186) and its row-by-row
+equivalence, at small sizes."""
+import numpy as np
+
+import oracle as O
+
+
+def _gdn_inputs(rng, M):
+    return dict(qkv=rng.standard_normal((M, 10240)).astype(np.float32),
+                z=rng.standard_normal((M, 6144)).astype(np.float32),
+                gates=rng.standard_normal((M, 96)).astype(np.float32))
+
+
+def _gdn_weights(rng):
+    return (O.bf16_bits((rng.standard_normal((10240, 4)) * 0.5).astype(np.float32)),
+            O.bf16_bits((rng.standard_normal(48) * 0.5).astype(np.float32)),
+            O.bf16_bits((rng.standard_normal(48) * 0.5).astype(np.float32)),
+            O.bf16_bits((1 + rng.standard_normal(128) * 0.1).astype(np.float32)))
+
+
+def test_gdn_commit_rules():
+    rng = np.random.default_rng(3)
+    w = _gdn_weights(rng)
+    state = (rng.standard_normal((48, 128, 128)) * 0.1).astype(np.float32)
+    hist = O.bf16_bits(rng.standard_normal((3, 10240)).astype(np.float32))
+    x = _gdn_inputs(rng, 4)
+    out_all, s_all, h_all = O.gdn_step(x["qkv"], x["z"], x["gates"], *w, 1e-6, state, hist)
+    out_p, s_p, h_p = O.gdn_step(x["qkv"], x["z"], x["gates"], *w, 1e-6, state, hist, n_commit=0)
+    assert np.array_equal(out_all, out_p)  # the outputs do not depend on the commit point
+    assert np.array_equal(s_p, state) and np.array_equal(h_p, hist)
+    assert np.array_equal(h_all, O.bf16_bits(x["qkv"][1:4]))
+    out_2, s_2, h_2 = O.gdn_step(x["qkv"], x["z"], x["gates"], *w, 1e-6, state, hist, n_commit=2)
+    assert np.array_equal(out_2, out_all)
+    assert np.array_equal(h_2, np.stack([hist[2], O.bf16_bits(x["qkv"][0]), O.bf16_bits(x["qkv"][1])]))
+    # the state committed after two rows, then two more rows, is the state after four
+    _, s_4, _ = O.gdn_step(x["qkv"][2:], x["z"][2:], x["gates"][2:], *w, 1e-6, s_2, h_2)
+    assert np.array_equal(s_4, s_all)
+    assert not np.array_equal(s_2, s_all)
+
+
+def test_gdn_rows_one_by_one():
+    rng = np.random.default_rng(4)
+    w = _gdn_weights(rng)
+    state = (rng.standard_normal((48, 128, 128)) * 0.1).astype(np.float32)
+    hist = O.bf16_bits(rng.standard_normal((3, 10240)).astype(np.float32))
+    x = _gdn_inputs(rng, 3)
+    out_all, s_all, h_all = O.gdn_step(x["qkv"], x["z"], x["gates"], *w, 1e-6, state, hist)
+    s, h = state, hist
+    for r in range(3):
+        out, s, h = O.gdn_step(x["qkv"][r:r + 1], x["z"][r:r + 1], x["gates"][r:r + 1], *w, 1e-6, s, h)
+        assert np.array_equal(out[0], out_all[r])
+    assert np.array_equal(s, s_all) and np.array_equal(h, h_all)

@@ -72,6 +72,8 @@ _SIGNATURES = {
     "yskn_b200_gated_product": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
     "yskn_b200_head_select": (_i, [_vp, _i, _i, _vp, _vp, _vp, _vp]),
     "yskn_b200_attention_prep": (_i, [_vp] * 6 + [C.c_float, _i, _i, _i] + [_vp] * 5),
+    "yskn_b200_gdn_gates": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp, _vp]),
+    "yskn_b200_gdn_step": (_i, [_vp] * 7 + [C.c_float, _i, _i, _vp, _vp, _vp, _vp]),
 }
 
 _lib = None
@@ -337,6 +339,20 @@ def attention_prep(q, k, v, q_norm, k_norm, positions, eps, query, gate, k_rot, 
     check(lib().yskn_b200_attention_prep(_ptr(q), _ptr(k), _ptr(v), _ptr(q_norm), _ptr(k_norm), _ptr(positions), eps,
                                          q.shape[0], q.shape[1], k.shape[1], _ptr(query), _ptr(gate), _ptr(k_rot),
                                          _ptr(v_rot), _stream(stream)), "attention_prep")
+
+
+def gdn_gates(hidden, inv_rms, wb, wa, gates, stream=None):
+    check(lib().yskn_b200_gdn_gates(_ptr(hidden), _ptr(inv_rms), _ptr(wb), _ptr(wa), hidden.shape[0], hidden.shape[1],
+                                    _ptr(gates), _stream(stream)), "gdn_gates")
+
+
+def gdn_step(qkv, z, gates, conv_w, a_log, dt_bias, norm_w, eps, state, history, out, n_commit=None, stream=None):
+    """One Gated DeltaNet pass over qkv.shape[0] rows, committing after n_commit rows
+    (default: all of them; 0 = provisional, state and history unchanged)."""
+    n_commit = qkv.shape[0] if n_commit is None else n_commit
+    check(lib().yskn_b200_gdn_step(_ptr(qkv), _ptr(z), _ptr(gates), _ptr(conv_w), _ptr(a_log), _ptr(dt_bias),
+                                   _ptr(norm_w), eps, qkv.shape[0], n_commit, _ptr(state), _ptr(history), _ptr(out),
+                                   _stream(stream)), "gdn_step")
 
 
 def _handles(mats):
