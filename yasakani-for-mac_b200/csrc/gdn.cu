@@ -12,14 +12,18 @@
 // (GDN-01 of the spec: their bits are not portable).
 //
 // B200 design:
-//  * gates: one 128-thread CTA per (row, output); thread p forms partial p (40 products in
-//    the spec's order), each warp is one xor_sum32 group (a shuffle butterfly: every lane
-//    ends with the same bits), the four groups combine in sum4 order.
-//  * step: one 128-thread CTA per value head, its 128x128 f32 state in shared memory for
-//    all rows (the recurrence is sequential over rows); thread j owns state column j, so
-//    the spec's 32-term sequential groups are per-thread loops and the column is read and
-//    written once per launch (saved when the committed row is reached). q/k of the head's key head are recomputed by its three value
-//    heads (128 channels each, cheap).
+//  * gates: one 128-thread CTA per (output, 8 rows); thread p forms partial p (40 products in
+//    the spec's order, eight bf16 pairs per 16-byte load of weights and input), each warp is
+//    one xor_sum32 group (a shuffle butterfly: every lane ends with the same bits), the four
+//    groups combine in sum4 order.
+//  * step: one 512-thread CTA per value head, its 128x128 f32 state in registers for all
+//    rows (the recurrence is sequential over rows); thread (g, j) holds rows 32g..32g+31 of
+//    state column j, so each of the spec's 32-term sequential groups is one thread's loop
+//    over its registers and the four group sums meet in shared memory for sum4. The state
+//    is read once per launch (32 coalesced loads per thread, in flight while the first
+//    row's convolution and gates are formed) and written once (when the committed row is
+//    reached); each row's raw inputs are loaded during the previous row's recurrence. Thread groups 0, 1 and 2 convolve the query, key and value channel j
+//    (q/k of the key head are recomputed by its three value heads: 128 channels each).
 //  * history: the three newest projected rows are written after the step, in place (another
 //    launch, since three CTAs read each key head's history).
 #include <cuda_bf16.h>
@@ -32,6 +36,7 @@ constexpr int GDN_DK = 128;   // channels per head
 constexpr int GDN_QK_HEADS = 16;
 constexpr int GDN_V_HEADS = 48;
 constexpr int GDN_QKV = 2 * GDN_QK_HEADS * GDN_DK + GDN_V_HEADS * GDN_DK;  // 10240
+constexpr int GDN_GATE_ROWS = 8;  // rows per gates CTA
 
 __device__ __forceinline__ float bf(float x) {
   return __uint_as_float((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(x)) << 16);
@@ -47,33 +52,45 @@ __device__ __forceinline__ float xor_sum32(float v) {
 }
 __device__ __forceinline__ float sum4(const float* v) { return __fadd_rn(__fadd_rn(__fadd_rn(v[0], v[1]), v[2]), v[3]); }
 
-// squares128 (03_GATED_DELTANET.md:24-27) of the value each of the 128 threads holds.
-__device__ __forceinline__ float squares128(float x, float* s4) {
-  const float g = xor_sum32(__fmul_rn(x, x));
-  __syncthreads();  // s4 is free
-  if ((threadIdx.x & 31) == 0) s4[threadIdx.x >> 5] = g;
-  __syncthreads();
-  return sum4(s4);
+__device__ __forceinline__ float sum4(float a, float b, float c, float d) {
+  return __fadd_rn(__fadd_rn(__fadd_rn(a, b), c), d);
+}
+
+// Adds the eight products of a 16-byte group of bf16 weights and inputs to `acc`, element 0
+// (the low half of the first word) first.
+__device__ __forceinline__ float dot8(float acc, uint4 w, uint4 x) {
+  const uint32_t ww[4] = {w.x, w.y, w.z, w.w}, xx[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    acc = __fadd_rn(acc, __fmul_rn(__uint_as_float(ww[k] << 16), __uint_as_float(xx[k] << 16)));
+    acc = __fadd_rn(acc, __fmul_rn(__uint_as_float(ww[k] & 0xffff0000u), __uint_as_float(xx[k] & 0xffff0000u)));
+  }
+  return acc;
 }
 
 // 03_GATED_DELTANET.md:57-76: the 96 dense gates of each row (b, then a).
 __global__ void __launch_bounds__(128) gdn_gates_kernel(const uint16_t* x, const float* inv_rms, const uint16_t* wb,
-                                                        const uint16_t* wa, int hidden, float* gates) {
-  __shared__ float s4[4];
-  const int o = blockIdx.x, row = blockIdx.y, p = threadIdx.x;
+                                                        const uint16_t* wa, int hidden, int M, float* gates) {
+  __shared__ float s4[2][4];
+  const int o = blockIdx.x, p = threadIdx.x;
   const uint16_t* w = o < GDN_V_HEADS ? wb + (size_t)o * hidden : wa + (size_t)(o - GDN_V_HEADS) * hidden;
-  const uint16_t* xr = x + (size_t)row * hidden;
-  float partial = 0.0f;
-  for (int chunk = 0; chunk < hidden / 1024; ++chunk)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int i = 8 * p + 1024 * chunk + e;
-      partial = __fadd_rn(partial, __fmul_rn(bf16f(w[i]), bf16f(xr[i])));
+  const int row0 = blockIdx.y * GDN_GATE_ROWS;
+  const int rows = M - row0 < GDN_GATE_ROWS ? M - row0 : GDN_GATE_ROWS;
+  const int chunks = hidden / 1024;
+  for (int rr = 0; rr < rows; ++rr) {
+    const int row = row0 + rr;
+    const uint16_t* xr = x + (size_t)row * hidden;
+    float partial = 0.0f;
+#pragma unroll 5
+    for (int chunk = 0; chunk < chunks; ++chunk) {
+      const int i = 1024 * chunk + 8 * p;
+      partial = dot8(partial, __ldg(reinterpret_cast<const uint4*>(w + i)), __ldg(reinterpret_cast<const uint4*>(xr + i)));
     }
-  const float g = xor_sum32(partial);
-  if ((p & 31) == 0) s4[p >> 5] = g;
-  __syncthreads();
-  if (p == 0) gates[(size_t)row * 2 * GDN_V_HEADS + o] = bf(__fmul_rn(sum4(s4), inv_rms[row]));
+    const float g = xor_sum32(partial);
+    if ((p & 31) == 0) s4[rr & 1][p >> 5] = g;
+    __syncthreads();  // (the other buffer is written only after every thread passed the next barrier)
+    if (p == 0) gates[(size_t)row * 2 * GDN_V_HEADS + o] = bf(__fmul_rn(sum4(s4[rr & 1]), inv_rms[row]));
+  }
 }
 
 struct GdnParams {
@@ -91,72 +108,132 @@ struct GdnParams {
   float* out;                // [M][6144]: the gated output (bf16 values), out_proj's x
 };
 
-// The convolved (bf16(silu(bf16(conv))) channel c of row `row` (03_GATED_DELTANET.md:86-100).
-__device__ __forceinline__ float gdn_conv(const GdnParams& p, int row, int c) {
-  auto past = [&](int r) { return r < 0 ? bf16f(p.history[(size_t)(3 + r) * GDN_QKV + c]) : bf(p.qkv[(size_t)r * GDN_QKV + c]); };
-  const uint16_t* w = p.conv_w + (size_t)c * 4;
-  float a = __fmul_rn(bf16f(w[0]), past(row - 3));
-  a = __fadd_rn(a, __fmul_rn(bf16f(w[1]), past(row - 2)));
-  a = __fadd_rn(a, __fmul_rn(bf16f(w[2]), past(row - 1)));
-  a = __fadd_rn(a, __fmul_rn(bf16f(w[3]), past(row)));
+constexpr int GDN_STEP_THREADS = 4 * GDN_DK;  // four threads per state column, one per 32-row group
+
+// One row's raw inputs of one thread, loaded a row ahead of their use: the four
+// convolution taps (oldest first) of channel c (none when c < 0), z of column j (group 0)
+// and the head's two gates.
+struct GdnRowIn {
+  float x[4];
+  float z, gb, ga;
+};
+
+__device__ __forceinline__ void gdn_load_row(const GdnParams& p, int row, int c, int vh, int j, GdnRowIn& in) {
+  if (c >= 0) {
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int r = row - 3 + t;  // 03_GATED_DELTANET.md:86-100, depth = row
+      in.x[t] = r < 0 ? bf16f(p.history[(size_t)(3 + r) * GDN_QKV + c]) : bf(p.qkv[(size_t)r * GDN_QKV + c]);
+    }
+  }
+  if (c >= 0 && c < GDN_QK_HEADS * GDN_DK) in.z = p.z[(size_t)row * GDN_V_HEADS * GDN_DK + GDN_DK * vh + j];
+  in.gb = p.gates[(size_t)row * 2 * GDN_V_HEADS + vh];
+  in.ga = p.gates[(size_t)row * 2 * GDN_V_HEADS + GDN_V_HEADS + vh];
+}
+
+// bf(silu(bf(conv))) of one channel from its taps and weights.
+__device__ __forceinline__ float gdn_conv(const float (&x)[4], const float (&w)[4]) {
+  float a = __fmul_rn(w[0], x[0]);
+  a = __fadd_rn(a, __fmul_rn(w[1], x[1]));
+  a = __fadd_rn(a, __fmul_rn(w[2], x[2]));
+  a = __fadd_rn(a, __fmul_rn(w[3], x[3]));
   return bf(silu(bf(a)));
 }
 
-__global__ void __launch_bounds__(128) gdn_step_kernel(const __grid_constant__ GdnParams p) {
-  extern __shared__ __align__(16) float R[];  // [128][128] this head's state
-  __shared__ float s_q[GDN_DK], s_k[GDN_DK], s4[4];
-  const int vh = blockIdx.x, kh = vh / 3, j = threadIdx.x;
-  float* state = p.state + (size_t)vh * GDN_DK * GDN_DK;
-  for (int i = 0; i < GDN_DK; ++i) R[i * GDN_DK + j] = state[i * GDN_DK + j];
+__global__ void __launch_bounds__(GDN_STEP_THREADS) gdn_step_kernel(const __grid_constant__ GdnParams p) {
+  __shared__ __align__(16) float s_q[GDN_DK];
+  __shared__ __align__(16) float s_k[GDN_DK];
+  __shared__ float s_v[GDN_DK];
+  __shared__ float s_part[2][4][GDN_DK];  // the four group sums of the two inner products
+  __shared__ float s_sq[2][4], s_so[4];   // per-warp squares: query, key; core
+  const int t = threadIdx.x, j = t & (GDN_DK - 1), grp = t >> 7, warp = t >> 5, lane = t & 31;
+  const int vh = blockIdx.x, kh = vh / 3, i0 = 32 * grp;
+  float* state = p.state + (size_t)vh * GDN_DK * GDN_DK + (size_t)i0 * GDN_DK + j;  // element (i0, j)
+  float R[32];  // state rows i0..i0+31 of column j
+#pragma unroll
+  for (int r = 0; r < 32; ++r) R[r] = state[r * GDN_DK];
+  // group 0: query channel j of the key head; 1: key channel; 2: value channel; 3: none
+  const int c = grp == 0   ? GDN_DK * kh + j
+                : grp == 1 ? GDN_QK_HEADS * GDN_DK + GDN_DK * kh + j
+                : grp == 2 ? 2 * GDN_QK_HEADS * GDN_DK + GDN_DK * vh + j
+                           : -1;
+  float cw[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  if (c >= 0) {
+    const uint2 w4 = __ldg(reinterpret_cast<const uint2*>(p.conv_w + (size_t)c * 4));
+    cw[0] = __uint_as_float(w4.x << 16), cw[1] = __uint_as_float(w4.x & 0xffff0000u);
+    cw[2] = __uint_as_float(w4.y << 16), cw[3] = __uint_as_float(w4.y & 0xffff0000u);
+  }
   const float a_log = bf16f(p.a_log[vh]), dt_bias = bf16f(p.dt_bias[vh]);
+  GdnRowIn cur;
+  gdn_load_row(p, 0, c, vh, j, cur);
   for (int row = 0; row < p.M; ++row) {
-    // 03_GATED_DELTANET.md:102-116: q/k of the key head, the value, beta and the decay.
-    const float q = gdn_conv(p, row, GDN_DK * kh + j);
-    const float k = gdn_conv(p, row, GDN_QK_HEADS * GDN_DK + GDN_DK * kh + j);
-    const float v = gdn_conv(p, row, 2 * GDN_QK_HEADS * GDN_DK + GDN_DK * vh + j);
-    const float rq = rsqrtf(__fadd_rn(squares128(q, s4), 1e-6f));
-    const float rk = rsqrtf(__fadd_rn(squares128(k, s4), 1e-6f));
-    __syncthreads();  // the previous row's readers of s_q / s_k are done
-    s_q[j] = __fmul_rn(__fmul_rn(q, rq), 0.08838834764831845f);
-    s_k[j] = __fmul_rn(k, rk);
+    GdnRowIn nxt;
+    if (row + 1 < p.M) gdn_load_row(p, row + 1, c, vh, j, nxt);
+    // 03_GATED_DELTANET.md:102-116: the convolved channel; squares of query and key per warp.
+    const float y = c >= 0 ? gdn_conv(cur.x, cw) : 0.0f;
+    if (grp < 2) {
+      const float g = xor_sum32(__fmul_rn(y, y));
+      if (lane == 0) s_sq[grp][warp & 3] = g;
+    } else if (grp == 2) {
+      s_v[j] = y;
+    }
     __syncthreads();
-    const float* g = p.gates + (size_t)row * 2 * GDN_V_HEADS;
-    const float beta = bf(sigmoid(g[vh]));
-    const float log_decay = __fmul_rn(-expf(a_log), softplus(__fadd_rn(g[GDN_V_HEADS + vh], dt_bias)));
+    if (grp == 0)
+      s_q[j] = __fmul_rn(__fmul_rn(y, rsqrtf(__fadd_rn(sum4(s_sq[0]), 1e-6f))), 0.08838834764831845f);
+    else if (grp == 1)
+      s_k[j] = __fmul_rn(y, rsqrtf(__fadd_rn(sum4(s_sq[1]), 1e-6f)));
+    const float beta = bf(sigmoid(cur.gb));
+    const float log_decay = __fmul_rn(-expf(a_log), softplus(__fadd_rn(cur.ga, dt_bias)));
     const float decay = expf(log_decay);
-    // 03_GATED_DELTANET.md:123-143: column j of the state.
-    float part[4];
+    __syncthreads();
+    // 03_GATED_DELTANET.md:123-143: rows i0..i0+31 of column j.
+    const float4* k4 = reinterpret_cast<const float4*>(s_k + i0);
+    const float4* q4 = reinterpret_cast<const float4*>(s_q + i0);
+    float acc = 0.0f;
 #pragma unroll
-    for (int grp = 0; grp < 4; ++grp) {
-      float acc = 0.0f;
-      for (int r = 0; r < 32; ++r) {
-        const int i = 32 * grp + r;
-        const float x = __fmul_rn(R[i * GDN_DK + j], decay);
-        R[i * GDN_DK + j] = x;
-        acc = __fadd_rn(acc, __fmul_rn(x, s_k[i]));
-      }
-      part[grp] = acc;
-    }
-    const float correction = __fmul_rn(__fsub_rn(v, sum4(part)), beta);
+    for (int r4 = 0; r4 < 8; ++r4) {
+      const float4 kk = k4[r4];
+      const float kv[4] = {kk.x, kk.y, kk.z, kk.w};
 #pragma unroll
-    for (int grp = 0; grp < 4; ++grp) {
-      float acc = 0.0f;
-      for (int r = 0; r < 32; ++r) {
-        const int i = 32 * grp + r;
-        const float x = __fadd_rn(R[i * GDN_DK + j], __fmul_rn(s_k[i], correction));
-        R[i * GDN_DK + j] = x;
-        acc = __fadd_rn(acc, __fmul_rn(x, s_q[i]));
+      for (int e = 0; e < 4; ++e) {
+        R[4 * r4 + e] = __fmul_rn(R[4 * r4 + e], decay);
+        acc = __fadd_rn(acc, __fmul_rn(R[4 * r4 + e], kv[e]));
       }
-      part[grp] = acc;
     }
-    const float core = bf(sum4(part));
+    s_part[0][grp][j] = acc;
+    __syncthreads();
+    const float correction =
+        __fmul_rn(__fsub_rn(s_v[j], sum4(s_part[0][0][j], s_part[0][1][j], s_part[0][2][j], s_part[0][3][j])), beta);
+    acc = 0.0f;
+#pragma unroll
+    for (int r4 = 0; r4 < 8; ++r4) {
+      const float4 kk = k4[r4], qq = q4[r4];
+      const float kv[4] = {kk.x, kk.y, kk.z, kk.w}, qv[4] = {qq.x, qq.y, qq.z, qq.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        R[4 * r4 + e] = __fadd_rn(R[4 * r4 + e], __fmul_rn(kv[e], correction));
+        acc = __fadd_rn(acc, __fmul_rn(R[4 * r4 + e], qv[e]));
+      }
+    }
+    s_part[1][grp][j] = acc;
+    __syncthreads();
     // 03_GATED_DELTANET.md:145-155: the output norm (weight used directly) and the z gate.
-    const float inv = rsqrtf(__fadd_rn(__fdiv_rn(squares128(core, s4), 128.0f), p.eps));
-    const float normalized = bf(__fmul_rn(bf16f(p.norm_w[j]), bf(__fmul_rn(core, inv))));
-    const float zz = p.z[(size_t)row * GDN_V_HEADS * GDN_DK + GDN_DK * vh + j];
-    p.out[(size_t)row * GDN_V_HEADS * GDN_DK + GDN_DK * vh + j] = bf(__fmul_rn(normalized, silu(zz)));
+    float core = 0.0f;
+    if (grp == 0) {
+      core = bf(sum4(s_part[1][0][j], s_part[1][1][j], s_part[1][2][j], s_part[1][3][j]));
+      const float g = xor_sum32(__fmul_rn(core, core));
+      if (lane == 0) s_so[warp] = g;
+    }
+    __syncthreads();
+    if (grp == 0) {
+      const float inv = rsqrtf(__fadd_rn(__fdiv_rn(sum4(s_so), 128.0f), p.eps));
+      const float normalized = bf(__fmul_rn(bf16f(p.norm_w[j]), bf(__fmul_rn(core, inv))));
+      p.out[(size_t)row * GDN_V_HEADS * GDN_DK + GDN_DK * vh + j] = bf(__fmul_rn(normalized, silu(cur.z)));
+    }
     if (row + 1 == p.n_commit)
-      for (int i = 0; i < GDN_DK; ++i) state[i * GDN_DK + j] = R[i * GDN_DK + j];
+#pragma unroll
+      for (int r = 0; r < 32; ++r) state[r * GDN_DK] = R[r];
+    cur = nxt;
   }
 }
 
@@ -183,9 +260,12 @@ extern "C" YSKN_B200_API int yskn_b200_gdn_gates(const uint16_t* d_hidden, const
                                                 const uint16_t* d_wa, int M, int hidden, float* d_gates, void* stream) {
   if (!d_hidden || !d_inv_rms || !d_wb || !d_wa || !d_gates || M < 1 || hidden <= 0 || hidden % 1024)
     return fail(YSKN_EINVAL, "gdn_gates: null argument, M < 1 or hidden not a multiple of 1024");
-  if (M > 65535) return fail(YSKN_EINVAL, "gdn_gates: at most 65535 rows per call");
-  gdn_gates_kernel<<<dim3(2 * GDN_V_HEADS, M), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      d_hidden, d_inv_rms, d_wb, d_wa, hidden, d_gates);
+  if (((uintptr_t)d_hidden | (uintptr_t)d_wb | (uintptr_t)d_wa) & 15)
+    return fail(YSKN_EINVAL, "gdn_gates: hidden rows and weights must be 16-byte aligned");
+  const int groups = (M + GDN_GATE_ROWS - 1) / GDN_GATE_ROWS;
+  if (groups > 65535) return fail(YSKN_EINVAL, "gdn_gates: too many rows per call");
+  gdn_gates_kernel<<<dim3(2 * GDN_V_HEADS, groups), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      d_hidden, d_inv_rms, d_wb, d_wa, hidden, M, d_gates);
   return cuda_fail(cudaGetLastError(), "gdn_gates_kernel");
 }
 
@@ -196,19 +276,10 @@ extern "C" YSKN_B200_API int yskn_b200_gdn_step(const float* d_qkv, const float*
   if (!d_qkv || !d_z || !d_gates || !d_conv_w || !d_a_log || !d_dt_bias || !d_norm_w || !d_state || !d_history ||
       !d_out || M < 1 || n_commit < 0 || n_commit > M)
     return fail(YSKN_EINVAL, "gdn_step: null argument, M < 1 or n_commit outside 0..M");
-  static bool attr_set[64] = {};
-  constexpr int smem = GDN_DK * GDN_DK * sizeof(float);
-  int dev = 0;
-  if (cudaError_t e = cudaGetDevice(&dev)) return cuda_fail(e, "gdn_step: cudaGetDevice");
-  if (dev < 0 || dev >= 64) return fail(YSKN_EINVAL, "gdn_step: device index out of range");
-  if (!attr_set[dev]) {
-    if (cudaError_t e = cudaFuncSetAttribute(gdn_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem))
-      return cuda_fail(e, "gdn_step_kernel attributes");
-    attr_set[dev] = true;
-  }
+  if ((uintptr_t)d_conv_w & 7) return fail(YSKN_EINVAL, "gdn_step: convolution weights must be 8-byte aligned");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   GdnParams p{d_qkv, d_z, d_gates, d_conv_w, d_a_log, d_dt_bias, d_norm_w, eps, M, n_commit, d_state, d_history, d_out};
-  gdn_step_kernel<<<GDN_V_HEADS, 128, smem, st>>>(p);
+  gdn_step_kernel<<<GDN_V_HEADS, GDN_STEP_THREADS, 0, st>>>(p);
   if (cudaError_t e = cudaGetLastError()) return cuda_fail(e, "gdn_step_kernel");
   if (n_commit == 0) return YSKN_OK;
   // After the step (the same stream): every head has read the old history.
