@@ -819,6 +819,117 @@ def run_reference_gemm(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+STACK_METRIC = "27B-shape decode tok/s (64-layer hybrid stack, batch 1)"
+
+
+def stack_config(args):
+    return {"workload": "config 5: %d-layer hybrid stack (every 4th layer attention 24q/4kv x 256 with a 4-bit KV "
+                        "cache of %d rows, the rest Gated DeltaNet 16/48 heads x 128), hidden 5120, MLP 17408, vocab "
+                        "151936, bits=%d body and head, batch 1, greedy token fed back on the device" %
+                        (args.layers, args.stack_ctx, args.bits),
+            "global_batch": 1, "parallelism": "replicas" if int(os.environ.get("WORLD_SIZE", "1")) > 1 else "1 GPU",
+            "l2": "weights of one token (~13 GB) far exceed L2"}
+
+
+def run_stack(args, rank, world, local_rank):
+    """The whole decode pass per token as one CUDA graph (yskn_b200/stack.py). N > 1 runs
+    independent replicas (no tensor-parallel stack): value = tokens/s over all ranks."""
+    import torch
+    import yskn_b200 as Y
+    from yskn_b200 import stack as S
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    st = S.Stack(dev, layers=args.layers, ctx=args.stack_ctx, bits=args.bits, seed=1 + rank)
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        st.decode(stream)  # eager once: per-device set-up happens outside capture
+    torch.cuda.synchronize()
+    Y.check(Y.status(stream), "status")
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        st.decode(stream)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            graph.replay()
+    barrier()
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    ids = [v.strip() for v in visible.split(",") if v.strip()]
+    sampler = ClockSampler(ids[local_rank] if local_rank < len(ids) else str(local_rank))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with sampler:
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(stream)
+        barrier()
+    ms = e0.elapsed_time(e1)
+    # end to end: the host supplies each token (4 bytes from pinned memory) and reads the
+    # next one back (4 bytes) before the following step, as a chat loop does
+    tok_in = torch.zeros(1, dtype=torch.int32).pin_memory()
+    tok_out = torch.zeros(1, dtype=torch.int32).pin_memory()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e2.record(stream)
+        for _ in range(args.steps):
+            st.token.copy_(tok_in, non_blocking=True)
+            graph.replay()
+            tok_out.copy_(st.token, non_blocking=True)
+            stream.synchronize()
+            tok_in.copy_(tok_out)
+        e3.record(stream)
+    barrier()
+    e2e_ms = e2.elapsed_time(e3)
+    Y.check(Y.status(stream), "status")
+    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms, e2e_ms = t.tolist()
+    del graph
+    if rank != 0:
+        return
+    value = world * args.steps / (ms * 1e-3)
+    e2e_value = world * args.steps / (e2e_ms * 1e-3)
+    tb = S.token_bytes(args.layers, S.Stack.__init__.__defaults__[1], args.stack_ctx, args.bits)
+    peaks = measured_peaks()
+    peak = peaks.get("hbm_gbs", HBM_FALLBACK_GBS)
+    achieved = tb / (ms / args.steps * 1e-3) / 1e9
+    cpu = None
+    if world == 1 and not args.skip_cpu:
+        W = make_weights(args.bits)
+        prepare_cpu(W, args.bits)
+        xs = make_inputs(1)
+        threads = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        n, nbytes = 0, 0
+        while time.perf_counter() - t0 < 10.0 or n < 1:
+            nbytes += cpu_layer_step(W, xs, 1.0, threads)
+            n += 1
+        dt = time.perf_counter() - t0
+        cpu = {"value": (nbytes / dt) / tb, "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": "%d full layer-set steps of the CPU operator port (%.1f s), its code bytes/s divided by "
+                         "one token's bytes (linear operators only; no mixer, attention or head work)" % (n, dt)}
+    line = {"metric": STACK_METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "i8", "data": "synthetic (seeded random codes and weights)",
+            "config": stack_config(args),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "bytes_per_token": tb,
+                         "kernel": "the whole decode pass (all kernels of one token), algorithmic bytes per token",
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
+            "gpu_launches": args.steps * st.launches_per_token(),
+            "clocks": sampler.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -827,7 +938,9 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--bits", type=int, default=8, choices=[6, 8])
     ap.add_argument("--skip-cpu", action="store_true")
-    ap.add_argument("--workload", default="linear", choices=["linear", "kv4", "gemm"])
+    ap.add_argument("--workload", default="linear", choices=["linear", "kv4", "gemm", "stack"])
+    ap.add_argument("--layers", type=int, default=64, help="stack: layers (every fourth attention)")
+    ap.add_argument("--stack-ctx", type=int, default=4096, help="stack: KV cache rows per attention layer")
     ap.add_argument("--gemm-m", type=int, default=4096, help="gemm: activation rows (4096 prefill, 8 verify)")
     ap.add_argument("--ctx", type=int, default=32768, help="kv4: cache rows per layer")
     ap.add_argument("--kv-splits", type=int, default=-1, help="kv4: 0 reference schedule, -1 one wave over the SMs")
@@ -845,7 +958,8 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local_rank))
     try:
-        {"kv4": run_kv, "gemm": run_gemm}.get(args.workload, run_b200)(args, rank, world, local_rank)
+        {"kv4": run_kv, "gemm": run_gemm, "stack": run_stack}.get(args.workload, run_b200)(args, rank, world,
+                                                                                              local_rank)
     finally:
         if world > 1:
             import torch

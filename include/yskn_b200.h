@@ -253,6 +253,12 @@ YSKN_B200_API int yskn_b200_gdn_step(const float* d_qkv, const float* d_z, const
                                      uint16_t* d_history,
                                      float* d_out, void* stream);
 
+/* bf16 -> f32 copy of n values (exact): an operator's f32 input from a bf16 producer, such as
+ * the attention output before o_proj (the reference quantises that bf16 vector directly,
+ * docs/spec/04_ATTENTION.md; the operator here takes f32 input). No counterpart of its own
+ * in the reference. */
+YSKN_B200_API int yskn_b200_widen_bf16(const uint16_t* d_in, int64_t n, float* d_out, void* stream);
+
 /* Exact weighted integer sums (the operator core). Replaces
  * crates/yskn-engine/src/model.rs:948-962 `Compute::weighted_sums` (bit-identical to
  * crates/yskn-ref/src/compressed_linear.rs:205-252) and the reference's launch_lnord /

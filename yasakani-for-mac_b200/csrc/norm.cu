@@ -88,9 +88,21 @@ __global__ void __launch_bounds__(256) gated_product_kernel(const float* gate, c
   }
 }
 
+// bf16 -> f32, exact (an operator's input from a bf16 producer such as the attention).
+__global__ void __launch_bounds__(256) widen_bf16_kernel(const uint16_t* in, int64_t n, float* out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = bf16_to_f32(in[i]);
+}
+
 }  // namespace yskn
 
 using namespace yskn;
+
+extern "C" YSKN_B200_API int yskn_b200_widen_bf16(const uint16_t* d_in, int64_t n, float* d_out, void* stream) {
+  if (!d_in || !d_out || n < 1 || n > (int64_t)INT32_MAX * 256) return fail(YSKN_EINVAL, "widen_bf16: bad argument");
+  widen_bf16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(d_in, n, d_out);
+  return cuda_fail(cudaGetLastError(), "widen_bf16_kernel");
+}
 
 extern "C" YSKN_B200_API int yskn_b200_gated_product(const float* d_gate, const float* d_up, int M, int n,
                                                     float* d_out, void* stream) {

@@ -73,6 +73,7 @@ _SIGNATURES = {
     "yskn_b200_head_select": (_i, [_vp, _i, _i, _vp, _vp, _vp, _vp]),
     "yskn_b200_attention_prep": (_i, [_vp] * 6 + [C.c_float, _i, _i, _i] + [_vp] * 5),
     "yskn_b200_gdn_gates": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp, _vp]),
+    "yskn_b200_widen_bf16": (_i, [_vp, C.c_int64, _vp, _vp]),
     "yskn_b200_gdn_step": (_i, [_vp] * 7 + [C.c_float, _i, _i, _vp, _vp, _vp, _vp]),
 }
 
@@ -339,6 +340,11 @@ def attention_prep(q, k, v, q_norm, k_norm, positions, eps, query, gate, k_rot, 
     check(lib().yskn_b200_attention_prep(_ptr(q), _ptr(k), _ptr(v), _ptr(q_norm), _ptr(k_norm), _ptr(positions), eps,
                                          q.shape[0], q.shape[1], k.shape[1], _ptr(query), _ptr(gate), _ptr(k_rot),
                                          _ptr(v_rot), _stream(stream)), "attention_prep")
+
+
+def widen_bf16(src, out, stream=None):
+    """out (f32) = the bf16 values of src (16-bit tensor), element count of src."""
+    check(lib().yskn_b200_widen_bf16(_ptr(src), src.numel(), _ptr(out), _stream(stream)), "widen_bf16")
 
 
 def gdn_gates(hidden, inv_rms, wb, wa, gates, stream=None):

@@ -1,0 +1,199 @@
+"""The 27B-shape decode pass at batch 1, built from the library's calls.
+
+The hybrid stack of the reference's headline model shape: `layers` layers, every fourth a
+full-attention layer (24 query heads of 256 with gates, 4 KV heads, a 4-bit quantised
+cache) and the others Gated DeltaNet layers (16 q/k and 48 value heads of 128, recurrent
+state), each followed by the gated MLP; hidden 5120, MLP 17408, coded embedding and head
+over `vocab` rows; every compressed matrix at one trellis width (bits=8: 4 bits per
+weight). One token runs as the reference's decode pass does (src/engine35.cpp:1268-1284,
+layer order src/engine35.cpp:773-799): embedding row -> per layer (residual + norm ->
+mixer -> residual + norm -> MLP) -> final norm -> head logits -> greedy token, the token
+fed back on the device, so the pass is one CUDA graph per token.
+
+Weights are seeded random code words generated on the device (every bit string is a
+valid code) with synthetic value tables and row scales; norms, gates and convolution
+weights are seeded bf16; the KV caches hold `ctx` synthetic rows and each token encodes
+its own K/V row at position `ctx`. No model file is shipped with the reference.
+"""
+import numpy as np
+
+import yskn_b200 as Y
+from yskn_b200 import synthetic
+
+HIDDEN, FFN = 5120, 17408
+N_QH, N_KVH, HEAD = 24, 4, 256
+QKV, ZDIM = 10240, 6144
+EPS = 1e-6
+SIGN_RULE = "mulberry32_7919_13"
+
+
+def layer_kinds(layers):
+    """'attn' for every fourth layer (3, 7, ...), else 'gdn' (src/engine35.cpp:255-263)."""
+    return ["attn" if i % 4 == 3 else "gdn" for i in range(layers)]
+
+
+def weight_bytes(layers, vocab, bits=8):
+    """Code bytes of every compressed matrix of the stack (embedding and head included)."""
+    per = {"gdn": [(QKV, HIDDEN), (ZDIM, HIDDEN), (HIDDEN, ZDIM)],
+           "attn": [(N_QH * 2 * HEAD, HIDDEN), (N_KVH * HEAD, HIDDEN), (N_KVH * HEAD, HIDDEN), (HIDDEN, N_QH * HEAD)]}
+    mlp = [(FFN, HIDDEN), (FFN, HIDDEN), (HIDDEN, FFN)]
+    total = 2 * vocab * HIDDEN * bits // 16
+    for k in layer_kinds(layers):
+        total += sum(r * c * bits // 16 for r, c in per[k] + mlp)
+    return total
+
+
+def token_bytes(layers, vocab, ctx, bits=8):
+    """Algorithmic bytes one token must move: every compressed matrix's codes except the
+    embedding table (one row of it), the dense bf16 gate weights, each GDN state read and
+    written, each attention layer's K/V cache rows (1,056 bytes per row: 4 heads x K, V x
+    (128 + 4)), one new row encoded per attention layer."""
+    kinds = layer_kinds(layers)
+    gdn, attn = kinds.count("gdn"), kinds.count("attn")
+    codes = weight_bytes(layers, vocab, bits) - vocab * HIDDEN * bits // 16 + HIDDEN * bits // 16
+    return codes + gdn * (2 * 2 * 48 * HIDDEN + 2 * 4 * 48 * 128 * 128) + attn * 1056 * (ctx + 1)
+
+
+class Stack:
+    """Seeded weights, caches, states and buffers of the stack on one device."""
+
+    def __init__(self, device, layers=64, vocab=151936, ctx=8192, bits=8, seed=1):
+        import torch
+        self.torch, self.dev = torch, device
+        self.layers, self.vocab, self.ctx, self.bits = layers, vocab, ctx, bits
+        self.gen = torch.Generator(device=device)
+        self.gen.manual_seed(seed)
+        self.rng = np.random.default_rng(seed)
+        self._signs = {}
+        self._keep = []
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(device)  # noqa: E731
+        bfb = lambda a: t(self._bf16(a).view(np.int16))  # noqa: E731
+        self.kinds = layer_kinds(layers)
+        self.L = []
+        for i, kind in enumerate(self.kinds):
+            L = {"kind": kind, "in_norm": bfb(self._normal(HIDDEN) * 0.1), "post_norm": bfb(self._normal(HIDDEN) * 0.1),
+                 "gate": self._matrix(FFN, HIDDEN), "up": self._matrix(FFN, HIDDEN), "down": self._matrix(HIDDEN, FFN)}
+            if kind == "gdn":
+                L.update(qkv=self._matrix(QKV, HIDDEN), z=self._matrix(ZDIM, HIDDEN), out=self._matrix(HIDDEN, ZDIM),
+                         wb=bfb(self._normal(48 * HIDDEN).reshape(48, HIDDEN) * 0.02),
+                         wa=bfb(self._normal(48 * HIDDEN).reshape(48, HIDDEN) * 0.02),
+                         conv=bfb(self._normal(QKV * 4).reshape(QKV, 4) * 0.5),
+                         a_log=bfb(self._normal(48) * 0.5), dt_bias=bfb(self._normal(48) * 0.5),
+                         norm_w=bfb(1.0 + self._normal(128) * 0.1),
+                         state=torch.zeros((48, 128, 128), dtype=torch.float32, device=device),
+                         history=torch.zeros((3, QKV), dtype=torch.int16, device=device))
+            else:
+                cap = ctx + 1
+                cache = torch.randint(-2 ** 31, 2 ** 31, (2, N_KVH, cap, 32), dtype=torch.int32, device=device,
+                                      generator=self.gen)
+                scales = 0.02 + 0.18 * torch.rand((2, N_KVH, cap), device=device, generator=self.gen)
+                L.update(q=self._matrix(N_QH * 2 * HEAD, HIDDEN), k=self._matrix(N_KVH * HEAD, HIDDEN),
+                         v=self._matrix(N_KVH * HEAD, HIDDEN), o=self._matrix(HIDDEN, N_QH * HEAD),
+                         q_norm=bfb(self._normal(HEAD) * 0.1), k_norm=bfb(self._normal(HEAD) * 0.1),
+                         cache=cache, scales=scales)
+            self.L.append(L)
+        self.final_norm = bfb(self._normal(HIDDEN) * 0.1)
+        self.head = self._matrix(vocab, HIDDEN, rotate=False)
+        emb_codes = torch.randint(-2 ** 31, 2 ** 31, (vocab * (HIDDEN // 256) * 4 * bits,), dtype=torch.int32,
+                                  device=device, generator=self.gen)
+        lut16, sc16 = synthetic.model_tables(vocab, int(self.rng.integers(1 << 30)))
+        self._keep.append(emb_codes)
+        self.embedding = Y.Embedding([(emb_codes, bits, lut16, sc16)], vocab, HIDDEN, self._sign(0, HIDDEN))
+        # the synthetic KV profile (the codebook of synthetic.kv_codebook_bf16): one table per
+        # (side, head) group, multipliers 0.9 / 1.0 / 1.1
+        codes = ((np.arange(256) * 73 + 19) % 2049 - 1024).astype(np.int16)
+        self.kv_tables = t(np.tile(codes, (2 * N_KVH, 1)))
+        self.kv_gains = t(np.full(2 * N_KVH, 257.0 / 256.0, np.float32))
+        self.kv_mults = t(np.array([0.9, 1.0, 1.1], np.float32))
+        self.kv_groups = t(np.arange(2 * N_KVH, dtype=np.int32))
+        self.kv_dest = t(np.array([h * (ctx + 1) + ctx for h in range(2 * N_KVH)], np.int64))
+        self.kv_book = t(np.tile(synthetic.kv_codebook_bf16(), (N_KVH, 1)).view(np.int16))
+        self.positions = t(np.array([ctx], np.int32))
+        # activations
+        f32 = lambda *s: torch.zeros(s, dtype=torch.float32, device=device)  # noqa: E731
+        i16 = lambda *s: torch.zeros(s, dtype=torch.int16, device=device)  # noqa: E731
+        self.token = torch.zeros(1, dtype=torch.int32, device=device)
+        self.h, self.xg = i16(1, HIDDEN), i16(1, HIDDEN)
+        self.x, self.inv, self.proj = f32(1, HIDDEN), f32(1), f32(1, HIDDEN)
+        self.qkv_o, self.z_o, self.gates, self.g_out = f32(1, QKV), f32(1, ZDIM), f32(1, 96), f32(1, ZDIM)
+        self.q_o, self.k_o, self.v_o = f32(1, N_QH, 2 * HEAD), f32(1, N_KVH, HEAD), f32(1, N_KVH, HEAD)
+        self.query, self.a_gate, self.a_out = i16(1, N_QH, HEAD), i16(1, N_QH, HEAD), i16(1, N_QH, HEAD)
+        self.kv_rows = f32(2 * N_KVH, HEAD)
+        self.a_in = f32(1, N_QH * HEAD)
+        self.g_o, self.u_o, self.m_o = f32(1, FFN), f32(1, FFN), f32(1, FFN)
+        self.logits = f32(1, vocab)
+        first = {k: next(L for L in self.L if L["kind"] == k) for k in set(self.kinds)}
+        sets = [[self.head], [first[self.kinds[0]]["gate"], first[self.kinds[0]]["up"]], [self.L[0]["down"]]]
+        if "gdn" in first:
+            sets += [[first["gdn"]["qkv"], first["gdn"]["z"]], [first["gdn"]["out"]]]
+        if "attn" in first:
+            sets += [[first["attn"]["q"], first["attn"]["k"], first["attn"]["v"]], [first["attn"]["o"]]]
+        self.work = torch.empty(max(Y.linear_work_bytes(s, 1) for s in sets), dtype=torch.uint8, device=device)
+        self.kv_work = torch.empty(max(16, Y.kv4_attention_work_bytes(1, N_QH, ctx + 1, 0)), dtype=torch.uint8,
+                                   device=device)
+
+    def _normal(self, n):
+        return self.rng.standard_normal(n).astype(np.float32)
+
+    @staticmethod
+    def _bf16(a):
+        u = np.asarray(a, np.float32).view(np.uint32).astype(np.uint64)
+        return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+    def _sign(self, offset, n):
+        if (offset, n) not in self._signs:
+            self._signs[(offset, n)] = Y.signs(SIGN_RULE, 7, offset, n)
+        return self._signs[(offset, n)]
+
+    def _matrix(self, rows, cols, rotate=True):
+        torch = self.torch
+        words = torch.randint(-2 ** 31, 2 ** 31, (rows * (cols // 256) * 4 * self.bits,), dtype=torch.int32,
+                              device=self.dev, generator=self.gen)
+        lut16, sc16 = synthetic.model_tables(rows, int(self.rng.integers(1 << 30)))
+        self._keep.append(words)
+        return Y.Matrix(words, "warp", rows, rows, cols, self.bits, lut16, sc16, self._sign(0, cols),
+                        self._sign(cols, rows) if rotate else None)
+
+    def decode(self, stream=None):
+        """One token: reads self.token, writes the next greedy token into it."""
+        s = stream
+        self.embedding.lookup(self.token, self.h, stream=s)
+        proj = None
+        for L in self.L:
+            Y.residual_prepare(self.h, proj, L["in_norm"], EPS, self.x, self.inv, gate=self.xg, stream=s)
+            if L["kind"] == "gdn":
+                Y.linear([L["qkv"], L["z"]], self.x, self.work, [self.qkv_o, self.z_o], inv_rms=self.inv, stream=s)
+                Y.gdn_gates(self.xg, self.inv, L["wb"], L["wa"], self.gates, stream=s)
+                Y.gdn_step(self.qkv_o, self.z_o, self.gates, L["conv"], L["a_log"], L["dt_bias"], L["norm_w"], EPS,
+                           L["state"], L["history"], self.g_out, stream=s)
+                Y.linear([L["out"]], self.g_out, self.work, [self.proj], stream=s)
+            else:
+                Y.linear([L["q"], L["k"], L["v"]], self.x, self.work, [self.q_o, self.k_o, self.v_o],
+                         inv_rms=self.inv, stream=s)
+                Y.attention_prep(self.q_o, self.k_o, self.v_o, L["q_norm"], L["k_norm"], self.positions, EPS,
+                                 self.query, self.a_gate, self.kv_rows[:N_KVH].view(1, N_KVH, HEAD),
+                                 self.kv_rows[N_KVH:].view(1, N_KVH, HEAD), stream=s)
+                cache, scales = L["cache"], L["scales"]
+                Y.kv_encode(self.kv_rows, self.kv_groups, self.kv_tables, self.kv_gains, self.kv_mults, 4, True,
+                            cache.view(-1, 32), scales.view(-1), dest=self.kv_dest, stream=s)
+                Y.kv4_attention(self.query, cache[0], scales[0], cache[1], scales[1], self.kv_book, self.kv_book,
+                                self.ctx + 1, self.kv_work, self.a_out, gate=self.a_gate, stream=s)
+                Y.widen_bf16(self.a_out.view(1, -1), self.a_in, stream=s)
+                Y.linear([L["o"]], self.a_in, self.work, [self.proj], stream=s)
+            Y.residual_prepare(self.h, self.proj, L["post_norm"], EPS, self.x, self.inv, stream=s)
+            Y.linear([L["gate"], L["up"]], self.x, self.work, [self.g_o, self.u_o], inv_rms=self.inv, stream=s)
+            Y.gated_product(self.g_o, self.u_o, self.m_o, stream=s)
+            Y.linear([L["down"]], self.m_o, self.work, [self.proj], stream=s)
+            proj = self.proj
+        Y.residual_prepare(self.h, proj, self.final_norm, EPS, self.x, self.inv, stream=s)
+        Y.linear([self.head], self.x, self.work, [self.logits], inv_rms=self.inv, stream=s)
+        Y.head_select(self.logits, token=self.token, stream=s)
+
+    def launches_per_token(self):
+        """This library's kernel launches in decode(), one per call except the GDN step
+        (step + history): embedding, final norm, head operator, head select; per layer the
+        input norm and the MLP (post norm, gate/up operator, gated product, down operator);
+        GDN mixer: operator, gates, step (2), out operator; attention mixer: operator,
+        preparation, KV encode, attention, widening, o operator."""
+        gdn, attn = self.kinds.count("gdn"), self.kinds.count("attn")
+        return 4 + self.layers * 5 + gdn * 5 + attn * 6

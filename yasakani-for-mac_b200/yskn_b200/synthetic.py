@@ -41,16 +41,21 @@ def _unit(seed, n):
     return (stream64(seed, n) >> np.uint64(11)).astype(np.float64) / 2.0 ** 53
 
 
+def model_tables(physical_rows, seed):
+    """(fp16 table bits [8192], fp16 row scale bits [physical_rows]) of model_matrix."""
+    r = np.sqrt(-2.0 * np.log(np.maximum(_unit(seed + 1, 4096), 1e-300)))
+    u2 = _unit(seed + 2, 4096)
+    table = np.concatenate([r * np.cos(2 * np.pi * u2), r * np.sin(2 * np.pi * u2)]).astype(np.float32)
+    scales = (0.02 * (1.0 + 0.2 * (_unit(seed + 3, physical_rows) - 0.5))).astype(np.float32)
+    return f16_bits(table), f16_bits(scales)
+
+
 def model_matrix(rows, cols, bits, seed, physical_rows=None):
     """(warp-layout code words u32, fp16 table bits [8192], fp16 row scale bits [phys])."""
     phys = physical_rows or rows
     n_words = phys * (cols // 256) * 4 * bits
     words = (stream64(seed, n_words) & np.uint64(0xFFFFFFFF)).astype(np.uint32)
-    r = np.sqrt(-2.0 * np.log(np.maximum(_unit(seed + 1, 4096), 1e-300)))
-    u2 = _unit(seed + 2, 4096)
-    table = np.concatenate([r * np.cos(2 * np.pi * u2), r * np.sin(2 * np.pi * u2)]).astype(np.float32)
-    scales = (0.02 * (1.0 + 0.2 * (_unit(seed + 3, phys) - 0.5))).astype(np.float32)
-    return words, f16_bits(table), f16_bits(scales)
+    return (words,) + model_tables(phys, seed)
 
 
 def normal(seed, n):
