@@ -60,18 +60,28 @@ __global__ void __launch_bounds__(HEAD_THREADS) head_select_kernel(const float* 
   int id[HEAD_K];
 #pragma unroll
   for (int k = 0; k < HEAD_K; ++k) v[k] = -FLT_MAX, id[k] = INT_MAX;
-  for (int i = threadIdx.x; i < n; i += HEAD_THREADS) {
-    const float x = __ldg(row + i);
-    if (!before(x, i, v[HEAD_K - 1], id[HEAD_K - 1])) continue;  // NaN and -inf stop here
-    float cv = x;
-    int ci = i;
+  constexpr int BATCH = 8;  // loads in flight per thread
+  for (int i0 = threadIdx.x; i0 < n; i0 += BATCH * HEAD_THREADS) {
+    float xs[BATCH];
 #pragma unroll
-    for (int k = 0; k < HEAD_K; ++k) {  // insert, keeping the list in order
-      if (before(cv, ci, v[k], id[k])) {
-        const float tv = v[k];
-        const int ti = id[k];
-        v[k] = cv, id[k] = ci;
-        cv = tv, ci = ti;
+    for (int u = 0; u < BATCH; ++u) {
+      const int i = i0 + u * HEAD_THREADS;
+      xs[u] = i < n ? __ldg(row + i) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < BATCH; ++u) {  // in increasing index order, as one element at a time
+      const int i = i0 + u * HEAD_THREADS;
+      if (i >= n || !before(xs[u], i, v[HEAD_K - 1], id[HEAD_K - 1])) continue;  // NaN and -inf stop here
+      float cv = xs[u];
+      int ci = i;
+#pragma unroll
+      for (int k = 0; k < HEAD_K; ++k) {  // insert, keeping the list in order
+        if (before(cv, ci, v[k], id[k])) {
+          const float tv = v[k];
+          const int ti = id[k];
+          v[k] = cv, id[k] = ci;
+          cv = tv, ci = ti;
+        }
       }
     }
   }

@@ -14,11 +14,13 @@
 // (yskn_b200_linear's inv_rms), so the normalised vector is never formed, as in the
 // reference.
 //
-// B200 design: one 128-thread CTA per row. Thread t owns partial sum t of every 512-column
-// block (elements t, t+128, t+256, t+384), so the spec's reduction — four products
-// added from +0, an XOR butterfly over each group of 32 partials, the four group sums in
-// order — is a per-thread loop, one warp shuffle butterfly and one ordered add; every
-// element is read and written once.
+// B200 design: one 1024-thread CTA per row, eight 128-thread groups; group s takes the
+// 512-column blocks s, s+8, ... and its thread t owns partial sum t of each (elements t,
+// t+128, t+256, t+384), so the spec's reduction — four products added from +0, an XOR
+// butterfly over each group of 32 partials — is a per-thread loop and one warp shuffle
+// butterfly, all blocks of a row at once (a decode row is latency-bound); the group sums
+// wait in shared memory and one thread adds them in the spec's order (four per block from
+// +0, blocks in order). Every element is read and written once.
 #include <cuda_bf16.h>
 
 #include "common.cuh"
@@ -26,21 +28,20 @@
 namespace yskn {
 
 constexpr int NORM_THREADS = 128;
+constexpr int NORM_GROUPS = 8;  // 128-thread groups per CTA
 
 __device__ __forceinline__ float bf16_to_f32(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
 __device__ __forceinline__ uint16_t f32_to_bf16(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }
 
-__global__ void __launch_bounds__(NORM_THREADS) residual_prepare_kernel(uint16_t* hidden, const float* projection,
-                                                                        const uint16_t* norm_weight, int cols,
-                                                                        float eps, float* input, float* inv_rms,
-                                                                        uint16_t* gate) {
-  __shared__ float s_group[NORM_THREADS / 32];
-  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+__global__ void __launch_bounds__(NORM_THREADS * NORM_GROUPS) residual_prepare_kernel(
+    uint16_t* hidden, const float* projection, const uint16_t* norm_weight, int cols, float eps, float* input,
+    float* inv_rms, uint16_t* gate) {
+  extern __shared__ float s_group[];  // [cols / 512][4] group sums
+  const int t = threadIdx.x & (NORM_THREADS - 1), lane = t & 31, warp = t >> 5, s = threadIdx.x / NORM_THREADS;
   const size_t row = blockIdx.x;
   uint16_t* h = hidden + row * cols;
   const float* pr = projection ? projection + row * cols : nullptr;
-  float total = 0.0f;  // meaningful in thread 0
-  for (int b = 0; b < cols; b += 512) {
+  for (int b = 512 * s; b < cols; b += 512 * NORM_GROUPS) {
     float partial = 0.0f;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -57,17 +58,19 @@ __global__ void __launch_bounds__(NORM_THREADS) residual_prepare_kernel(uint16_t
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) partial = __fadd_rn(partial, __shfl_xor_sync(0xffffffffu, partial, off));
-    if (lane == 0) s_group[warp] = partial;
-    __syncthreads();
-    if (t == 0) {
+    if (lane == 0) s_group[(b / 512) * 4 + warp] = partial;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float total = 0.0f;
+    for (int b = 0; b < cols / 512; ++b) {
       float block = 0.0f;
 #pragma unroll
-      for (int g = 0; g < NORM_THREADS / 32; ++g) block = __fadd_rn(block, s_group[g]);
+      for (int g = 0; g < NORM_THREADS / 32; ++g) block = __fadd_rn(block, s_group[4 * b + g]);
       total = __fadd_rn(total, block);
     }
-    __syncthreads();
+    inv_rms[row] = rsqrtf(__fadd_rn(__fdiv_rn(total, (float)cols), eps));
   }
-  if (t == 0) inv_rms[row] = rsqrtf(__fadd_rn(__fdiv_rn(total, (float)cols), eps));
 }
 
 // MLP nonlinear step (src/q35_kernels.cu:1402-1421, 113-116; docs/spec/
@@ -120,11 +123,13 @@ extern "C" YSKN_B200_API int yskn_b200_residual_prepare(uint16_t* d_hidden, cons
                                                        void* stream) {
   if (!d_hidden || !d_norm_weight || !d_input || !d_inv_rms || M < 1 || cols <= 0 || cols % 512)
     return fail(YSKN_EINVAL, "residual_prepare: null argument, M < 1, or cols not a multiple of 512");
+  if (cols > 512 * 3072) return fail(YSKN_EINVAL, "residual_prepare: cols above 1572864");
+  const size_t smem = (size_t)(cols / 512) * 4 * sizeof(float);  // at most 48 KB
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   for (int m0 = 0; m0 < M; m0 += 65535) {
     const int n = M - m0 < 65535 ? M - m0 : 65535;
     const size_t off = (size_t)m0 * cols;
-    residual_prepare_kernel<<<n, NORM_THREADS, 0, st>>>(d_hidden + off, d_projection ? d_projection + off : nullptr,
+    residual_prepare_kernel<<<n, NORM_THREADS * NORM_GROUPS, smem, st>>>(d_hidden + off, d_projection ? d_projection + off : nullptr,
                                                          d_norm_weight, cols, eps, d_input + off, d_inv_rms + m0,
                                                          d_gate ? d_gate + off : nullptr);
     if (cudaError_t e = cudaGetLastError()) return cuda_fail(e, "residual_prepare_kernel");

@@ -129,7 +129,7 @@ class Stack:
         if "attn" in first:
             sets += [[first["attn"]["q"], first["attn"]["k"], first["attn"]["v"]], [first["attn"]["o"]]]
         self.work = torch.empty(max(Y.linear_work_bytes(s, 1) for s in sets), dtype=torch.uint8, device=device)
-        self.kv_work = torch.empty(max(16, Y.kv4_attention_work_bytes(1, N_QH, ctx + 1, 0)), dtype=torch.uint8,
+        self.kv_work = torch.empty(max(16, Y.kv4_attention_work_bytes(1, N_QH, ctx + 1, -1)), dtype=torch.uint8,
                                    device=device)
 
     def _normal(self, n):
@@ -177,7 +177,7 @@ class Stack:
                 Y.kv_encode(self.kv_rows, self.kv_groups, self.kv_tables, self.kv_gains, self.kv_mults, 4, True,
                             cache.view(-1, 32), scales.view(-1), dest=self.kv_dest, stream=s)
                 Y.kv4_attention(self.query, cache[0], scales[0], cache[1], scales[1], self.kv_book, self.kv_book,
-                                self.ctx + 1, self.kv_work, self.a_out, gate=self.a_gate, stream=s)
+                                self.ctx + 1, self.kv_work, self.a_out, gate=self.a_gate, n_splits=-1, stream=s)
                 Y.widen_bf16(self.a_out.view(1, -1), self.a_in, stream=s)
                 Y.linear([L["o"]], self.a_in, self.work, [self.proj], stream=s)
             Y.residual_prepare(self.h, self.proj, L["post_norm"], EPS, self.x, self.inv, stream=s)
