@@ -61,6 +61,7 @@ struct PrepParams {
 constexpr int PREP_WARPS = 8;
 
 __global__ void __launch_bounds__(PREP_WARPS * 32) attention_prep_kernel(const __grid_constant__ PrepParams p) {
+  pdl_begin();
   const int lane = threadIdx.x & 31;
   const int heads = p.n_qh + 2 * p.n_kvh;  // query heads, then key heads, then value heads
   const int item = blockIdx.x * PREP_WARPS + (threadIdx.x >> 5);
@@ -150,7 +151,7 @@ extern "C" YSKN_B200_API int yskn_b200_attention_prep(const float* d_q, const fl
   PrepParams p{d_q, d_k, d_v, d_q_norm, d_k_norm, d_positions, eps, M, n_qh, n_kvh, d_query, d_gate, d_k_rot, d_v_rot};
   const int64_t items = (int64_t)M * (n_qh + 2 * n_kvh);
   if (items > (int64_t)INT32_MAX) return fail(YSKN_EINVAL, "attention_prep: too many rows");
-  attention_prep_kernel<<<(unsigned)((items + PREP_WARPS - 1) / PREP_WARPS), PREP_WARPS * 32, 0,
-                          reinterpret_cast<cudaStream_t>(stream)>>>(p);
-  return cuda_fail(cudaGetLastError(), "attention_prep_kernel");
+  return cuda_fail(launch_pdl(attention_prep_kernel, (unsigned)((items + PREP_WARPS - 1) / PREP_WARPS),
+                              PREP_WARPS * 32, 0, reinterpret_cast<cudaStream_t>(stream), p),
+                   "attention_prep_kernel");
 }

@@ -4,6 +4,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "yskn_b200.h"
 
@@ -25,6 +26,33 @@ enum : unsigned {
 unsigned* device_error_word();
 
 __device__ __forceinline__ void raise_device_error(unsigned* word, unsigned bits) { atomicOr(word, bits); }
+
+// Programmatic dependent launch for the small kernels between operators: launched with
+// launch_pdl, a kernel may be scheduled while the previous kernel of the stream drains; its
+// first statement, pdl_begin(), waits for that kernel's completion and memory (before any
+// access to memory) and then lets the next kernel of the stream be scheduled early, so a
+// following operator loads its tables while this kernel runs. Both are no-ops in a kernel
+// launched without the attribute.
+__device__ __forceinline__ void pdl_begin() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Thread-local error message (src/c_api.cpp:11-14 keeps one per thread as well).
 int fail(int code, const std::string& msg);

@@ -72,6 +72,7 @@ __device__ __forceinline__ float dot8(float acc, uint4 w, uint4 x) {
 __global__ void __launch_bounds__(128) gdn_gates_kernel(const uint16_t* x, const float* inv_rms, const uint16_t* wb,
                                                         const uint16_t* wa, int hidden, int M, float* gates) {
   __shared__ float s4[2][4];
+  pdl_begin();
   const int o = blockIdx.x, p = threadIdx.x;
   const uint16_t* w = o < GDN_V_HEADS ? wb + (size_t)o * hidden : wa + (size_t)(o - GDN_V_HEADS) * hidden;
   const int row0 = blockIdx.y * GDN_GATE_ROWS;
@@ -146,6 +147,7 @@ __global__ void __launch_bounds__(GDN_STEP_THREADS) gdn_step_kernel(const __grid
   __shared__ float s_v[GDN_DK];
   __shared__ float s_part[2][4][GDN_DK];  // the four group sums of the two inner products
   __shared__ float s_sq[2][4], s_so[4];   // per-warp squares: query, key; core
+  pdl_begin();
   const int t = threadIdx.x, j = t & (GDN_DK - 1), grp = t >> 7, warp = t >> 5, lane = t & 31;
   const int vh = blockIdx.x, kh = vh / 3, i0 = 32 * grp;
   float* state = p.state + (size_t)vh * GDN_DK * GDN_DK + (size_t)i0 * GDN_DK + j;  // element (i0, j)
@@ -242,6 +244,7 @@ __global__ void __launch_bounds__(GDN_STEP_THREADS) gdn_step_kernel(const __grid
 // row than a, so
 // each thread (one channel) reads every old value before it writes over it.
 __global__ void gdn_history_kernel(const float* qkv, int M, uint16_t* history) {
+  pdl_begin();
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= GDN_QKV) return;
 #pragma unroll
@@ -264,9 +267,10 @@ extern "C" YSKN_B200_API int yskn_b200_gdn_gates(const uint16_t* d_hidden, const
     return fail(YSKN_EINVAL, "gdn_gates: hidden rows and weights must be 16-byte aligned");
   const int groups = (M + GDN_GATE_ROWS - 1) / GDN_GATE_ROWS;
   if (groups > 65535) return fail(YSKN_EINVAL, "gdn_gates: too many rows per call");
-  gdn_gates_kernel<<<dim3(2 * GDN_V_HEADS, groups), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      d_hidden, d_inv_rms, d_wb, d_wa, hidden, M, d_gates);
-  return cuda_fail(cudaGetLastError(), "gdn_gates_kernel");
+  return cuda_fail(launch_pdl(gdn_gates_kernel, dim3(2 * GDN_V_HEADS, groups), 128, 0,
+                              reinterpret_cast<cudaStream_t>(stream), d_hidden, d_inv_rms, d_wb, d_wa, hidden, M,
+                              d_gates),
+                   "gdn_gates_kernel");
 }
 
 extern "C" YSKN_B200_API int yskn_b200_gdn_step(const float* d_qkv, const float* d_z, const float* d_gates,
@@ -279,10 +283,10 @@ extern "C" YSKN_B200_API int yskn_b200_gdn_step(const float* d_qkv, const float*
   if ((uintptr_t)d_conv_w & 7) return fail(YSKN_EINVAL, "gdn_step: convolution weights must be 8-byte aligned");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   GdnParams p{d_qkv, d_z, d_gates, d_conv_w, d_a_log, d_dt_bias, d_norm_w, eps, M, n_commit, d_state, d_history, d_out};
-  gdn_step_kernel<<<GDN_V_HEADS, GDN_STEP_THREADS, 0, st>>>(p);
-  if (cudaError_t e = cudaGetLastError()) return cuda_fail(e, "gdn_step_kernel");
+  if (cudaError_t e = launch_pdl(gdn_step_kernel, GDN_V_HEADS, GDN_STEP_THREADS, 0, st, p))
+    return cuda_fail(e, "gdn_step_kernel");
   if (n_commit == 0) return YSKN_OK;
   // After the step (the same stream): every head has read the old history.
-  gdn_history_kernel<<<(GDN_QKV + 255) / 256, 256, 0, st>>>(d_qkv, n_commit, d_history);
-  return cuda_fail(cudaGetLastError(), "gdn_history_kernel");
+  return cuda_fail(launch_pdl(gdn_history_kernel, (GDN_QKV + 255) / 256, 256, 0, st, d_qkv, n_commit, d_history),
+                   "gdn_history_kernel");
 }

@@ -55,6 +55,7 @@ __device__ Cand block_best(Cand c, Cand* s_warp) {
 __global__ void __launch_bounds__(HEAD_THREADS) head_select_kernel(const float* logits, int n, int32_t* token,
                                                                    float* top_v, int32_t* top_id) {
   __shared__ Cand s_warp[HEAD_THREADS / 32];
+  pdl_begin();
   const float* row = logits + (size_t)blockIdx.x * n;
   float v[HEAD_K];
   int id[HEAD_K];
@@ -112,10 +113,11 @@ extern "C" YSKN_B200_API int yskn_b200_head_select(const float* d_logits, int M,
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   for (int m0 = 0; m0 < M; m0 += 65535) {
     const int rows = M - m0 < 65535 ? M - m0 : 65535;
-    head_select_kernel<<<rows, HEAD_THREADS, 0, st>>>(d_logits + (size_t)m0 * n, n, d_token ? d_token + m0 : nullptr,
-                                                      d_top8_logits ? d_top8_logits + (size_t)m0 * HEAD_K : nullptr,
-                                                      d_top8_ids ? d_top8_ids + (size_t)m0 * HEAD_K : nullptr);
-    if (cudaError_t e = cudaGetLastError()) return cuda_fail(e, "head_select_kernel");
+    if (cudaError_t e = launch_pdl(head_select_kernel, rows, HEAD_THREADS, 0, st, d_logits + (size_t)m0 * n, n,
+                                   d_token ? d_token + m0 : nullptr,
+                                   d_top8_logits ? d_top8_logits + (size_t)m0 * HEAD_K : nullptr,
+                                   d_top8_ids ? d_top8_ids + (size_t)m0 * HEAD_K : nullptr))
+      return cuda_fail(e, "head_select_kernel");
   }
   return YSKN_OK;
 }

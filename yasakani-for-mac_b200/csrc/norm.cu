@@ -37,6 +37,7 @@ __global__ void __launch_bounds__(NORM_THREADS * NORM_GROUPS) residual_prepare_k
     uint16_t* hidden, const float* projection, const uint16_t* norm_weight, int cols, float eps, float* input,
     float* inv_rms, uint16_t* gate) {
   extern __shared__ float s_group[];  // [cols / 512][4] group sums
+  pdl_begin();
   const int t = threadIdx.x & (NORM_THREADS - 1), lane = t & 31, warp = t >> 5, s = threadIdx.x / NORM_THREADS;
   const size_t row = blockIdx.x;
   uint16_t* h = hidden + row * cols;
@@ -78,6 +79,7 @@ __global__ void __launch_bounds__(NORM_THREADS * NORM_GROUPS) residual_prepare_k
 // out = bf16(bf16(g / (1 + expf(-g))) * u), written as f32 so it is the down projection's
 // x directly. expf is CUDA's, as in the reference. Four elements per thread.
 __global__ void __launch_bounds__(256) gated_product_kernel(const float* gate, const float* up, int64_t n, float* out) {
+  pdl_begin();
   const int64_t i0 = 4 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x);
   if (i0 >= n) return;
   const int k_end = n - i0 < 4 ? (int)(n - i0) : 4;
@@ -93,6 +95,7 @@ __global__ void __launch_bounds__(256) gated_product_kernel(const float* gate, c
 
 // bf16 -> f32, exact (an operator's input from a bf16 producer such as the attention).
 __global__ void __launch_bounds__(256) widen_bf16_kernel(const uint16_t* in, int64_t n, float* out) {
+  pdl_begin();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) out[i] = bf16_to_f32(in[i]);
 }
@@ -103,8 +106,9 @@ using namespace yskn;
 
 extern "C" YSKN_B200_API int yskn_b200_widen_bf16(const uint16_t* d_in, int64_t n, float* d_out, void* stream) {
   if (!d_in || !d_out || n < 1 || n > (int64_t)INT32_MAX * 256) return fail(YSKN_EINVAL, "widen_bf16: bad argument");
-  widen_bf16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(d_in, n, d_out);
-  return cuda_fail(cudaGetLastError(), "widen_bf16_kernel");
+  return cuda_fail(launch_pdl(widen_bf16_kernel, (unsigned)((n + 255) / 256), 256, 0,
+                              reinterpret_cast<cudaStream_t>(stream), d_in, n, d_out),
+                   "widen_bf16_kernel");
 }
 
 extern "C" YSKN_B200_API int yskn_b200_gated_product(const float* d_gate, const float* d_up, int M, int n,
@@ -112,9 +116,9 @@ extern "C" YSKN_B200_API int yskn_b200_gated_product(const float* d_gate, const 
   if (!d_gate || !d_up || !d_out || M < 1 || n < 1) return fail(YSKN_EINVAL, "gated_product: bad argument");
   const int64_t total = (int64_t)M * n;
   const int64_t threads = (total + 3) / 4;
-  gated_product_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      d_gate, d_up, total, d_out);
-  return cuda_fail(cudaGetLastError(), "gated_product_kernel");
+  return cuda_fail(launch_pdl(gated_product_kernel, (unsigned)((threads + 255) / 256), 256, 0,
+                              reinterpret_cast<cudaStream_t>(stream), d_gate, d_up, total, d_out),
+                   "gated_product_kernel");
 }
 
 extern "C" YSKN_B200_API int yskn_b200_residual_prepare(uint16_t* d_hidden, const float* d_projection,
@@ -129,10 +133,10 @@ extern "C" YSKN_B200_API int yskn_b200_residual_prepare(uint16_t* d_hidden, cons
   for (int m0 = 0; m0 < M; m0 += 65535) {
     const int n = M - m0 < 65535 ? M - m0 : 65535;
     const size_t off = (size_t)m0 * cols;
-    residual_prepare_kernel<<<n, NORM_THREADS * NORM_GROUPS, smem, st>>>(d_hidden + off, d_projection ? d_projection + off : nullptr,
-                                                         d_norm_weight, cols, eps, d_input + off, d_inv_rms + m0,
-                                                         d_gate ? d_gate + off : nullptr);
-    if (cudaError_t e = cudaGetLastError()) return cuda_fail(e, "residual_prepare_kernel");
+    if (cudaError_t e = launch_pdl(residual_prepare_kernel, n, NORM_THREADS * NORM_GROUPS, smem, st, d_hidden + off,
+                                   d_projection ? d_projection + off : nullptr, d_norm_weight, cols, eps,
+                                   d_input + off, d_inv_rms + m0, d_gate ? d_gate + off : nullptr))
+      return cuda_fail(e, "residual_prepare_kernel");
   }
   return YSKN_OK;
 }
