@@ -422,6 +422,18 @@ def run_b200(args, rank, world, local_rank):
         dt = time.perf_counter() - t0
         cpu = {"value": nbytes / dt / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
                "sample": "%d full layer-set steps (quantise + threaded int64 sums + restore), %.1f s" % (n, dt)}
+    # The metric's second half at N=1: the 27B-shape decode pass (config 5, --workload stack
+    # reports it alone with its own roofline and CPU line).
+    decode = None
+    if world == 1 and not args.skip_stack:
+        from yskn_b200 import stack as S
+        sms, se2e, _ = measure_stack(dev, 64, 4096, args.bits, 20, 3)
+        tb = S.token_bytes(64, S.VOCAB, 4096, args.bits)
+        decode = {"metric": STACK_METRIC, "value": 20 / (sms * 1e-3), "unit": "tok/s", "ms_per_token": sms / 20,
+                  "e2e_tok_s": 20 / (se2e * 1e-3), "tokens": 20, "warmup": 3,
+                  "hbm_frac": tb / (sms / 20 * 1e-3) / 1e9 / peak, "bytes_per_token": tb,
+                  "config": "64 layers (48 GDN + 16 attention, KV cache 4096 rows), vocab 151936, bits=%d, "
+                            "seeded random weights, one CUDA graph per token" % args.bits}
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "strong" if world > 1 else "weak",
@@ -440,7 +452,8 @@ def run_b200(args, rank, world, local_rank):
             # every rank (row-parallel calls included: their exchange is in the kernel).
             "gpu_launches": args.steps * len(CALLS),
             "clocks": sampler.summary(),
-            "step_bytes": step_bytes, "us_per_call_alone": [round(1e3 * x, 2) for x in gemv_ms]}
+            "step_bytes": step_bytes, "us_per_call_alone": [round(1e3 * x, 2) for x in gemv_ms],
+            "decode_27b": decode}
     print(json.dumps(line), flush=True)
 
 
@@ -831,15 +844,14 @@ def stack_config(args):
             "l2": "weights of one token (~13 GB) far exceed L2"}
 
 
-def run_stack(args, rank, world, local_rank):
-    """The whole decode pass per token as one CUDA graph (yskn_b200/stack.py). N > 1 runs
-    independent replicas (no tensor-parallel stack): value = tokens/s over all ranks."""
+def measure_stack(dev, layers, ctx, bits, steps, warmup, world=1, seed=1, sampler=None):
+    """Times the decode pass (yskn_b200/stack.py) replayed as one CUDA graph per token:
+    returns (device ms for `steps` tokens, e2e ms with the host's 4-byte token in and out
+    per token, launches per token)."""
     import torch
     import yskn_b200 as Y
     from yskn_b200 import stack as S
-    dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
-    st = S.Stack(dev, layers=args.layers, ctx=args.stack_ctx, bits=args.bits, seed=1 + rank)
+    st = S.Stack(dev, layers=layers, ctx=ctx, bits=bits, seed=seed)
     stream = torch.cuda.Stream(dev)
     with torch.cuda.stream(stream):
         st.decode(stream)  # eager once: per-device set-up happens outside capture
@@ -855,17 +867,15 @@ def run_stack(args, rank, world, local_rank):
         torch.cuda.synchronize()
 
     with torch.cuda.stream(stream):
-        for _ in range(max(3, args.warmup)):
+        for _ in range(max(3, warmup)):
             graph.replay()
     barrier()
-    visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
-    ids = [v.strip() for v in visible.split(",") if v.strip()]
-    sampler = ClockSampler(ids[local_rank] if local_rank < len(ids) else str(local_rank))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with sampler:
+    import contextlib
+    with sampler if sampler is not None else contextlib.nullcontext():
         with torch.cuda.stream(stream):
             e0.record(stream)
-            for _ in range(args.steps):
+            for _ in range(steps):
                 graph.replay()
             e1.record(stream)
         barrier()
@@ -877,7 +887,7 @@ def run_stack(args, rank, world, local_rank):
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         e2.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             st.token.copy_(tok_in, non_blocking=True)
             graph.replay()
             tok_out.copy_(st.token, non_blocking=True)
@@ -887,16 +897,33 @@ def run_stack(args, rank, world, local_rank):
     barrier()
     e2e_ms = e2.elapsed_time(e3)
     Y.check(Y.status(stream), "status")
+    launches = st.launches_per_token()
+    del graph, st
+    torch.cuda.empty_cache()
+    return ms, e2e_ms, launches
+
+
+def run_stack(args, rank, world, local_rank):
+    """The whole decode pass per token as one CUDA graph (yskn_b200/stack.py). N > 1 runs
+    independent replicas (no tensor-parallel stack): value = tokens/s over all ranks."""
+    import torch
+    from yskn_b200 import stack as S
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    ids = [v.strip() for v in visible.split(",") if v.strip()]
+    sampler = ClockSampler(ids[local_rank] if local_rank < len(ids) else str(local_rank))
+    ms, e2e_ms, launches = measure_stack(dev, args.layers, args.stack_ctx, args.bits, args.steps, args.warmup,
+                                         world, 1 + rank, sampler)
     t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     ms, e2e_ms = t.tolist()
-    del graph
     if rank != 0:
         return
     value = world * args.steps / (ms * 1e-3)
     e2e_value = world * args.steps / (e2e_ms * 1e-3)
-    tb = S.token_bytes(args.layers, S.Stack.__init__.__defaults__[1], args.stack_ctx, args.bits)
+    tb = S.token_bytes(args.layers, S.VOCAB, args.stack_ctx, args.bits)
     peaks = measured_peaks()
     peak = peaks.get("hbm_gbs", HBM_FALLBACK_GBS)
     achieved = tb / (ms / args.steps * 1e-3) / 1e9
@@ -925,7 +952,7 @@ def run_stack(args, rank, world, local_rank):
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
-            "gpu_launches": args.steps * st.launches_per_token(),
+            "gpu_launches": args.steps * launches,
             "clocks": sampler.summary()}
     print(json.dumps(line), flush=True)
 
@@ -938,6 +965,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--bits", type=int, default=8, choices=[6, 8])
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-stack", action="store_true", help="linear: leave out the 27B-shape decode pass")
     ap.add_argument("--workload", default="linear", choices=["linear", "kv4", "gemm", "stack"])
     ap.add_argument("--layers", type=int, default=64, help="stack: layers (every fourth attention)")
     ap.add_argument("--stack-ctx", type=int, default=4096, help="stack: KV cache rows per attention layer")

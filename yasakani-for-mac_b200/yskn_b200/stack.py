@@ -20,7 +20,7 @@ import numpy as np
 import yskn_b200 as Y
 from yskn_b200 import synthetic
 
-HIDDEN, FFN = 5120, 17408
+HIDDEN, FFN, VOCAB = 5120, 17408, 151936
 N_QH, N_KVH, HEAD = 24, 4, 256
 QKV, ZDIM = 10240, 6144
 EPS = 1e-6
@@ -57,7 +57,7 @@ def token_bytes(layers, vocab, ctx, bits=8):
 class Stack:
     """Seeded weights, caches, states and buffers of the stack on one device."""
 
-    def __init__(self, device, layers=64, vocab=151936, ctx=8192, bits=8, seed=1):
+    def __init__(self, device, layers=64, vocab=VOCAB, ctx=4096, bits=8, seed=1):
         import torch
         self.torch, self.dev = torch, device
         self.layers, self.vocab, self.ctx, self.bits = layers, vocab, ctx, bits
