@@ -903,6 +903,39 @@ def measure_stack(dev, layers, ctx, bits, steps, warmup, world=1, seed=1, sample
     return ms, e2e_ms, launches
 
 
+def run_reference_stack(args, rank, world):
+    """CPU arm of --workload stack: the operator port on the host cores over the layer set,
+    its code bytes per second divided by one token's bytes (linears only, an upper bound
+    on a CPU decode rate; the mixers, attention and head are not timed). Rank 0 only."""
+    from yskn_b200 import stack as S
+    if rank != 0:
+        return
+    W = make_weights(args.bits)
+    prepare_cpu(W, args.bits)
+    xs = make_inputs(1)
+    threads = os.cpu_count() or 1
+    tb = S.token_bytes(args.layers, S.VOCAB, args.stack_ctx, args.bits)
+    for _ in range(max(1, min(args.warmup, 3))):
+        cpu_layer_step(W, xs, 1.0, threads)
+    t0 = time.perf_counter()
+    n, nbytes = 0, 0
+    while n < args.steps and (time.perf_counter() - t0 < 60.0 or n < 1):
+        nbytes += cpu_layer_step(W, xs, 1.0, threads)
+        n += 1
+    dt = time.perf_counter() - t0
+    value = (nbytes / dt) / tb
+    sample = ("%d full layer-set steps of the CPU operator port (%.1f s), code bytes/s divided by one token's "
+              "bytes (linears only)" % (n, dt))
+    print(json.dumps({"impl": "reference", "metric": STACK_METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+                      "steps": n, "warmup": args.warmup, "ms_per_step": 1e3 / value, "higher_is_better": True,
+                      "scaling": "weak", "vs_baseline": None, "dtype": "i8", "data": "synthetic",
+                      "config": stack_config(args),
+                      "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+                                       "sample": sample},
+                      "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+          flush=True)
+
+
 def run_stack(args, rank, world, local_rank):
     """The whole decode pass per token as one CUDA graph (yskn_b200/stack.py). N > 1 runs
     independent replicas (no tensor-parallel stack): value = tokens/s over all ranks."""
@@ -977,7 +1010,8 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        {"kv4": run_reference_kv, "gemm": run_reference_gemm}.get(args.workload, run_reference)(args, rank, world)
+        {"kv4": run_reference_kv, "gemm": run_reference_gemm, "stack": run_reference_stack}.get(
+            args.workload, run_reference)(args, rank, world)
         return
     if world > 1:
         import datetime
