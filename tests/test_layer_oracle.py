@@ -51,3 +51,18 @@ def test_gdn_rows_one_by_one():
         out, s, h = O.gdn_step(x["qkv"][r:r + 1], x["z"][r:r + 1], x["gates"][r:r + 1], *w, 1e-6, s, h)
         assert np.array_equal(out[0], out_all[r])
     assert np.array_equal(s, s_all) and np.array_equal(h, h_all)
+
+
+def test_cache_rotation_round_trip():
+    """The attention-input rotation (signs, H256, 1/16; docs/spec/04_ATTENTION.md:80-100)
+    is undone by the KV oracle's inverse rotation, written separately from the reference's
+    decoder (H256, 1/16, signs): bit for bit on small integers, where every butterfly sum is
+    exact, and within float rounding on normal values; the rotation keeps the norm."""
+    import kv
+    rng = np.random.default_rng(9)
+    x = rng.integers(-8, 9, 256).astype(np.float32)
+    assert np.array_equal(kv.inverse_rotate(O.rotate_cache(x)), x)
+    y = rng.standard_normal(256).astype(np.float32)
+    back = kv.inverse_rotate(O.rotate_cache(y))
+    assert np.abs(back - y).max() <= 1e-5 * np.abs(y).max()
+    assert abs(np.linalg.norm(O.rotate_cache(y)) - np.linalg.norm(y)) <= 1e-5 * np.linalg.norm(y)
