@@ -77,3 +77,27 @@ def test_kv_attention_argument_errors_are_returned():
     assert L.yskn_b200_kv4_attention_work_bytes(1, 24, 2048, 0) == 24 * 31 * 260 * 4
     assert L.yskn_b200_kv4_attention_work_bytes(8, 24, 4100, 0) == 8 * 24 * 42 * 260 * 4
     assert L.yskn_b200_kv4_attention_work_bytes(1, 24, 100, 65) == -1
+
+
+def test_layer_op_argument_errors_are_returned():
+    """The layer ops between operators reject bad shapes and commit counts with EINVAL and a
+    message before any device work (fake, never dereferenced pointers)."""
+    import yskn_b200
+    L = yskn_b200.lib()
+    p = 4096  # stands for a device pointer; 16-byte aligned
+    EINVAL = yskn_b200.EINVAL
+    cases = [
+        L.yskn_b200_residual_prepare(p, None, p, 1, 500, 1e-6, p, p, None, None),      # cols % 512
+        L.yskn_b200_residual_prepare(p, None, p, 0, 512, 1e-6, p, p, None, None),      # M < 1
+        L.yskn_b200_gated_product(p, p, 0, 16, p, None),                               # M < 1
+        L.yskn_b200_head_select(p, 1, 16, None, None, None, None),                     # no output
+        L.yskn_b200_attention_prep(p, p, p, p, p, p, 1e-6, 0, 24, 4, p, p, p, p, None),  # M < 1
+        L.yskn_b200_gdn_gates(p, p, p, p, 1, 1000, p, None),                           # hidden % 1024
+        L.yskn_b200_gdn_gates(p + 2, p, p, p, 1, 1024, p, None),                       # unaligned rows
+        L.yskn_b200_gdn_step(p, p, p, p, p, p, p, 1e-6, 2, 3, p, p, p, None),          # n_commit > M
+        L.yskn_b200_gdn_step(p, p, p, p, p, p, p, 1e-6, 2, -1, p, p, p, None),         # n_commit < 0
+        L.yskn_b200_widen_bf16(p, 0, p, None),                                         # n < 1
+    ]
+    for i, rc in enumerate(cases):
+        assert rc == EINVAL, i
+    assert yskn_b200.last_error()
