@@ -66,3 +66,32 @@ def test_cache_rotation_round_trip():
     back = kv.inverse_rotate(O.rotate_cache(y))
     assert np.abs(back - y).max() <= 1e-5 * np.abs(y).max()
     assert abs(np.linalg.norm(O.rotate_cache(y)) - np.linalg.norm(y)) <= 1e-5 * np.linalg.norm(y)
+
+
+def _scan_top8(logits):
+    """The reference's candidate comparison as a scalar scan (docs/spec/06_OUTPUT_HEAD_SAMPLER.md:
+    31-64): start from (-FLT_MAX, INT_MAX), a candidate enters when it has the larger logit,
+    or the same logit and the smaller id; NaN compares false and never enters."""
+    top = [(np.float32(-3.4028234663852886e38), 2**31 - 1)] * 8
+    for i, v in enumerate(np.asarray(logits, np.float32)):
+        c = (v, i)
+        for k in range(8):
+            tv, ti = top[k]
+            if c[0] > tv or (c[0] == tv and c[1] < ti):
+                top[k], c = c, top[k]
+    return top
+
+
+def test_head_select_matches_a_scalar_scan():
+    rng = np.random.default_rng(11)
+    rows = [rng.standard_normal(300).astype(np.float32),
+            np.round(rng.standard_normal(300) * 2).astype(np.float32),  # many ties
+            np.full(20, np.nan, np.float32),
+            np.array([np.nan, -np.inf, -3.4028234663852886e38, 1.0, np.inf, 1.0, np.nan], np.float32),
+            np.array([-np.inf] * 5 + [2.0], np.float32)]
+    for r in rows:
+        token, vals, ids = O.head_select(r)
+        want = _scan_top8(r)
+        assert [int(i) for i in ids] == [i for _, i in want]
+        assert np.array_equal(vals.view(np.uint32), np.array([v for v, _ in want], np.float32).view(np.uint32))
+        assert token == want[0][1]
