@@ -95,3 +95,41 @@ def test_head_select_matches_a_scalar_scan():
         assert [int(i) for i in ids] == [i for _, i in want]
         assert np.array_equal(vals.view(np.uint32), np.array([v for v, _ in want], np.float32).view(np.uint32))
         assert token == want[0][1]
+
+
+def _f(x):
+    return np.float32(x)
+
+
+def _scalar_total_squares(h):
+    """docs/spec/05_RESIDUAL_NORM_MLP.md:70-101 one operation at a time: per 512 block, 128
+    partials of four squares from +0, xor_sum32 of each group of 32 (every lane updated from
+    the old values), the group sums added from +0, blocks added in order from +0."""
+    total = _f(0.0)
+    for b in range(0, h.size, 512):
+        part = []
+        for t in range(128):
+            s = _f(0.0)
+            for j in range(4):
+                x = h[b + t + 128 * j]
+                s = _f(s + _f(x * x))
+            part.append(s)
+        block = _f(0.0)
+        for g in range(4):
+            a = part[32 * g:32 * g + 32]
+            for off in (16, 8, 4, 2, 1):
+                a = [_f(a[i] + a[i ^ off]) for i in range(32)]
+            block = _f(block + a[0])
+        total = _f(total + block)
+    return total
+
+
+def test_residual_sum_of_squares_matches_a_scalar_restatement():
+    rng = np.random.default_rng(13)
+    for scale in (1e-3, 1.0, 300.0):
+        hidden = O.bf16_bits((rng.standard_normal(1024) * scale).astype(np.float32))
+        proj = (rng.standard_normal(1024) * scale).astype(np.float32)
+        h, _, inv, _ = O.residual_prepare(hidden, proj, O.bf16_bits(np.zeros(1024, np.float32)), 1e-6)
+        total = _scalar_total_squares(O.bf16_float(h))
+        mean = _f(_f(total / _f(1024.0)) + _f(1e-6))
+        assert np.float32(inv).view(np.uint32) == np.float32(1.0 / np.sqrt(np.float64(mean))).view(np.uint32)
