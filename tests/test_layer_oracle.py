@@ -133,3 +133,35 @@ def test_residual_sum_of_squares_matches_a_scalar_restatement():
         total = _scalar_total_squares(O.bf16_float(h))
         mean = _f(_f(total / _f(1024.0)) + _f(1e-6))
         assert np.float32(inv).view(np.uint32) == np.float32(1.0 / np.sqrt(np.float64(mean))).view(np.uint32)
+
+
+def test_gdn_gates_match_a_scalar_restatement():
+    """docs/spec/03_GATED_DELTANET.md:57-76 one operation at a time for a few outputs of one
+    row (hidden 2048: two chunks of 1024)."""
+    rng = np.random.default_rng(17)
+    hidden = 2048
+    x = O.bf16_bits(rng.standard_normal(hidden).astype(np.float32))
+    wb = O.bf16_bits((rng.standard_normal((48, hidden)) * 0.05).astype(np.float32))
+    wa = O.bf16_bits((rng.standard_normal((48, hidden)) * 0.05).astype(np.float32))
+    inv = np.float32(0.731)
+    got = O.gdn_gates(x, inv, wb, wa)
+    xf = O.bf16_float(x)
+    for o in (0, 17, 47, 48, 70, 95):
+        w = O.bf16_float(wb[o] if o < 48 else wa[o - 48])
+        partial = []
+        for p in range(128):
+            s = _f(0.0)
+            for chunk in range(hidden // 1024):
+                for e in range(8):
+                    i = 8 * p + 1024 * chunk + e
+                    s = _f(s + _f(w[i] * xf[i]))
+            partial.append(s)
+        grouped = []
+        for g in range(4):
+            a = partial[32 * g:32 * g + 32]
+            for off in (16, 8, 4, 2, 1):
+                a = [_f(a[i] + a[i ^ off]) for i in range(32)]
+            grouped.append(a[0])
+        s4 = _f(_f(_f(grouped[0] + grouped[1]) + grouped[2]) + grouped[3])
+        want = O.bf16_float(O.bf16_bits(_f(s4 * inv)))
+        assert np.float32(got[o]).view(np.uint32) == np.float32(want).view(np.uint32), o
