@@ -165,3 +165,35 @@ def test_gdn_gates_match_a_scalar_restatement():
         s4 = _f(_f(_f(grouped[0] + grouped[1]) + grouped[2]) + grouped[3])
         want = O.bf16_float(O.bf16_bits(_f(s4 * inv)))
         assert np.float32(got[o]).view(np.uint32) == np.float32(want).view(np.uint32), o
+
+
+def _bf(x):
+    return O.bf16_float(O.bf16_bits(_f(x)))
+
+
+def test_head_norm_and_rope_match_a_scalar_restatement():
+    """docs/spec/04_ATTENTION.md:27-66 one operation at a time for one 256-channel head:
+    xor_sum32 of each group's squares added from +0, the inverse RMS, bf16(y * inv * (1 + w)),
+    then RoPE on channels (i, i + 32), i < 32, with bf16 cos/sin and the spec's roundings."""
+    rng = np.random.default_rng(19)
+    y = O.bf16_float(O.bf16_bits(rng.standard_normal(256).astype(np.float32) * 3))
+    w_bits = O.bf16_bits((rng.standard_normal(256) * 0.1).astype(np.float32))
+    w = O.bf16_float(w_bits)
+    pos, eps = 1234, 1e-6
+    got = O.rope(O.normalize_head(y, w_bits, eps), pos)
+    total = _f(0.0)
+    for g in range(8):
+        a = [_f(y[32 * g + i] * y[32 * g + i]) for i in range(32)]
+        for off in (16, 8, 4, 2, 1):
+            a = [_f(a[i] + a[i ^ off]) for i in range(32)]
+        total = _f(total + a[0])
+    inv = _f(1.0 / np.sqrt(np.float64(_f(_f(total / _f(256.0)) + _f(eps)))))
+    n = [_bf(_f(_f(y[i] * inv) * _f(_f(1.0) + w[i]))) for i in range(256)]
+    freq = np.array(O.ROPE_FREQ_BITS, np.uint32).view(np.float32)
+    want = list(n)
+    for i in range(32):
+        arg = _f(_f(pos) * freq[i])
+        c, s = _bf(np.cos(arg)), _bf(np.sin(arg))
+        want[i] = _bf(_bf(n[i] * c) + _bf(-n[i + 32] * s))
+        want[i + 32] = _bf(_bf(n[i + 32] * c) + _bf(n[i] * s))
+    assert np.array_equal(np.asarray(got, np.float32).view(np.uint32), np.array(want, np.float32).view(np.uint32))
