@@ -197,3 +197,75 @@ def test_head_norm_and_rope_match_a_scalar_restatement():
         want[i] = _bf(_bf(n[i] * c) + _bf(-n[i + 32] * s))
         want[i + 32] = _bf(_bf(n[i + 32] * c) + _bf(n[i] * s))
     assert np.array_equal(np.asarray(got, np.float32).view(np.uint32), np.array(want, np.float32).view(np.uint32))
+
+
+def test_gdn_step_matches_a_scalar_restatement_for_one_head():
+    """docs/spec/03_GATED_DELTANET.md:86-155 one operation at a time for value head 7 (key
+    head 2) of one row after a history: convolution, q/k normalisation, beta and decay,
+    the two 32-term passes per group over the state column, the output norm and z gate."""
+    rng = np.random.default_rng(29)
+    conv_bits, a_log_bits, dt_bits, norm_bits = _gdn_weights(rng)
+    state = (rng.standard_normal((48, 128, 128)) * 0.1).astype(np.float32)
+    hist = O.bf16_bits(rng.standard_normal((3, 10240)).astype(np.float32))
+    x = _gdn_inputs(rng, 1)
+    out, new_state, _ = O.gdn_step(x["qkv"], x["z"], x["gates"], conv_bits, a_log_bits, dt_bits, norm_bits, 1e-6,
+                                   state, hist)
+    vh, kh = 7, 2
+    cw = O.bf16_float(conv_bits).reshape(-1, 4)
+    hf = O.bf16_float(hist)
+    silu = lambda v: _f(_f(v) / _f(_f(1.0) + np.exp(-_f(v))))  # noqa: E731
+
+    def conv(c):
+        taps = [hf[0, c], hf[1, c], hf[2, c], _bf(x["qkv"][0, c])]
+        a = _f(cw[c, 0] * taps[0])
+        for t in range(1, 4):
+            a = _f(a + _f(cw[c, t] * taps[t]))
+        return _bf(silu(_bf(a)))
+
+    def squares128(v):
+        parts = []
+        for g in range(4):
+            a = [_f(v[32 * g + i] * v[32 * g + i]) for i in range(32)]
+            for off in (16, 8, 4, 2, 1):
+                a = [_f(a[i] + a[i ^ off]) for i in range(32)]
+            parts.append(a[0])
+        return _f(_f(_f(parts[0] + parts[1]) + parts[2]) + parts[3])
+
+    q = [conv(128 * kh + j) for j in range(128)]
+    k = [conv(2048 + 128 * kh + j) for j in range(128)]
+    v = [conv(4096 + 128 * vh + j) for j in range(128)]
+    rq = _f(1.0 / np.sqrt(np.float64(_f(squares128(q) + _f(1e-6)))))
+    rk = _f(1.0 / np.sqrt(np.float64(_f(squares128(k) + _f(1e-6)))))
+    query = [_f(_f(qq * rq) * _f(0.08838834764831845)) for qq in q]
+    key = [_f(kk * rk) for kk in k]
+    g = x["gates"][0]
+    beta = _bf(_f(_f(1.0) / _f(_f(1.0) + np.exp(-_f(g[vh])))))
+    xa = _f(g[48 + vh] + O.bf16_float(dt_bits)[vh])
+    sp = xa if xa > _f(20.0) else _f(np.log1p(np.exp(xa)))
+    decay = np.exp(_f(-np.exp(O.bf16_float(a_log_bits)[vh]) * sp))
+    R = state[vh].copy()
+    core = []
+    for j in range(128):
+        parts = []
+        for grp in range(4):
+            acc = _f(0.0)
+            for r in range(32):
+                i = 32 * grp + r
+                R[i, j] = _f(R[i, j] * decay)
+                acc = _f(acc + _f(R[i, j] * key[i]))
+            parts.append(acc)
+        corr = _f(_f(v[j] - _f(_f(_f(parts[0] + parts[1]) + parts[2]) + parts[3])) * beta)
+        parts = []
+        for grp in range(4):
+            acc = _f(0.0)
+            for r in range(32):
+                i = 32 * grp + r
+                R[i, j] = _f(R[i, j] + _f(key[i] * corr))
+                acc = _f(acc + _f(R[i, j] * query[i]))
+            parts.append(acc)
+        core.append(_bf(_f(_f(_f(parts[0] + parts[1]) + parts[2]) + parts[3])))
+    inv = _f(1.0 / np.sqrt(np.float64(_f(_f(squares128(core) / _f(128.0)) + _f(1e-6)))))
+    nw = O.bf16_float(norm_bits)
+    want = [_bf(_f(_bf(_f(nw[j] * _bf(_f(core[j] * inv)))) * silu(x["z"][0, 128 * vh + j]))) for j in range(128)]
+    assert np.array_equal(out[0, 128 * vh:128 * vh + 128].view(np.uint32), np.array(want, np.float32).view(np.uint32))
+    assert np.array_equal(new_state[vh].view(np.uint32), R.view(np.uint32))
