@@ -309,6 +309,20 @@ YSKN_B200_API int yskn_b200_rescale(const float* d_alpha, const float* d_row_max
 YSKN_B200_API yskn_b200_tp* yskn_b200_tp_create(int world, int rank, int max_physical_rows, void* ipc_handle_out);
 YSKN_B200_API int yskn_b200_tp_connect(yskn_b200_tp* tp, const void* handles /* world x 64 bytes, rank order */);
 YSKN_B200_API void yskn_b200_tp_destroy(yskn_b200_tp* tp);
+/* No counterpart in the reference. For one process that drives several GPUs (one
+ * thread per device, peer access enabled): this rank's exchange area as a device
+ * pointer, and a connect that takes the peers' areas as device pointers reachable from
+ * this rank's device (world entries in rank order; this rank's own entry is ignored),
+ * instead of IPC handles. A pointer of a rank that never runs its launches is allowed:
+ * this rank's waits on it then end with YSKN_ETIMEDOUT. */
+YSKN_B200_API void* yskn_b200_tp_area(yskn_b200_tp* tp);
+YSKN_B200_API int yskn_b200_tp_connect_peers(yskn_b200_tp* tp, void* const* peer_areas);
+/* No counterpart in the reference. Limit of each wait phase of yskn_b200_linear_rowpar
+ * on the peers (the row maxima, then the block sums), in seconds at the device's
+ * maximum SM clock; default 1 s, accepted 1e-6 .. 60. One deadline covers a whole
+ * phase of a CTA and a timeout ends the CTA's later waits at once, so a launch whose
+ * peer never arrives ends within about two limits with YSKN_ETIMEDOUT. */
+YSKN_B200_API int yskn_b200_tp_set_wait(yskn_b200_tp* tp, double seconds);
 YSKN_B200_API int yskn_b200_linear_rowpar(yskn_b200_tp* tp, const yskn_b200_matrix* mat, const float* d_x_local, int M,
                                           const float* d_inv_rms, float* d_y, void* stream);
 

@@ -212,3 +212,41 @@ def test_tp_rowpar_one_launch_two_gpus_bit_identical(cuda):
         assert set(out) == set(ref)
         for k, y in out.items():
             assert np.array_equal(y.view(np.uint32), ref[k].view(np.uint32)), k
+
+
+def test_rowpar_wait_for_a_peer_that_never_arrives_times_out(cuda):
+    """A row-parallel launch whose peer never runs (world 2, rank 0 alone on one GPU; the
+    peer's exchange area is valid memory that no kernel serves) gives up within a short
+    wait limit and reports YSKN_ETIMEDOUT; the device stays usable afterwards."""
+    import time
+    import torch
+    import yskn_b200
+    rows, cols = 2048, 4096
+    words, lut16, sc16 = fixtures.model_matrix(rows, cols, 8, 23)
+    si = O.signs("mulberry32_7919_13", 7, 0, cols)
+    so = O.signs("mulberry32_7919_13", 7, cols, rows)
+    dw = _dev(words.view(np.int32))
+    shard = yskn_b200.Matrix(dw, "warp", rows, rows, cols, 8, lut16, sc16, si, so, shard=(0, rows, 0, cols // 2))
+    ex0 = yskn_b200.TpExchange(2, 0, rows)
+    ex1 = yskn_b200.TpExchange(2, 1, rows)  # the absent peer's area: never connected, never launched
+    ex0.connect_peers([None, ex1.area])
+    ex0.set_wait(0.002)
+    x = _dev(fixtures.normal(5, cols // 2).reshape(1, cols // 2))
+    y = torch.empty((1, rows), dtype=torch.float32, device="cuda")
+    assert yskn_b200.status() == 0
+    t0 = time.time()
+    yskn_b200.linear_rowpar(ex0, shard, x, y)
+    rc = yskn_b200.status()
+    elapsed = time.time() - t0
+    assert rc == yskn_b200.ETIMEDOUT
+    assert elapsed < 2.0, elapsed  # two 2 ms limits, not one limit per polled word
+    # The context still works: a plain operator call is correct.
+    m = yskn_b200.Matrix(dw, "warp", rows, rows, cols, 8, lut16, sc16, si, so)
+    xf = fixtures.normal(6, cols).reshape(1, cols)
+    work = torch.empty(yskn_b200.linear_work_bytes([m], 1), dtype=torch.uint8, device="cuda")
+    yskn_b200.linear([m], _dev(xf), work, [y])
+    ref = O.linear(words, "warp", rows, cols, 8, lut16, sc16, xf, si, so)
+    assert yskn_b200.status() == 0
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+    ex0.close()
+    ex1.close()

@@ -4,8 +4,9 @@ The no-allocation entry point exists for callers that must not have the library
 allocate device memory (a process whose HBM is already handed to its own pool, or a
 latency-critical loop where cudaMalloc could synchronise the device). It keeps its
 scratch in a static device array shared by every call on the device, so the test
-makes two calls in a row (different shapes and inputs) and checks each against the
-regular entry point bit for bit (integer sums: the tolerance is zero). This file is
+makes three calls in a row (different shapes and inputs; the third is three launches)
+and checks each against the regular entry point bit for bit (integer sums: the
+tolerance is zero). This file is
 collected last so that a run that stops at the first failure has run every other test.
 """
 import numpy as np
@@ -38,7 +39,8 @@ def test_noalloc_matches_the_regular_entry_point_on_two_calls(cuda):
     import torch
     import yskn_b200
     mats, _keep = _matrices()
-    for call, (M, group) in enumerate([(1, mats), (13, mats[:2])]):
+    # M = 40 runs as three GEMV launches of 16, 16 and 8 rows that reuse the static array.
+    for call, (M, group) in enumerate([(1, mats), (13, mats[:2]), (40, mats)]):
         rnd = fixtures.FixtureRandom(0xA110C + call)
         act = _dev(rnd.take(M * 5120).astype(np.uint8).view(np.int8).reshape(M, 5120))
         scales = _dev(rnd.take(M * 10).view(np.int32).reshape(M, 10))

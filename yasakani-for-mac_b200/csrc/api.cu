@@ -438,6 +438,34 @@ YSKN_B200_API int yskn_b200_tp_connect(yskn_b200_tp* t, const void* handles) {
   return YSKN_OK;
 }
 
+YSKN_B200_API void* yskn_b200_tp_area(yskn_b200_tp* t) {
+  if (!t) return fail(YSKN_EINVAL, "tp_area: null exchange"), nullptr;
+  return t->local;
+}
+
+YSKN_B200_API int yskn_b200_tp_connect_peers(yskn_b200_tp* t, void* const* peer_areas) {
+  if (!t || !peer_areas || t->connected) return fail(YSKN_EINVAL, "tp_connect_peers: bad arguments");
+  for (int q = 0; q < t->view.world; ++q) {
+    if (q == t->view.rank) continue;
+    if (!peer_areas[q] || (reinterpret_cast<uintptr_t>(peer_areas[q]) & 255u))
+      return fail(YSKN_EINVAL, "tp_connect_peers: a peer area is null or not 256-byte aligned");
+  }
+  for (int q = 0; q < t->view.world; ++q)
+    if (q != t->view.rank) t->view.base[q] = reinterpret_cast<char*>(peer_areas[q]);
+  t->connected = true;
+  return YSKN_OK;
+}
+
+YSKN_B200_API int yskn_b200_tp_set_wait(yskn_b200_tp* t, double seconds) {
+  if (!t || !(seconds >= 1e-6 && seconds <= 60.0)) return fail(YSKN_EINVAL, "tp_set_wait: need 1e-6 <= seconds <= 60");
+  int dev = 0, khz = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, dev);
+  if (e != cudaSuccess) return cuda_fail(e, "tp_set_wait");
+  t->view.wait_cycles = std::max(1ll, (long long)(seconds * 1e3 * (double)khz));
+  return YSKN_OK;
+}
+
 YSKN_B200_API void yskn_b200_tp_destroy(yskn_b200_tp* t) {
   if (!t) return;
   cudaDeviceSynchronize();

@@ -132,7 +132,9 @@ struct TpView {
   size_t off_maxbox;                // u64 [2][world][TP_MAX_M]: row maxima (f32 bits) by source rank
   size_t off_recv;                  // u64 x2 [2][world][TP_MAX_M][max_blocks * 512]: int64 block sums by source
   size_t bytes;
+  long long wait_cycles;            // limit of each wait phase on the peers, in SM clock cycles
 };
+constexpr long long TP_DEFAULT_WAIT_CYCLES = 2000000000ll;  // ~1 s at B200 clocks
 inline TpView tp_layout(int world, int rank, int max_blocks) {
   auto up = [](size_t v) { return (v + 255) / 256 * 256; };
   TpView v{};
@@ -143,6 +145,7 @@ inline TpView tp_layout(int world, int rank, int max_blocks) {
   v.off_maxbox = 256;
   v.off_recv = v.off_maxbox + up(2 * (size_t)world * TP_MAX_M * 8);
   v.bytes = v.off_recv + up(2 * (size_t)world * TP_MAX_M * max_blocks * 512 * 16);
+  v.wait_cycles = TP_DEFAULT_WAIT_CYCLES;
   return v;
 }
 

@@ -229,10 +229,11 @@ __device__ __forceinline__ void gpu_acquire() { asm volatile("fence.acq_rel.gpu;
 // Cross-GPU exchange of the row-parallel operator. Each 32-bit datum goes to a peer's
 // area as one 64-bit word (datum | epoch << 32) with a plain (volatile) store over
 // NVLink; an aligned 64-bit access is single-copy atomic, so a receiver that reads a
-// word carrying its epoch has the datum too, without fences. Receivers poll their own
-// area for at most TP_WAIT_LIMIT clock cycles (then the device error word gets
-// DERR_TIMEOUT and the call's output is not valid).
-constexpr long long TP_WAIT_LIMIT = 2000000000ll;  // ~1 s
+// word carrying its epoch has the datum too, without fences. Every wait of a CTA on its
+// peers runs against deadlines of TpView::wait_cycles clock cycles taken once per wait
+// phase (not per word), and a CTA-wide abort flag ends every later wait at once: a
+// peer that never arrives costs a launch at most two limits, after which the device
+// error word holds DERR_TIMEOUT and the call's output is not valid.
 __device__ __forceinline__ uint64_t ll_word(uint32_t datum, uint32_t epoch) {
   return (uint64_t)datum | ((uint64_t)epoch << 32);
 }
@@ -253,18 +254,18 @@ __device__ __forceinline__ uint64_t ld_ll(const uint64_t* p) {
   return v;
 }
 // The int64 sum of two epoch-tagged words (low half first), polling until both carry
-// `epoch`; `ok` turns false on a timeout.
-__device__ __forceinline__ long long recv_sum(const uint64_t* p, uint32_t epoch, bool& ok) {
+// `epoch` or the clock passes `deadline`. Once `ok` is false (this lane timed out
+// before, or the CTA's abort flag is up) it returns 0 without polling.
+__device__ __forceinline__ long long recv_sum(const uint64_t* p, uint32_t epoch, long long deadline,
+                                              const volatile int* abort_flag, bool& ok) {
+  if (!ok) return 0;
   ulonglong2 v = ld_ll2(p);
-  if ((uint32_t)(v.x >> 32) != epoch || (uint32_t)(v.y >> 32) != epoch) {
-    const long long t0 = clock64();
-    do {
-      if (clock64() - t0 > TP_WAIT_LIMIT) {
-        ok = false;
-        break;
-      }
-      v = ld_ll2(p);
-    } while ((uint32_t)(v.x >> 32) != epoch || (uint32_t)(v.y >> 32) != epoch);
+  while ((uint32_t)(v.x >> 32) != epoch || (uint32_t)(v.y >> 32) != epoch) {
+    if (clock64() > deadline || *abort_flag) {
+      ok = false;
+      return 0;
+    }
+    v = ld_ll2(p);
   }
   return (long long)(((uint64_t)(uint32_t)v.y << 32) | (uint32_t)v.x);
 }
@@ -424,10 +425,12 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
   // and the slot parity that double-buffers the exchange.
   __shared__ unsigned s_epoch;
   __shared__ float s_rowmax[TP_MAX_M];
+  __shared__ int s_abort;  // row-parallel: a wait on a peer gave up; later waits return at once
   const bool tp = FUSED && p.tp.world > 1;
   if (tp && threadIdx.x == 0) {
     const unsigned long long prev = atomicAdd(tp_at<unsigned long long>(p.tp, p.tp.rank, p.tp.off_counter), 1ull);
     s_epoch = (unsigned)(prev / gridDim.x) + 1u;
+    s_abort = 0;
   }
   if (FUSED) {  // the rows' common integer grids (compressed_linear.rs:113-128)
     if (threadIdx.x < p.mv) {
@@ -450,12 +453,12 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         const uint64_t* box = tp_at<uint64_t>(p.tp, me, p.tp.off_maxbox) + (size_t)par * W * TP_MAX_M;
         bool ok = true;
         float mx = 0.0f;
-        for (int src = 0; src < W; ++src) {
+        const long long deadline = clock64() + p.tp.wait_cycles;  // one limit for all sources
+        for (int src = 0; src < W && ok; ++src) {
           const uint64_t* w = box + src * TP_MAX_M + lane;
           uint64_t v = ld_ll(w);
-          const long long t0 = clock64();
           while ((uint32_t)(v >> 32) != epoch) {
-            if (clock64() - t0 > TP_WAIT_LIMIT) {
+            if (clock64() > deadline) {
               ok = false;
               break;
             }
@@ -463,7 +466,10 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
           }
           mx = fmaxf(mx, __uint_as_float((uint32_t)v));
         }
-        if (!ok) raise_device_error(p.err, DERR_TIMEOUT);
+        if (!ok) {
+          s_abort = 1;
+          raise_device_error(p.err, DERR_TIMEOUT);
+        }
         s_rowmax[lane] = mx;
       }
     }
@@ -692,10 +698,13 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
     const int W = p.tp.world, me = p.tp.rank;
     const size_t slot = (size_t)p.tp.max_blocks * 512 * 2;
     const uint64_t* recv = tp_at<uint64_t>(p.tp, me, p.tp.off_recv);
+    // One deadline for all of this warp's blocks; after a timeout (here or in another
+    // warp of the CTA) the remaining words are not polled.
+    const long long deadline = clock64() + p.tp.wait_cycles;
+    bool ok = true;
     while (done_mask) {
       const int blk = blk_lo + __ffs(done_mask) - 1;
       done_mask &= done_mask - 1;
-      bool ok = true;
       for (int tok = 0; tok < p.mv; ++tok) {
         int64_t* mine = S.out + (size_t)tok * S.out_ld + blk * 512;
 #pragma unroll
@@ -705,13 +714,19 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
           for (int src = 0; src < W; ++src) {
             if (src == me) continue;
             const uint64_t* w = recv + (((size_t)par * W + src) * TP_MAX_M + tok) * slot + (size_t)blk * 1024 + 2 * r;
-            s.x += recv_sum(w, epoch, ok);
-            s.y += recv_sum(w + 2, epoch, ok);
+            s.x += recv_sum(w, epoch, deadline, &s_abort, ok);
+            s.y += recv_sum(w + 2, epoch, deadline, &s_abort, ok);
           }
           __stcg(reinterpret_cast<longlong2*>(mine + r), s);
         }
       }
-      if (__any_sync(0xffffffffu, !ok) && lane == 0) raise_device_error(p.err, DERR_TIMEOUT);
+      if (__any_sync(0xffffffffu, !ok)) {
+        ok = false;
+        if (lane == 0) {
+          s_abort = 1;
+          raise_device_error(p.err, DERR_TIMEOUT);
+        }
+      }
       restore_block(blk);
     }
   }

@@ -44,6 +44,9 @@ _SIGNATURES = {
     "yskn_b200_tp_create": (_vp, [_i, _i, _i, _vp]),
     "yskn_b200_tp_connect": (_i, [_vp, _vp]),
     "yskn_b200_tp_destroy": (None, [_vp]),
+    "yskn_b200_tp_area": (_vp, [_vp]),
+    "yskn_b200_tp_connect_peers": (_i, [_vp, _vp]),
+    "yskn_b200_tp_set_wait": (_i, [_vp, C.c_double]),
     "yskn_b200_linear_rowpar": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp]),
     "yskn_b200_restore": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
     "yskn_b200_linear_work_bytes": (_i64, [_vp, _i, _i]),
@@ -425,6 +428,23 @@ class TpExchange:
         if len(blob) != TP_HANDLE_BYTES * self.world:
             raise ValueError("one %d-byte handle per rank expected" % TP_HANDLE_BYTES)
         check(lib().yskn_b200_tp_connect(self.handle, blob), "tp_connect")
+
+    @property
+    def area(self):
+        """This rank's exchange area as a device address (yskn_b200_tp_area)."""
+        return lib().yskn_b200_tp_area(self.handle)
+
+    def connect_peers(self, areas):
+        """Connect with the peers' areas given as device addresses in rank order (one
+        process driving several devices); this rank's own entry is ignored."""
+        if len(areas) != self.world:
+            raise ValueError("one area per rank expected")
+        arr = (C.c_void_p * self.world)(*[a or 0 for a in areas])
+        check(lib().yskn_b200_tp_connect_peers(self.handle, arr), "tp_connect_peers")
+
+    def set_wait(self, seconds):
+        """Limit of each wait phase on the peers (yskn_b200_tp_set_wait)."""
+        check(lib().yskn_b200_tp_set_wait(self.handle, float(seconds)), "tp_set_wait")
 
     def close(self):
         if self.handle:
