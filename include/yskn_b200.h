@@ -259,6 +259,25 @@ YSKN_B200_API int yskn_b200_gdn_step(const float* d_qkv, const float* d_z, const
  * in the reference. */
 YSKN_B200_API int yskn_b200_widen_bf16(const uint16_t* d_in, int64_t n, float* d_out, void* stream);
 
+/* The scalar contract's portable functions (crates/yskn-ref/src/portable_math.rs:106-434)
+ * as the library's kernels evaluate them, over n floats: fn YSKN_PM_EXP .. YSKN_PM_RSQRT
+ * write d_y; YSKN_PM_SINCOS writes the cosine to d_y and the sine to d_y2 (0 and 0 for
+ * a non-finite angle or one outside the reduction's range). The layer kernels (residual
+ * normalisation, gated product, attention inputs, Gated DeltaNet, the attention's split
+ * combine and gate) call exactly these, so their results equal yskn-ref's bit for bit.
+ * No counterpart of its own in the reference (its CUDA engine's portable mode,
+ * src/pm_math.cuh, is internal). */
+#define YSKN_PM_EXP 0
+#define YSKN_PM_EXP2 1
+#define YSKN_PM_LOG 2
+#define YSKN_PM_LOG1P 3
+#define YSKN_PM_SIGMOID 4
+#define YSKN_PM_SILU 5
+#define YSKN_PM_SOFTPLUS 6
+#define YSKN_PM_RSQRT 7
+#define YSKN_PM_SINCOS 8
+YSKN_B200_API int yskn_b200_portable_math(int fn, const float* d_x, int64_t n, float* d_y, float* d_y2, void* stream);
+
 /* Exact weighted integer sums (the operator core). Replaces
  * crates/yskn-engine/src/model.rs:948-962 `Compute::weighted_sums` (bit-identical to
  * crates/yskn-ref/src/compressed_linear.rs:205-252) and the reference's launch_lnord /

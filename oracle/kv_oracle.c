@@ -18,6 +18,9 @@ uint16_t orc_f32_to_bf16(float value);
 #define KV_OK 0
 #define KV_EINVAL -1
 
+float orc_pm_exp(float value);
+float orc_pm_exp2(float value);
+
 static float half_r(float x) { return orc_f16_to_f32(orc_f32_to_f16(x)); }
 static float bfloat_r(float x) {
   uint32_t u = (uint32_t)orc_f32_to_bf16(x) << 16;
@@ -341,8 +344,10 @@ int orc_kv_encode(const float* row, int position, int mode, int bits, const int1
  * prefix_schedule splits, per-row 32-slot tiles (D9), online softmax with exp2,
  * BF16 prefix value weights, separate FP32 self term, packed value mean, split
  * combination with exp, division. Output: the rotated head (before the inverse
- * cache rotation). Parity with the GPU kernel is checked within a tolerance:
- * exp2/exp here are libm's, and the GPU sums in its own order.
+ * cache rotation). exp2 and exp are the reference's portable functions
+ * (portable_math.rs:111-156,212-216, restated in portable_math.c), so this
+ * reproduces attend_head bit for bit (pinned by attention.rs:1244-1306); the GPU
+ * kernel sums in its own order and is checked within a tolerance.
  *   kb/vb: [length][256] bases as floats (bf16 values or int8 integers); ks/vs: scales. */
 static const float LOG2E = 1.4426950408889634f;
 int orc_kv_attend_head(const float* q, const float* kb, const float* ks, const float* vb, const float* vs,
@@ -378,10 +383,10 @@ int orc_kv_attend_head(const float* q, const float* kb, const float* ks, const f
         }
         if (sc[k] > nm) nm = sc[k];
       }
-      const float rescale = exp2f((mx - nm) * LOG2E);
+      const float rescale = orc_pm_exp2((mx - nm) * LOG2E);
       const float smx = nm * LOG2E;
       mx = nm;
-      for (int k = 0; k < 32; ++k) pr[k] = vis[k] ? exp2f(sc[k] * LOG2E - smx) : 0.0f;
+      for (int k = 0; k < 32; ++k) pr[k] = vis[k] ? orc_pm_exp2(sc[k] * LOG2E - smx) : 0.0f;
       float part[4] = {0, 0, 0, 0};
       for (int lane = 0; lane < 4; ++lane)
         for (int grp = 0; grp < 4; ++grp) part[lane] += pr[8 * grp + 2 * lane] + pr[8 * grp + 2 * lane + 1];
@@ -416,8 +421,8 @@ int orc_kv_attend_head(const float* q, const float* kb, const float* ks, const f
       }
       const float score = part[0] * (ks[self] * 0.0625f);
       const float nm = mx > score ? mx : score;
-      const float rescale = exp2f((mx - nm) * LOG2E);
-      const float p = exp2f((score - nm) * LOG2E);
+      const float rescale = orc_pm_exp2((mx - nm) * LOG2E);
+      const float p = orc_pm_exp2((score - nm) * LOG2E);
       mx = nm;
       den = den * rescale + p;
       const float w = p * vs[self];
@@ -431,7 +436,7 @@ int orc_kv_attend_head(const float* q, const float* kb, const float* ks, const f
   float largest = -1e30f;
   for (int s = 0; s < padded; ++s) largest = smax[s] > largest ? smax[s] : largest;
   float scl[64];
-  for (int s = 0; s < padded; ++s) scl[s] = smax[s] > -1e29f ? expf(smax[s] - largest) : 0.0f;
+  for (int s = 0; s < padded; ++s) scl[s] = smax[s] > -1e29f ? orc_pm_exp(smax[s] - largest) : 0.0f;
   float total = 0.0f;
   for (int s = 0; s < padded; ++s) total += scl[s] * sden[s];
   if (!(total > 0.0f)) return KV_EINVAL;

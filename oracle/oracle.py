@@ -23,8 +23,8 @@ def build():
 def lib():
     global _lib
     if _lib is None:
-        src = os.path.join(HERE, "yskn_oracle.c")
-        if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(src):
+        srcs = [os.path.join(HERE, f) for f in ("yskn_oracle.c", "kv_oracle.c", "portable_math.c", "Makefile")]
+        if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < max(os.path.getmtime(f) for f in srcs):
             build()
         _lib = C.CDLL(LIB_PATH)
         _lib.orc_f16_to_f32.restype = C.c_float
@@ -36,6 +36,17 @@ def lib():
         _lib.orc_state.restype = C.c_uint16
         _lib.orc_state.argtypes = [C.c_void_p, C.c_int, C.c_int64, C.c_int64, C.c_int, C.c_int64, C.c_int64, C.c_int]
         _lib.orc_hadamard512.argtypes = [C.c_void_p]
+        for name in ("exp", "exp2", "log", "log1p", "sigmoid", "silu", "softplus", "rsqrt", "sqrt_rn"):
+            f = getattr(_lib, "orc_pm_" + name)
+            f.restype = C.c_float
+            f.argtypes = [C.c_float]
+        for name in ("exp_d", "log_d"):
+            f = getattr(_lib, "orc_pm_" + name)
+            f.restype = C.c_double
+            f.argtypes = [C.c_double]
+        _lib.orc_pm_sincos.argtypes = [C.c_float, C.c_void_p, C.c_void_p]
+        _lib.orc_pm_map.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_int64]
+        _lib.orc_pm_sincos_map.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64]
     return _lib
 
 
@@ -52,6 +63,37 @@ def _check(rc, what):
         raise OverflowError("%s: compressed integer accumulation exceeds i64" % what)
     if rc != 0:
         raise OracleError("%s failed (%d)" % (what, rc))
+
+
+# ---------------------------------------------------------------- portable math --
+# crates/yskn-ref/src/portable_math.rs restated in portable_math.c: the scalar
+# reference computes every exponential, logarithm, inverse square root and rotary
+# sine/cosine with these functions, so the layer oracles below call them too.
+_PM_FN = {"exp": 0, "exp2": 1, "log": 2, "log1p": 3, "sigmoid": 4, "silu": 5, "softplus": 6, "rsqrt": 7,
+          "sqrt_rn": 8}
+
+
+def pm(name, x):
+    """Elementwise portable function `name` over float32 values (same shape out)."""
+    shape = np.shape(x)
+    a = np.ascontiguousarray(np.asarray(x, np.float32).reshape(-1))
+    out = np.empty_like(a)
+    _check(lib().orc_pm_map(_PM_FN[name], _p(a), _p(out), C.c_int64(a.size)), "portable " + name)
+    return out.reshape(shape) if shape else np.float32(out[0])
+
+
+def pm_scalar(name, x):
+    """One portable binary32 function value (portable_math.rs), or exp_d / log_d in binary64."""
+    return getattr(lib(), "orc_pm_" + name)(x)
+
+
+def pm_sincos(angle):
+    """portable_math.rs:406-434 over float32 angles -> (cos, sin) float32 arrays."""
+    shape = np.shape(angle)
+    a = np.ascontiguousarray(np.asarray(angle, np.float32).reshape(-1))
+    c, s = np.empty_like(a), np.empty_like(a)
+    _check(lib().orc_pm_sincos_map(_p(a), _p(c), _p(s), C.c_int64(a.size)), "portable sincos")
+    return c.reshape(shape), s.reshape(shape)
 
 
 def signs(rule, seed, offset, n):
@@ -164,12 +206,12 @@ def block_sum_squares(values):
 
 
 def residual_prepare(hidden_bits, projection, norm_bits, eps):
-    """docs/spec/05_RESIDUAL_NORM_MLP.md:53-141 (src/q35_kernels.cu:1437-1463) for one row:
-    hidden = bf16(hidden + bf16(projection)) (no addition when projection is None), the
-    exact sum of squares, inverse RMS = 1/sqrt(total/cols + eps) (here correctly rounded
-    from double; the reference calls the CUDA rsqrtf, so a device result may differ by
-    that function's error bound), input = hidden * (1 + norm weight) in float32, and the
-    gate copy bf16(input). Returns (hidden_bits, input_f32, inv_rms, gate_bits)."""
+    """docs/spec/05_RESIDUAL_NORM_MLP.md:53-141, residual_norm_mlp.rs:14-61,120-135 for one
+    row: hidden = bf16(hidden + bf16(projection)) (no addition when projection is None),
+    the exact sum of squares, inverse RMS = rsqrt(total/cols + eps) with the portable
+    rsqrt (rounded square root, rounded division), input = hidden * (1 + norm weight) in
+    float32, and the gate copy bf16(input). Returns (hidden_bits, input_f32, inv_rms,
+    gate_bits)."""
     h = bf16_float(hidden_bits)
     if projection is not None:
         h = bf16_float(bf16_bits(h + bf16_float(bf16_bits(projection))))
@@ -178,21 +220,19 @@ def residual_prepare(hidden_bits, projection, norm_bits, eps):
     for b in range(0, cols, 512):
         total = np.float32(total + block_sum_squares(h[b:b + 512]))
     mean = np.float32(np.float32(total / np.float32(cols)) + np.float32(eps))
-    inv_rms = np.float32(1.0 / np.sqrt(np.float64(mean)))
+    inv_rms = pm("rsqrt", mean)
     gain = np.float32(1.0) + bf16_float(norm_bits)
     x = h * gain
     return bf16_bits(h), x, inv_rms, bf16_bits(x)
 
 
 def gated_product(gate, up):
-    """docs/spec/05_RESIDUAL_NORM_MLP.md:156-176: bf16(bf16(g / (1 + exp(-g))) * u) with
-    g = bf16(gate), u = bf16(up), float32 arithmetic (numpy's float32 exp stands in for
-    CUDA's expf; they can differ in the last bit)."""
+    """docs/spec/05_RESIDUAL_NORM_MLP.md:156-176, residual_norm_mlp.rs:137-156:
+    bf16(bf16(silu(g)) * u) with g = bf16(gate), u = bf16(up) and the portable silu
+    g / (1 + exp(-g)), float32 arithmetic."""
     g = bf16_float(bf16_bits(gate))
     u = bf16_float(bf16_bits(up))
-    with np.errstate(over="ignore"):  # exp(-g) overflows to +inf for g below about -88, as expf does
-        e = np.exp(-g)
-    silu = bf16_float(bf16_bits(g / (np.float32(1.0) + e)))
+    silu = bf16_float(bf16_bits(pm("silu", g)))
     return bf16_float(bf16_bits(silu * u))
 
 
@@ -248,22 +288,23 @@ def _xor_sum32(v):
 
 
 def normalize_head(y, weight_bits, eps):
-    """docs/spec/04_ATTENTION.md:27-37 (the inverse RMS correctly rounded; the reference
-    calls CUDA's rsqrtf, whose bits are not portable)."""
+    """docs/spec/04_ATTENTION.md:27-37; attention.rs:732-755 (the portable rsqrt:
+    the rounded square root, then a rounded division)."""
     y = np.asarray(y, np.float32)
     total = np.float32(0.0)
     for g in range(8):
         total = np.float32(total + _xor_sum32(y[32 * g:32 * g + 32] * y[32 * g:32 * g + 32]))
-    inv = np.float32(1.0 / np.sqrt(np.float64(np.float32(total / np.float32(256.0)) + np.float32(eps))))
+    inv = pm("rsqrt", np.float32(np.float32(total / np.float32(256.0)) + np.float32(eps)))
     return bf16_float(bf16_bits((y * inv) * (np.float32(1.0) + bf16_float(weight_bits))))
 
 
 def rope(n, position):
-    """docs/spec/04_ATTENTION.md:54-66 (numpy's float32 cos/sin stand in for CUDA's)."""
+    """docs/spec/04_ATTENTION.md:54-66; attention.rs:757-775 (the portable sincos)."""
     freq = np.array(ROPE_FREQ_BITS, np.uint32).view(np.float32)
     arg = np.float32(position) * freq
-    c = bf16_float(bf16_bits(np.cos(arg)))
-    s = bf16_float(bf16_bits(np.sin(arg)))
+    cos, sin = pm_sincos(arg)
+    c = bf16_float(bf16_bits(cos))
+    s = bf16_float(bf16_bits(sin))
     r = np.asarray(n, np.float32).copy()
     a, b = r[:32].copy(), r[32:64].copy()
     r[:32] = bf16_float(bf16_bits(bf16_float(bf16_bits(a * c)) + bf16_float(bf16_bits(-b * s))))
@@ -296,22 +337,27 @@ def _squares128(x):
 
 
 def _silu(x):
-    with np.errstate(over="ignore"):
-        return np.float32(x) / (np.float32(1.0) + np.exp(-np.float32(x)))
+    """portable_math.rs:201-203: x / (1 + exp(-x)) with the portable exp."""
+    return pm("silu", x)
 
 
 def gdn_gates(x_bits, inv_rms, wb_bits, wa_bits):
-    """docs/spec/03_GATED_DELTANET.md:57-76 for one row: 96 gates (b, then a)."""
+    """docs/spec/03_GATED_DELTANET.md:57-76, gated_deltanet.rs:612-644 for one row: the
+    gates of wb's rows, then wa's (96 at the 27B shape). Partition p of 128 sums elements
+    8p + 1024c + e (e < 8) over ceil(hidden / 1024) chunks, skipping indices past the end."""
     x = bf16_float(x_bits)
     w = np.concatenate([bf16_float(wb_bits), bf16_float(wa_bits)])
     out = np.empty(w.shape[0], np.float32)
     p = np.arange(128)
+    n = x.size
     for o in range(w.shape[0]):
         partial = np.zeros(128, np.float32)
-        for chunk in range(x.size // 1024):
+        for chunk in range(-(-n // 1024)):
             for e in range(8):
                 i = 8 * p + 1024 * chunk + e
-                partial = partial + w[o, i] * x[i]
+                ok = i < n
+                j = np.minimum(i, n - 1)
+                partial = np.where(ok, partial + w[o, j] * x[j], partial).astype(np.float32)
         out[o] = bf16_float(bf16_bits(_sum4([_xor_sum32(partial[32 * g:32 * g + 32]) for g in range(4)]) *
                                       np.float32(inv_rms)))
     return out
@@ -319,10 +365,10 @@ def gdn_gates(x_bits, inv_rms, wb_bits, wa_bits):
 
 def gdn_step(qkv, z, gates, conv_bits, a_log_bits, dt_bias_bits, norm_bits, eps, state, history_bits,
              n_commit=None):
-    """docs/spec/03_GATED_DELTANET.md:78-186, ordinary causal rows, numpy float32 with
-    correctly rounded 1/sqrt and numpy's exp/log1p for CUDA's rsqrtf/expf/log1pf. Commits
-    after n_commit rows (default all; 0 = provisional). Returns (out [M][6144], the
-    committed state [48][128][128], the committed history bits [3][10240])."""
+    """docs/spec/03_GATED_DELTANET.md:78-186 and gated_deltanet.rs:332-577, ordinary
+    causal rows, numpy float32 with the reference's portable rsqrt/exp/sigmoid/softplus/
+    silu. Commits after n_commit rows (default all; 0 = provisional). Returns (out
+    [M][6144], the committed state [48][128][128], the committed history bits [3][10240])."""
     qkv = np.asarray(qkv, np.float32)
     M = qkv.shape[0]
     proj = bf16_float(bf16_bits(qkv))
@@ -345,16 +391,15 @@ def gdn_step(qkv, z, gates, conv_bits, a_log_bits, dt_bias_bits, norm_bits, eps,
             q = conv[128 * kh:128 * kh + 128]
             k = conv[2048 + 128 * kh:2048 + 128 * kh + 128]
             v = conv[4096 + 128 * vh:4096 + 128 * vh + 128]
-            rq = np.float32(1.0 / np.sqrt(np.float64(np.float32(_squares128(q) + np.float32(1e-6)))))
-            rk = np.float32(1.0 / np.sqrt(np.float64(np.float32(_squares128(k) + np.float32(1e-6)))))
+            rq = pm("rsqrt", np.float32(_squares128(q) + np.float32(1e-6)))
+            rk = pm("rsqrt", np.float32(_squares128(k) + np.float32(1e-6)))
             query = (q * rq) * np.float32(0.08838834764831845)
             key = k * rk
             g = np.asarray(gates[row], np.float32)
-            with np.errstate(over="ignore"):
-                beta = bf16_float(bf16_bits(np.float32(1.0) / (np.float32(1.0) + np.exp(-g[vh]))))
-                x = np.float32(g[48 + vh] + dt_bias[vh])
-                sp = x if x > np.float32(20.0) else np.float32(np.log1p(np.exp(x)))
-                decay = np.exp(np.float32(-np.exp(a_log[vh]) * sp))
+            beta = bf16_float(bf16_bits(pm("sigmoid", g[vh])))
+            x = np.float32(g[48 + vh] + dt_bias[vh])
+            sp = pm("softplus", x)
+            decay = pm("exp", np.float32(-pm("exp", a_log[vh]) * sp))
             R = state[vh]
             parts = []
             for grp in range(4):
@@ -374,8 +419,7 @@ def gdn_step(qkv, z, gates, conv_bits, a_log_bits, dt_bias_bits, norm_bits, eps,
                     acc = acc + R[i] * query[i]
                 parts.append(acc)
             core = bf16_float(bf16_bits(_sum4(parts)))
-            inv = np.float32(1.0 / np.sqrt(np.float64(np.float32(_squares128(core) / np.float32(128.0)) +
-                                                      np.float32(eps))))
+            inv = pm("rsqrt", np.float32(np.float32(_squares128(core) / np.float32(128.0)) + np.float32(eps)))
             normalized = bf16_float(bf16_bits(norm_w * bf16_float(bf16_bits(core * inv))))
             out[row, 128 * vh:128 * vh + 128] = bf16_float(bf16_bits(normalized *
                                                                      _silu(z[row, 128 * vh:128 * vh + 128])))

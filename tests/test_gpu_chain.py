@@ -1,10 +1,11 @@
 """One MLP block as the reference's decode loop runs it (docs/spec/05_RESIDUAL_NORM_MLP.md:
 12-44), through the library's calls: residual + normalisation -> gate/up operator (one
 call, inverse RMS in its restore) -> gated product -> down operator (no inverse RMS) ->
-residual + normalisation of the next layer. Each stage is checked against the oracle
-given the device's input to that stage: the operators and the residual steps bit for
-bit, the inverse RMS within 2 ulp and the gated product within one bf16 ulp on at most
-0.1 % of the elements (CUDA's rsqrtf and expf, as the reference).
+residual + normalisation of the next layer. The oracle runs the same chain on its own,
+from the same inputs only (never the device's intermediate values), and every stage's
+device output equals it bit for bit: the operators' integer sums and restores, the
+residual steps, and the inverse RMS and SiLU through the scalar contract's portable
+functions.
 """
 import numpy as np
 import pytest
@@ -74,21 +75,23 @@ def test_mlp_block_chain(cuda):
     assert yskn_b200.status() == 0
 
     X, INV, G, U, MLP, D = (t.cpu().numpy() for t in (x, inv, g, u, mlp, d))
-    for m in range(M):
-        h, xm, r, _ = O.residual_prepare(hidden[m], attn_out[m], w_post, eps)
-        assert np.array_equal(h1.cpu().numpy().view(np.uint16)[m], h)
-        assert np.array_equal(_bits(X[m]), _bits(xm))
-        assert abs(int(np.float32(INV[m]).view(np.int32)) - int(np.float32(r).view(np.int32))) <= 2
-    assert np.array_equal(_bits(G), _bits(_oracle_linear(gate_spec, FFN, HIDDEN, X, INV)))
-    assert np.array_equal(_bits(U), _bits(_oracle_linear(up_spec, FFN, HIDDEN, X, INV)))
-    want_mlp = O.gated_product(G, U)
-    diff = _bits(MLP) != _bits(want_mlp)
-    assert diff.mean() <= 1e-3
-    assert np.abs((_bits(MLP) >> 16).astype(np.int64) - (_bits(want_mlp) >> 16).astype(np.int64)).max() <= 1
-    assert np.array_equal(_bits(D), _bits(_oracle_linear(down_spec, HIDDEN, FFN, MLP)))
-    H2 = dh.cpu().numpy().view(np.uint16)
-    X2 = x2.cpu().numpy()
-    for m in range(M):
-        h, xm, _, _ = O.residual_prepare(h1.cpu().numpy().view(np.uint16)[m], D[m], w_next, eps)
-        assert np.array_equal(H2[m], h)
-        assert np.array_equal(_bits(X2[m]), _bits(xm))
+    # The oracle's own chain.
+    stage1 = [O.residual_prepare(hidden[m], attn_out[m], w_post, eps) for m in range(M)]
+    h_o = np.stack([st[0] for st in stage1])
+    x_o = np.stack([st[1] for st in stage1])
+    inv_o = np.array([st[2] for st in stage1], np.float32)
+    g_o = _oracle_linear(gate_spec, FFN, HIDDEN, x_o, inv_o)
+    u_o = _oracle_linear(up_spec, FFN, HIDDEN, x_o, inv_o)
+    mlp_o = O.gated_product(g_o, u_o)
+    d_o = _oracle_linear(down_spec, HIDDEN, FFN, mlp_o)
+    stage2 = [O.residual_prepare(h_o[m], d_o[m], w_next, eps) for m in range(M)]
+    assert np.array_equal(h1.cpu().numpy().view(np.uint16), h_o)
+    assert np.array_equal(_bits(X), _bits(x_o))
+    assert np.array_equal(_bits(INV), _bits(inv_o))
+    assert np.array_equal(_bits(G), _bits(g_o))
+    assert np.array_equal(_bits(U), _bits(u_o))
+    assert np.array_equal(_bits(MLP), _bits(mlp_o))
+    assert np.array_equal(_bits(D), _bits(d_o))
+    assert np.array_equal(dh.cpu().numpy().view(np.uint16), np.stack([st[0] for st in stage2]))
+    assert np.array_equal(_bits(x2.cpu().numpy()), _bits(np.stack([st[1] for st in stage2])))
+    assert np.array_equal(_bits(inv2.cpu().numpy()), _bits(np.array([st[2] for st in stage2], np.float32)))

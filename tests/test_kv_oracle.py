@@ -5,6 +5,8 @@ Pins:
     (crates/yskn-ref/src/kv_codec_tests.rs:427-470): every encode path (packed,
     int8, residual with basis and mean, guard, Viterbi) byte for byte;
   * the prefix schedule's expected plans (crates/yskn-ref/src/attention.rs:1117-1138);
+  * attend_head's 256 output bit patterns of the length-76 int8-row case
+    (crates/yskn-ref/src/attention.rs:1244-1306), with the portable exp2/exp;
   * packed_state of the vectorised decoder against the C restatement of
     kv_codec.rs:467-475, and attend_head against plain float64 softmax attention.
 """
@@ -113,3 +115,18 @@ def test_inverse_rotation_is_orthogonal_up_to_scale():
     v = np.random.default_rng(3).standard_normal(256).astype(np.float32)
     r = kv.inverse_rotate(v)
     assert abs(np.linalg.norm(r) - np.linalg.norm(v)) < 1e-4 * np.linalg.norm(v)  # H256/16 is orthonormal
+
+
+def test_length_76_attention_pins_absolute_tile_output_bits():
+    """attention.rs:1244-1306: a query over 75 int8 prefix rows plus the self row; the 31
+    splits of prefix_schedule(76) cross 32-key tile boundaries at absolute positions."""
+    c = np.arange(256)
+    query = (((c * 7) % 29).astype(np.float32) - np.float32(14.0)) * np.float32(0.03125)
+    kb = np.stack([(((p * 13 + c * 7) % 255) - 127).astype(np.float32) for p in range(76)])
+    vb = np.stack([(((p * 19 + (c % 16) * 11) % 255) - 127).astype(np.float32) for p in range(76)])
+    ks = np.array([(p % 7 + 1) * 0.0078125 for p in range(76)], np.float32)
+    vs = np.array([(p % 11 + 1) * 0.015625 for p in range(76)], np.float32)
+    out = kv.attend_head(query, kb, ks, vb, vs, None, 76, 31)
+    expected = [0xbede440b, 0xbeacaee9, 0x3ce1ab7d, 0xbdb714de, 0xbd938526, 0x3ef5474a, 0x3e3fbe6c, 0x3f4c2f7e,
+                0x3f26e245, 0x3f811d5b, 0x3f09e0ce, 0x3f0e8ea2, 0xbde6e0e7, 0xbeb1494b, 0xbccde3de, 0xbf2b79d6]
+    assert out.view(np.uint32).tolist() == expected * 16

@@ -97,6 +97,16 @@ def test_head_select_matches_a_scalar_scan():
         assert token == want[0][1]
 
 
+def _rsqrt(x):
+    """portable_math.rs:106-109 one step at a time: the square root rounded to binary32
+    (numpy's float32 sqrt is correctly rounded), then a rounded division."""
+    return _f(_f(1.0) / np.sqrt(_f(x)))
+
+
+def _pexp(x):
+    return _f(O.pm_scalar("exp", float(_f(x))))
+
+
 def _f(x):
     return np.float32(x)
 
@@ -132,7 +142,7 @@ def test_residual_sum_of_squares_matches_a_scalar_restatement():
         h, _, inv, _ = O.residual_prepare(hidden, proj, O.bf16_bits(np.zeros(1024, np.float32)), 1e-6)
         total = _scalar_total_squares(O.bf16_float(h))
         mean = _f(_f(total / _f(1024.0)) + _f(1e-6))
-        assert np.float32(inv).view(np.uint32) == np.float32(1.0 / np.sqrt(np.float64(mean))).view(np.uint32)
+        assert np.float32(inv).view(np.uint32) == _rsqrt(mean).view(np.uint32)
 
 
 def test_gdn_gates_match_a_scalar_restatement():
@@ -187,13 +197,14 @@ def test_head_norm_and_rope_match_a_scalar_restatement():
         for off in (16, 8, 4, 2, 1):
             a = [_f(a[i] + a[i ^ off]) for i in range(32)]
         total = _f(total + a[0])
-    inv = _f(1.0 / np.sqrt(np.float64(_f(_f(total / _f(256.0)) + _f(eps)))))
+    inv = _rsqrt(_f(_f(total / _f(256.0)) + _f(eps)))
     n = [_bf(_f(_f(y[i] * inv) * _f(_f(1.0) + w[i]))) for i in range(256)]
     freq = np.array(O.ROPE_FREQ_BITS, np.uint32).view(np.float32)
     want = list(n)
     for i in range(32):
         arg = _f(_f(pos) * freq[i])
-        c, s = _bf(np.cos(arg)), _bf(np.sin(arg))
+        cs, sn = O.pm_sincos(np.float32(arg))
+        c, s = _bf(cs), _bf(sn)
         want[i] = _bf(_bf(n[i] * c) + _bf(-n[i + 32] * s))
         want[i + 32] = _bf(_bf(n[i + 32] * c) + _bf(n[i] * s))
     assert np.array_equal(np.asarray(got, np.float32).view(np.uint32), np.array(want, np.float32).view(np.uint32))
@@ -213,7 +224,7 @@ def test_gdn_step_matches_a_scalar_restatement_for_one_head():
     vh, kh = 7, 2
     cw = O.bf16_float(conv_bits).reshape(-1, 4)
     hf = O.bf16_float(hist)
-    silu = lambda v: _f(_f(v) / _f(_f(1.0) + np.exp(-_f(v))))  # noqa: E731
+    silu = lambda v: _f(_f(v) / _f(_f(1.0) + _pexp(-_f(v))))  # noqa: E731
 
     def conv(c):
         taps = [hf[0, c], hf[1, c], hf[2, c], _bf(x["qkv"][0, c])]
@@ -234,15 +245,15 @@ def test_gdn_step_matches_a_scalar_restatement_for_one_head():
     q = [conv(128 * kh + j) for j in range(128)]
     k = [conv(2048 + 128 * kh + j) for j in range(128)]
     v = [conv(4096 + 128 * vh + j) for j in range(128)]
-    rq = _f(1.0 / np.sqrt(np.float64(_f(squares128(q) + _f(1e-6)))))
-    rk = _f(1.0 / np.sqrt(np.float64(_f(squares128(k) + _f(1e-6)))))
+    rq = _rsqrt(_f(squares128(q) + _f(1e-6)))
+    rk = _rsqrt(_f(squares128(k) + _f(1e-6)))
     query = [_f(_f(qq * rq) * _f(0.08838834764831845)) for qq in q]
     key = [_f(kk * rk) for kk in k]
     g = x["gates"][0]
-    beta = _bf(_f(_f(1.0) / _f(_f(1.0) + np.exp(-_f(g[vh])))))
+    beta = _bf(_f(_f(1.0) / _f(_f(1.0) + _pexp(-_f(g[vh])))))
     xa = _f(g[48 + vh] + O.bf16_float(dt_bits)[vh])
-    sp = xa if xa > _f(20.0) else _f(np.log1p(np.exp(xa)))
-    decay = np.exp(_f(-np.exp(O.bf16_float(a_log_bits)[vh]) * sp))
+    sp = xa if xa > _f(20.0) else _f(O.pm_scalar("log1p", _pexp(xa)))
+    decay = _pexp(_f(-_pexp(O.bf16_float(a_log_bits)[vh]) * sp))
     R = state[vh].copy()
     core = []
     for j in range(128):
@@ -264,7 +275,7 @@ def test_gdn_step_matches_a_scalar_restatement_for_one_head():
                 acc = _f(acc + _f(R[i, j] * query[i]))
             parts.append(acc)
         core.append(_bf(_f(_f(_f(parts[0] + parts[1]) + parts[2]) + parts[3])))
-    inv = _f(1.0 / np.sqrt(np.float64(_f(_f(squares128(core) / _f(128.0)) + _f(1e-6)))))
+    inv = _rsqrt(_f(_f(squares128(core) / _f(128.0)) + _f(1e-6)))
     nw = O.bf16_float(norm_bits)
     want = [_bf(_f(_bf(_f(nw[j] * _bf(_f(core[j] * inv)))) * silu(x["z"][0, 128 * vh + j]))) for j in range(128)]
     assert np.array_equal(out[0, 128 * vh:128 * vh + 128].view(np.uint32), np.array(want, np.float32).view(np.uint32))

@@ -5,11 +5,12 @@
 // :1091-1104), the cache rotation (src/kvx_codec.cuh:11-48); scalar spec docs/spec/
 // 04_ATTENTION.md:15-106 with the helpers of 03_GATED_DELTANET.md:5-32. Per row and head:
 //   y = bf16(projection); the query heads' gate halves are saved as bf16;
-//   queries and keys: normalised by the head's RMS (8 groups of 32, xor_sum32, rsqrtf) times
-//   (1 + weight), bf16; RoPE on channels i, i+32 (i < 32) with bf16(cosf/sinf(p * freq[i]));
+//   queries and keys: normalised by the head's RMS (8 groups of 32, xor_sum32, rsqrt) times
+//   (1 + weight), bf16; RoPE on channels i, i+32 (i < 32) with bf16(cos/sin(p * freq[i]));
 //   every query, key and value: x * cache_sign -> H256 (distances 1..128) -> * 1/16;
 //   queries rounded to bf16, keys and values left in f32 (the encoder's input).
-// cosf, sinf and rsqrtf are CUDA's, as in the reference (ATT-02 of the spec).
+// rsqrt and sincos are the scalar contract's portable functions (attention.rs:732-775,
+// portable_math.rs:106-109,406-434; pmath.cuh), so every output equals yskn-ref's bits.
 //
 // B200 design: one warp per (row, head); lane l holds channels l + 32g (g = 0..7), so a
 // group of 32 channels is one value per lane (xor_sum32 is a shuffle butterfly), RoPE's
@@ -18,6 +19,7 @@
 #include <cuda_bf16.h>
 
 #include "common.cuh"
+#include "pmath.cuh"
 
 namespace yskn {
 
@@ -56,6 +58,7 @@ struct PrepParams {
   uint16_t* gate;   // bf16 [M][n_qh][256]
   float* k_rot;     // [M][n_kvh][256]
   float* v_rot;     // [M][n_kvh][256]
+  unsigned* err;    // device error word
 };
 
 constexpr int PREP_WARPS = 8;
@@ -91,14 +94,16 @@ __global__ void __launch_bounds__(PREP_WARPS * 32) attention_prep_kernel(const _
       for (int off = 16; off > 0; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
       total = __fadd_rn(total, s);
     }
-    const float inv = rsqrtf(__fadd_rn(__fdiv_rn(total, 256.0f), p.eps));
+    const float inv = pm_rsqrt(__fadd_rn(__fdiv_rn(total, 256.0f), p.eps));
     const uint16_t* w = kind == 0 ? p.q_norm : p.k_norm;
 #pragma unroll
     for (int g = 0; g < 8; ++g)
       x[g] = bf(__fmul_rn(__fmul_rn(x[g], inv), __fadd_rn(1.0f, __uint_as_float((uint32_t)w[32 * g + lane] << 16))));
     // RoPE on channels (lane, lane + 32) = slots 0 and 1.
     const float arg = __fmul_rn((float)p.positions[m], __uint_as_float(c_rope_freq[lane]));
-    const float c = bf(cosf(arg)), s = bf(sinf(arg));
+    float cs, sn;
+    if (!pm_sincos(arg, &cs, &sn)) raise_device_error(p.err, DERR_RANGE);  // a position beyond the reduction's range
+    const float c = bf(cs), s = bf(sn);
     const float n0 = x[0], n1 = x[1];
     x[0] = bf(__fadd_rn(bf(__fmul_rn(n0, c)), bf(__fmul_rn(-n1, s))));
     x[1] = bf(__fadd_rn(bf(__fmul_rn(n1, c)), bf(__fmul_rn(n0, s))));
@@ -148,7 +153,8 @@ extern "C" YSKN_B200_API int yskn_b200_attention_prep(const float* d_q, const fl
   if (!d_q || !d_k || !d_v || !d_q_norm || !d_k_norm || !d_positions || !d_query || !d_gate || !d_k_rot || !d_v_rot ||
       M < 1 || n_qh < 1 || n_kvh < 1)
     return fail(YSKN_EINVAL, "attention_prep: null argument or empty shape");
-  PrepParams p{d_q, d_k, d_v, d_q_norm, d_k_norm, d_positions, eps, M, n_qh, n_kvh, d_query, d_gate, d_k_rot, d_v_rot};
+  PrepParams p{d_q, d_k, d_v, d_q_norm, d_k_norm, d_positions, eps, M, n_qh, n_kvh, d_query, d_gate, d_k_rot, d_v_rot,
+               device_error_word()};
   const int64_t items = (int64_t)M * (n_qh + 2 * n_kvh);
   if (items > (int64_t)INT32_MAX) return fail(YSKN_EINVAL, "attention_prep: too many rows");
   return cuda_fail(launch_pdl(attention_prep_kernel, (unsigned)((items + PREP_WARPS - 1) / PREP_WARPS),

@@ -8,8 +8,9 @@
 // commits after n_commit rows (:160-186): the state is saved when row + 1 == n_commit and
 // the history takes the newest committed rows; n_commit = 0 is the provisional
 // verification pass that changes neither. The
-// transcendental helpers are CUDA's expf, rsqrtf and log1pf, as in the reference
-// (GDN-01 of the spec: their bits are not portable).
+// transcendental helpers are the scalar contract's portable exp, rsqrt, sigmoid, softplus
+// and silu (gated_deltanet.rs:332-577, portable_math.rs; pmath.cuh), so the outputs and
+// the state equal yskn-ref's bits.
 //
 // B200 design:
 //  * gates: one 128-thread CTA per (output, 8 rows); thread p forms partial p (40 products in
@@ -29,6 +30,7 @@
 #include <cuda_bf16.h>
 
 #include "common.cuh"
+#include "pmath.cuh"
 
 namespace yskn {
 
@@ -42,9 +44,6 @@ __device__ __forceinline__ float bf(float x) {
   return __uint_as_float((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(x)) << 16);
 }
 __device__ __forceinline__ float bf16f(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
-__device__ __forceinline__ float silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
-__device__ __forceinline__ float sigmoid(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x))); }
-__device__ __forceinline__ float softplus(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
 __device__ __forceinline__ float xor_sum32(float v) {
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
@@ -138,7 +137,7 @@ __device__ __forceinline__ float gdn_conv(const float (&x)[4], const float (&w)[
   a = __fadd_rn(a, __fmul_rn(w[1], x[1]));
   a = __fadd_rn(a, __fmul_rn(w[2], x[2]));
   a = __fadd_rn(a, __fmul_rn(w[3], x[3]));
-  return bf(silu(bf(a)));
+  return bf(pm_silu(bf(a)));
 }
 
 __global__ void __launch_bounds__(GDN_STEP_THREADS) gdn_step_kernel(const __grid_constant__ GdnParams p) {
@@ -181,12 +180,12 @@ __global__ void __launch_bounds__(GDN_STEP_THREADS) gdn_step_kernel(const __grid
     }
     __syncthreads();
     if (grp == 0)
-      s_q[j] = __fmul_rn(__fmul_rn(y, rsqrtf(__fadd_rn(sum4(s_sq[0]), 1e-6f))), 0.08838834764831845f);
+      s_q[j] = __fmul_rn(__fmul_rn(y, pm_rsqrt(__fadd_rn(sum4(s_sq[0]), 1e-6f))), 0.08838834764831845f);
     else if (grp == 1)
-      s_k[j] = __fmul_rn(y, rsqrtf(__fadd_rn(sum4(s_sq[1]), 1e-6f)));
-    const float beta = bf(sigmoid(cur.gb));
-    const float log_decay = __fmul_rn(-expf(a_log), softplus(__fadd_rn(cur.ga, dt_bias)));
-    const float decay = expf(log_decay);
+      s_k[j] = __fmul_rn(y, pm_rsqrt(__fadd_rn(sum4(s_sq[1]), 1e-6f)));
+    const float beta = bf(pm_sigmoid(cur.gb));
+    const float log_decay = __fmul_rn(-pm_exp(a_log), pm_softplus(__fadd_rn(cur.ga, dt_bias)));
+    const float decay = pm_exp(log_decay);
     __syncthreads();
     // 03_GATED_DELTANET.md:123-143: rows i0..i0+31 of column j.
     const float4* k4 = reinterpret_cast<const float4*>(s_k + i0);
@@ -228,9 +227,9 @@ __global__ void __launch_bounds__(GDN_STEP_THREADS) gdn_step_kernel(const __grid
     }
     __syncthreads();
     if (grp == 0) {
-      const float inv = rsqrtf(__fadd_rn(__fdiv_rn(sum4(s_so), 128.0f), p.eps));
+      const float inv = pm_rsqrt(__fadd_rn(__fdiv_rn(sum4(s_so), 128.0f), p.eps));
       const float normalized = bf(__fmul_rn(bf16f(p.norm_w[j]), bf(__fmul_rn(core, inv))));
-      p.out[(size_t)row * GDN_V_HEADS * GDN_DK + GDN_DK * vh + j] = bf(__fmul_rn(normalized, silu(cur.z)));
+      p.out[(size_t)row * GDN_V_HEADS * GDN_DK + GDN_DK * vh + j] = bf(__fmul_rn(normalized, pm_silu(cur.z)));
     }
     if (row + 1 == p.n_commit)
 #pragma unroll

@@ -40,7 +40,7 @@
 // (a funnel shift for a word's first state) and one LOP3.
 // Then the warps' (max, den, O) are merged, the self row added (FP32 weight, as the
 // spec keeps it separate) and den * mean; the CTA writes its split partial. The splits
-// of a (query row, KV head) are combined (padded to a power of two, native expf),
+// of a (query row, KV head) are combined (padded to a power of two, the portable exp),
 // divided, inverse-rotated (H256 with the hash signs), rounded to BF16 and multiplied by
 // the BF16 sigmoid of the gate: when the grid is one wave of CTAs, by the last G CTAs to
 // arrive (an arrival counter in a static device array), one query head each with the
@@ -54,6 +54,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "pmath.cuh"
 
 namespace yskn {
 
@@ -170,7 +171,7 @@ __device__ __forceinline__ float kv_cache_sign(int channel) {  // attention.rs:9
 }
 
 // The split combination of one query head's partials (q35_combine_kernel; spec
-// 04_ATTENTION.md:428-453: pad to a power of two, native expf, divide), the inverse
+// 04_ATTENTION.md:428-453: pad to a power of two, the portable exp, divide), the inverse
 // cache rotation, BF16 and the gate, by one warp: lane l owns channels 8l..8l+7, so
 // the H256 strides 1..4 stay in the lane and 8..128 are lane shuffles (ascending).
 // One warp: the splits' weights comb[s] = exp(max_s - max) (zero for the padding) and
@@ -195,7 +196,7 @@ __device__ __forceinline__ float kv_split_weights(const float* P, int n_splits, 
   for (int i = 0; i < 2; ++i) {
     const int s = lane + 32 * i;
     if (s >= padded) break;
-    const float f = ms[i] > -1e29f ? expf(ms[i] - mx) : 0.0f;
+    const float f = ms[i] > -1e29f ? pm_exp(ms[i] - mx) : 0.0f;
     comb[s] = f;
     if (s < n_splits) tot += f * ds[i];
   }
@@ -322,7 +323,7 @@ __device__ void finish_head(const KvParams& p, float (&v)[8], uint4 gate8, size_
     if (p.gate) {
       const uint32_t gw = (&gate8.x)[e >> 1];
       const float gv = __uint_as_float((e & 1) ? (gw & 0xffff0000u) : (gw << 16));
-      const float sg = __bfloat162float(__float2bfloat16_rn(1.0f / (1.0f + expf(-gv))));
+      const float sg = __bfloat162float(__float2bfloat16_rn(pm_sigmoid(gv)));
       o = r * sg;
     }
     const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(o));

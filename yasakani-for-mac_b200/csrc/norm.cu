@@ -7,7 +7,7 @@
 // docs/spec/05_RESIDUAL_NORM_MLP.md:53-141. Per token row (cols a multiple of 512):
 //   hidden[i] = bf16(hidden[i] + bf16(projection[i]))         (skipped without a projection)
 //   sum of squares of hidden, in the spec's reduction shape, per 512 columns, blocks in order
-//   inverse_rms = rsqrtf(total / cols + eps)
+//   inverse_rms = rsqrt(total / cols + eps)                  (the portable rsqrt: rounded sqrt, rounded division)
 //   input[i] = hidden[i] * (1 + norm_weight[i])               (binary32, the next operator's x)
 //   gate[i] = bf16(input[i])                                   (optional copy)
 // The next compressed operator quantises `input` and applies inverse_rms in its restore
@@ -24,6 +24,7 @@
 #include <cuda_bf16.h>
 
 #include "common.cuh"
+#include "pmath.cuh"
 
 namespace yskn {
 
@@ -70,14 +71,15 @@ __global__ void __launch_bounds__(NORM_THREADS * NORM_GROUPS) residual_prepare_k
       for (int g = 0; g < NORM_THREADS / 32; ++g) block = __fadd_rn(block, s_group[4 * b + g]);
       total = __fadd_rn(total, block);
     }
-    inv_rms[row] = rsqrtf(__fadd_rn(__fdiv_rn(total, (float)cols), eps));
+    inv_rms[row] = pm_rsqrt(__fadd_rn(__fdiv_rn(total, (float)cols), eps));
   }
 }
 
 // MLP nonlinear step (src/q35_kernels.cu:1402-1421, 113-116; docs/spec/
 // 05_RESIDUAL_NORM_MLP.md:156-176): with g = bf16(gate), u = bf16(up),
-// out = bf16(bf16(g / (1 + expf(-g))) * u), written as f32 so it is the down projection's
-// x directly. expf is CUDA's, as in the reference. Four elements per thread.
+// out = bf16(bf16(silu(g)) * u), written as f32 so it is the down projection's x directly;
+// silu(g) = g / (1 + exp(-g)) with the portable exp of the scalar contract
+// (residual_norm_mlp.rs:137-156, portable_math.rs:201-203). Four elements per thread.
 __global__ void __launch_bounds__(256) gated_product_kernel(const float* gate, const float* up, int64_t n, float* out) {
   pdl_begin();
   const int64_t i0 = 4 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x);
@@ -88,7 +90,7 @@ __global__ void __launch_bounds__(256) gated_product_kernel(const float* gate, c
     if (k >= k_end) break;
     const float g = bf16_to_f32(f32_to_bf16(gate[i0 + k]));
     const float u = bf16_to_f32(f32_to_bf16(up[i0 + k]));
-    const float silu = bf16_to_f32(f32_to_bf16(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g)))));
+    const float silu = bf16_to_f32(f32_to_bf16(pm_silu(g)));
     out[i0 + k] = bf16_to_f32(f32_to_bf16(__fmul_rn(silu, u)));
   }
 }

@@ -77,6 +77,7 @@ _SIGNATURES = {
     "yskn_b200_attention_prep": (_i, [_vp] * 6 + [C.c_float, _i, _i, _i] + [_vp] * 5),
     "yskn_b200_gdn_gates": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp, _vp]),
     "yskn_b200_widen_bf16": (_i, [_vp, C.c_int64, _vp, _vp]),
+    "yskn_b200_portable_math": (_i, [_i, _vp, C.c_int64, _vp, _vp, _vp]),
     "yskn_b200_gdn_step": (_i, [_vp] * 7 + [C.c_float, _i, _i, _vp, _vp, _vp, _vp]),
 }
 
@@ -477,6 +478,17 @@ def linear(mats, x, work, ys, inv_rms=None, stream=None):
     yp = (C.c_void_p * len(ys))(*[y.data_ptr() for y in ys])
     check(lib().yskn_b200_linear(_handles(mats), len(mats), _ptr(x), x.shape[0], _ptr(inv_rms), _ptr(work), yp,
                                  _stream(stream)), "linear")
+
+
+PORTABLE_FN = {"exp": 0, "exp2": 1, "log": 2, "log1p": 3, "sigmoid": 4, "silu": 5, "softplus": 6, "rsqrt": 7,
+               "sincos": 8}
+
+
+def portable_math(name, x, y, y2=None, stream=None):
+    """yskn_b200_portable_math: the device portable function `name` over the f32 tensor x
+    into y (sincos: cosine into y, sine into y2)."""
+    check(lib().yskn_b200_portable_math(PORTABLE_FN[name], _ptr(x), x.numel(), _ptr(y), _ptr(y2), _stream(stream)),
+          "portable_math")
 
 
 def status(stream=None):

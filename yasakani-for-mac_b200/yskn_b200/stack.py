@@ -57,7 +57,8 @@ def token_bytes(layers, vocab, ctx, bits=8):
 class Stack:
     """Seeded weights, caches, states and buffers of the stack on one device."""
 
-    def __init__(self, device, layers=64, vocab=VOCAB, ctx=4096, bits=8, seed=1):
+    def __init__(self, device, layers=64, vocab=VOCAB, ctx=4096, bits=8, seed=1, kinds=None):
+        """kinds: an explicit list of layer kinds ('gdn' / 'attn'), else layer_kinds(layers)."""
         import torch
         self.torch, self.dev = torch, device
         self.layers, self.vocab, self.ctx, self.bits = layers, vocab, ctx, bits
@@ -68,7 +69,8 @@ class Stack:
         self._keep = []
         t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(device)  # noqa: E731
         bfb = lambda a: t(self._bf16(a).view(np.int16))  # noqa: E731
-        self.kinds = layer_kinds(layers)
+        self.kinds = list(kinds) if kinds is not None else layer_kinds(layers)
+        self.layers = layers = len(self.kinds)
         self.L = []
         for i, kind in enumerate(self.kinds):
             L = {"kind": kind, "in_norm": bfb(self._normal(HIDDEN) * 0.1), "post_norm": bfb(self._normal(HIDDEN) * 0.1),
@@ -98,6 +100,7 @@ class Stack:
                                   device=device, generator=self.gen)
         lut16, sc16 = synthetic.model_tables(vocab, int(self.rng.integers(1 << 30)))
         self._keep.append(emb_codes)
+        self.embedding_source = (emb_codes, lut16, sc16)
         self.embedding = Y.Embedding([(emb_codes, bits, lut16, sc16)], vocab, HIDDEN, self._sign(0, HIDDEN))
         # the synthetic KV profile (the codebook of synthetic.kv_codebook_bf16): one table per
         # (side, head) group, multipliers 0.9 / 1.0 / 1.1
@@ -151,8 +154,10 @@ class Stack:
                               device=self.dev, generator=self.gen)
         lut16, sc16 = synthetic.model_tables(rows, int(self.rng.integers(1 << 30)))
         self._keep.append(words)
-        return Y.Matrix(words, "warp", rows, rows, cols, self.bits, lut16, sc16, self._sign(0, cols),
-                        self._sign(cols, rows) if rotate else None)
+        m = Y.Matrix(words, "warp", rows, rows, cols, self.bits, lut16, sc16, self._sign(0, cols),
+                     self._sign(cols, rows) if rotate else None)
+        m.source = (words, lut16, sc16, rotate)  # what a checker needs to rebuild the matrix
+        return m
 
     def decode(self, stream=None):
         """One token: reads self.token, writes the next greedy token into it."""
