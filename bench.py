@@ -46,8 +46,9 @@ LAYER = [("q_proj", 12288, 5120), ("k_proj", 1024, 5120), ("v_proj", 1024, 5120)
 ROW_PARALLEL = {"o_proj", "out_proj", "down_proj"}
 CALLS = [["q_proj", "k_proj", "v_proj"], ["o_proj"], ["in_proj_qkv", "in_proj_z"], ["out_proj"],
          ["gate_proj", "up_proj"], ["down_proj"]]
-# DRAM bytes (read + write) of the six fused gemv_kernel launches of one step, from one
-# ncu capture of this workload (profiles/gemv_kernel_layer_bits8.md); None where not captured.
+# DRAM bytes (read + write) of the six fused operator launches of one step, summed over one
+# ncu capture of this workload (bits 8, M 1: dram__bytes_read.sum + dram__bytes_write.sum);
+# a static capture, not measured in the run. None where no capture exists.
 GEMV_TRAFFIC = {(8, 1): 247_838_976}
 METRIC = "compressed GEMV HBM TB/s (one hybrid layer's linear set, batch-1 decode)"
 UNIT = "TB/s"
@@ -66,15 +67,20 @@ def measured_peaks():
 HBM_FALLBACK_GBS = 6650.0  # an earlier copy-bandwidth measurement on this pool, used without the file
 
 
-def make_weights(bits, seed0=1000):
-    import yskn_b200 as Y
+def make_weights(bits, seed0=1000, signs=None):
+    """The layer set's synthetic matrices. `signs(rule, seed, offset, n)` makes the sign
+    streams: the library's host helper for the B200 arm, the oracle's for the CPU arm (so
+    the reference arm never loads the product library)."""
     from yskn_b200 import synthetic
+    if signs is None:
+        import yskn_b200 as Y
+        signs = Y.signs
     out = {}
     for i, (name, rows, cols) in enumerate(LAYER):
         words, lut16, sc16 = synthetic.model_matrix(rows, cols, bits, seed0 + 17 * i)
         out[name] = dict(rows=rows, cols=cols, words=words, lut16=lut16, sc16=sc16,
-                         s_in=Y.signs("mulberry32_7919_13", 7, 0, cols),
-                         s_out=Y.signs("mulberry32_7919_13", 7, cols, rows))
+                         s_in=signs("mulberry32_7919_13", 7, 0, cols),
+                         s_out=signs("mulberry32_7919_13", 7, cols, rows))
     return out
 
 
@@ -183,7 +189,8 @@ def prepare_cpu(W, bits):
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    W = make_weights(args.bits)
+    import oracle as O
+    W = make_weights(args.bits, signs=O.signs)
     prepare_cpu(W, args.bits)
     xs = make_inputs(1)
     threads = os.cpu_count() or 1
@@ -209,7 +216,7 @@ def run_reference(args, rank, world):
             "config": config(args),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    return line
 
 
 def config(args):
@@ -404,7 +411,7 @@ def run_b200(args, rank, world, local_rank):
     peaks = measured_peaks()
     peak = peaks.get("hbm_gbs", HBM_FALLBACK_GBS)
     # The timed region is the dominant kernel's launches back to back (six fused
-    # gemv_kernel launches per step and rank, nothing else: the row-parallel exchange
+    # trellis_sums_kernel launches per step and rank, nothing else: the row-parallel exchange
     # runs inside them), so its average launch duration is the timed region's device
     # time / launches (inter-launch gaps in); per GPU, against one GPU's HBM peak.
     achieved = gemv_local * args.steps / (ms * 1e-3) / 1e9
@@ -441,7 +448,7 @@ def run_b200(args, rank, world, local_rank):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
                          "traffic": GEMV_TRAFFIC.get((args.bits, M)) if world == 1 else None,
-                         "kernel": "gemv_kernel (fused operator: quantise + weighted sums + restore; the 6 launches "
+                         "kernel": "trellis_sums_kernel (fused operator: quantise + weighted sums + restore; the 6 launches "
                                    "of each step, timed over the timed region)" + (
                                        "; rank 0's shards, row-parallel calls exchanging over NVLink in-kernel"
                                        if world > 1 else ""),
@@ -454,7 +461,48 @@ def run_b200(args, rank, world, local_rank):
             "clocks": sampler.summary(),
             "step_bytes": step_bytes, "us_per_call_alone": [round(1e3 * x, 2) for x in gemv_ms],
             "decode_27b": decode}
-    print(json.dumps(line), flush=True)
+    if world == 1 and not args.no_configs:
+        line["configs"] = other_configs(args, rank, world, local_rank)
+    return line
+
+
+def _summary(line, **extra):
+    """The figures of a sub-measurement that the default line carries."""
+    keep = ("metric", "value", "unit", "ms_per_step", "roofline", "e2e", "config", "gpu_launches", "clocks")
+    out = {k: line[k] for k in keep if k in line}
+    out.update(extra)
+    return out
+
+
+def other_configs(args, rank, world, local_rank):
+    """The path's other configurations, measured in the same run at N=1 so the default
+    line records every one (each with its own roofline; no CPU baselines here, the
+    dedicated --workload runs carry those): config 2 at the format's lowest width
+    (bits 6), config 3 at M=4096 (tcgen05 GEMM) and M=8 (verify), config 4 at 32k and 2k."""
+    import copy
+    import torch
+    out = {}
+
+    def sub(name, fn, **kw):
+        a = copy.copy(args)
+        a.skip_cpu, a.skip_stack, a.no_configs = True, True, True
+        a.steps = min(args.steps, 50)
+        for k, v in kw.items():
+            setattr(a, k, v)
+        try:
+            out[name] = _summary(fn(a, rank, world, local_rank))
+        except Exception as e:  # a sub-measurement that fails is reported, not hidden
+            out[name] = {"error": "%s: %s" % (type(e).__name__, e)}
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+
+    if args.bits != 6:
+        sub("linear_bits6", run_b200, bits=6)
+    sub("gemm_4096", run_gemm, gemm_m=4096)
+    sub("verify_8", run_gemm, gemm_m=8)
+    sub("kv4_32k", run_kv, ctx=32768)
+    sub("kv4_2k", run_kv, ctx=2048)
+    return out
 
 
 # --------------------------------------------------------------------- KV attention
@@ -655,7 +703,7 @@ def run_kv(args, rank, world, local_rank):
                     "d2h_bytes_per_step": int(d2h)},
             "gpu_launches": steps * 2 * KV_LAYERS,
             "clocks": sampler.summary(), "step_bytes": step_bytes}
-    print(json.dumps(line), flush=True)
+    return line
 
 
 def run_reference_kv(args, rank, world):
@@ -674,7 +722,7 @@ def run_reference_kv(args, rank, world):
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": kv_config(args, KV_LAYERS),
             "cpu_baseline": {"value": value, "unit": "GB/s", "cores": 1, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    return line
 
 
 # ------------------------------------------------------------------------------ GEMM
@@ -682,7 +730,7 @@ def run_reference_kv(args, rank, world):
 # (4096: prefill, 8: speculative verify) on one 17408 x 5120 bits=8 matrix; M >= 64 runs
 # the tcgen05 GEMM (predecode + kind::i8 MMA), smaller M the decode GEMV.
 GEMM_N, GEMM_K = 17408, 5120
-I8_PEAK_TOPS = 4375.8  # profiles/tcgen05_i8_peak.md (own kind::i8 measurement on this pool)
+I8_PEAK_TOPS = 4375.8  # own tcgen05 kind::i8 dense peak on this pool (peak/i8_peak.cu microbenchmark)
 
 
 def gemm_config(args):
@@ -782,11 +830,11 @@ def run_gemm(args, rank, world, local_rank):
             "scaling": "weak", "vs_baseline": None, "dtype": "i8", "data": "synthetic", "config": gemm_config(args),
             "roofline": ({"bound": "tensor", "achieved": achieved, "peak": I8_PEAK_TOPS, "unit": "TOPS",
                           "frac": achieved / I8_PEAK_TOPS, "traffic": None,
-                          "kernel": "predecode_kernel + gemm_kernel (weighted sums), device time",
-                          "peak_source": "own tcgen05 kind::i8 measurement, profiles/tcgen05_i8_peak.md"}
+                          "kernel": "trellis_predecode_kernel + trellis_mma_kernel (weighted sums), device time",
+                          "peak_source": "own tcgen05 kind::i8 microbenchmark (peak/i8_peak.cu) on this pool"}
                          if tensor else
                          {"bound": "hbm", "achieved": (N * K / 2 + 8192 + M * K + 8 * M * N) / (sums_ms * 1e-3) / 1e9,
-                          "peak": hbm_peak, "unit": "GB/s", "traffic": None, "kernel": "gemv_kernel (weighted sums)",
+                          "peak": hbm_peak, "unit": "GB/s", "traffic": None, "kernel": "trellis_sums_kernel (weighted sums)",
                           "frac": (N * K / 2 + 8192 + M * K + 8 * M * N) / (sums_ms * 1e-3) / 1e9 / hbm_peak,
                           "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in measured_peaks() else "fallback"}),
             "cpu_baseline": cpu,
@@ -794,7 +842,7 @@ def run_gemm(args, rank, world, local_rank):
                     "d2h_bytes_per_step": 4 * M * N},
             "gpu_launches": args.steps * (4 if tensor else 1), "clocks": sampler.summary(),
             "weighted_sums_ms": sums_ms}
-    print(json.dumps(line), flush=True)
+    return line
 
 
 def run_reference_gemm(args, rank, world):
@@ -829,7 +877,7 @@ def run_reference_gemm(args, rank, world):
                              "sample": "%d tokens x 2048-row blocks of the 17408 x 5120 matrix, %d samples of "
                                        "%.0f s (threaded int64 sums)" % (m, len(vals), budget)},
             "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    return line
 
 
 STACK_METRIC = "27B-shape decode tok/s (64-layer hybrid stack, batch 1)"
@@ -910,7 +958,8 @@ def run_reference_stack(args, rank, world):
     from yskn_b200 import stack as S
     if rank != 0:
         return
-    W = make_weights(args.bits)
+    import oracle as O
+    W = make_weights(args.bits, signs=O.signs)
     prepare_cpu(W, args.bits)
     xs = make_inputs(1)
     threads = os.cpu_count() or 1
@@ -926,14 +975,13 @@ def run_reference_stack(args, rank, world):
     value = (nbytes / dt) / tb
     sample = ("%d full layer-set steps of the CPU operator port (%.1f s), code bytes/s divided by one token's "
               "bytes (linears only)" % (n, dt))
-    print(json.dumps({"impl": "reference", "metric": STACK_METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+    return ({"impl": "reference", "metric": STACK_METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
                       "steps": n, "warmup": args.warmup, "ms_per_step": 1e3 / value, "higher_is_better": True,
                       "scaling": "weak", "vs_baseline": None, "dtype": "i8", "data": "synthetic",
                       "config": stack_config(args),
                       "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
                                        "sample": sample},
-                      "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
-          flush=True)
+                      "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
 
 
 def run_stack(args, rank, world, local_rank):
@@ -987,7 +1035,7 @@ def run_stack(args, rank, world, local_rank):
             "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
             "gpu_launches": args.steps * launches,
             "clocks": sampler.summary()}
-    print(json.dumps(line), flush=True)
+    return line
 
 
 def main():
@@ -1005,13 +1053,16 @@ def main():
     ap.add_argument("--gemm-m", type=int, default=4096, help="gemm: activation rows (4096 prefill, 8 verify)")
     ap.add_argument("--ctx", type=int, default=32768, help="kv4: cache rows per layer")
     ap.add_argument("--kv-splits", type=int, default=-1, help="kv4: 0 reference schedule, -1 one wave over the SMs")
+    ap.add_argument("--no-configs", action="store_true", help="linear: leave out the other configurations' figures")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        {"kv4": run_reference_kv, "gemm": run_reference_gemm, "stack": run_reference_stack}.get(
+        line = {"kv4": run_reference_kv, "gemm": run_reference_gemm, "stack": run_reference_stack}.get(
             args.workload, run_reference)(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
         return
     if world > 1:
         import datetime
@@ -1020,8 +1071,10 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local_rank))
     try:
-        {"kv4": run_kv, "gemm": run_gemm, "stack": run_stack}.get(args.workload, run_b200)(args, rank, world,
-                                                                                              local_rank)
+        line = {"kv4": run_kv, "gemm": run_gemm, "stack": run_stack}.get(args.workload, run_b200)(args, rank, world,
+                                                                                                     local_rank)
+        if line is not None and rank == 0:
+            print(json.dumps(line), flush=True)
     finally:
         if world > 1:
             import torch

@@ -8,11 +8,11 @@
 //
 // B200 design (replaces the reference's mt_predecode2_kernel + mt_gemm6_kernel,
 // src/q35_g6.cu:35-277, and pfa_kernel, src/pfa.cu:85-321):
-//  1. predecode_kernel: the codes of the matrix -> dense int8 W [N][Kc] (K-major)
+//  1. trellis_predecode_kernel: the codes of the matrix -> dense int8 W [N][Kc] (K-major)
 //     in a workspace, once per call (decoding inside the MMA loop would cost
 //     shared-memory bandwidth the tensor cores need; this is the reference's own
 //     choice for >= 256 rows, q35_g6.cu:35-69).
-//  2. gemm_kernel: persistent, one CTA per SM looping over 128 x 128 output tiles
+//  2. trellis_mma_kernel: persistent, one CTA per SM looping over 128 x 128 output tiles
 //     (128 activation rows x 128 weight rows) in a grouped raster. Warp 0 streams
 //     128-byte K chunks of both operands with TMA (128B swizzle, 5-stage mbarrier
 //     ring, counted across tiles); one thread of warp 1 issues
@@ -112,7 +112,7 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 // tile (8 rows x 256 columns); lane (n, q) decodes its 32 steps into 64 bytes of
 // row n. The table is read straight from L1 (4096 x 2 bytes).
 template <int BITS>
-__global__ void __launch_bounds__(256) predecode_kernel(const uint32_t* __restrict__ codes,
+__global__ void __launch_bounds__(256) trellis_predecode_kernel(const uint32_t* __restrict__ codes,
                                                         const uint16_t* __restrict__ lut, int row_blocks, int S,
                                                         int Kc, int8_t* __restrict__ W) {
   __shared__ uint16_t s_lut[4096];
@@ -166,7 +166,7 @@ struct GemmParams {
 constexpr int GM_GROUP = 16;  // activation tiles per raster group
 
 __global__ void __launch_bounds__(GM_THREADS, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap map_act, const __grid_constant__ CUtensorMap map_w,
+    trellis_mma_kernel(const __grid_constant__ CUtensorMap map_act, const __grid_constant__ CUtensorMap map_w,
                 const __grid_constant__ GemmParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -401,13 +401,13 @@ int launch_predecode(const MatrixDev& m, int8_t* W, cudaStream_t st) {
   const int64_t tiles = (int64_t)rb * S;
   const int blocks = (int)std::min<int64_t>(ceil_div(tiles, 8), 148 * 16);
   switch (m.bits) {
-    case 4: predecode_kernel<4><<<blocks, 256, 0, st>>>(m.codes, m.lut8, rb, S, m.cols, W); break;
-    case 5: predecode_kernel<5><<<blocks, 256, 0, st>>>(m.codes, m.lut8, rb, S, m.cols, W); break;
-    case 6: predecode_kernel<6><<<blocks, 256, 0, st>>>(m.codes, m.lut8, rb, S, m.cols, W); break;
-    case 7: predecode_kernel<7><<<blocks, 256, 0, st>>>(m.codes, m.lut8, rb, S, m.cols, W); break;
-    default: predecode_kernel<8><<<blocks, 256, 0, st>>>(m.codes, m.lut8, rb, S, m.cols, W); break;
+    case 4: trellis_predecode_kernel<4><<<blocks, 256, 0, st>>>(m.codes, m.lut8, rb, S, m.cols, W); break;
+    case 5: trellis_predecode_kernel<5><<<blocks, 256, 0, st>>>(m.codes, m.lut8, rb, S, m.cols, W); break;
+    case 6: trellis_predecode_kernel<6><<<blocks, 256, 0, st>>>(m.codes, m.lut8, rb, S, m.cols, W); break;
+    case 7: trellis_predecode_kernel<7><<<blocks, 256, 0, st>>>(m.codes, m.lut8, rb, S, m.cols, W); break;
+    default: trellis_predecode_kernel<8><<<blocks, 256, 0, st>>>(m.codes, m.lut8, rb, S, m.cols, W); break;
   }
-  return cuda_fail(cudaGetLastError(), "predecode_kernel");
+  return cuda_fail(cudaGetLastError(), "trellis_predecode_kernel");
 }
 
 int launch_gemm(const MatrixDev& m, const int8_t* act, const int32_t* scales, int M, int64_t* out, int out_rows,
@@ -418,8 +418,8 @@ int launch_gemm(const MatrixDev& m, const int8_t* act, const int32_t* scales, in
   if (int rc = make_map(&map_w, W, m.phys_pad8, m.cols)) return rc;
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
-  std::call_once(once, [] { attr = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GM_SMEM); });
-  if (attr != cudaSuccess) return cuda_fail(attr, "gemm_kernel attributes");
+  std::call_once(once, [] { attr = cudaFuncSetAttribute(trellis_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GM_SMEM); });
+  if (attr != cudaSuccess) return cuda_fail(attr, "trellis_mma_kernel attributes");
   GemmParams p{};
   p.scales = scales;
   p.out = out;
@@ -434,8 +434,8 @@ int launch_gemm(const MatrixDev& m, const int8_t* act, const int32_t* scales, in
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int grid = (int)std::min<int64_t>((int64_t)p.n_tiles * p.m_tiles, sms);  // persistent: one CTA per SM
-  gemm_kernel<<<grid, GM_THREADS, GM_SMEM, st>>>(map_act, map_w, p);
-  return cuda_fail(cudaGetLastError(), "gemm_kernel");
+  trellis_mma_kernel<<<grid, GM_THREADS, GM_SMEM, st>>>(map_act, map_w, p);
+  return cuda_fail(cudaGetLastError(), "trellis_mma_kernel");
 }
 
 }  // namespace yskn

@@ -294,7 +294,7 @@ struct Ranges {
 // rotation the int64 sums go to `out` and the warp that completes the last 8-row
 // block of a 512-row block (a counter per 512-row block) restores and rotates it.
 template <int BITS, bool M1, bool ACT_SMEM, bool FUSED>
-__global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
+__global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(16) uint8_t s_lut[];
   // Which matrix this CTA serves.
   int si = 0;
@@ -771,10 +771,10 @@ static int launch_one(const GemvParams& p, int grid, cudaStream_t st) {
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(gemv_kernel<BITS, M1, ACT_SMEM, FUSED>,
+    attr_err = cudaFuncSetAttribute(trellis_sums_kernel<BITS, M1, ACT_SMEM, FUSED>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT);
   });
-  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "gemv_kernel attributes");
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "trellis_sums_kernel attributes");
   const size_t smem = table_smem_bytes() + (ACT_SMEM ? act_smem_bytes(p.mv, p.Kc, FUSED) : 0);
   // Launched as a programmatic dependent of the previous kernel on the stream: the CTAs
   // may start on SMs that kernel has left and fetch their table and first codes while it
@@ -789,7 +789,7 @@ static int launch_one(const GemvParams& p, int grid, cudaStream_t st) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cuda_fail(cudaLaunchKernelEx(&cfg, gemv_kernel<BITS, M1, ACT_SMEM, FUSED>, p), "gemv_kernel");
+  return cuda_fail(cudaLaunchKernelEx(&cfg, trellis_sums_kernel<BITS, M1, ACT_SMEM, FUSED>, p), "trellis_sums_kernel");
 }
 
 template <int BITS>
