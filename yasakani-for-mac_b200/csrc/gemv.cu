@@ -129,23 +129,35 @@ __device__ __forceinline__ void load_unit(Unit<BITS>& u, const uint32_t* tile0, 
   }
 }
 
-// Bits [LO, HI) of the 32-bit window of V = [carry | w0 .. w_{BITS-1} | 0]
-// starting at bit p (other bits of the result are unspecified). Everything is a
-// compile-time constant after unrolling; a funnel shift (half rate on B200) is
-// used only when the needed bits straddle two words, otherwise one plain shift.
-template <int BITS, int LO, int HI>
-__device__ __forceinline__ uint32_t window(uint32_t carry, const uint32_t (&w)[BITS], int p) {
-  const int i = p >> 5, sh = p & 31;
-  const uint32_t lo = i == 0 ? carry : w[i - 1];
-  const uint32_t hi = i >= BITS ? 0u : w[i];
-  if (sh == 0) return lo;
-  if (sh + HI <= 32) return lo >> sh;         // only the low word contributes
-  if (sh + LO >= 32) return hi << (32 - sh);  // only the high word contributes
-  return __funnelshift_r(lo, hi, sh);
+template <int BITS>
+__device__ __forceinline__ uint32_t lut_copy_off(int lane) {
+  return BITS == 8 ? (uint32_t)(lane >> 1) << 3 : (uint32_t)(lane >> 1) << 1;
 }
 
-// Shared-memory byte address of state(step i) in this lane's table copy, one shift
-// (a funnel shift where the bits straddle two words) and one LOP3 either way.
+// hi32(a * b) + c and lo32(a * b) + c in one instruction each: with b a power of two they
+// are a right or left shift and an add.
+__device__ __forceinline__ uint32_t mad_hi(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("mad.hi.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+__device__ __forceinline__ uint32_t mad_lo(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+// One table entry at a shared-memory address (zero-extended).
+__device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
+  uint32_t v;
+  asm("ld.shared.u16 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
+// Shared-memory address of state(step i) in this lane's table copy. V = [carry | w0 ..
+// w_{BITS-1} | 0] is the lane's code words with the previous lane's last word in front;
+// the state's 12 bits end at bit 32 + BITS(i+1) of V, and the 17-bit window that
+// starts 5 bits below that end's state start holds them. Masked, they give the address
+// bits of the table image:
 // * bits = 8: the stored bytes carry the state's bits at 0,1 and 6..15 of bytes
 //   (i-1, i) (stream8_store, common.cuh); shifted left by one and masked, they fill
 //   address bits 1,2 and 7..16 around the copy (lane/2) in bits 3..6, so copy c sits
@@ -154,15 +166,24 @@ __device__ __forceinline__ uint32_t window(uint32_t carry, const uint32_t (&w)[B
 // * other bits: 4096 slots of 32 bytes (slot s holds 16 copies of entry s), the state
 //   in address bits 5..16, the copy in bits 1..4. Four lanes share the 4 banks
 //   {c, c+8, c+16, c+24} picked by the state's two low bits: ~3 wavefronts.
+// base is the image's shared address plus the lane's copy offset (the masked state
+// bits never overlap the copy field, so adding the copy equals or-ing it). Where the
+// state's bits come from one word, the mask and one multiply-add form the address
+// (hi32(x * 2^(32-sh)) + base is (x >> sh) + base, lo32(x * 2^k) + base is (x << k) +
+// base); where they straddle two words, a funnel shift, the mask and an add. All shift
+// amounts are compile-time constants after unrolling.
 template <int BITS>
-__device__ __forceinline__ uint32_t lut_addr(uint32_t carry, const uint32_t (&w)[BITS], int i, uint32_t copy_off) {
-  const int P = 32 + BITS * (i + 1) - 12;  // first bit of the state in V
-  if constexpr (BITS == 8) return (window<BITS, 1, 17>(carry, w, P - 5) & 0x1ff86u) | copy_off;
-  return (window<BITS, 5, 17>(carry, w, P - 5) & 0x1ffe0u) | copy_off;
-}
-template <int BITS>
-__device__ __forceinline__ uint32_t lut_copy_off(int lane) {
-  return BITS == 8 ? (uint32_t)(lane >> 1) << 3 : (uint32_t)(lane >> 1) << 1;
+__device__ __forceinline__ uint32_t lut_abs(uint32_t carry, const uint32_t (&w)[BITS], int i, uint32_t base) {
+  constexpr uint32_t MASK = BITS == 8 ? 0x1ff86u : 0x1ffe0u;
+  constexpr int LO = BITS == 8 ? 1 : 5, HI = 17;
+  const int p = 32 + BITS * (i + 1) - 12 - 5;
+  const int wi = p >> 5, sh = p & 31;
+  const uint32_t lo = wi == 0 ? carry : w[wi - 1];
+  const uint32_t hi = wi >= BITS ? 0u : w[wi];
+  if (sh == 0) return (lo & MASK) + base;
+  if (sh + HI <= 32) return mad_hi(lo & (MASK << sh), 1u << (32 - sh), base);
+  if (sh + LO >= 32) return mad_lo(hi & (MASK >> (32 - sh)), 1u << (32 - sh), base);
+  return (__funnelshift_r(lo, hi, sh) & MASK) + base;
 }
 
 // lo | hi << 16 on the FMA pipe (lo, hi are zero-extended 16-bit entries).
@@ -184,9 +205,8 @@ __device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, ui
 // a0p / a1p: the 64 activation bytes of quarter q for tokens n and n + 8 (shared
 // memory or global, same column permutation as the B fragments).
 template <int BITS, bool M1>
-__device__ __forceinline__ void sequence_mma(const uint32_t (&w)[BITS], int lane, const uint8_t* __restrict__ lut,
-                                             uint32_t copy_off, const uint4* a0p, const uint4* a1p, bool row0,
-                                             bool row1, int (&c)[4]) {
+__device__ __forceinline__ void sequence_mma(const uint32_t (&w)[BITS], int lane, uint32_t lut_base, const uint4* a0p,
+                                             const uint4* a1p, bool row0, bool row1, int (&c)[4]) {
   uint32_t carry = __shfl_up_sync(0xffffffffu, w[BITS - 1], 1);
   if ((lane & 3) == 0) carry = 0u;  // zeros before the start of the sequence (docs/FORMAT.md:121-128)
 #pragma unroll
@@ -202,9 +222,7 @@ __device__ __forceinline__ void sequence_mma(const uint32_t (&w)[BITS], int lane
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int i0 = 4 * t + 2 * h;
-        const uint32_t lo = *reinterpret_cast<const uint16_t*>(lut + lut_addr<BITS>(carry, w, i0, copy_off));
-        const uint32_t hi = *reinterpret_cast<const uint16_t*>(lut + lut_addr<BITS>(carry, w, i0 + 1, copy_off));
-        b[h] = pack_pair(lo, hi);
+        b[h] = pack_pair(lds_u16(lut_abs<BITS>(carry, w, i0, lut_base)), lds_u16(lut_abs<BITS>(carry, w, i0 + 1, lut_base)));
       }
       const uint32_t a0 = half ? x0.z : x0.x, a2 = half ? x0.w : x0.y;
       const uint32_t a1 = half ? x1.z : x1.x, a3 = half ? x1.w : x1.y;
@@ -486,6 +504,10 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
   if (t_begin >= t_end) return;
 
   const uint32_t copy_off = lut_copy_off<BITS>(lane);
+  // The lane's table copy as a shared-memory address. Passed through a volatile move
+  // after the barriers above, so no lookup that depends on it can be scheduled earlier.
+  uint32_t lut_base;
+  asm volatile("mov.u32 %0, %1;" : "=r"(lut_base) : "r"(smem_u32(s_lut) + copy_off));
   const int q = lane & 3, n = lane >> 2;
   const int tok0 = n < p.mv ? n : p.mv - 1;
   const int tok1 = n + 8 < p.mv ? n + 8 : p.mv - 1;
@@ -598,8 +620,8 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
     const uint4* a1p = reinterpret_cast<const uint4*>(act1 + col);
     // A half unit at either end of the range holds one tile (the integer dot of a half
     // group, scaled by the group's scale, adds up exactly with the other half's).
-    if (2 * u >= t_begin) sequence_mma<BITS, M1>(cur.w[0], lane, s_lut, copy_off, a0p, a1p, row0, row1, c);
-    if (2 * u + 1 < t_end) sequence_mma<BITS, M1>(cur.w[1], lane, s_lut, copy_off, a0p + 16, a1p + 16, row0, row1, c);
+    if (2 * u >= t_begin) sequence_mma<BITS, M1>(cur.w[0], lane, lut_base, a0p, a1p, row0, row1, c);
+    if (2 * u + 1 < t_end) sequence_mma<BITS, M1>(cur.w[1], lane, lut_base, a0p + 16, a1p + 16, row0, row1, c);
     const long long s0 = sc0[g], s1 = sc1[g];
     const long long t[4] = {s0 * c[0], s0 * c[1], s1 * c[2], s1 * c[3]};
     if (p.checked) {
@@ -946,6 +968,7 @@ int launch_linear_fused(const MatrixDev* mats, int n_mats, const float* x, int M
     if (M > 1 && mats[i].s_out && (s.base + 1) / (64 * 2 * (int64_t)p.G) + 2 > 32)
       return fail(YSKN_EINVAL, "fused linear: too many rows per warp");
   }
+
   return launch_bits_any(mats[0].bits, p, grid, true, st);
 }
 
