@@ -71,3 +71,21 @@ def test_head_operator_then_selection(cuda):
     for m in range(M):
         t, v, i = O.head_select(want_logits[m])
         assert tok[m] == t and np.array_equal(ti[m], i) and np.array_equal(tv[m], v)
+
+
+@pytest.mark.parametrize("M,n", [(70, 3000), (2, 300), (64, 151936)])
+def test_both_selection_levels_and_repeated_calls(cuda, M, n):
+    """Up to 64 rows of at least 592 logits take the two-level selection (148 chunks per row,
+    the last chunk's CTA merges); more rows or shorter rows take one CTA per row. Two calls
+    in a row give the same result (the two-level arrival counters return to zero)."""
+    rng = np.random.default_rng(M * 7 + n)
+    logits = rng.standard_normal((M, n)).astype(np.float32)
+    logits[:, rng.integers(0, n, 5)] = 2.5  # ties inside and across chunks
+    first = _select(logits)
+    second = _select(logits)
+    for a, b in zip(first, second):
+        assert np.array_equal(a, b)
+    tok, tv, ti = first
+    for m in range(M):
+        t, v, i = O.head_select(logits[m])
+        assert tok[m] == t and np.array_equal(ti[m], i) and np.array_equal(tv[m], v), m

@@ -9,10 +9,17 @@
 // the top 8 are the first eight of that order, unfilled places (fewer than eight
 // eligible logits) keep (-FLT_MAX, INT_MAX).
 //
-// B200 design: one CTA per row; every thread keeps the best eight of a strided share of
-// the row in registers (an insertion into a sorted list), then eight rounds of a
-// block-wide maximum over the threads' current heads pick the row's order, the winner
-// of each round stepping to its next entry. The row is read once.
+// B200 design: the candidates are totally ordered, so the first eight of a row are the
+// first eight of the union of any partition's first eights. Rows up to HEAD_SPLIT_ROWS per
+// call run in two levels inside one launch: HEAD_CHUNKS CTAs per row each take a
+// contiguous chunk of the row and write its first eight to scratch; the last CTA of the
+// row to arrive (a counter per row, reset by that CTA) merges the chunks' candidates.
+// Both levels use the same block selection: every thread keeps the best eight of a
+// strided share in registers (an insertion into a sorted list), then eight rounds of a
+// block-wide maximum over the threads' current heads pick the order, the winner of each
+// round stepping to its next entry. Larger calls take one CTA per row. The row is read
+// once either way. The scratch and the counters are static device arrays: calls on one
+// device that overlap on the GPU (different streams at the same time) race on them.
 #include <cfloat>
 #include <climits>
 
@@ -22,6 +29,9 @@ namespace yskn {
 
 constexpr int HEAD_THREADS = 512;
 constexpr int HEAD_K = 8;
+constexpr int HEAD_CHUNKS = 148;     // CTAs per row in the two-level selection
+constexpr int HEAD_SPLIT_ROWS = 64;  // rows per call handled in two levels
+constexpr int HEAD_SPLIT_THREADS = 256;
 
 struct Cand {
   float v;
@@ -35,6 +45,7 @@ __device__ __forceinline__ Cand shfl_cand(Cand c, int lane_mask) {
   return {__shfl_xor_sync(0xffffffffu, c.v, lane_mask), __shfl_xor_sync(0xffffffffu, c.id, lane_mask)};
 }
 
+template <int THREADS>
 __device__ Cand block_best(Cand c, Cand* s_warp) {
   for (int off = 16; off > 0; off >>= 1) {
     const Cand o = shfl_cand(c, off);
@@ -44,7 +55,7 @@ __device__ Cand block_best(Cand c, Cand* s_warp) {
   __syncthreads();  // s_warp is free (previous round read it)
   if (lane == 0) s_warp[warp] = c;
   __syncthreads();
-  c = lane < HEAD_THREADS / 32 ? s_warp[lane] : Cand{-FLT_MAX, INT_MAX};
+  c = lane < THREADS / 32 ? s_warp[lane] : Cand{-FLT_MAX, INT_MAX};
   for (int off = 16; off > 0; off >>= 1) {
     const Cand o = shfl_cand(c, off);
     if (before(o.v, o.id, c.v, c.id)) c = o;
@@ -52,54 +63,113 @@ __device__ Cand block_best(Cand c, Cand* s_warp) {
   return c;  // every lane of every warp holds the block's best
 }
 
-__global__ void __launch_bounds__(HEAD_THREADS) head_select_kernel(const float* logits, int n, int32_t* token,
-                                                                   float* top_v, int32_t* top_id) {
-  __shared__ Cand s_warp[HEAD_THREADS / 32];
-  pdl_begin();
-  const float* row = logits + (size_t)blockIdx.x * n;
-  float v[HEAD_K];
-  int id[HEAD_K];
+// One candidate into a thread's sorted list of eight (the list keeps the first eight seen
+// of the order; NaN and -inf never enter).
+__device__ __forceinline__ void insert8(float (&v)[HEAD_K], int (&id)[HEAD_K], float cv, int ci) {
+  if (!before(cv, ci, v[HEAD_K - 1], id[HEAD_K - 1])) return;
 #pragma unroll
-  for (int k = 0; k < HEAD_K; ++k) v[k] = -FLT_MAX, id[k] = INT_MAX;
-  constexpr int BATCH = 8;  // loads in flight per thread
-  for (int i0 = threadIdx.x; i0 < n; i0 += BATCH * HEAD_THREADS) {
-    float xs[BATCH];
-#pragma unroll
-    for (int u = 0; u < BATCH; ++u) {
-      const int i = i0 + u * HEAD_THREADS;
-      xs[u] = i < n ? __ldg(row + i) : 0.0f;
-    }
-#pragma unroll
-    for (int u = 0; u < BATCH; ++u) {  // in increasing index order, as one element at a time
-      const int i = i0 + u * HEAD_THREADS;
-      if (i >= n || !before(xs[u], i, v[HEAD_K - 1], id[HEAD_K - 1])) continue;  // NaN and -inf stop here
-      float cv = xs[u];
-      int ci = i;
-#pragma unroll
-      for (int k = 0; k < HEAD_K; ++k) {  // insert, keeping the list in order
-        if (before(cv, ci, v[k], id[k])) {
-          const float tv = v[k];
-          const int ti = id[k];
-          v[k] = cv, id[k] = ci;
-          cv = tv, ci = ti;
-        }
-      }
+  for (int k = 0; k < HEAD_K; ++k) {
+    if (before(cv, ci, v[k], id[k])) {
+      const float tv = v[k];
+      const int ti = id[k];
+      v[k] = cv, id[k] = ci;
+      cv = tv, ci = ti;
     }
   }
+}
+
+// The block's first eight from every thread's list, in order: out(r, best) for r = 0..7.
+template <int THREADS, typename Out>
+__device__ __forceinline__ void block_first8(const float (&v)[HEAD_K], const int (&id)[HEAD_K], Cand* s_warp, Out out) {
   int head = 0;  // the next entry of this thread's list
   for (int r = 0; r < HEAD_K; ++r) {
     Cand mine{-FLT_MAX, INT_MAX};
 #pragma unroll
     for (int k = 0; k < HEAD_K; ++k)
       if (k == head) mine = {v[k], id[k]};
-    const Cand best = block_best(mine, s_warp);
+    const Cand best = block_best<THREADS>(mine, s_warp);
     if (head < HEAD_K && mine.id == best.id && mine.v == best.v && best.id != INT_MAX) ++head;
-    if (threadIdx.x == 0) {
-      if (r == 0 && token) token[blockIdx.x] = best.id;
-      if (top_v) top_v[(size_t)blockIdx.x * HEAD_K + r] = best.v;
-      if (top_id) top_id[(size_t)blockIdx.x * HEAD_K + r] = best.id;
+    if (threadIdx.x == 0) out(r, best);
+  }
+}
+
+// Strided share [lo, hi) of a row of logits into a thread's list (8 loads in flight).
+template <int THREADS>
+__device__ __forceinline__ void scan_share(const float* row, int lo, int hi, float (&v)[HEAD_K], int (&id)[HEAD_K]) {
+  constexpr int BATCH = 8;
+  for (int i0 = lo + threadIdx.x; i0 < hi; i0 += BATCH * THREADS) {
+    float xs[BATCH];
+#pragma unroll
+    for (int u = 0; u < BATCH; ++u) {
+      const int i = i0 + u * THREADS;
+      xs[u] = i < hi ? __ldg(row + i) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < BATCH; ++u) {  // in increasing index order, as one element at a time
+      const int i = i0 + u * THREADS;
+      if (i < hi) insert8(v, id, xs[u], i);
     }
   }
+}
+
+__global__ void __launch_bounds__(HEAD_THREADS) head_select_kernel(const float* logits, int n, int32_t* token,
+                                                                   float* top_v, int32_t* top_id) {
+  __shared__ Cand s_warp[HEAD_THREADS / 32];
+  pdl_begin();
+  float v[HEAD_K];
+  int id[HEAD_K];
+#pragma unroll
+  for (int k = 0; k < HEAD_K; ++k) v[k] = -FLT_MAX, id[k] = INT_MAX;
+  scan_share<HEAD_THREADS>(logits + (size_t)blockIdx.x * n, 0, n, v, id);
+  const size_t r0 = blockIdx.x;
+  block_first8<HEAD_THREADS>(v, id, s_warp, [&](int r, Cand best) {
+    if (r == 0 && token) token[r0] = best.id;
+    if (top_v) top_v[r0 * HEAD_K + r] = best.v;
+    if (top_id) top_id[r0 * HEAD_K + r] = best.id;
+  });
+}
+
+// Two-level scratch: the first eight of every chunk of every row, and one arrival counter
+// per row (zero between launches: the merging CTA resets it).
+__device__ Cand g_head_part[HEAD_SPLIT_ROWS][HEAD_CHUNKS][HEAD_K];
+__device__ unsigned g_head_arrivals[HEAD_SPLIT_ROWS];
+
+// grid (HEAD_CHUNKS, rows): CTA (c, m) selects within chunk c of row m; the row's last
+// arriving CTA merges the HEAD_CHUNKS x 8 candidates into the row's first eight.
+__global__ void __launch_bounds__(HEAD_SPLIT_THREADS) head_select_split_kernel(const float* logits, int n,
+                                                                               int32_t* token, float* top_v,
+                                                                               int32_t* top_id) {
+  __shared__ Cand s_warp[HEAD_SPLIT_THREADS / 32];
+  __shared__ bool s_last;
+  pdl_begin();
+  const int c = blockIdx.x, m = blockIdx.y;
+  const int chunk = (n + HEAD_CHUNKS - 1) / HEAD_CHUNKS;
+  const int lo = min(n, c * chunk), hi = min(n, lo + chunk);
+  float v[HEAD_K];
+  int id[HEAD_K];
+#pragma unroll
+  for (int k = 0; k < HEAD_K; ++k) v[k] = -FLT_MAX, id[k] = INT_MAX;
+  scan_share<HEAD_SPLIT_THREADS>(logits + (size_t)m * n, lo, hi, v, id);
+  block_first8<HEAD_SPLIT_THREADS>(v, id, s_warp, [&](int r, Cand best) { g_head_part[m][c][r] = best; });
+  if (threadIdx.x == 0) {
+    __threadfence();  // this chunk's eight before the arrival
+    s_last = atomicAdd(&g_head_arrivals[m], 1u) == HEAD_CHUNKS - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();  // the other chunks' eights after seeing the final count
+#pragma unroll
+  for (int k = 0; k < HEAD_K; ++k) v[k] = -FLT_MAX, id[k] = INT_MAX;
+  for (int i = threadIdx.x; i < HEAD_CHUNKS * HEAD_K; i += HEAD_SPLIT_THREADS) {
+    const Cand* p = &g_head_part[m][i / HEAD_K][i % HEAD_K];
+    insert8(v, id, __ldcg(&p->v), __ldcg(&p->id));  // through L2: other SMs wrote them in this launch
+  }
+  block_first8<HEAD_SPLIT_THREADS>(v, id, s_warp, [&](int r, Cand best) {
+    if (r == 0 && token) token[m] = best.id;
+    if (top_v) top_v[(size_t)m * HEAD_K + r] = best.v;
+    if (top_id) top_id[(size_t)m * HEAD_K + r] = best.id;
+  });
+  if (threadIdx.x == 0) g_head_arrivals[m] = 0u;
 }
 
 }  // namespace yskn
@@ -111,6 +181,10 @@ extern "C" YSKN_B200_API int yskn_b200_head_select(const float* d_logits, int M,
   if (!d_logits || M < 1 || n < 1 || (!d_token && !d_top8_logits && !d_top8_ids))
     return fail(YSKN_EINVAL, "head_select: null logits, M < 1, n < 1 or no output");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (M <= HEAD_SPLIT_ROWS && n >= 4 * HEAD_CHUNKS)
+    return cuda_fail(launch_pdl(head_select_split_kernel, dim3(HEAD_CHUNKS, M), HEAD_SPLIT_THREADS, 0, st, d_logits, n,
+                                d_token, d_top8_logits, d_top8_ids),
+                     "head_select_split_kernel");
   for (int m0 = 0; m0 < M; m0 += 65535) {
     const int rows = M - m0 < 65535 ? M - m0 : 65535;
     if (cudaError_t e = launch_pdl(head_select_kernel, rows, HEAD_THREADS, 0, st, d_logits + (size_t)m0 * n, n,

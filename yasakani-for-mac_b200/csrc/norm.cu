@@ -44,17 +44,28 @@ __global__ void __launch_bounds__(NORM_THREADS * NORM_GROUPS) residual_prepare_k
   uint16_t* h = hidden + row * cols;
   const float* pr = projection ? projection + row * cols : nullptr;
   for (int b = 512 * s; b < cols; b += 512 * NORM_GROUPS) {
+    // Every load of the block first (the stores below may alias them as far as the
+    // compiler knows, which would otherwise serialise one memory round trip per element).
+    uint16_t hv[4], wv[4];
+    float pv[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = b + t + 128 * j;
+      hv[j] = h[i];
+      wv[j] = norm_weight[i];
+      pv[j] = pr ? pr[i] : 0.0f;
+    }
     float partial = 0.0f;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int i = b + t + 128 * j;
-      float x = bf16_to_f32(h[i]);
+      float x = bf16_to_f32(hv[j]);
       if (pr) {
-        x = bf16_to_f32(f32_to_bf16(__fadd_rn(x, bf16_to_f32(f32_to_bf16(pr[i])))));
+        x = bf16_to_f32(f32_to_bf16(__fadd_rn(x, bf16_to_f32(f32_to_bf16(pv[j])))));
         h[i] = f32_to_bf16(x);  // exact: x already has bf16 precision
       }
       partial = __fadd_rn(partial, __fmul_rn(x, x));
-      const float in = __fmul_rn(x, __fadd_rn(1.0f, bf16_to_f32(norm_weight[i])));
+      const float in = __fmul_rn(x, __fadd_rn(1.0f, bf16_to_f32(wv[j])));
       input[row * cols + i] = in;
       if (gate) gate[row * cols + i] = f32_to_bf16(in);
     }
