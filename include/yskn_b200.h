@@ -345,6 +345,39 @@ YSKN_B200_API int yskn_b200_tp_set_wait(yskn_b200_tp* tp, double seconds);
 YSKN_B200_API int yskn_b200_linear_rowpar(yskn_b200_tp* tp, const yskn_b200_matrix* mat, const float* d_x_local, int M,
                                           const float* d_inv_rms, float* d_y, void* stream);
 
+/* The per-layer chain between projections in the operators themselves (replaces the
+ * reference's fused epilogue/prologue kernels: the FIN restore of src/lnord.cu:119-170 and
+ * q35_res_norm_xsm_kernel, src/q35_kernels.cu:1402-1474, which restore a projection, add it
+ * to the residual stream, normalise and quantise the next operator's input in one pass;
+ * scalar order residual_norm_mlp.rs:14-61,120-156 and compressed_linear.rs:57-135).
+ *
+ * yskn_b200_linear_residual: the whole operator of ONE matrix with an output rotation whose
+ * rows (a multiple of 512, physical rows = rows) are added to the residual stream: from an
+ * f32 input d_x [M][cols] or an int8 input d_act [M][cols] with group scales d_alpha
+ * [M][cols/512] (exactly one of the two), it updates d_hidden (bf16 [M][rows]) to
+ * bf16(h + bf16(y)) and writes the next projection's input: d_act_out int8 [M][rows] and
+ * d_alpha_out [M][rows/512] (the quantiser of compressed_linear.rs:57-112 applied to
+ * h * (1 + w) with d_norm_weight bf16 [rows] and the next matrix's input signs
+ * d_next_signs), d_bss_out [M][rows/512] (each 512-block's sum of squares of h in the
+ * spec's order) and, if d_gate_out, the bf16 copy of h * (1 + w) (the dense gates' input).
+ * yskn_b200_linear_q8: the whole operator of up to 3 matrices from such an int8 input; with
+ * d_bss it forms each row's 1/rms = rsqrt(sum of the block sums / cols + eps) and uses it in
+ * the restore (and stores it to d_inv_rms_out if given).
+ * yskn_b200_gated_product_q8: the MLP product of yskn_b200_gated_product quantised at once
+ * for the down projection (its input signs d_signs): d_act int8 [M][n], d_alpha [M][n/512].
+ * All three give bit for bit what the separate calls (restore, residual_prepare, quantize)
+ * give; decode shapes only (M = 1..16 with the input in shared memory). */
+YSKN_B200_API int yskn_b200_linear_residual(const yskn_b200_matrix* mat, const float* d_x, const int8_t* d_act,
+                                            const float* d_alpha, int M, uint16_t* d_hidden,
+                                            const uint16_t* d_norm_weight, const int8_t* d_next_signs,
+                                            int8_t* d_act_out, float* d_alpha_out, float* d_bss_out,
+                                            uint16_t* d_gate_out, void* stream);
+YSKN_B200_API int yskn_b200_linear_q8(const yskn_b200_matrix* const* mats, int n_mats, const int8_t* d_act,
+                                      const float* d_alpha, const float* d_bss, float eps, int M, float* d_inv_rms_out,
+                                      float* const* d_y, void* stream);
+YSKN_B200_API int yskn_b200_gated_product_q8(const float* d_gate, const float* d_up, int M, int n,
+                                             const int8_t* d_signs, int8_t* d_act, float* d_alpha, void* stream);
+
 /* Restore + output rotation (replaces src/a8_prologue.cuh:10-15 xsum_combine and the
  * restore part of src/q35_kernels.cu:1402-1474; compressed_linear.rs:288-370):
  * y[m][r] = f32(ws)*row_quantum[m] (*inv_rms[m]) *tau[r]; then, if rotate_out, per

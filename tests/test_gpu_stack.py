@@ -248,3 +248,32 @@ def test_two_layer_stack_matches_the_composed_oracle(cuda):
     assert np.array_equal(_host_u16(st2.h)[0], h)
     assert np.array_equal(st2.logits.cpu().numpy()[0].view(np.uint32), logits.view(np.uint32))
     assert int(st2.token.item()) == O.head_select(logits)[0]
+
+
+def test_fused_chain_pass_equals_the_separate_calls(cuda):
+    """The decode pass with the chain between projections inside the operators (532 launches
+    per token) and with the separate residual/normalisation and product calls (660): the
+    same tokens, hidden rows, logits and recurrent states, bit for bit, over three tokens."""
+    import torch
+    import yskn_b200 as Y
+    from yskn_b200 import stack as S
+
+    def run(fused):
+        st = S.Stack(cuda, layers=4, vocab=4096, ctx=128, seed=13)
+        stream = torch.cuda.Stream(cuda)
+        toks = []
+        for _ in range(3):
+            with torch.cuda.stream(stream):
+                st.decode(stream, fused=fused)
+            torch.cuda.synchronize()
+            toks.append(int(st.token.item()))
+        assert Y.status(stream) == 0
+        return toks, st.h.clone(), st.logits.clone(), [L["state"].clone() for L in st.L if L["kind"] == "gdn"]
+
+    a = run(True)
+    b = run(False)
+    assert a[0] == b[0]
+    assert torch.equal(a[1], b[1])
+    assert torch.equal(a[2].view(torch.int32), b[2].view(torch.int32))
+    for x, y in zip(a[3], b[3]):
+        assert torch.equal(x.view(torch.int32), y.view(torch.int32))

@@ -1,6 +1,7 @@
 """Host-side arithmetic of the 27B-shape decode pass (yskn_b200/stack.py): the layer pattern,
 the code bytes of the stack against the reference's config-5 figure, the algorithmic bytes of
-one token and the launch count (660 per token, as the launch list of one token shows)."""
+one token and the launch count (532 per token with the chain between projections inside the
+operators, 660 with separate calls)."""
 import types
 
 from yskn_b200 import stack as S
@@ -23,4 +24,7 @@ def test_bytes():
 
 def test_launches_per_token():
     fake = types.SimpleNamespace(kinds=S.layer_kinds(64), layers=64)
-    assert S.Stack.launches_per_token(fake) == 660
+    assert S.Stack.launches_per_token(fake, fused=False) == 660
+    # the chain inside the operators: no residual_prepare after the first layer's, no
+    # separate quantiser for down (the MLP product is quantised in place)
+    assert S.Stack.launches_per_token(fake) == 532

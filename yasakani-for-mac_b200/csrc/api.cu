@@ -662,6 +662,61 @@ YSKN_B200_API int yskn_b200_linear(const yskn_b200_matrix* const* mats, int n_ma
   return finish_checked(Kc, stream);
 }
 
+YSKN_B200_API int yskn_b200_linear_q8(const yskn_b200_matrix* const* mats, int n_mats, const int8_t* d_act,
+                                      const float* d_alpha, const float* d_bss, float eps, int M, float* d_inv_rms_out,
+                                      float* const* d_y, void* stream) {
+  if (int rc = check_group(mats, n_mats)) return rc;
+  const int Kc = mats[0]->dev.cols;
+  if (M < 1 || !d_act || !d_alpha || !d_y || !aligned16(d_act) || (d_bss && !(eps > 0.0f)))
+    return fail(YSKN_EINVAL, "linear_q8: bad arguments (aligned int8 input, group scales, outputs, eps > 0 with bss)");
+  if (!fused_linear_fits(M, Kc)) return fail(YSKN_EINVAL, "linear_q8: M must be 1..16 with the input in shared memory");
+  MatrixDev devs[3];
+  for (int i = 0; i < n_mats; ++i) {
+    if (!d_y[i]) return fail(YSKN_EINVAL, "linear_q8: null output");
+    devs[i] = mats[i]->dev;
+  }
+  const GemvScratch* sc = current_scratch();
+  if (!sc) return fail(YSKN_EINVAL, "linear_q8: no matrix was created on this device");
+  FusedIO io;
+  io.q_act = d_act;
+  io.q_alpha = d_alpha;
+  io.q_bss = d_bss;
+  io.q_eps = eps;
+  io.inv_out = d_bss ? d_inv_rms_out : nullptr;
+  if (int rc = launch_linear_fused(devs, n_mats, nullptr, M, nullptr, d_y, *sc, as_stream(stream), io)) return rc;
+  return finish_checked(Kc, stream);
+}
+
+YSKN_B200_API int yskn_b200_linear_residual(const yskn_b200_matrix* mat, const float* d_x, const int8_t* d_act,
+                                            const float* d_alpha, int M, uint16_t* d_hidden,
+                                            const uint16_t* d_norm_weight, const int8_t* d_next_signs,
+                                            int8_t* d_act_out, float* d_alpha_out, float* d_bss_out,
+                                            uint16_t* d_gate_out, void* stream) {
+  if (!mat || M < 1 || (!d_x == !d_act) || (d_act && !d_alpha) || !d_hidden || !d_norm_weight || !d_next_signs ||
+      !d_act_out || !d_alpha_out || !d_bss_out || (d_x && !aligned16(d_x)) || (d_act && !aligned16(d_act)) ||
+      !aligned16(d_act_out) || (reinterpret_cast<uintptr_t>(d_hidden) & 3) ||
+      (d_gate_out && (reinterpret_cast<uintptr_t>(d_gate_out) & 3)))
+    return fail(YSKN_EINVAL, "linear_residual: bad arguments (exactly one of f32 or int8 input, aligned buffers)");
+  const MatrixDev& d = mat->dev;
+  if (!fused_linear_fits(M, d.cols))
+    return fail(YSKN_EINVAL, "linear_residual: M must be 1..16 with the input in shared memory");
+  const GemvScratch* sc = current_scratch();
+  if (!sc) return fail(YSKN_EINVAL, "linear_residual: no matrix was created on this device");
+  FusedIO io;
+  io.q_act = d_act;
+  io.q_alpha = d_alpha;
+  io.res_hidden = d_hidden;
+  io.res_norm_w = d_norm_weight;
+  io.res_next_signs = d_next_signs;
+  io.res_act = d_act_out;
+  io.res_alpha = d_alpha_out;
+  io.res_bss = d_bss_out;
+  io.res_gate = d_gate_out;
+  float* no_y[1] = {nullptr};
+  if (int rc = launch_linear_fused(&d, 1, d_x, M, nullptr, no_y, *sc, as_stream(stream), io)) return rc;
+  return finish_checked(d.cols, stream);
+}
+
 static int kv_check(int M, int n_qh, int n_kvh, int length, int capacity, int kb, int n_splits) {
   if (M < 1 || n_qh < 1 || n_kvh < 1 || n_qh % n_kvh != 0 || n_qh / n_kvh > KV_MAX_GROUP)
     return fail(YSKN_EINVAL, "kv4 attention: query heads must be a multiple (at most 8x) of the KV heads");

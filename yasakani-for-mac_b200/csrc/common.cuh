@@ -164,8 +164,35 @@ int launch_gemv(const MatrixDev* mats, int n_mats, const int8_t* act, const int3
 // The whole decode operator in one launch (quantise, sums, restore): M <= 16 rows
 // whose activations fit in shared memory next to the table, fewer than 512 groups.
 bool fused_linear_fits(int M, int Kc);
+// The f1 chain's options of the fused operator (all null: plain f32 input, f32 output).
+// Quantised input: q_act [M][Kc] int8 and q_alpha [M][Kc/512] group scales from the
+// producing kernel (the in-kernel quantiser is skipped); with q_bss [M][Kc/512] block sums
+// of squares the rows' 1/rms is formed in the kernel (and stored to inv_out if given).
+// Residual output (res_hidden set; one matrix with an output rotation, rows a multiple of
+// 512): the restored rows are added to the bf16 residual stream, which is normalised with
+// res_norm_w and quantised with the next operator's input signs res_next_signs into
+// res_act / res_alpha, its block sums of squares into res_bss, and (if res_gate) a bf16
+// copy of the unnormalised input; y is not written.
+struct FusedIO {
+  const int8_t* q_act = nullptr;
+  const float* q_alpha = nullptr;
+  const float* q_bss = nullptr;
+  float q_eps = 0.0f;
+  float* inv_out = nullptr;
+  uint16_t* res_hidden = nullptr;
+  const uint16_t* res_norm_w = nullptr;
+  const int8_t* res_next_signs = nullptr;
+  int8_t* res_act = nullptr;
+  float* res_alpha = nullptr;
+  float* res_bss = nullptr;
+  uint16_t* res_gate = nullptr;
+};
 int launch_linear_fused(const MatrixDev* mats, int n_mats, const float* x, int M, const float* inv_rms,
-                        float* const* y, const GemvScratch& scratch, cudaStream_t st);
+                        float* const* y, const GemvScratch& scratch, cudaStream_t st, const FusedIO& io = FusedIO());
+// Gated product followed by the down projection's quantiser (per 512-element group):
+// act [M][n] int8 and alpha [M][n/512] (n a multiple of 512).
+int launch_gated_product_q8(const float* gate, const float* up, int M, int n, const int8_t* signs, int8_t* act,
+                            float* alpha, cudaStream_t st);
 // The row-parallel operator of one rank in one launch: this rank's 512-column groups
 // of a matrix with an output rotation, the row maxima and the int64 block sums
 // exchanged with the peers through `tp`, the whole output restored on every rank.

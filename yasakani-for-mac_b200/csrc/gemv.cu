@@ -48,6 +48,7 @@
 #include <mutex>
 
 #include "async.cuh"
+#include "pmath.cuh"
 #include "quant.cuh"
 
 namespace yskn {
@@ -92,6 +93,19 @@ struct GemvParams {
   const float* x;
   const int8_t* s_in;
   const float* inv_rms;
+  // Fused operator with a quantised input (q_act != nullptr): the int8 rows [mv][Kc] and
+  // group scales [mv][G] from the producing kernel, replacing the in-kernel quantiser; with
+  // q_bss the rows' 1/rms is formed here from their per-512-block sums of squares
+  // (rsqrt(sum / Kc + q_eps), blocks added in order from +0) and, if inv_out, stored.
+  const int8_t* q_act;
+  const float* q_alpha;
+  const float* q_bss;
+  float q_eps;
+  float* inv_out;
+  // Residual epilogue (res.hidden != nullptr; one matrix with an output rotation): the
+  // restored rows go into the residual stream and become the next operator's quantised
+  // input (residual_block512), token m's arrays at m * rows (alpha, bss at m * rows / 512).
+  ResidualOut res;
   // Row-parallel tensor-parallel operator (tp.world > 1): exchange areas of all ranks.
   TpView tp;
 };
@@ -385,6 +399,21 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
                                   : reinterpret_cast<const char*>(S.s_out) + 128 * (l - t_lines);
       asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
     }
+    if (p.res.hidden) {
+      // Likewise the residual epilogue's rows: the residual stream (each token), the norm
+      // weights and the next operator's input signs. L2 is the point of coherence, so the
+      // stream's lines may be brought in before the previous kernel has finished.
+      const size_t h_lines = ((size_t)p.mv * S.y_rows * 2 + 127) / 128, w_lines = ((size_t)S.y_rows * 2 + 127) / 128;
+      const size_t n_lines = h_lines + w_lines + s_lines;
+      for (size_t l = (size_t)(blockIdx.x - S.cta_begin) * blockDim.x + threadIdx.x; l < n_lines;
+           l += (size_t)S.n_ctas * blockDim.x) {
+        const char* a = l < h_lines ? reinterpret_cast<const char*>(p.res.hidden) + 128 * l
+                        : l < h_lines + w_lines
+                            ? reinterpret_cast<const char*>(p.res.norm_w) + 128 * (l - h_lines)
+                            : reinterpret_cast<const char*>(p.res.s_next) + 128 * (l - h_lines - w_lines);
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
+      }
+    }
   }
   // Everything above reads only the matrix (codes, table), which no kernel writes. The
   // inputs, the scales and every scratch word may belong to the previous kernel on the
@@ -395,12 +424,38 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
   // do not all read the same input lines at the same moment.
   const int item_rot = FUSED ? (int)(blockIdx.x % (unsigned)items) : 0;
   auto item_of = [&](int k) { return k + item_rot < items ? k + item_rot : k + item_rot - items; };
-  if (FUSED && warp < items) {
+  if (FUSED && !p.q_act && warp < items) {
     const int it = item_of(warp);
     load_group512(p.x + (size_t)(it / G) * Kc + (it % G) * 512, p.s_in + (it % G) * 512, lane, nxt);
   }
+  __shared__ float s_inv[TP_MAX_M];  // quantised input with block sums of squares: the rows' 1/rms
   {
-    if (FUSED) {
+    if (FUSED && p.q_act) {
+      // Quantised input: stage the int8 rows and the group scales (8 independent 16-byte
+      // loads per thread before their stores); each row's 1/rms from its block sums.
+      const int vec = Kc / 16, total = p.mv * vec;
+      for (int base = 0; base < total; base += 8 * GEMV_WARPS * 32) {
+        uint4 v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int idx = base + threadIdx.x + k * GEMV_WARPS * 32;
+          if (idx < total) v[k] = __ldcg(reinterpret_cast<const uint4*>(p.q_act + (size_t)(idx / vec) * Kc) + idx % vec);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int idx = base + threadIdx.x + k * GEMV_WARPS * 32;
+          if (idx < total) reinterpret_cast<uint4*>(s_act + (idx / vec) * act_ld)[idx % vec] = v[k];
+        }
+      }
+      for (int idx = threadIdx.x; idx < p.mv * G; idx += blockDim.x) s_alpha[idx] = __ldcg(p.q_alpha + idx);
+      if (p.q_bss && threadIdx.x < p.mv) {
+        float total_sq = 0.0f;
+        for (int g = 0; g < G; ++g) total_sq = __fadd_rn(total_sq, __ldcg(p.q_bss + threadIdx.x * G + g));
+        const float inv = pm_rsqrt(__fadd_rn(__fdiv_rn(total_sq, (float)Kc), p.q_eps));
+        s_inv[threadIdx.x] = inv;
+        if (p.inv_out && blockIdx.x == 0) p.inv_out[threadIdx.x] = inv;
+      }
+    } else if (FUSED) {
       // A warp's groups in turn, each one's inputs requested before the previous is quantised.
       bool bad = false;
       for (int k = warp; k < items; k += GEMV_WARPS) {
@@ -528,6 +583,8 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
   const int blk_lo = (t_begin / T2) >> 6;
   unsigned done_mask = 0;
 
+  // The rows' 1/rms for the restore: formed here from a quantised input's block sums, or given.
+  const float* inv_base = (FUSED && p.q_act && p.q_bss) ? s_inv : p.inv_rms;
   // Final sums of rows row0, row0 + 1 for tokens n, n + 8 (the C fragment): stored
   // as int64, or (fused operator, rows without an output rotation) restored to f32.
   auto emit = [&](const long long (&v)[4], int row0) {
@@ -536,8 +593,8 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
       const int tok = n + (i >> 1) * 8, row = row0 + (i & 1);
       if constexpr (FUSED) {
         if (tok < p.mv && row < S.y_rows) {
-          const float t = restore_value(v[i], s_rq[tok], p.inv_rms ? p.inv_rms + tok : nullptr, __ldg(S.tau + row));
-          bad |= !finite32(t) || (p.inv_rms && !finite32(p.inv_rms[tok]));
+          const float t = restore_value(v[i], s_rq[tok], inv_base ? inv_base + tok : nullptr, __ldg(S.tau + row));
+          bad |= !finite32(t) || (inv_base && !finite32(inv_base[tok]));
           S.y[(size_t)tok * S.y_rows + row] = t;
         }
       } else {
@@ -549,15 +606,44 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
   // the sums and the block's counter for the next launch.
   // Several tokens: restored after the streaming loop (see done_mask), tokens in turn,
   // each token's sums requested before the previous token is transformed.
+  // Residual epilogue: token tok's block, restored, into the residual stream and the next
+  // operator's quantised input.
+  auto residual = [&](const int64_t* wsr, int tok, int blk) {
+    const int rows = S.y_rows;
+    ResidualOut o = p.res;
+    o.hidden += (size_t)tok * rows;
+    o.act += (size_t)tok * rows;
+    o.alpha += (size_t)tok * (rows / 512);
+    o.bss += (size_t)tok * (rows / 512);
+    if (o.gate) o.gate += (size_t)tok * rows;
+    residual_restore512(wsr, S.tau, S.s_out, s_rq[tok], inv_base ? inv_base + tok : nullptr, o, blk * 512, lane, bad);
+  };
+  auto clear_sums = [&](int64_t* wsr, int blk) {  // the rows this lane read (the restore's lane mapping)
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      __stcg(reinterpret_cast<longlong2*>(wsr + blk * 512 + 64 * k + 2 * lane), make_longlong2(0, 0));
+  };
+  // One token, no residual output: the block restored inside the streaming loop by the
+  // warp that completed it (kept free of the residual code, which would raise the loop's
+  // register pressure; the residual epilogue runs after the loop).
+  auto restore_plain = [&](int blk) {
+    restore_block512(S.out, s_rq[0], inv_base, S.tau, S.s_out, blk * 512, S.y_rows, S.y, lane, bad);
+    clear_sums(S.out, blk);
+    if (lane == 0) S.blk_counters[blk] = 0u;
+  };
   auto restore_block = [&](int blk) {
-    if constexpr (M1) {
+    if (FUSED && p.res.hidden) {
       for (int tok = 0; tok < p.mv; ++tok) {
         int64_t* wsr = S.out + (size_t)tok * S.out_ld;
-        restore_block512(wsr, s_rq[tok], p.inv_rms ? p.inv_rms + tok : nullptr, S.tau, S.s_out, blk * 512, S.y_rows,
+        residual(wsr, tok, blk);
+        clear_sums(wsr, blk);
+      }
+    } else if constexpr (M1) {
+      for (int tok = 0; tok < p.mv; ++tok) {
+        int64_t* wsr = S.out + (size_t)tok * S.out_ld;
+        restore_block512(wsr, s_rq[tok], inv_base ? inv_base + tok : nullptr, S.tau, S.s_out, blk * 512, S.y_rows,
                          S.y + (size_t)tok * S.y_rows, lane, bad);
-#pragma unroll
-        for (int k = 0; k < 8; ++k)  // the rows this lane read (restore_block512's lane mapping)
-          __stcg(reinterpret_cast<longlong2*>(wsr + blk * 512 + 64 * k + 2 * lane), make_longlong2(0, 0));
+        clear_sums(wsr, blk);
       }
     } else {
       Rows512 rr;
@@ -567,10 +653,8 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
       for (int tok = 0; tok < p.mv; ++tok) {
         int64_t* wsr = S.out + (size_t)tok * S.out_ld;
         if (tok + 1 < p.mv) load_sums512(wsr + S.out_ld, blk * 512, lane, wn);
-#pragma unroll
-        for (int k = 0; k < 8; ++k)  // the rows this lane read, cleared after their reads
-          __stcg(reinterpret_cast<longlong2*>(wsr + blk * 512 + 64 * k + 2 * lane), make_longlong2(0, 0));
-        restore_loaded512(w, rr, s_rq[tok], p.inv_rms ? p.inv_rms + tok : nullptr, blk * 512, S.y_rows,
+        clear_sums(wsr, blk);  // after their reads
+        restore_loaded512(w, rr, s_rq[tok], inv_base ? inv_base + tok : nullptr, blk * 512, S.y_rows,
                           S.y + (size_t)tok * S.y_rows, lane, bad);
 #pragma unroll
         for (int k = 0; k < 8; ++k) w[k] = wn[k];
@@ -667,8 +751,8 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
               send_block(blk);
               done_mask |= 1u << (blk - blk_lo);
             } else {
-              if constexpr (M1)
-                restore_block(blk);
+              if (M1 && !p.res.hidden)
+                restore_plain(blk);
               else
                 done_mask |= 1u << (blk - blk_lo);
             }
@@ -752,8 +836,8 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
       restore_block(blk);
     }
   }
-  if constexpr (FUSED && !M1) {
-    if (!tp) {
+  if constexpr (FUSED) {
+    if (!tp && (!M1 || p.res.hidden)) {  // several tokens, or the residual epilogue
       while (done_mask) {
         const int blk = blk_lo + __ffs(done_mask) - 1;
         done_mask &= done_mask - 1;
@@ -939,8 +1023,10 @@ bool fused_linear_fits(int M, int Kc) {
 }
 
 int launch_linear_fused(const MatrixDev* mats, int n_mats, const float* x, int M, const float* inv_rms,
-                        float* const* y, const GemvScratch& scratch, cudaStream_t st) {
+                        float* const* y, const GemvScratch& scratch, cudaStream_t st, const FusedIO& io) {
   if (!fused_linear_fits(M, mats[0].cols)) return fail(YSKN_EINVAL, "fused linear: shape out of range");
+  if (io.res_hidden && (n_mats != 1 || !mats[0].s_out || mats[0].rows != mats[0].phys || mats[0].rows % 512))
+    return fail(YSKN_EINVAL, "fused linear: the residual output needs one rotated matrix of whole 512-row blocks");
   int out_rows[GEMV_MAX_SEG];
   for (int i = 0; i < n_mats; ++i) out_rows[i] = mats[i].phys;
   GemvParams p;
@@ -950,6 +1036,13 @@ int launch_linear_fused(const MatrixDev* mats, int n_mats, const float* x, int M
   p.s_in = mats[0].s_in;
   p.inv_rms = inv_rms;
   p.mv = M;
+  p.q_act = io.q_act;
+  p.q_alpha = io.q_alpha;
+  p.q_bss = io.q_bss;
+  p.q_eps = io.q_eps;
+  p.inv_out = io.inv_out;
+  p.res = ResidualOut{io.res_hidden, io.res_norm_w, io.res_next_signs, io.res_act, io.res_alpha, io.res_bss,
+                      io.res_gate};
   int64_t sums_used = 0;  // rotated rows add into the zero-kept scratch sums
   for (int i = 0; i < n_mats; ++i) {
     GemvSeg& s = p.seg[i];
@@ -965,7 +1058,7 @@ int launch_linear_fused(const MatrixDev* mats, int n_mats, const float* x, int M
     s.y_rows = mats[i].rows;
     // With several tokens a warp restores the rotated blocks it completed after its last
     // unit (a 32-bit mask of them).
-    if (M > 1 && mats[i].s_out && (s.base + 1) / (64 * 2 * (int64_t)p.G) + 2 > 32)
+    if ((M > 1 || io.res_hidden) && mats[i].s_out && (s.base + 1) / (64 * 2 * (int64_t)p.G) + 2 > 32)
       return fail(YSKN_EINVAL, "fused linear: too many rows per warp");
   }
 

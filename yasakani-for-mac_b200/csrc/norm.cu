@@ -25,6 +25,7 @@
 
 #include "common.cuh"
 #include "pmath.cuh"
+#include "quant.cuh"
 
 namespace yskn {
 
@@ -106,6 +107,52 @@ __global__ void __launch_bounds__(256) gated_product_kernel(const float* gate, c
   }
 }
 
+// The gated product of one 512-element group, quantised at once for the down projection
+// (the f1 chain): the same values as gated_product_kernel, then the operator's quantiser
+// (quantize_loaded512: signs, H512, half, alpha, int8) on them, so the down operator starts
+// from int8 rows instead of quantising the f32 product in every CTA. One 128-thread CTA
+// per (group, row): every thread forms four products (the SiLU is the costly part), then
+// warp 0 quantises the group from shared memory (lane l: elements 16l..16l+15).
+__global__ void __launch_bounds__(128) gated_product_q8_kernel(const float* gate, const float* up, int n,
+                                                               const int8_t* signs, int8_t* act, float* alpha,
+                                                               unsigned* err) {
+  __shared__ __align__(16) float s_prod[512];
+  pdl_begin();
+  const int g = blockIdx.x, m = blockIdx.y;
+  const size_t base = (size_t)m * n + (size_t)g * 512;
+  {
+    const float4 gv = *reinterpret_cast<const float4*>(gate + base + 4 * threadIdx.x);
+    const float4 uv = *reinterpret_cast<const float4*>(up + base + 4 * threadIdx.x);
+    const float gs[4] = {gv.x, gv.y, gv.z, gv.w}, us[4] = {uv.x, uv.y, uv.z, uv.w};
+    float o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float gg = bf16_to_f32(f32_to_bf16(gs[e]));
+      const float uu = bf16_to_f32(f32_to_bf16(us[e]));
+      o[e] = bf16_to_f32(f32_to_bf16(__fmul_rn(bf16_to_f32(f32_to_bf16(pm_silu(gg))), uu)));
+    }
+    reinterpret_cast<float4*>(s_prod)[threadIdx.x] = make_float4(o[0], o[1], o[2], o[3]);
+  }
+  __syncthreads();
+  if (threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
+  Group512In in;
+  in.s = __ldg(reinterpret_cast<const int4*>(signs + (size_t)g * 512 + 16 * lane));
+#pragma unroll
+  for (int q = 0; q < 4; ++q) in.x[q] = reinterpret_cast<const float4*>(s_prod)[4 * lane + q];
+  bool bad = false;
+  const float a = quantize_loaded512(in, act + base, lane, bad);
+  if (lane == 0) alpha[(size_t)m * (n / 512) + g] = a;
+  if (__any_sync(0xffffffffu, bad) && lane == 0) raise_device_error(err, DERR_NONFINITE);
+}
+
+int launch_gated_product_q8(const float* gate, const float* up, int M, int n, const int8_t* signs, int8_t* act,
+                            float* alpha, cudaStream_t st) {
+  return cuda_fail(launch_pdl(gated_product_q8_kernel, dim3((unsigned)(n / 512), (unsigned)M), 128, 0, st, gate, up,
+                              n, signs, act, alpha, device_error_word()),
+                   "gated_product_q8_kernel");
+}
+
 // bf16 -> f32, exact (an operator's input from a bf16 producer such as the attention).
 __global__ void __launch_bounds__(256) widen_bf16_kernel(const uint16_t* in, int64_t n, float* out) {
   pdl_begin();
@@ -132,6 +179,16 @@ extern "C" YSKN_B200_API int yskn_b200_gated_product(const float* d_gate, const 
   return cuda_fail(launch_pdl(gated_product_kernel, (unsigned)((threads + 255) / 256), 256, 0,
                               reinterpret_cast<cudaStream_t>(stream), d_gate, d_up, total, d_out),
                    "gated_product_kernel");
+}
+
+extern "C" YSKN_B200_API int yskn_b200_gated_product_q8(const float* d_gate, const float* d_up, int M, int n,
+                                                       const int8_t* d_signs, int8_t* d_act, float* d_alpha,
+                                                       void* stream) {
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (!d_gate || !d_up || !d_signs || !d_act || !d_alpha || M < 1 || M > 65535 || n < 512 || n % 512 ||
+      !a16(d_gate) || !a16(d_up) || !a16(d_signs) || !a16(d_act))
+    return fail(YSKN_EINVAL, "gated_product_q8: null or unaligned argument, M outside 1..65535, or n not a multiple of 512");
+  return launch_gated_product_q8(d_gate, d_up, M, n, d_signs, d_act, d_alpha, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" YSKN_B200_API int yskn_b200_residual_prepare(uint16_t* d_hidden, const float* d_projection,

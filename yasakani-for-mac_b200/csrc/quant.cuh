@@ -14,6 +14,7 @@
 // element's value after every stage is the same binary32 value the scalar loop
 // produces, so the parallel transform is bit-identical.
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -179,10 +180,10 @@ __device__ __forceinline__ void load_sums512(const int64_t* wsr, int r0, int lan
 #pragma unroll
   for (int k = 0; k < 8; ++k) w[k] = __ldcg(reinterpret_cast<const longlong2*>(wsr + r0 + 64 * k + 2 * lane));
 }
-__device__ __forceinline__ void restore_loaded512(const longlong2 (&w)[8], const Rows512& rr, float rq,
-                                                  const float* inv_rms_m, int r0, int n_rows, float* __restrict__ yr,
-                                                  int lane, bool& bad) {
-  float v[16];
+// The block's outputs y (restored, H512, / sqrt(512), output signs) in v[2k + b] for rows
+// r0 + 64k + 2l + b, from sums already loaded.
+__device__ __forceinline__ void restore_values512(const longlong2 (&w)[8], const Rows512& rr, float rq,
+                                                  const float* inv_rms_m, int lane, bool& bad, float (&v)[16]) {
   if (inv_rms_m) bad |= !finite32(*inv_rms_m);
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
@@ -217,17 +218,187 @@ __device__ __forceinline__ void restore_loaded512(const longlong2 (&w)[8], const
   }
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
+    v[2 * k] = __fmul_rn(__fmul_rn(v[2 * k], kHadamardNorm), (float)rr.sg[k].x);
+    v[2 * k + 1] = __fmul_rn(__fmul_rn(v[2 * k + 1], kHadamardNorm), (float)rr.sg[k].y);
+    bad |= !finite32(v[2 * k]) | !finite32(v[2 * k + 1]);
+  }
+}
+// Rows r0 + 64k + 2l + b of y (rows >= n_rows not stored).
+__device__ __forceinline__ void store_rows512(const float (&v)[16], int r0, int n_rows, float* __restrict__ yr,
+                                              int lane) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
     const int r = r0 + 64 * k + 2 * lane;
-    const float t0 = __fmul_rn(__fmul_rn(v[2 * k], kHadamardNorm), (float)rr.sg[k].x);
-    const float t1 = __fmul_rn(__fmul_rn(v[2 * k + 1], kHadamardNorm), (float)rr.sg[k].y);
-    bad |= !finite32(t0) | !finite32(t1);
     float* dst = yr + r;
     if (r + 1 < n_rows && (reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
-      *reinterpret_cast<float2*>(dst) = make_float2(t0, t1);
+      *reinterpret_cast<float2*>(dst) = make_float2(v[2 * k], v[2 * k + 1]);
     } else {
-      if (r < n_rows) dst[0] = t0;
-      if (r + 1 < n_rows) dst[1] = t1;
+      if (r < n_rows) dst[0] = v[2 * k];
+      if (r + 1 < n_rows) dst[1] = v[2 * k + 1];
     }
+  }
+}
+__device__ __forceinline__ void restore_loaded512(const longlong2 (&w)[8], const Rows512& rr, float rq,
+                                                  const float* inv_rms_m, int r0, int n_rows, float* __restrict__ yr,
+                                                  int lane, bool& bad) {
+  float v[16];
+  restore_values512(w, rr, rq, inv_rms_m, lane, bad, v);
+  store_rows512(v, r0, n_rows, yr, lane);
+}
+
+// ---------------------------------------------------------------------------------------
+// Residual epilogue (the f1 chain): a restored and rotated 512-row block of a projection
+// whose output is added to the residual stream, the block's part of the next RMS
+// normalisation and the next operator's quantised input, in the restore's lane mapping
+// (lane l holds rows 64k + 2l + b). Every step keeps the scalar order of the reference
+// (residual_norm_mlp.rs:14-61,120-135; compressed_linear.rs:57-112):
+//   h = bf16(h + bf16(y));  x = h * (1 + w);  gate copy bf16(x);
+//   block sum of squares of h: partial t = sum_{j<4} h[t + 128 j]^2 from +0, an XOR butterfly
+//   (offsets 16..1) over each group of 32 partials, the four group sums added in order;
+//   quantiser: x * s_next -> H512 (strides 1..256 ascending) -> half(v / sqrt(512)) ->
+//   alpha = max |v| / 127 -> q = clamp(rne(v / alpha), +-127).
+struct ResidualOut {
+  uint16_t* hidden;        // bf16 [rows] of this token (in and out)
+  const uint16_t* norm_w;  // bf16 [rows]
+  const int8_t* s_next;    // the next operator's input signs [rows]
+  int8_t* act;             // int8 [rows] of this token
+  float* alpha;            // [rows / 512] of this token
+  float* bss;              // [rows / 512] of this token
+  uint16_t* gate;          // bf16 [rows] of this token, or nullptr
+};
+
+__device__ __forceinline__ float bf16_round(float x) {
+  return __uint_as_float((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(x)) << 16);
+}
+
+// Restores token block r0 of the int64 sums wsr (restore_values512) and applies the
+// residual epilogue to it. Every load the block needs is issued first, together: the sums,
+// the row scales and output signs, and the residual-stream, norm-weight and next-sign words
+// (the stores below go through some of the same pointers, so the compiler could not move
+// the later loads ahead of them). The caller clears the sums afterwards.
+__device__ __forceinline__ void residual_restore512(const int64_t* wsr, const float* __restrict__ tau,
+                                                        const int8_t* __restrict__ s_out, float rq,
+                                                        const float* inv_rms_m, const ResidualOut o, int r0, int lane,
+                                                        bool& bad) {
+  longlong2 ws[8];
+  Rows512 rr;
+  load_sums512(wsr, r0, lane, ws);
+  load_rows512(tau, s_out, r0, lane, rr);
+  uint32_t hws[8], wws[8], sws[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int r = r0 + 64 * k + 2 * lane;
+    hws[k] = __ldcg(reinterpret_cast<const unsigned int*>(o.hidden + r));
+    wws[k] = __ldg(reinterpret_cast<const unsigned int*>(o.norm_w + r));
+    sws[k] = (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(o.s_next + r));
+  }
+  float v[16];  // the block's outputs y; then the updated residual stream h
+  restore_values512(ws, rr, rq, inv_rms_m, lane, bad, v);
+  float x[16];  // the next operator's unnormalised input h * (1 + w)
+  // residual and the next normalisation's input
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int r = r0 + 64 * k + 2 * lane;
+    const uint32_t hw = hws[k], ww = wws[k];
+    uint32_t hn = 0, gw = 0;
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      const float h = __uint_as_float((b ? hw & 0xffff0000u : hw << 16));
+      const float w = __uint_as_float((b ? ww & 0xffff0000u : ww << 16));
+      const float nh = bf16_round(__fadd_rn(h, bf16_round(v[2 * k + b])));
+      const float xv = __fmul_rn(nh, __fadd_rn(1.0f, w));
+      x[2 * k + b] = xv;
+      v[2 * k + b] = nh;
+      hn |= (__float_as_uint(nh) >> 16) << (16 * b);
+      gw |= (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(xv)) << (16 * b);
+      bad |= !finite32(nh) | !finite32(xv);
+    }
+    *reinterpret_cast<uint32_t*>(o.hidden + r) = hn;
+    if (o.gate) *reinterpret_cast<uint32_t*>(o.gate + r) = gw;
+  }
+  // block sum of squares of h: lane l holds partials 2l + b (k even) and 64 + 2l + b (k odd)
+  float pt[2][2];
+#pragma unroll
+  for (int hi = 0; hi < 2; ++hi)
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      float s = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s = __fadd_rn(s, __fmul_rn(v[2 * (2 * j + hi) + b], v[2 * (2 * j + hi) + b]));
+      pt[hi][b] = s;
+    }
+  // XOR offsets 16, 8, 4, 2 on the partial index are lane offsets 8, 4, 2, 1; offset 1 is b.
+#pragma unroll
+  for (int lm = 8; lm > 0; lm >>= 1)
+#pragma unroll
+    for (int hi = 0; hi < 2; ++hi)
+#pragma unroll
+      for (int b = 0; b < 2; ++b) pt[hi][b] = __fadd_rn(pt[hi][b], __shfl_xor_sync(0xffffffffu, pt[hi][b], lm));
+  const float g_lo = __fadd_rn(pt[0][0], pt[0][1]), g_hi = __fadd_rn(pt[1][0], pt[1][1]);
+  // groups 0, 1, 2, 3: (lanes 0..15, k even), (lanes 16..31, k even), (0..15, k odd), (16..31, k odd)
+  const float G0 = __shfl_sync(0xffffffffu, g_lo, 0), G1 = __shfl_sync(0xffffffffu, g_lo, 16);
+  const float G2 = __shfl_sync(0xffffffffu, g_hi, 0), G3 = __shfl_sync(0xffffffffu, g_hi, 16);
+  const float block = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, G0), G1), G2), G3);
+  // the next operator's quantiser on x * s_next
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint32_t sw = sws[k];
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      const uint32_t flip = (sw << (24 - 8 * b)) & 0x80000000u;  // sign bit of byte b
+      x[2 * k + b] = __uint_as_float(__float_as_uint(x[2 * k + b]) ^ flip);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {  // stride 1
+    const float lower = x[2 * k], upper = x[2 * k + 1];
+    x[2 * k] = __fadd_rn(lower, upper);
+    x[2 * k + 1] = __fsub_rn(lower, upper);
+  }
+#pragma unroll
+  for (int mask = 1; mask < 32; mask <<= 1) {  // strides 2..32
+    const float s = (lane & mask) ? -1.0f : 1.0f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) x[e] = cross_butterfly(x[e], __shfl_xor_sync(0xffffffffu, x[e], mask), s);
+  }
+#pragma unroll
+  for (int kb = 1; kb < 8; kb <<= 1) {  // strides 64, 128, 256
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (k & kb) continue;
+#pragma unroll
+      for (int b = 0; b < 2; ++b) {
+        const float lower = x[2 * k + b], upper = x[2 * (k + kb) + b];
+        x[2 * k + b] = __fadd_rn(lower, upper);
+        x[2 * (k + kb) + b] = __fsub_rn(lower, upper);
+      }
+    }
+  }
+  float mx = 0.0f;
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    x[e] = __half2float(__float2half_rn(__fmul_rn(x[e], kHadamardNorm)));
+    bad |= !finite32(x[e]);
+    mx = fmaxf(mx, fabsf(x[e]));
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  const float scale = __fdiv_rn(mx, 127.0f);
+  const float rcp = __frcp_rn(scale);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    uint32_t w2 = 0;
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      int q = scale > 0.0f ? quotient_rne(x[2 * k + b], scale, rcp) : 0;
+      q = max(-127, min(127, q));
+      w2 |= (uint32_t)(q & 0xff) << (8 * b);
+    }
+    *reinterpret_cast<uint16_t*>(o.act + r0 + 64 * k + 2 * lane) = (uint16_t)w2;
+  }
+  if (lane == 0) {
+    o.alpha[r0 / 512] = scale;
+    o.bss[r0 / 512] = block;
   }
 }
 

@@ -78,6 +78,9 @@ _SIGNATURES = {
     "yskn_b200_gdn_gates": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp, _vp]),
     "yskn_b200_widen_bf16": (_i, [_vp, C.c_int64, _vp, _vp]),
     "yskn_b200_portable_math": (_i, [_i, _vp, C.c_int64, _vp, _vp, _vp]),
+    "yskn_b200_linear_residual": (_i, [_vp] * 4 + [_i] + [_vp] * 8),
+    "yskn_b200_linear_q8": (_i, [_vp, _i, _vp, _vp, _vp, C.c_float, _i, _vp, _vp, _vp]),
+    "yskn_b200_gated_product_q8": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp]),
     "yskn_b200_gdn_step": (_i, [_vp] * 7 + [C.c_float, _i, _i, _vp, _vp, _vp, _vp]),
 }
 
@@ -121,7 +124,12 @@ def check(rc, what=""):
 
 
 def _ptr(t):
-    return None if t is None else C.c_void_p(t.data_ptr())
+    """A device tensor's address, or a raw device address given as an int."""
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return C.c_void_p(t)
+    return C.c_void_p(t.data_ptr())
 
 
 def _stream(stream):
@@ -478,6 +486,30 @@ def linear(mats, x, work, ys, inv_rms=None, stream=None):
     yp = (C.c_void_p * len(ys))(*[y.data_ptr() for y in ys])
     check(lib().yskn_b200_linear(_handles(mats), len(mats), _ptr(x), x.shape[0], _ptr(inv_rms), _ptr(work), yp,
                                  _stream(stream)), "linear")
+
+
+def linear_residual(mat, hidden, norm_weight, next_signs, act_out, alpha_out, bss_out, x=None, act=None,
+                    alpha=None, gate_out=None, stream=None):
+    """yskn_b200_linear_residual: restore `mat` from x (f32) or act/alpha (int8) into the
+    residual stream `hidden` (bf16 as int16) and write the next operator's int8 input."""
+    M = (x if x is not None else act).shape[0]
+    check(lib().yskn_b200_linear_residual(mat.handle, _ptr(x), _ptr(act), _ptr(alpha), M, _ptr(hidden),
+                                          _ptr(norm_weight), _ptr(next_signs), _ptr(act_out), _ptr(alpha_out),
+                                          _ptr(bss_out), _ptr(gate_out), _stream(stream)), "linear_residual")
+
+
+def linear_q8(mats, act, alpha, ys, bss=None, eps=0.0, inv_rms_out=None, stream=None):
+    """yskn_b200_linear_q8: the operator from an int8 input (and block sums of squares)."""
+    yp = (C.c_void_p * len(ys))(*[y.data_ptr() for y in ys])
+    check(lib().yskn_b200_linear_q8(_handles(mats), len(mats), _ptr(act), _ptr(alpha), _ptr(bss), float(eps),
+                                    act.shape[0], _ptr(inv_rms_out), yp, _stream(stream)), "linear_q8")
+
+
+def gated_product_q8(gate, up, signs, act, alpha, stream=None):
+    """yskn_b200_gated_product_q8: the MLP product quantised for the down projection."""
+    M, n = gate.shape
+    check(lib().yskn_b200_gated_product_q8(_ptr(gate), _ptr(up), M, n, _ptr(signs), _ptr(act), _ptr(alpha),
+                                           _stream(stream)), "gated_product_q8")
 
 
 PORTABLE_FN = {"exp": 0, "exp2": 1, "log": 2, "log1p": 3, "sigmoid": 4, "silu": 5, "softplus": 6, "rsqrt": 7,

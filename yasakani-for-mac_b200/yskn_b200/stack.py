@@ -124,6 +124,11 @@ class Stack:
         self.kv_rows = f32(2 * N_KVH, HEAD)
         self.a_in = f32(1, N_QH * HEAD)
         self.g_o, self.u_o, self.m_o = f32(1, FFN), f32(1, FFN), f32(1, FFN)
+        # the chain between projections (yskn_b200_linear_residual / linear_q8 / gated_product_q8):
+        # the next operator's int8 input, group scales and block sums of squares
+        i8 = lambda *s: torch.zeros(s, dtype=torch.int8, device=device)  # noqa: E731
+        self.act, self.alpha, self.bss = i8(1, HIDDEN), f32(1, HIDDEN // 512), f32(1, HIDDEN // 512)
+        self.act_m, self.alpha_m = i8(1, FFN), f32(1, FFN // 512)
         self.logits = f32(1, vocab)
         first = {k: next(L for L in self.L if L["kind"] == k) for k in set(self.kinds)}
         sets = [[self.head], [first[self.kinds[0]]["gate"], first[self.kinds[0]]["up"]], [self.L[0]["down"]]]
@@ -159,8 +164,62 @@ class Stack:
         m.source = (words, lut16, sc16, rotate)  # what a checker needs to rebuild the matrix
         return m
 
-    def decode(self, stream=None):
-        """One token: reads self.token, writes the next greedy token into it."""
+    def decode(self, stream=None, fused=True):
+        """One token: reads self.token, writes the next greedy token into it. fused: the
+        chain between projections inside the operators (residual, normalisation and the next
+        quantiser in the restore of o/out/down; the MLP product quantised for down), else the
+        separate residual_prepare / gated_product calls; both give the same bits."""
+        if not fused:
+            return self._decode_separate(stream)
+        s = stream
+        self.embedding.lookup(self.token, self.h, stream=s)
+        Y.residual_prepare(self.h, None, self.L[0]["in_norm"], EPS, self.x, self.inv, gate=self.xg, stream=s)
+        for i, L in enumerate(self.L):
+            if i + 1 < len(self.L):
+                nL = self.L[i + 1]
+                next_norm, next_first = nL["in_norm"], nL["qkv"] if nL["kind"] == "gdn" else nL["q"]
+            else:
+                next_norm, next_first = self.final_norm, self.head
+            if L["kind"] == "gdn":
+                mats, outs = [L["qkv"], L["z"]], [self.qkv_o, self.z_o]
+            else:
+                mats, outs = [L["q"], L["k"], L["v"]], [self.q_o, self.k_o, self.v_o]
+            if i == 0:
+                Y.linear(mats, self.x, self.work, outs, inv_rms=self.inv, stream=s)
+            else:
+                Y.linear_q8(mats, self.act, self.alpha, outs, bss=self.bss, eps=EPS, inv_rms_out=self.inv, stream=s)
+            if L["kind"] == "gdn":
+                Y.gdn_gates(self.xg, self.inv, L["wb"], L["wa"], self.gates, stream=s)
+                Y.gdn_step(self.qkv_o, self.z_o, self.gates, L["conv"], L["a_log"], L["dt_bias"], L["norm_w"], EPS,
+                           L["state"], L["history"], self.g_out, stream=s)
+                mixer_out, mixer_in = L["out"], self.g_out
+            else:
+                self._attention(L, s)
+                mixer_out, mixer_in = L["o"], self.a_in
+            Y.linear_residual(mixer_out, self.h, L["post_norm"], L["gate"].signs_in_ptr, self.act, self.alpha,
+                              self.bss, x=mixer_in, stream=s)
+            Y.linear_q8([L["gate"], L["up"]], self.act, self.alpha, [self.g_o, self.u_o], bss=self.bss, eps=EPS,
+                        stream=s)
+            Y.gated_product_q8(self.g_o, self.u_o, L["down"].signs_in_ptr, self.act_m, self.alpha_m, stream=s)
+            Y.linear_residual(L["down"], self.h, next_norm, next_first.signs_in_ptr, self.act, self.alpha, self.bss,
+                              act=self.act_m, alpha=self.alpha_m, gate_out=self.xg, stream=s)
+        Y.linear_q8([self.head], self.act, self.alpha, [self.logits], bss=self.bss, eps=EPS, stream=s)
+        Y.head_select(self.logits, token=self.token, stream=s)
+
+    def _attention(self, L, s):
+        """The attention mixer between q/k/v and o: inputs, the new K/V rows into the cache,
+        attention with the gate, the bf16 output widened to o_proj's f32 input."""
+        Y.attention_prep(self.q_o, self.k_o, self.v_o, L["q_norm"], L["k_norm"], self.positions, EPS,
+                         self.query, self.a_gate, self.kv_rows[:N_KVH].view(1, N_KVH, HEAD),
+                         self.kv_rows[N_KVH:].view(1, N_KVH, HEAD), stream=s)
+        cache, scales = L["cache"], L["scales"]
+        Y.kv_encode(self.kv_rows, self.kv_groups, self.kv_tables, self.kv_gains, self.kv_mults, 4, True,
+                    cache.view(-1, 32), scales.view(-1), dest=self.kv_dest, stream=s)
+        Y.kv4_attention(self.query, cache[0], scales[0], cache[1], scales[1], self.kv_book, self.kv_book,
+                        self.ctx + 1, self.kv_work, self.a_out, gate=self.a_gate, n_splits=-1, stream=s)
+        Y.widen_bf16(self.a_out.view(1, -1), self.a_in, stream=s)
+
+    def _decode_separate(self, stream=None):
         s = stream
         self.embedding.lookup(self.token, self.h, stream=s)
         proj = None
@@ -194,11 +253,18 @@ class Stack:
         Y.linear([self.head], self.x, self.work, [self.logits], inv_rms=self.inv, stream=s)
         Y.head_select(self.logits, token=self.token, stream=s)
 
-    def launches_per_token(self):
+    def launches_per_token(self, fused=True):
         """This library's kernel launches in decode(), one per call except the GDN step
-        (step + history): embedding, final norm, head operator, head select; per layer the
-        input norm and the MLP (post norm, gate/up operator, gated product, down operator);
-        GDN mixer: operator, gates, step (2), out operator; attention mixer: operator,
-        preparation, KV encode, attention, widening, o operator."""
+        (step + history). Fused chain: embedding, the first layer's normalisation, head
+        operator, head select; per layer the mixer's input operator, the mixer's output
+        operator (with the residual and the next quantiser), gate/up, the quantised product
+        and down (with the residual); GDN mixer in between: gates, step (2); attention:
+        preparation, KV encode, attention, widening. Separate calls: embedding, final
+        norm, head operator, head select; per layer the input norm and the MLP (post norm,
+        gate/up operator, gated product, down operator); GDN mixer: operator, gates, step
+        (2), out operator; attention mixer: operator, preparation, KV encode, attention,
+        widening, o operator."""
         gdn, attn = self.kinds.count("gdn"), self.kinds.count("attn")
+        if fused:
+            return 4 + self.layers * 5 + gdn * 3 + attn * 4
         return 4 + self.layers * 5 + gdn * 5 + attn * 6
