@@ -13,13 +13,17 @@ per call at M=1), captured in one CUDA graph. The metric is HBM throughput of th
 algorithmic bytes per step / step time. Codes per step (243.8 MB at bits=8) exceed
 the 126 MB L2, so no L2 flush is needed between steps.
 
-With --gpus N > 1 (torchrun, one rank per GPU) the same layer step runs tensor-
-parallel (yskn_b200/tp.py): q/k/v, qkv/z and gate/up column-parallel over whole
-512-row blocks (k/v replicated at 4 and 8 GPUs), o/out/down row-parallel over
-512-column groups, each one launch per rank that exchanges the row maxima and the
-exact int64 block sums with the other ranks over NVLink (yskn_b200_linear_rowpar);
-the value is the whole layer's bytes over the max-over-ranks step time (strong
-scaling).
+With --gpus N > 1 (torchrun, one rank per GPU) every rank streams the linear set of
+its own layer (independent matrices, as the layers of a model held on different GPUs;
+no collective on the data path): the value is all ranks' bytes over the max-over-ranks
+step time (weak scaling). The same line carries, measured on all ranks:
+* `layer_tp`: one layer's set tensor-parallel (yskn_b200/tp.py): q/k/v, qkv/z and gate/up
+  column-parallel over whole 512-row blocks (k/v replicated at 4 and 8 GPUs), o/out/down
+  row-parallel over 512-column groups, each one launch per rank that exchanges the row
+  maxima and the exact int64 block sums over NVLink (yskn_b200_linear_rowpar); the
+  whole layer's bytes over the step time (strong scaling; `--layer-tp` makes it the line);
+* `decode_27b`: the 27B-shape decode pass tensor-parallel (yskn_b200/tp_stack.py), one
+  token stream over all ranks, tokens bit-identical to one GPU.
 
 `--impl reference` times the CPU path instead: the C restatement (oracle/) of the
 reference's CPU engine (crates/yskn-engine kernel + pool, crates/yskn-ref quantiser
@@ -220,13 +224,18 @@ def run_reference(args, rank, world):
 
 
 def config(args):
+    if args.gpus > 1 and args.layer_tp:
+        par = "tp%d (column-parallel q/k/v, qkv/z, gate/up; row-parallel o, out, down)" % args.gpus
+    elif args.gpus > 1:
+        par = "layers%d: each rank streams its own layer's linear set (independent matrices), no collective" % args.gpus
+    else:
+        par = "single"
     return {"workload": "one hybrid layer's full linear set (q,k,v,o; GDN in_proj_qkv,in_proj_z,out_proj; "
                         "gate,up,down), batch-1 decode, hidden 5120",
             "bits": args.bits, "bits_per_weight": args.bits / 2, "M": 1,
             "codes_mb_per_step": sum(r * c * args.bits // 16 for _, r, c in LAYER) / 1e6,
             "l2": "inputs larger than L2: every step streams all codes (>126 MB); no flush",
-            "parallelism": "tp%d (column-parallel q/k/v, qkv/z, gate/up; row-parallel o, out, down)" % args.gpus
-            if args.gpus > 1 else "single"}
+            "parallelism": par}
 
 
 def run_b200(args, rank, world, local_rank):
@@ -235,25 +244,27 @@ def run_b200(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     from yskn_b200 import tp
-    W = make_weights(args.bits)
+    tp_mode = world > 1 and args.layer_tp
+    # N > 1 without tensor parallelism: every rank its own layer's matrices (another seed)
+    W = make_weights(args.bits, seed0=1000 + (0 if tp_mode else 7919 * rank))
     # N > 1: tensor parallelism over whole 512-blocks (yskn_b200/tp.py). Column-parallel
     # projections keep whole 512-row blocks per rank (replicated when there are fewer
     # blocks than ranks: k/v at 4 and 8 GPUs); o/out/down are row-parallel, one launch
     # per rank and call with their exchange over NVLink (yskn_b200_linear_rowpar).
     mats, rowpar = {}, {}
     exchange = None
-    if world > 1:
+    if tp_mode:
         exchange = tp.make_exchange(max(r for n, r, _ in LAYER if n in ROW_PARALLEL))
     for name, w in W.items():
         dw = torch.from_numpy(w["words"].view(np.int32)).to(dev)
         args_m = (dw, "warp", w["rows"], w["rows"], w["cols"], args.bits, w["lut16"], w["sc16"], w["s_in"],
                   w["s_out"])
-        if world > 1 and name in ROW_PARALLEL:
+        if tp_mode and name in ROW_PARALLEL:
             rowpar[name] = tp.RowParallelLinear(*args_m, exchange=exchange)
             mats[name] = rowpar[name].mat
         else:
             shard = None
-            if world > 1:
+            if tp_mode:
                 ranges = tp.split_blocks(w["rows"], world)
                 r0, r1 = ranges[rank] if all(a < b for a, b in ranges) else (0, w["rows"])
                 shard = (r0, r1, 0, w["cols"])
@@ -386,7 +397,7 @@ def run_b200(args, rank, world, local_rank):
     ms, e2e_ms = t.tolist()
     # This rank's algorithmic bytes per step (its shards: codes, table, row scales, signs,
     # f32 input slice, f32 outputs), and its copies.
-    if world == 1:
+    if not tp_mode:
         gemv_local = algorithmic_bytes(args.bits, M)
     else:
         gemv_local = 0
@@ -403,11 +414,34 @@ def run_b200(args, rank, world, local_rank):
     if world > 1:
         torch.distributed.all_reduce(tot)
     h2d, d2h = tot.tolist()
+    # N > 1: the tensor-parallel layer set and decode pass, measured on every rank.
+    layer_tp = decode = None
+    if world > 1 and not tp_mode and not args.no_configs:
+        import copy
+        a = copy.copy(args)
+        a.layer_tp, a.skip_stack, a.no_configs, a.skip_cpu = True, True, True, True
+        a.steps = min(args.steps, 100)
+        r = run_b200(a, rank, world, local_rank)
+        layer_tp = _summary(r, us_per_call_alone=r["us_per_call_alone"]) if r else None
+    if not args.skip_stack and not tp_mode:
+        from yskn_b200 import stack as S
+        sms, se2e, _ = measure_stack(dev, 64, 4096, args.bits, 20, 3, world)
+        tb = S.token_bytes(64, S.VOCAB, 4096, args.bits)
+        peak_d = measured_peaks().get("hbm_gbs", HBM_FALLBACK_GBS)
+        decode = {"metric": STACK_METRIC, "value": 20 / (sms * 1e-3), "unit": "tok/s", "ms_per_token": sms / 20,
+                  "e2e_tok_s": 20 / (se2e * 1e-3), "tokens": 20, "warmup": 3,
+                  "hbm_frac": tb / (sms / 20 * 1e-3) / 1e9 / (peak_d * world), "bytes_per_token": tb,
+                  "scaling": "strong" if world > 1 else "single",
+                  "config": "64 layers (48 GDN + 16 attention, KV cache 4096 rows), vocab 151936, bits=%d, "
+                            "seeded random weights, one CUDA graph per token%s" % (
+                                args.bits, "; tensor-parallel over %d GPUs (yskn_b200/tp_stack.py)" % world
+                                if world > 1 else "")}
     if rank != 0:
         return
     step_bytes = algorithmic_bytes(args.bits, M)
-    value = step_bytes * args.steps / (ms * 1e-3) / 1e12  # one layer step for the whole job (strong scaling)
-    e2e_value = step_bytes * e2e_steps / (e2e_ms * 1e-3) / 1e12
+    jobs = 1 if tp_mode else world  # layer sets per step over all ranks
+    value = jobs * step_bytes * args.steps / (ms * 1e-3) / 1e12
+    e2e_value = jobs * step_bytes * e2e_steps / (e2e_ms * 1e-3) / 1e12
     peaks = measured_peaks()
     peak = peaks.get("hbm_gbs", HBM_FALLBACK_GBS)
     # The timed region is the dominant kernel's launches back to back (six fused
@@ -429,29 +463,17 @@ def run_b200(args, rank, world, local_rank):
         dt = time.perf_counter() - t0
         cpu = {"value": nbytes / dt / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
                "sample": "%d full layer-set steps (quantise + threaded int64 sums + restore), %.1f s" % (n, dt)}
-    # The metric's second half at N=1: the 27B-shape decode pass (config 5, --workload stack
-    # reports it alone with its own roofline and CPU line).
-    decode = None
-    if world == 1 and not args.skip_stack:
-        from yskn_b200 import stack as S
-        sms, se2e, _ = measure_stack(dev, 64, 4096, args.bits, 20, 3)
-        tb = S.token_bytes(64, S.VOCAB, 4096, args.bits)
-        decode = {"metric": STACK_METRIC, "value": 20 / (sms * 1e-3), "unit": "tok/s", "ms_per_token": sms / 20,
-                  "e2e_tok_s": 20 / (se2e * 1e-3), "tokens": 20, "warmup": 3,
-                  "hbm_frac": tb / (sms / 20 * 1e-3) / 1e9 / peak, "bytes_per_token": tb,
-                  "config": "64 layers (48 GDN + 16 attention, KV cache 4096 rows), vocab 151936, bits=%d, "
-                            "seeded random weights, one CUDA graph per token" % args.bits}
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-            "scaling": "strong" if world > 1 else "weak",
+            "scaling": "strong" if tp_mode else "weak",
             "vs_baseline": None, "dtype": "i8", "data": "synthetic", "config": config(args),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
-                         "traffic": GEMV_TRAFFIC.get((args.bits, M)) if world == 1 else None,
+                         "traffic": GEMV_TRAFFIC.get((args.bits, M)) if not tp_mode else None,
                          "kernel": "trellis_sums_kernel (fused operator: quantise + weighted sums + restore; the 6 launches "
                                    "of each step, timed over the timed region)" + (
                                        "; rank 0's shards, row-parallel calls exchanging over NVLink in-kernel"
-                                       if world > 1 else ""),
+                                       if tp_mode else "; per rank" if world > 1 else ""),
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
@@ -461,6 +483,8 @@ def run_b200(args, rank, world, local_rank):
             "clocks": sampler.summary(),
             "step_bytes": step_bytes, "us_per_call_alone": [round(1e3 * x, 2) for x in gemv_ms],
             "decode_27b": decode}
+    if world > 1 and not tp_mode:
+        line["layer_tp"] = layer_tp
     if world == 1 and not args.no_configs:
         line["configs"] = other_configs(args, rank, world, local_rank)
     return line
@@ -888,18 +912,25 @@ def stack_config(args):
                         "cache of %d rows, the rest Gated DeltaNet 16/48 heads x 128), hidden 5120, MLP 17408, vocab "
                         "151936, bits=%d body and head, batch 1, greedy token fed back on the device" %
                         (args.layers, args.stack_ctx, args.bits),
-            "global_batch": 1, "parallelism": "replicas" if int(os.environ.get("WORLD_SIZE", "1")) > 1 else "1 GPU",
+            "global_batch": 1,
+            "parallelism": "tp%d (yskn_b200/tp_stack.py)" % int(os.environ.get("WORLD_SIZE", "1"))
+            if int(os.environ.get("WORLD_SIZE", "1")) > 1 else "1 GPU",
             "l2": "weights of one token (~13 GB) far exceed L2"}
 
 
 def measure_stack(dev, layers, ctx, bits, steps, warmup, world=1, seed=1, sampler=None):
-    """Times the decode pass (yskn_b200/stack.py) replayed as one CUDA graph per token:
-    returns (device ms for `steps` tokens, e2e ms with the host's 4-byte token in and out
-    per token, launches per token)."""
+    """Times the decode pass (yskn_b200/stack.py; N > 1 tensor-parallel, yskn_b200/
+    tp_stack.py, every rank) replayed as one CUDA graph per token: returns (device ms for
+    `steps` tokens, max over ranks; e2e ms with the host's 4-byte token in and out per
+    token; launches per token of one rank)."""
     import torch
     import yskn_b200 as Y
     from yskn_b200 import stack as S
-    st = S.Stack(dev, layers=layers, ctx=ctx, bits=bits, seed=seed)
+    if world > 1:
+        from yskn_b200.tp_stack import TPStack
+        st = TPStack(dev, layers=layers, ctx=ctx, bits=bits, seed=seed)
+    else:
+        st = S.Stack(dev, layers=layers, ctx=ctx, bits=bits, seed=seed)
     stream = torch.cuda.Stream(dev)
     with torch.cuda.stream(stream):
         st.decode(stream)  # eager once: per-device set-up happens outside capture
@@ -946,7 +977,13 @@ def measure_stack(dev, layers, ctx, bits, steps, warmup, world=1, seed=1, sample
     e2e_ms = e2.elapsed_time(e3)
     Y.check(Y.status(stream), "status")
     launches = st.launches_per_token()
-    del graph, st
+    del graph  # holds an NCCL call at N > 1: released before the exchange and the process group
+    if world > 1:
+        st.close()
+        t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, e2e_ms = t.tolist()
+    del st
     torch.cuda.empty_cache()
     return ms, e2e_ms, launches
 
@@ -985,8 +1022,9 @@ def run_reference_stack(args, rank, world):
 
 
 def run_stack(args, rank, world, local_rank):
-    """The whole decode pass per token as one CUDA graph (yskn_b200/stack.py). N > 1 runs
-    independent replicas (no tensor-parallel stack): value = tokens/s over all ranks."""
+    """The whole decode pass per token as one CUDA graph (yskn_b200/stack.py). N > 1 runs it
+    tensor-parallel (yskn_b200/tp_stack.py): one token stream over all ranks, value =
+    tokens/s of that stream (strong scaling)."""
     import torch
     from yskn_b200 import stack as S
     dev = torch.device("cuda", local_rank)
@@ -995,19 +1033,15 @@ def run_stack(args, rank, world, local_rank):
     ids = [v.strip() for v in visible.split(",") if v.strip()]
     sampler = ClockSampler(ids[local_rank] if local_rank < len(ids) else str(local_rank))
     ms, e2e_ms, launches = measure_stack(dev, args.layers, args.stack_ctx, args.bits, args.steps, args.warmup,
-                                         world, 1 + rank, sampler)
-    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    ms, e2e_ms = t.tolist()
+                                         world, 1, sampler)
     if rank != 0:
         return
-    value = world * args.steps / (ms * 1e-3)
-    e2e_value = world * args.steps / (e2e_ms * 1e-3)
+    value = args.steps / (ms * 1e-3)
+    e2e_value = args.steps / (e2e_ms * 1e-3)
     tb = S.token_bytes(args.layers, S.VOCAB, args.stack_ctx, args.bits)
     peaks = measured_peaks()
     peak = peaks.get("hbm_gbs", HBM_FALLBACK_GBS)
-    achieved = tb / (ms / args.steps * 1e-3) / 1e9
+    achieved = tb / (ms / args.steps * 1e-3) / 1e9 / world  # per GPU (each streams 1/N of the weights)
     cpu = None
     if world == 1 and not args.skip_cpu:
         W = make_weights(args.bits)
@@ -1024,7 +1058,8 @@ def run_stack(args, rank, world, local_rank):
                "sample": "%d full layer-set steps of the CPU operator port (%.1f s), its code bytes/s divided by "
                          "one token's bytes (linear operators only; no mixer, attention or head work)" % (n, dt)}
     line = {"metric": STACK_METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak",
             "vs_baseline": None, "dtype": "i8", "data": "synthetic (seeded random codes and weights)",
             "config": stack_config(args),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
@@ -1054,6 +1089,8 @@ def main():
     ap.add_argument("--ctx", type=int, default=32768, help="kv4: cache rows per layer")
     ap.add_argument("--kv-splits", type=int, default=-1, help="kv4: 0 reference schedule, -1 one wave over the SMs")
     ap.add_argument("--no-configs", action="store_true", help="linear: leave out the other configurations' figures")
+    ap.add_argument("--layer-tp", action="store_true",
+                    help="linear, N > 1: one layer's set tensor-parallel (strong scaling) instead of a set per rank")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

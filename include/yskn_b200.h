@@ -105,6 +105,19 @@ YSKN_B200_API yskn_b200_matrix* yskn_b200_matrix_create_shard(const uint32_t* d_
                                                               const int8_t* signs_in_host,
                                                               const int8_t* signs_out_host, int row_begin,
                                                               int row_end, int col_begin, int col_end);
+/* A shard of several row ranges (row_ranges: n_ranges pairs begin, end; 1..16), stored
+ * one after another: the handle's row i is the i-th row of the ranges in order (every
+ * range but the last whole 8-row blocks of real rows; whole 512-row blocks with an output
+ * rotation). One rank's rows of a projection whose parts split separately, such as the
+ * query, key and value rows of in_proj_qkv for the heads the rank runs. No counterpart in
+ * the reference (one GPU). */
+YSKN_B200_API yskn_b200_matrix* yskn_b200_matrix_create_rows(const uint32_t* d_codes, int layout, int rows,
+                                                             int physical_rows, int cols, int bits,
+                                                             const uint16_t* lut16_host,
+                                                             const uint16_t* scale16_host,
+                                                             const int8_t* signs_in_host,
+                                                             const int8_t* signs_out_host, int n_ranges,
+                                                             const int* row_ranges, int col_begin, int col_end);
 YSKN_B200_API void yskn_b200_matrix_destroy(yskn_b200_matrix* m);
 /* rows, physical_rows, cols, bits, has_output_rotation, packed bytes. */
 YSKN_B200_API int yskn_b200_matrix_info(const yskn_b200_matrix* m, int64_t* out6);
@@ -217,6 +230,16 @@ YSKN_B200_API int yskn_b200_gated_product(const float* d_gate, const float* d_up
  * [M][8] and d_top8_ids int32 [M][8] in that order; any output may be NULL (not all). */
 YSKN_B200_API int yskn_b200_head_select(const float* d_logits, int M, int n, int32_t* d_token, float* d_top8_logits,
                                         int32_t* d_top8_ids, void* stream);
+/* The head split over vocabulary rows (tensor parallelism; the reference's head runs on one
+ * GPU, src/misc_kernels.cu:59-88): the greedy token and top 8 of the whole row from the
+ * parts' yskn_b200_head_select top 8: part q's f32 logits and int32 ids [M][8] start
+ * part_stride elements after part q - 1's (8 M when the parts are packed), its ids local to
+ * it (h_id_offsets[q], a host array, is its first row's id). The order is the same, so the
+ * result is bit-identical to yskn_b200_head_select over the whole row. n_parts 1..8;
+ * outputs as yskn_b200_head_select's. */
+YSKN_B200_API int yskn_b200_head_merge(const float* d_part_logits, const int32_t* d_part_ids, int64_t part_stride,
+                                       const int32_t* h_id_offsets, int n_parts, int M, int32_t* d_token,
+                                       float* d_top8_logits, int32_t* d_top8_ids, void* stream);
 
 /* Attention inputs from the q/k/v projection outputs (replaces the head preparation of
  * the q35 attention, src/q35_kernels.cu:1013-1059 and :1091-1104, and the cache rotation
@@ -252,6 +275,24 @@ YSKN_B200_API int yskn_b200_gdn_step(const float* d_qkv, const float* d_z, const
                                      const uint16_t* d_norm_w, float eps, int M, int n_commit, float* d_state,
                                      uint16_t* d_history,
                                      float* d_out, void* stream);
+/* The same two steps for a run of value heads, as one tensor-parallel rank holds them (the
+ * reference runs the whole layer on one GPU, src/engine35.cpp:768-842; the split by value
+ * head with its key heads is this library's). gates_heads: d_wb, d_wa the n_heads rows of
+ * the run, d_gates f32 [M][2 n_heads] (b, then a). step_heads: value heads v_head0 ..
+ * v_head0 + n_v_heads - 1 (value head h reads key head h / 3), with the query and key
+ * channels of key heads qk_head0 .. qk_head0 + qk_channels / 128 - 1; d_qkv f32 [M][W],
+ * W = 2 qk_channels + 128 n_v_heads, each row [query | key | value channels]; d_conv_w
+ * bf16 [W][4]; d_history bf16 [3][W]; d_z and d_out f32 [M][128 n_v_heads]; d_a_log,
+ * d_dt_bias [n_v_heads]; d_state f32 [n_v_heads][128][128]. Each head's results are the
+ * whole layer's bits for that head. */
+YSKN_B200_API int yskn_b200_gdn_gates_heads(const uint16_t* d_hidden, const float* d_inv_rms, const uint16_t* d_wb,
+                                            const uint16_t* d_wa, int n_heads, int M, int hidden, float* d_gates,
+                                            void* stream);
+YSKN_B200_API int yskn_b200_gdn_step_heads(const float* d_qkv, const float* d_z, const float* d_gates,
+                                           const uint16_t* d_conv_w, const uint16_t* d_a_log,
+                                           const uint16_t* d_dt_bias, const uint16_t* d_norm_w, float eps, int M,
+                                           int n_commit, int n_v_heads, int v_head0, int qk_head0, int qk_channels,
+                                           float* d_state, uint16_t* d_history, float* d_out, void* stream);
 
 /* bf16 -> f32 copy of n values (exact): an operator's f32 input from a bf16 producer, such as
  * the attention output before o_proj (the reference quantises that bf16 vector directly,
@@ -344,6 +385,21 @@ YSKN_B200_API int yskn_b200_tp_connect_peers(yskn_b200_tp* tp, void* const* peer
 YSKN_B200_API int yskn_b200_tp_set_wait(yskn_b200_tp* tp, double seconds);
 YSKN_B200_API int yskn_b200_linear_rowpar(yskn_b200_tp* tp, const yskn_b200_matrix* mat, const float* d_x_local, int M,
                                           const float* d_inv_rms, float* d_y, void* stream);
+/* The row-parallel operator with the residual epilogue of yskn_b200_linear_residual (the
+ * reference's FIN epilogue, src/lnord.cu:119-170, and q35_res_norm_xsm_kernel,
+ * src/q35_kernels.cu:1427-1474, which run on one GPU): this rank's columns of the input,
+ * as f32 d_x_local [M][cols of the shard] or as int8 d_act_local with group scales
+ * d_alpha_local [M][cols / 512] (exactly one; the int8 form is the local output of
+ * yskn_b200_gated_product_q8); every rank updates the whole residual stream d_hidden and
+ * writes the whole next input (d_act_out, d_alpha_out, d_bss_out, d_gate_out as in
+ * yskn_b200_linear_residual), bit-identical to one GPU's yskn_b200_linear_residual. The
+ * matrix's rows are a multiple of 512 (physical rows = rows). */
+YSKN_B200_API int yskn_b200_linear_rowpar_residual(yskn_b200_tp* tp, const yskn_b200_matrix* mat,
+                                                   const float* d_x_local, const int8_t* d_act_local,
+                                                   const float* d_alpha_local, int M, uint16_t* d_hidden,
+                                                   const uint16_t* d_norm_weight, const int8_t* d_next_signs,
+                                                   int8_t* d_act_out, float* d_alpha_out, float* d_bss_out,
+                                                   uint16_t* d_gate_out, void* stream);
 
 /* The per-layer chain between projections in the operators themselves (replaces the
  * reference's fused epilogue/prologue kernels: the FIN restore of src/lnord.cu:119-170 and

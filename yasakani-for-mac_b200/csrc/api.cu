@@ -266,25 +266,47 @@ YSKN_B200_API int yskn_b200_pack(const uint32_t* d_words, int layout, int physic
 // A matrix handle for physical rows [row0, row1) and columns [col0, col1) of a source
 // tensor of src_rows x src_phys x src_cols (the whole tensor, or one tensor-parallel
 // shard). The lookup table is per tensor, so every shard quantises it identically.
+// A matrix handle for the physical rows of n_ranges ranges [row0, row1) (stored in
+// that order: the handle's rows are the ranges' rows one after another) and columns
+// [col0, col1) of a source tensor of src_rows x src_phys x src_cols (the whole tensor,
+// one tensor-parallel shard, or the row blocks one rank needs of several parts of it).
 static yskn_b200_matrix* create_matrix(const uint32_t* d_codes, int layout, int src_rows, int src_phys, int src_cols,
                                        int bits, const uint16_t* lut16_host, const uint16_t* scale16_src,
-                                       const int8_t* signs_in_src, const int8_t* signs_out_src, int row0, int row1,
-                                       int col0, int col1) {
+                                       const int8_t* signs_in_src, const int8_t* signs_out_src, int n_ranges,
+                                       const int* ranges, int col0, int col1) {
   if (check_shape(layout, src_phys, src_cols, bits)) return nullptr;
   if (src_rows <= 0 || src_rows > src_phys) return fail(YSKN_EINVAL, "rows must be in 1..physical_rows"), nullptr;
   if (!d_codes || !aligned16(d_codes) || !lut16_host || !scale16_src || !signs_in_src)
     return fail(YSKN_EINVAL, "matrix_create: missing or misaligned input"), nullptr;
-  if (row0 < 0 || row1 > src_phys || row0 >= row1 || row0 % 8 || col0 < 0 || col1 > src_cols || col0 >= col1 ||
-      col0 % 512 || col1 % 512 || row0 >= src_rows)
-    return fail(YSKN_EINVAL, "shard: rows [row0, row1) need row0 % 8 == 0 and real rows; columns whole 512-groups"),
-           nullptr;
-  const int physical_rows = row1 - row0, cols = col1 - col0;
-  const int rows = std::min(src_rows, row1) - row0;
-  const uint16_t* scale16_host = scale16_src + row0;
+  if (n_ranges < 1 || n_ranges > 16 || !ranges)
+    return fail(YSKN_EINVAL, "shard: 1 to 16 row ranges"), nullptr;
+  if (col0 < 0 || col1 > src_cols || col0 >= col1 || col0 % 512 || col1 % 512)
+    return fail(YSKN_EINVAL, "shard: columns must be whole 512-groups of the tensor"), nullptr;
+  int physical_rows = 0, rows = 0;
+  for (int k = 0; k < n_ranges; ++k) {
+    const int r0 = ranges[2 * k], r1 = ranges[2 * k + 1];
+    // Every range but the last holds real rows only, a whole number of 8-row blocks.
+    if (r0 < 0 || r1 > src_phys || r0 >= r1 || r0 % 8 || r0 >= src_rows ||
+        (k + 1 < n_ranges && (r1 > src_rows || (r1 - r0) % 8)))
+      return fail(YSKN_EINVAL, "shard: rows [row0, row1) need row0 % 8 == 0 and real rows; every range but the last "
+                               "whole 8-row blocks of real rows"),
+             nullptr;
+    if (signs_out_src && ((r1 - r0) % 512 || r0 % 512))
+      return fail(YSKN_EINVAL, "an output rotation needs whole 512-row blocks"), nullptr;
+    physical_rows += r1 - r0;
+    rows += std::min(src_rows, r1) - r0;
+  }
+  const int cols = col1 - col0;
+  std::vector<uint16_t> scale16_rows(physical_rows);
+  std::vector<int8_t> signs_out_rows(signs_out_src ? physical_rows : 0);
+  for (int k = 0, o = 0; k < n_ranges; ++k)
+    for (int r = ranges[2 * k]; r < ranges[2 * k + 1]; ++r, ++o) {
+      scale16_rows[o] = scale16_src[r];
+      if (signs_out_src) signs_out_rows[o] = signs_out_src[r];
+    }
+  const uint16_t* scale16_host = scale16_rows.data();
   const int8_t* signs_in_host = signs_in_src + col0;
-  const int8_t* signs_out_host = signs_out_src ? signs_out_src + row0 : nullptr;
-  if (signs_out_host && (physical_rows % 512 || row0 % 512))
-    return fail(YSKN_EINVAL, "an output rotation needs whole 512-row blocks"), nullptr;
+  const int8_t* signs_out_host = signs_out_src ? signs_out_rows.data() : nullptr;
   for (int i = 0; i < cols; ++i)
     if (signs_in_host[i] != 1 && signs_in_host[i] != -1) return fail(YSKN_EINVAL, "signs must be -1 or +1"), nullptr;
   if (signs_out_host)
@@ -348,9 +370,14 @@ static yskn_b200_matrix* create_matrix(const uint32_t* d_codes, int layout, int 
   if (e == cudaSuccess) e = cudaMemcpy(small + off_sin, signs_in_host, cols, cudaMemcpyHostToDevice);
   if (e == cudaSuccess && signs_out_host)
     e = cudaMemcpy(small + off_sout, signs_out_host, physical_rows, cudaMemcpyHostToDevice);
-  int rc = e == cudaSuccess ? launch_pack_range(d_codes, layout, src_phys, src_cols, row0, col0, physical_rows, cols,
-                                                bits, reinterpret_cast<uint32_t*>(m->codes), nullptr)
-                            : cuda_fail(e, "matrix_create: copy");
+  int rc = e == cudaSuccess ? YSKN_OK : cuda_fail(e, "matrix_create: copy");
+  for (int k = 0, done = 0; k < n_ranges && rc == YSKN_OK; ++k) {  // each range's 8-row blocks after the previous
+    const int r0 = ranges[2 * k], n = ranges[2 * k + 1] - r0;
+    char* dst = reinterpret_cast<char*>(m->codes) + (int64_t)done * (cols / 256) * bits * 16;
+    rc = launch_pack_range(d_codes, layout, src_phys, src_cols, r0, col0, n, cols, bits, reinterpret_cast<uint32_t*>(dst),
+                           nullptr);
+    done += n;
+  }
   if (rc == YSKN_OK) rc = cuda_fail(cudaDeviceSynchronize(), "matrix_create: pack");
   if (rc != YSKN_OK) {
     cudaFree(m->codes);
@@ -378,8 +405,9 @@ YSKN_B200_API yskn_b200_matrix* yskn_b200_matrix_create(const uint32_t* d_codes,
                                                         int physical_rows, int cols, int bits,
                                                         const uint16_t* lut16_host, const uint16_t* scale16_host,
                                                         const int8_t* signs_in_host, const int8_t* signs_out_host) {
+  const int all[2] = {0, physical_rows};
   return create_matrix(d_codes, layout, rows, physical_rows, cols, bits, lut16_host, scale16_host, signs_in_host,
-                       signs_out_host, 0, physical_rows, 0, cols);
+                       signs_out_host, 1, all, 0, cols);
 }
 
 YSKN_B200_API yskn_b200_matrix* yskn_b200_matrix_create_shard(const uint32_t* d_codes, int layout, int rows,
@@ -389,8 +417,20 @@ YSKN_B200_API yskn_b200_matrix* yskn_b200_matrix_create_shard(const uint32_t* d_
                                                               const int8_t* signs_in_host,
                                                               const int8_t* signs_out_host, int row_begin, int row_end,
                                                               int col_begin, int col_end) {
+  const int range[2] = {row_begin, row_end};
   return create_matrix(d_codes, layout, rows, physical_rows, cols, bits, lut16_host, scale16_host, signs_in_host,
-                       signs_out_host, row_begin, row_end, col_begin, col_end);
+                       signs_out_host, 1, range, col_begin, col_end);
+}
+
+YSKN_B200_API yskn_b200_matrix* yskn_b200_matrix_create_rows(const uint32_t* d_codes, int layout, int rows,
+                                                             int physical_rows, int cols, int bits,
+                                                             const uint16_t* lut16_host,
+                                                             const uint16_t* scale16_host,
+                                                             const int8_t* signs_in_host,
+                                                             const int8_t* signs_out_host, int n_ranges,
+                                                             const int* row_ranges, int col_begin, int col_end) {
+  return create_matrix(d_codes, layout, rows, physical_rows, cols, bits, lut16_host, scale16_host, signs_in_host,
+                       signs_out_host, n_ranges, row_ranges, col_begin, col_end);
 }
 
 YSKN_B200_API int yskn_b200_rescale(const float* d_alpha, const float* d_row_max, int M, int groups,
@@ -482,6 +522,33 @@ YSKN_B200_API int yskn_b200_linear_rowpar(yskn_b200_tp* t, const yskn_b200_matri
   const GemvScratch* sc = current_scratch();
   if (!sc) return fail(YSKN_EINVAL, "linear_rowpar: no matrix was created on this device");
   return launch_linear_rowpar(mat->dev, t->view, d_x_local, M, d_inv_rms, d_y, *sc, as_stream(stream));
+}
+
+YSKN_B200_API int yskn_b200_linear_rowpar_residual(yskn_b200_tp* t, const yskn_b200_matrix* mat,
+                                                   const float* d_x_local, const int8_t* d_act_local,
+                                                   const float* d_alpha_local, int M, uint16_t* d_hidden,
+                                                   const uint16_t* d_norm_weight, const int8_t* d_next_signs,
+                                                   int8_t* d_act_out, float* d_alpha_out, float* d_bss_out,
+                                                   uint16_t* d_gate_out, void* stream) {
+  if (!t || !t->connected || !mat || M < 1 || (!d_x_local == !d_act_local) || (d_act_local && !d_alpha_local) ||
+      !d_hidden || !d_norm_weight || !d_next_signs || !d_act_out || !d_alpha_out || !d_bss_out ||
+      (d_x_local && !aligned16(d_x_local)) || (d_act_local && !aligned16(d_act_local)) || !aligned16(d_act_out) ||
+      (reinterpret_cast<uintptr_t>(d_hidden) & 3) || (d_gate_out && (reinterpret_cast<uintptr_t>(d_gate_out) & 3)))
+    return fail(YSKN_EINVAL, "linear_rowpar_residual: bad arguments (connected exchange, exactly one of f32 or int8 "
+                             "input, aligned buffers)");
+  const GemvScratch* sc = current_scratch();
+  if (!sc) return fail(YSKN_EINVAL, "linear_rowpar_residual: no matrix was created on this device");
+  FusedIO io;
+  io.q_act = d_act_local;
+  io.q_alpha = d_alpha_local;
+  io.res_hidden = d_hidden;
+  io.res_norm_w = d_norm_weight;
+  io.res_next_signs = d_next_signs;
+  io.res_act = d_act_out;
+  io.res_alpha = d_alpha_out;
+  io.res_bss = d_bss_out;
+  io.res_gate = d_gate_out;
+  return launch_linear_rowpar(mat->dev, t->view, d_x_local, M, nullptr, nullptr, *sc, as_stream(stream), io);
 }
 
 YSKN_B200_API void yskn_b200_matrix_destroy(yskn_b200_matrix* m) {

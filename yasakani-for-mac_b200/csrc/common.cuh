@@ -196,8 +196,10 @@ int launch_gated_product_q8(const float* gate, const float* up, int M, int n, co
 // The row-parallel operator of one rank in one launch: this rank's 512-column groups
 // of a matrix with an output rotation, the row maxima and the int64 block sums
 // exchanged with the peers through `tp`, the whole output restored on every rank.
+// With io: an int8 input (q_act, q_alpha) instead of x_local, and the residual epilogue
+// (res_*) instead of y, as in launch_linear_fused.
 int launch_linear_rowpar(const MatrixDev& mat, const TpView& tp, const float* x_local, int M, const float* inv_rms,
-                         float* y, const GemvScratch& scratch, cudaStream_t st);
+                         float* y, const GemvScratch& scratch, cudaStream_t st, const FusedIO& io = FusedIO());
 int launch_quantize(const float* x, const int8_t* signs, int M, int Kc, int8_t* act, float* alpha, int32_t* scales,
                     float* row_quantum, cudaStream_t st);
 int launch_restore(int64_t* ws, int ws_ld, const float* row_quantum, const float* inv_rms, const float* tau,

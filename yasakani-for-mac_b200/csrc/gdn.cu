@@ -27,6 +27,9 @@
 //    (q/k of the key head are recomputed by its three value heads: 128 channels each).
 //  * history: the three newest projected rows are written after the step, in place (another
 //    launch, since three CTAs read each key head's history).
+//  * tensor parallelism: a rank runs a run of value heads with the key heads they read
+//    (the *_heads entry points); every head's arithmetic is the whole layer's, so the runs
+//    of all ranks together give the whole layer's bits.
 #include <cuda_bf16.h>
 
 #include "common.cuh"
@@ -37,7 +40,6 @@ namespace yskn {
 constexpr int GDN_DK = 128;   // channels per head
 constexpr int GDN_QK_HEADS = 16;
 constexpr int GDN_V_HEADS = 48;
-constexpr int GDN_QKV = 2 * GDN_QK_HEADS * GDN_DK + GDN_V_HEADS * GDN_DK;  // 10240
 constexpr int GDN_GATE_ROWS = 8;  // rows per gates CTA
 
 __device__ __forceinline__ float bf(float x) {
@@ -69,11 +71,12 @@ __device__ __forceinline__ float dot8(float acc, uint4 w, uint4 x) {
 
 // 03_GATED_DELTANET.md:57-76: the 96 dense gates of each row (b, then a).
 __global__ void __launch_bounds__(128) gdn_gates_kernel(const uint16_t* x, const float* inv_rms, const uint16_t* wb,
-                                                        const uint16_t* wa, int hidden, int M, float* gates) {
+                                                        const uint16_t* wa, int n_heads, int hidden, int M,
+                                                        float* gates) {
   __shared__ float s4[2][4];
   pdl_begin();
   const int o = blockIdx.x, p = threadIdx.x;
-  const uint16_t* w = o < GDN_V_HEADS ? wb + (size_t)o * hidden : wa + (size_t)(o - GDN_V_HEADS) * hidden;
+  const uint16_t* w = o < n_heads ? wb + (size_t)o * hidden : wa + (size_t)(o - n_heads) * hidden;
   const int row0 = blockIdx.y * GDN_GATE_ROWS;
   const int rows = M - row0 < GDN_GATE_ROWS ? M - row0 : GDN_GATE_ROWS;
   const int chunks = hidden / 1024;
@@ -89,23 +92,28 @@ __global__ void __launch_bounds__(128) gdn_gates_kernel(const uint16_t* x, const
     const float g = xor_sum32(partial);
     if ((p & 31) == 0) s4[rr & 1][p >> 5] = g;
     __syncthreads();  // (the other buffer is written only after every thread passed the next barrier)
-    if (p == 0) gates[(size_t)row * 2 * GDN_V_HEADS + o] = bf(__fmul_rn(sum4(s4[rr & 1]), inv_rms[row]));
+    if (p == 0) gates[(size_t)row * 2 * n_heads + o] = bf(__fmul_rn(sum4(s4[rr & 1]), inv_rms[row]));
   }
 }
 
+// A run of value heads: n_v heads from global head v0, with the query and key channels of
+// global key heads qk0 .. qk0 + qk_ch / 128 - 1 (value head h reads key head h / 3). A
+// row of the projected input is [query channels | key channels | value channels], W wide
+// (the whole layer: v0 = qk0 = 0, n_v = 48, qk_ch = 2048, W = 10240).
 struct GdnParams {
-  const float* qkv;       // [M][10240] restored in_proj_qkv
-  const float* z;         // [M][6144] restored in_proj_z
-  const float* gates;     // [M][96]
-  const uint16_t* conv_w; // bf16 [10240][4], oldest coefficient first
-  const uint16_t* a_log;  // bf16 [48]
+  const float* qkv;       // [M][W] restored in_proj_qkv rows of the run
+  const float* z;         // [M][128 n_v] restored in_proj_z rows of the run
+  const float* gates;     // [M][2 n_v]: b, then a
+  const uint16_t* conv_w; // bf16 [W][4], oldest coefficient first
+  const uint16_t* a_log;  // bf16 [n_v]
   const uint16_t* dt_bias;
   const uint16_t* norm_w; // bf16 [128]
   float eps;
   int M, n_commit;
-  float* state;              // [48][128][128]
-  const uint16_t* history;   // bf16 [3][10240], oldest first
-  float* out;                // [M][6144]: the gated output (bf16 values), out_proj's x
+  float* state;              // [n_v][128][128]
+  const uint16_t* history;   // bf16 [3][W], oldest first
+  float* out;                // [M][128 n_v]: the gated output (bf16 values), out_proj's x
+  int n_v, v0, qk0, qk_ch, W;
 };
 
 constexpr int GDN_STEP_THREADS = 4 * GDN_DK;  // four threads per state column, one per 32-row group
@@ -123,12 +131,12 @@ __device__ __forceinline__ void gdn_load_row(const GdnParams& p, int row, int c,
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
       const int r = row - 3 + t;  // 03_GATED_DELTANET.md:86-100, depth = row
-      in.x[t] = r < 0 ? bf16f(p.history[(size_t)(3 + r) * GDN_QKV + c]) : bf(p.qkv[(size_t)r * GDN_QKV + c]);
+      in.x[t] = r < 0 ? bf16f(p.history[(size_t)(3 + r) * p.W + c]) : bf(p.qkv[(size_t)r * p.W + c]);
     }
   }
-  if (c >= 0 && c < GDN_QK_HEADS * GDN_DK) in.z = p.z[(size_t)row * GDN_V_HEADS * GDN_DK + GDN_DK * vh + j];
-  in.gb = p.gates[(size_t)row * 2 * GDN_V_HEADS + vh];
-  in.ga = p.gates[(size_t)row * 2 * GDN_V_HEADS + GDN_V_HEADS + vh];
+  if (c >= 0 && c < p.qk_ch) in.z = p.z[(size_t)row * p.n_v * GDN_DK + GDN_DK * vh + j];
+  in.gb = p.gates[(size_t)row * 2 * p.n_v + vh];
+  in.ga = p.gates[(size_t)row * 2 * p.n_v + p.n_v + vh];
 }
 
 // bf(silu(bf(conv))) of one channel from its taps and weights.
@@ -148,15 +156,15 @@ __global__ void __launch_bounds__(GDN_STEP_THREADS) gdn_step_kernel(const __grid
   __shared__ float s_sq[2][4], s_so[4];   // per-warp squares: query, key; core
   pdl_begin();
   const int t = threadIdx.x, j = t & (GDN_DK - 1), grp = t >> 7, warp = t >> 5, lane = t & 31;
-  const int vh = blockIdx.x, kh = vh / 3, i0 = 32 * grp;
+  const int vh = blockIdx.x, kh = (p.v0 + vh) / 3 - p.qk0, i0 = 32 * grp;  // local value and key head
   float* state = p.state + (size_t)vh * GDN_DK * GDN_DK + (size_t)i0 * GDN_DK + j;  // element (i0, j)
   float R[32];  // state rows i0..i0+31 of column j
 #pragma unroll
   for (int r = 0; r < 32; ++r) R[r] = state[r * GDN_DK];
   // group 0: query channel j of the key head; 1: key channel; 2: value channel; 3: none
   const int c = grp == 0   ? GDN_DK * kh + j
-                : grp == 1 ? GDN_QK_HEADS * GDN_DK + GDN_DK * kh + j
-                : grp == 2 ? 2 * GDN_QK_HEADS * GDN_DK + GDN_DK * vh + j
+                : grp == 1 ? p.qk_ch + GDN_DK * kh + j
+                : grp == 2 ? 2 * p.qk_ch + GDN_DK * vh + j
                            : -1;
   float cw[4] = {0.0f, 0.0f, 0.0f, 0.0f};
   if (c >= 0) {
@@ -229,7 +237,7 @@ __global__ void __launch_bounds__(GDN_STEP_THREADS) gdn_step_kernel(const __grid
     if (grp == 0) {
       const float inv = pm_rsqrt(__fadd_rn(__fdiv_rn(sum4(s_so), 128.0f), p.eps));
       const float normalized = bf(__fmul_rn(bf16f(p.norm_w[j]), bf(__fmul_rn(core, inv))));
-      p.out[(size_t)row * GDN_V_HEADS * GDN_DK + GDN_DK * vh + j] = bf(__fmul_rn(normalized, pm_silu(cur.z)));
+      p.out[(size_t)row * p.n_v * GDN_DK + GDN_DK * vh + j] = bf(__fmul_rn(normalized, pm_silu(cur.z)));
     }
     if (row + 1 == p.n_commit)
 #pragma unroll
@@ -242,15 +250,15 @@ __global__ void __launch_bounds__(GDN_STEP_THREADS) gdn_step_kernel(const __grid
 // after the step: row a takes old row M + a when fewer than 3 - a new rows exist, a later
 // row than a, so
 // each thread (one channel) reads every old value before it writes over it.
-__global__ void gdn_history_kernel(const float* qkv, int M, uint16_t* history) {
+__global__ void gdn_history_kernel(const float* qkv, int M, int W, uint16_t* history) {
   pdl_begin();
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= GDN_QKV) return;
+  if (c >= W) return;
 #pragma unroll
   for (int a = 0; a < 3; ++a) {
     const int r = M - 3 + a;
-    history[(size_t)a * GDN_QKV + c] = r < 0 ? history[(size_t)(3 + r) * GDN_QKV + c]
-                                             : __bfloat16_as_ushort(__float2bfloat16_rn(qkv[(size_t)r * GDN_QKV + c]));
+    history[(size_t)a * W + c] = r < 0 ? history[(size_t)(3 + r) * W + c]
+                                       : __bfloat16_as_ushort(__float2bfloat16_rn(qkv[(size_t)r * W + c]));
   }
 }
 
@@ -258,34 +266,68 @@ __global__ void gdn_history_kernel(const float* qkv, int M, uint16_t* history) {
 
 using namespace yskn;
 
-extern "C" YSKN_B200_API int yskn_b200_gdn_gates(const uint16_t* d_hidden, const float* d_inv_rms, const uint16_t* d_wb,
-                                                const uint16_t* d_wa, int M, int hidden, float* d_gates, void* stream) {
-  if (!d_hidden || !d_inv_rms || !d_wb || !d_wa || !d_gates || M < 1 || hidden <= 0 || hidden % 1024)
-    return fail(YSKN_EINVAL, "gdn_gates: null argument, M < 1 or hidden not a multiple of 1024");
+static int gdn_gates(const uint16_t* d_hidden, const float* d_inv_rms, const uint16_t* d_wb, const uint16_t* d_wa,
+                     int n_heads, int M, int hidden, float* d_gates, void* stream) {
+  if (!d_hidden || !d_inv_rms || !d_wb || !d_wa || !d_gates || M < 1 || hidden <= 0 || hidden % 1024 || n_heads < 1 ||
+      n_heads > GDN_V_HEADS)
+    return fail(YSKN_EINVAL, "gdn_gates: null argument, M < 1, hidden not a multiple of 1024 or heads outside 1..48");
   if (((uintptr_t)d_hidden | (uintptr_t)d_wb | (uintptr_t)d_wa) & 15)
     return fail(YSKN_EINVAL, "gdn_gates: hidden rows and weights must be 16-byte aligned");
   const int groups = (M + GDN_GATE_ROWS - 1) / GDN_GATE_ROWS;
   if (groups > 65535) return fail(YSKN_EINVAL, "gdn_gates: too many rows per call");
-  return cuda_fail(launch_pdl(gdn_gates_kernel, dim3(2 * GDN_V_HEADS, groups), 128, 0,
-                              reinterpret_cast<cudaStream_t>(stream), d_hidden, d_inv_rms, d_wb, d_wa, hidden, M,
-                              d_gates),
+  return cuda_fail(launch_pdl(gdn_gates_kernel, dim3(2 * n_heads, groups), 128, 0, reinterpret_cast<cudaStream_t>(stream),
+                              d_hidden, d_inv_rms, d_wb, d_wa, n_heads, hidden, M, d_gates),
                    "gdn_gates_kernel");
+}
+
+static int gdn_step(const float* d_qkv, const float* d_z, const float* d_gates, const uint16_t* d_conv_w,
+                    const uint16_t* d_a_log, const uint16_t* d_dt_bias, const uint16_t* d_norm_w, float eps, int M,
+                    int n_commit, int n_v, int v0, int qk0, int qk_ch, float* d_state, uint16_t* d_history,
+                    float* d_out, void* stream) {
+  if (!d_qkv || !d_z || !d_gates || !d_conv_w || !d_a_log || !d_dt_bias || !d_norm_w || !d_state || !d_history ||
+      !d_out || M < 1 || n_commit < 0 || n_commit > M)
+    return fail(YSKN_EINVAL, "gdn_step: null argument, M < 1 or n_commit outside 0..M");
+  if (n_v < 1 || v0 < 0 || v0 + n_v > GDN_V_HEADS || qk0 < 0 || qk_ch < GDN_DK || qk_ch % GDN_DK ||
+      qk0 * GDN_DK + qk_ch > GDN_QK_HEADS * GDN_DK || v0 / 3 < qk0 || (v0 + n_v - 1) / 3 >= qk0 + qk_ch / GDN_DK)
+    return fail(YSKN_EINVAL, "gdn_step: the value heads need their key heads among the given query/key channels");
+  if ((uintptr_t)d_conv_w & 7) return fail(YSKN_EINVAL, "gdn_step: convolution weights must be 8-byte aligned");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int W = 2 * qk_ch + GDN_DK * n_v;
+  GdnParams p{d_qkv, d_z, d_gates, d_conv_w, d_a_log, d_dt_bias, d_norm_w, eps, M, n_commit, d_state, d_history,
+              d_out, n_v, v0, qk0, qk_ch, W};
+  if (cudaError_t e = launch_pdl(gdn_step_kernel, n_v, GDN_STEP_THREADS, 0, st, p)) return cuda_fail(e, "gdn_step_kernel");
+  if (n_commit == 0) return YSKN_OK;
+  // After the step (the same stream): every head has read the old history.
+  return cuda_fail(launch_pdl(gdn_history_kernel, (W + 255) / 256, 256, 0, st, d_qkv, n_commit, W, d_history),
+                   "gdn_history_kernel");
+}
+
+
+extern "C" YSKN_B200_API int yskn_b200_gdn_gates(const uint16_t* d_hidden, const float* d_inv_rms, const uint16_t* d_wb,
+                                                const uint16_t* d_wa, int M, int hidden, float* d_gates, void* stream) {
+  return gdn_gates(d_hidden, d_inv_rms, d_wb, d_wa, GDN_V_HEADS, M, hidden, d_gates, stream);
+}
+
+extern "C" YSKN_B200_API int yskn_b200_gdn_gates_heads(const uint16_t* d_hidden, const float* d_inv_rms,
+                                                      const uint16_t* d_wb, const uint16_t* d_wa, int n_heads, int M,
+                                                      int hidden, float* d_gates, void* stream) {
+  return gdn_gates(d_hidden, d_inv_rms, d_wb, d_wa, n_heads, M, hidden, d_gates, stream);
 }
 
 extern "C" YSKN_B200_API int yskn_b200_gdn_step(const float* d_qkv, const float* d_z, const float* d_gates,
                                                const uint16_t* d_conv_w, const uint16_t* d_a_log,
                                                const uint16_t* d_dt_bias, const uint16_t* d_norm_w, float eps, int M,
                                                int n_commit, float* d_state, uint16_t* d_history, float* d_out, void* stream) {
-  if (!d_qkv || !d_z || !d_gates || !d_conv_w || !d_a_log || !d_dt_bias || !d_norm_w || !d_state || !d_history ||
-      !d_out || M < 1 || n_commit < 0 || n_commit > M)
-    return fail(YSKN_EINVAL, "gdn_step: null argument, M < 1 or n_commit outside 0..M");
-  if ((uintptr_t)d_conv_w & 7) return fail(YSKN_EINVAL, "gdn_step: convolution weights must be 8-byte aligned");
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  GdnParams p{d_qkv, d_z, d_gates, d_conv_w, d_a_log, d_dt_bias, d_norm_w, eps, M, n_commit, d_state, d_history, d_out};
-  if (cudaError_t e = launch_pdl(gdn_step_kernel, GDN_V_HEADS, GDN_STEP_THREADS, 0, st, p))
-    return cuda_fail(e, "gdn_step_kernel");
-  if (n_commit == 0) return YSKN_OK;
-  // After the step (the same stream): every head has read the old history.
-  return cuda_fail(launch_pdl(gdn_history_kernel, (GDN_QKV + 255) / 256, 256, 0, st, d_qkv, n_commit, d_history),
-                   "gdn_history_kernel");
+  return gdn_step(d_qkv, d_z, d_gates, d_conv_w, d_a_log, d_dt_bias, d_norm_w, eps, M, n_commit, GDN_V_HEADS, 0, 0,
+                  GDN_QK_HEADS * GDN_DK, d_state, d_history, d_out, stream);
+}
+
+extern "C" YSKN_B200_API int yskn_b200_gdn_step_heads(const float* d_qkv, const float* d_z, const float* d_gates,
+                                                     const uint16_t* d_conv_w, const uint16_t* d_a_log,
+                                                     const uint16_t* d_dt_bias, const uint16_t* d_norm_w, float eps,
+                                                     int M, int n_commit, int n_v_heads, int v_head0, int qk_head0,
+                                                     int qk_channels, float* d_state, uint16_t* d_history,
+                                                     float* d_out, void* stream) {
+  return gdn_step(d_qkv, d_z, d_gates, d_conv_w, d_a_log, d_dt_bias, d_norm_w, eps, M, n_commit, n_v_heads, v_head0,
+                  qk_head0, qk_channels, d_state, d_history, d_out, stream);
 }

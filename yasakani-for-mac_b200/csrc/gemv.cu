@@ -1066,10 +1066,13 @@ int launch_linear_fused(const MatrixDev* mats, int n_mats, const float* x, int M
 }
 
 int launch_linear_rowpar(const MatrixDev& mat, const TpView& tp, const float* x_local, int M, const float* inv_rms,
-                         float* y, const GemvScratch& scratch, cudaStream_t st) {
+                         float* y, const GemvScratch& scratch, cudaStream_t st, const FusedIO& io) {
   if (!fused_linear_fits(M, mat.cols) || M > TP_MAX_M)
     return fail(YSKN_EINVAL, "row-parallel linear: M must be 1..16 with the input in shared memory");
   if (!mat.s_out) return fail(YSKN_EINVAL, "row-parallel linear: the matrix needs an output rotation");
+  if (io.q_bss) return fail(YSKN_EINVAL, "row-parallel linear: no input normalisation from block sums");
+  if (io.res_hidden && (mat.rows != mat.phys || mat.rows % 512))
+    return fail(YSKN_EINVAL, "row-parallel linear: the residual output needs whole 512-row blocks");
   if (mat.phys / 512 > tp.max_blocks) return fail(YSKN_EINVAL, "row-parallel linear: matrix taller than the exchange");
   const int out_rows = mat.phys;
   GemvParams p;
@@ -1084,6 +1087,10 @@ int launch_linear_rowpar(const MatrixDev& mat, const TpView& tp, const float* x_
   p.inv_rms = inv_rms;
   p.mv = M;
   p.tp = tp;
+  p.q_act = io.q_act;
+  p.q_alpha = io.q_alpha;
+  p.res = ResidualOut{io.res_hidden, io.res_norm_w, io.res_next_signs, io.res_act, io.res_alpha, io.res_bss,
+                      io.res_gate};
   GemvSeg& s = p.seg[0];
   s.out = reinterpret_cast<int64_t*>(scratch.fused_sums);
   if ((int64_t)M * mat.phys > scratch.fused_sums_len) return fail(YSKN_EINVAL, "row-parallel linear: sums scratch");

@@ -172,9 +172,60 @@ __global__ void __launch_bounds__(HEAD_SPLIT_THREADS) head_select_split_kernel(c
   if (threadIdx.x == 0) g_head_arrivals[m] = 0u;
 }
 
+// The first eight of each row from several parts' first eights (the parts partition the
+// row's ids; part q's ids are local, its first id is offset q): one thread per row inserts
+// every part's candidates. The order is total on the eligible candidates, so the result is
+// the first eight of the whole row, as head_select over the whole row gives.
+struct MergeOffsets {
+  int off[TP_MAX_WORLD];
+};
+
+__global__ void head_merge_kernel(const float* part_v, const int32_t* part_id, int64_t part_stride,
+                                  const MergeOffsets offs, int n_parts, int M, int32_t* token, float* top_v,
+                                  int32_t* top_id) {
+  pdl_begin();
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= M) return;
+  float v[HEAD_K];
+  int id[HEAD_K];
+#pragma unroll
+  for (int k = 0; k < HEAD_K; ++k) v[k] = -FLT_MAX, id[k] = INT_MAX;
+  for (int q = 0; q < n_parts; ++q)
+    for (int k = 0; k < HEAD_K; ++k) {
+      const size_t i = (size_t)q * part_stride + (size_t)m * HEAD_K + k;
+      const int li = part_id[i];
+      if (li == INT_MAX) continue;  // an unfilled place of that part
+      insert8(v, id, part_v[i], li + offs.off[q]);
+    }
+  if (token) token[m] = id[0];
+#pragma unroll
+  for (int k = 0; k < HEAD_K; ++k) {
+    if (top_v) top_v[(size_t)m * HEAD_K + k] = v[k];
+    if (top_id) top_id[(size_t)m * HEAD_K + k] = id[k];
+  }
+}
+
 }  // namespace yskn
 
 using namespace yskn;
+
+extern "C" YSKN_B200_API int yskn_b200_head_merge(const float* d_part_logits, const int32_t* d_part_ids,
+                                                 int64_t part_stride, const int32_t* h_id_offsets, int n_parts, int M,
+                                                 int32_t* d_token, float* d_top8_logits, int32_t* d_top8_ids,
+                                                 void* stream) {
+  if (!d_part_logits || !d_part_ids || !h_id_offsets || n_parts < 1 || n_parts > TP_MAX_WORLD || M < 1 ||
+      part_stride < (int64_t)M * HEAD_K || (!d_token && !d_top8_logits && !d_top8_ids))
+    return fail(YSKN_EINVAL, "head_merge: null argument, parts outside 1..8, M < 1, stride below 8 M or no output");
+  MergeOffsets offs{};
+  for (int q = 0; q < n_parts; ++q) {
+    if (h_id_offsets[q] < 0) return fail(YSKN_EINVAL, "head_merge: negative id offset");
+    offs.off[q] = h_id_offsets[q];
+  }
+  return cuda_fail(launch_pdl(head_merge_kernel, (M + 31) / 32, 32, 0, reinterpret_cast<cudaStream_t>(stream),
+                              d_part_logits, d_part_ids, part_stride, offs, n_parts, M, d_token, d_top8_logits,
+                              d_top8_ids),
+                   "head_merge_kernel");
+}
 
 extern "C" YSKN_B200_API int yskn_b200_head_select(const float* d_logits, int M, int n, int32_t* d_token,
                                                   float* d_top8_logits, int32_t* d_top8_ids, void* stream) {

@@ -82,6 +82,11 @@ _SIGNATURES = {
     "yskn_b200_linear_q8": (_i, [_vp, _i, _vp, _vp, _vp, C.c_float, _i, _vp, _vp, _vp]),
     "yskn_b200_gated_product_q8": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp]),
     "yskn_b200_gdn_step": (_i, [_vp] * 7 + [C.c_float, _i, _i, _vp, _vp, _vp, _vp]),
+    "yskn_b200_matrix_create_rows": (_vp, [_vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _i, _vp, _i, _i]),
+    "yskn_b200_gdn_gates_heads": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
+    "yskn_b200_gdn_step_heads": (_i, [_vp] * 7 + [C.c_float, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
+    "yskn_b200_linear_rowpar_residual": (_i, [_vp] * 5 + [_i] + [_vp] * 8),
+    "yskn_b200_head_merge": (_i, [_vp, _vp, _i64, _vp, _i, _i, _vp, _vp, _vp, _vp]),
 }
 
 _lib = None
@@ -152,7 +157,9 @@ class Matrix:
     def __init__(self, d_codes, layout, rows, physical_rows, cols, bits, lut16, scale16, signs_in, signs_out=None,
                  shard=None):
         """shard: (row_begin, row_end, col_begin, col_end) of the whole tensor described by
-        the other arguments (yskn_b200_matrix_create_shard), or None for the whole tensor."""
+        the other arguments (yskn_b200_matrix_create_shard), or None for the whole tensor;
+        or ([(row_begin, row_end), ...], col_begin, col_end): several row ranges stored one
+        after another (yskn_b200_matrix_create_rows)."""
         import numpy as np
         lut16 = np.ascontiguousarray(lut16, np.uint16)
         scale16 = np.ascontiguousarray(scale16, np.uint16)
@@ -163,14 +170,23 @@ class Matrix:
         if shard is None:
             h = lib().yskn_b200_matrix_create(*args)
             shard = (0, physical_rows, 0, cols)
+        elif len(shard) == 3:
+            ranges, c0, c1 = shard
+            flat = (C.c_int * (2 * len(ranges)))(*[int(v) for r in ranges for v in r])
+            h = lib().yskn_b200_matrix_create_rows(*args, len(ranges), flat, c0, c1)
         else:
             h = lib().yskn_b200_matrix_create_shard(*args, *shard)
         if not h:
             raise YsknError(EINVAL, "matrix_create: " + last_error())
         self.handle = C.c_void_p(h)
-        r0, r1, c0, c1 = shard
         self.shard = tuple(shard)
-        self.rows, self.physical_rows = min(rows, r1) - r0, r1 - r0
+        if len(shard) == 3:
+            ranges, c0, c1 = shard
+            self.rows = sum(min(rows, r1) - r0 for r0, r1 in ranges)
+            self.physical_rows = sum(r1 - r0 for r0, r1 in ranges)
+        else:
+            r0, r1, c0, c1 = shard
+            self.rows, self.physical_rows = min(rows, r1) - r0, r1 - r0
         self.cols, self.bits = c1 - c0, bits
         self.has_rotation = so is not None
 
@@ -364,6 +380,34 @@ def gdn_gates(hidden, inv_rms, wb, wa, gates, stream=None):
                                     _ptr(gates), _stream(stream)), "gdn_gates")
 
 
+def gdn_gates_heads(hidden, inv_rms, wb, wa, gates, stream=None):
+    """yskn_b200_gdn_gates_heads: the gates of the value heads whose rows wb, wa hold."""
+    check(lib().yskn_b200_gdn_gates_heads(_ptr(hidden), _ptr(inv_rms), _ptr(wb), _ptr(wa), wb.shape[0],
+                                          hidden.shape[0], hidden.shape[1], _ptr(gates), _stream(stream)),
+          "gdn_gates_heads")
+
+
+def gdn_step_heads(qkv, z, gates, conv_w, a_log, dt_bias, norm_w, eps, state, history, out, v_head0, qk_head0,
+                   qk_channels, n_commit=None, stream=None):
+    """yskn_b200_gdn_step_heads: the step of state.shape[0] value heads from v_head0, with
+    the query/key channels of key heads from qk_head0 (qk_channels each)."""
+    n_commit = qkv.shape[0] if n_commit is None else n_commit
+    check(lib().yskn_b200_gdn_step_heads(_ptr(qkv), _ptr(z), _ptr(gates), _ptr(conv_w), _ptr(a_log), _ptr(dt_bias),
+                                         _ptr(norm_w), eps, qkv.shape[0], n_commit, state.shape[0], v_head0,
+                                         qk_head0, qk_channels, _ptr(state), _ptr(history), _ptr(out),
+                                         _stream(stream)), "gdn_step_heads")
+
+
+def head_merge(part_logits, part_ids, offsets, token=None, top_logits=None, top_ids=None, stream=None):
+    """yskn_b200_head_merge: part_logits f32 / part_ids int32 [n_parts][M][8] (views whose
+    first dimension may be strided, the other two dense), offsets the parts' first ids."""
+    n_parts, M = part_logits.shape[0], part_logits.shape[1]
+    assert part_logits.stride(0) == part_ids.stride(0) and part_logits.stride(1) == 8 and part_ids.stride(1) == 8
+    offs = (C.c_int32 * n_parts)(*[int(o) for o in offsets])
+    check(lib().yskn_b200_head_merge(_ptr(part_logits), _ptr(part_ids), part_logits.stride(0), offs, n_parts, M,
+                                     _ptr(token), _ptr(top_logits), _ptr(top_ids), _stream(stream)), "head_merge")
+
+
 def gdn_step(qkv, z, gates, conv_w, a_log, dt_bias, norm_w, eps, state, history, out, n_commit=None, stream=None):
     """One Gated DeltaNet pass over qkv.shape[0] rows, committing after n_commit rows
     (default: all of them; 0 = provisional, state and history unchanged)."""
@@ -471,6 +515,17 @@ def linear_rowpar(exchange, mat, x_local, y, inv_rms=None, stream=None):
     """yskn_b200_linear_rowpar: the whole output of a row-parallel shard, on every rank."""
     check(lib().yskn_b200_linear_rowpar(exchange.handle, mat.handle, _ptr(x_local), x_local.shape[0], _ptr(inv_rms),
                                         _ptr(y), _stream(stream)), "linear_rowpar")
+
+
+def linear_rowpar_residual(exchange, mat, hidden, norm_weight, next_signs, act_out, alpha_out, bss_out, x=None,
+                           act=None, alpha=None, gate_out=None, stream=None):
+    """yskn_b200_linear_rowpar_residual: the row-parallel operator from this rank's input
+    columns (x f32, or act/alpha int8) into the whole residual stream and next input."""
+    M = (x if x is not None else act).shape[0]
+    check(lib().yskn_b200_linear_rowpar_residual(exchange.handle, mat.handle, _ptr(x), _ptr(act), _ptr(alpha), M,
+                                                 _ptr(hidden), _ptr(norm_weight), _ptr(next_signs), _ptr(act_out),
+                                                 _ptr(alpha_out), _ptr(bss_out), _ptr(gate_out), _stream(stream)),
+          "linear_rowpar_residual")
 
 
 def restore(ws, row_quantum, inv_rms, mat, rotate_out, n_rows, clear_ws, y, stream=None):

@@ -74,9 +74,11 @@ class Stack:
         self.L = []
         for i, kind in enumerate(self.kinds):
             L = {"kind": kind, "in_norm": bfb(self._normal(HIDDEN) * 0.1), "post_norm": bfb(self._normal(HIDDEN) * 0.1),
-                 "gate": self._matrix(FFN, HIDDEN), "up": self._matrix(FFN, HIDDEN), "down": self._matrix(HIDDEN, FFN)}
+                 "gate": self._matrix(FFN, HIDDEN, role="gate"), "up": self._matrix(FFN, HIDDEN, role="up"),
+                 "down": self._matrix(HIDDEN, FFN, role="down")}
             if kind == "gdn":
-                L.update(qkv=self._matrix(QKV, HIDDEN), z=self._matrix(ZDIM, HIDDEN), out=self._matrix(HIDDEN, ZDIM),
+                L.update(qkv=self._matrix(QKV, HIDDEN, role="qkv"), z=self._matrix(ZDIM, HIDDEN, role="z"),
+                         out=self._matrix(HIDDEN, ZDIM, role="out"),
                          wb=bfb(self._normal(48 * HIDDEN).reshape(48, HIDDEN) * 0.02),
                          wa=bfb(self._normal(48 * HIDDEN).reshape(48, HIDDEN) * 0.02),
                          conv=bfb(self._normal(QKV * 4).reshape(QKV, 4) * 0.5),
@@ -89,13 +91,13 @@ class Stack:
                 cache = torch.randint(-2 ** 31, 2 ** 31, (2, N_KVH, cap, 32), dtype=torch.int32, device=device,
                                       generator=self.gen)
                 scales = 0.02 + 0.18 * torch.rand((2, N_KVH, cap), device=device, generator=self.gen)
-                L.update(q=self._matrix(N_QH * 2 * HEAD, HIDDEN), k=self._matrix(N_KVH * HEAD, HIDDEN),
-                         v=self._matrix(N_KVH * HEAD, HIDDEN), o=self._matrix(HIDDEN, N_QH * HEAD),
+                L.update(q=self._matrix(N_QH * 2 * HEAD, HIDDEN, role="q"), k=self._matrix(N_KVH * HEAD, HIDDEN, role="k"),
+                         v=self._matrix(N_KVH * HEAD, HIDDEN, role="v"), o=self._matrix(HIDDEN, N_QH * HEAD, role="o"),
                          q_norm=bfb(self._normal(HEAD) * 0.1), k_norm=bfb(self._normal(HEAD) * 0.1),
                          cache=cache, scales=scales)
             self.L.append(L)
         self.final_norm = bfb(self._normal(HIDDEN) * 0.1)
-        self.head = self._matrix(vocab, HIDDEN, rotate=False)
+        self.head = self._matrix(vocab, HIDDEN, rotate=False, role="head")
         emb_codes = torch.randint(-2 ** 31, 2 ** 31, (vocab * (HIDDEN // 256) * 4 * bits,), dtype=torch.int32,
                                   device=device, generator=self.gen)
         lut16, sc16 = synthetic.model_tables(vocab, int(self.rng.integers(1 << 30)))
@@ -153,11 +155,16 @@ class Stack:
             self._signs[(offset, n)] = Y.signs(SIGN_RULE, 7, offset, n)
         return self._signs[(offset, n)]
 
-    def _matrix(self, rows, cols, rotate=True):
+    def _matrix(self, rows, cols, rotate=True, role=None):
         torch = self.torch
         words = torch.randint(-2 ** 31, 2 ** 31, (rows * (cols // 256) * 4 * self.bits,), dtype=torch.int32,
                               device=self.dev, generator=self.gen)
         lut16, sc16 = synthetic.model_tables(rows, int(self.rng.integers(1 << 30)))
+        return self._place(words, rows, cols, lut16, sc16, rotate, role)
+
+    def _place(self, words, rows, cols, lut16, sc16, rotate, role):
+        """The matrix this device runs of a seeded tensor (here the whole tensor; the
+        tensor-parallel stack keeps its rank's rows or columns). role names the projection."""
         self._keep.append(words)
         m = Y.Matrix(words, "warp", rows, rows, cols, self.bits, lut16, sc16, self._sign(0, cols),
                      self._sign(cols, rows) if rotate else None)
