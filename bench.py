@@ -7,9 +7,10 @@ decode, hidden 5120 -- attention q/k/v/o, Gated-DeltaNet in_proj_qkv/in_proj_z/
 out_proj, MLP gate/up/down -- on synthetic 27B-shape compressed weights (random
 code words, seeded N(0,1) value table, row scales ~0.02; bits=8 is the format's
 4-bit width, bits=6 the lowest). One step = the six operator calls of the layer
-(q/k/v, o, qkv/z, out, gate/up, down; matrices sharing an input go in one call):
-quantise x -> exact int64 weighted sums -> restore + output H512 (one fused launch
-per call at M=1), captured in one CUDA graph. The metric is HBM throughput of the compressed weights:
+(q/k/v, o, qkv/z, out, gate/up, down; matrices sharing an input go in one call), each
+from its input as the producer hands it over (int8 rows and group scales: the quantiser
+runs in the producing kernel) -> exact int64 weighted sums -> restore + output H512 (one
+launch per call at M=1, yskn_b200_linear_q8), captured in one CUDA graph. The metric is HBM throughput of the compressed weights:
 algorithmic bytes per step / step time. Codes per step (243.8 MB at bits=8) exceed
 the 126 MB L2, so no L2 flush is needed between steps.
 
@@ -98,13 +99,13 @@ LAYER_ROWS = {n: r for n, r, _ in LAYER}
 
 
 def algorithmic_bytes(bits, M):
-    """Minimum bytes one step must move: codes + int8 table + f32 row scales + signs
-    (in and out) per matrix, f32 input per call, f32 output per matrix."""
+    """Minimum bytes one step must move: codes + int8 table + f32 row scales + output signs
+    per matrix, its f32 output; int8 input rows + f32 group scales per call."""
     total = 0
     for name, rows, cols in LAYER:
         total += rows * cols * bits // 16 + 8192 + 4 * rows + rows + 4 * M * rows
     for c in CALLS:
-        total += 4 * M * LAYER_COLS[c[0]] + LAYER_COLS[c[0]]
+        total += M * LAYER_COLS[c[0]] + 4 * M * (LAYER_COLS[c[0]] // 512)
     return total
 
 
@@ -165,13 +166,24 @@ class ClockSampler:
         return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_layer_step(W, xs, fraction=1.0, threads=None):
-    """The CPU path for one step (the reference's CPU engine restated in C):
-    quantise, threaded weighted sums (first `fraction` of each matrix's rows), restore."""
+def cpu_inputs(W, xs):
+    """Each call's int8 input, integer group scales and row quanta (the quantiser, run once
+    outside the timed steps, as the GPU arm's inputs come quantised from their producer)."""
     import oracle as O
-    nbytes = 0
+    out = []
     for c, x in zip(CALLS, xs):
         act, _, A, rq = O.quantize_activation(x, W[c[0]]["s_in"])
+        out.append((act, A, rq))
+    return out
+
+
+def cpu_layer_step(W, qs, fraction=1.0, threads=None):
+    """The CPU path for one step (the reference's CPU engine restated in C): threaded
+    weighted sums from the quantised inputs (first `fraction` of each matrix's rows),
+    restore."""
+    import oracle as O
+    nbytes = 0
+    for c, (act, A, rq) in zip(CALLS, qs):
         for name in c:
             w = W[name]
             rows = max(32, int(w["rows"] * fraction) // 32 * 32)
@@ -196,7 +208,7 @@ def run_reference(args, rank, world):
     import oracle as O
     W = make_weights(args.bits, signs=O.signs)
     prepare_cpu(W, args.bits)
-    xs = make_inputs(1)
+    xs = cpu_inputs(W, make_inputs(1))
     threads = os.cpu_count() or 1
     t0 = time.perf_counter()
     cpu_layer_step(W, xs, 1.0, threads)
@@ -211,8 +223,8 @@ def run_reference(args, rank, world):
         nbytes += cpu_layer_step(W, xs, fraction, threads)
     dt = time.perf_counter() - t0
     value = nbytes / dt / 1e12
-    sample = ("each step: all 10 matrices of the layer set, first %.1f%% of rows (codes %.1f MB), quantise + "
-              "threaded int64 sums%s" % (100 * fraction, nbytes / args.steps / 1e6,
+    sample = ("each step: all 10 matrices of the layer set, first %.1f%% of rows (codes %.1f MB), threaded "
+              "int64 sums from the quantised inputs%s" % (100 * fraction, nbytes / args.steps / 1e6,
                                          " + restore" if fraction >= 1.0 else ""))
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
@@ -272,22 +284,38 @@ def run_b200(args, rank, world, local_rank):
         del dw
     M = 1
     xs_full = make_inputs(M)
-    # Row-parallel calls take this rank's column slice of their input.
-    xs_host = [np.ascontiguousarray(x[:, rowpar[c[0]].col_begin:rowpar[c[0]].col_end]) if c[0] in rowpar else x
-               for x, c in zip(xs_full, CALLS)]
+    # Each call's input as its producer hands it over: int8 rows and per-group scales (the
+    # quantiser runs in the producing kernel; yskn_b200_quantize here, once, untimed).
+    # Row-parallel calls take this rank's column slice (their integer grid is set in the
+    # launch from every rank's group scales).
+    q_host = []
+    for x, c in zip(xs_full, CALLS):
+        kc = x.shape[1]
+        act = torch.empty((M, kc), dtype=torch.int8, device=dev)
+        alpha = torch.empty((M, kc // 512), dtype=torch.float32, device=dev)
+        sgn = torch.from_numpy(np.ascontiguousarray(W[c[0]]["s_in"])).to(dev)
+        Y.quantize(torch.from_numpy(x).to(dev), sgn.data_ptr(), act, alpha,
+                   torch.empty((M, kc // 512), dtype=torch.int32, device=dev),
+                   torch.empty(M, dtype=torch.float32, device=dev))
+        a, al = act.cpu().numpy(), alpha.cpu().numpy()
+        if c[0] in rowpar:
+            c0, c1 = rowpar[c[0]].col_begin, rowpar[c[0]].col_end
+            a, al = a[:, c0:c1], al[:, c0 // 512:c1 // 512]
+        q_host += [np.ascontiguousarray(a).view(np.uint8), np.ascontiguousarray(al).view(np.uint8)]
     # A step's inputs (and its outputs) are views of one buffer, 256-byte aligned, so the
     # end-to-end step moves each direction with a single copy.
-    def packed(shapes, **kw):
+    def packed(shapes, dtype=torch.float32, **kw):
         offs, o = [], 0
         for s in shapes:
             offs.append(o)
-            o += -(-int(np.prod(s)) // 64) * 64
-        buf = torch.empty(o, dtype=torch.float32, **kw)
+            o += -(-int(np.prod(s)) // 256) * 256
+        buf = torch.empty(o, dtype=dtype, **kw)
         return buf, [buf[a:a + int(np.prod(s))].view(*s) for a, s in zip(offs, shapes)]
 
-    x_all, xs = packed([x.shape for x in xs_host], device=dev)
-    for v, x in zip(xs, xs_host):
-        v.copy_(torch.from_numpy(x))
+    x_all, xb = packed([q.shape for q in q_host], dtype=torch.uint8, device=dev)
+    for v, q in zip(xb, q_host):
+        v.copy_(torch.from_numpy(q))
+    xs = [(xb[2 * j].view(torch.int8), xb[2 * j + 1].view(torch.float32)) for j in range(len(CALLS))]
     out_shapes = [(M, mats[n].rows) for c in CALLS for n in c]
     y_all, y_flat = packed(out_shapes, device=dev)
     ys, k = [], 0
@@ -295,15 +323,18 @@ def run_b200(args, rank, world, local_rank):
         ys.append(y_flat[k:k + len(c)])
         k += len(c)
     group = [[mats[n] for n in c] for c in CALLS]
-    works = [torch.empty(Y.linear_work_bytes(g, M), dtype=torch.uint8, device=dev) for g in group]
     stream = torch.cuda.Stream(dev)
 
+    def call(j):  # the operator from int8 input: sums + restore (+ H512) in one launch
+        c, (act, alpha), y = CALLS[j], xs[j], ys[j]
+        if c[0] in rowpar:
+            Y.linear_rowpar_q8(exchange, rowpar[c[0]].mat, act, alpha, y[0], stream=stream)
+        else:
+            Y.linear_q8(group[j], act, alpha, y, stream=stream)
+
     def step():
-        for c, g, x, wk, y in zip(CALLS, group, xs, works, ys):
-            if c[0] in rowpar:
-                rowpar[c[0]](x, y[0], stream=stream)
-            else:
-                Y.linear(g, x, wk, y, stream=stream)
+        for j in range(len(CALLS)):
+            call(j)
 
     with torch.cuda.stream(stream):
         step()
@@ -341,13 +372,10 @@ def run_b200(args, rank, world, local_rank):
         reps = max(20, min(200, args.steps))
         gemv_ms = [0.0] * len(CALLS)
         graphs = []
-        for c, g, x, wk, y in zip(CALLS, group, xs, works, ys):
+        for j in range(len(CALLS)):
             gg = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gg, stream=stream):
-                if c[0] in rowpar:
-                    rowpar[c[0]](x, y[0], stream=stream)
-                else:
-                    Y.linear(g, x, wk, y, stream=stream)
+                call(j)
             graphs.append(gg)
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in CALLS]
         with torch.cuda.stream(stream):
@@ -363,9 +391,9 @@ def run_b200(args, rank, world, local_rank):
         # End to end through the public API, every step: pinned host input in,
         # the six operator calls, host output back; captured as one graph per
         # step the way a decode loop runs it (as the reference engine does).
-        xh_all, xh = packed([x.shape for x in xs_host], pin_memory=True)
-        for v, x in zip(xh, xs_host):
-            v.copy_(torch.from_numpy(x))
+        xh_all, xh = packed([q.shape for q in q_host], dtype=torch.uint8, pin_memory=True)
+        for v, q in zip(xh, q_host):
+            v.copy_(torch.from_numpy(q))
         yh_all, _ = packed(out_shapes, pin_memory=True)
         e2e_graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(e2e_graph, stream=stream):
@@ -403,12 +431,12 @@ def run_b200(args, rank, world, local_rank):
         gemv_local = 0
         for c in CALLS:
             kc = mats[c[0]].cols
-            gemv_local += 4 * M * kc + kc
+            gemv_local += M * kc + 4 * M * (kc // 512)
             for n in c:
                 m = mats[n]
                 out_rows = LAYER_ROWS[n] if n in rowpar else m.rows
                 gemv_local += m.physical_rows * kc * args.bits // 16 + 8192 + 5 * m.physical_rows + 4 * M * out_rows
-    h2d_local = 4 * x_all.numel()  # the copies as issued (inputs + alignment padding)
+    h2d_local = x_all.numel()  # the copies as issued (inputs + alignment padding)
     d2h_local = 4 * y_all.numel()
     tot = torch.tensor([h2d_local, d2h_local], dtype=torch.int64, device=dev)
     if world > 1:
@@ -457,12 +485,14 @@ def run_b200(args, rank, world, local_rank):
         t0 = time.perf_counter()
         n = 0
         nbytes = 0
+        qs = cpu_inputs(W, xs_full)
         while time.perf_counter() - t0 < 10.0 or n < 2:
-            nbytes += cpu_layer_step(W, xs_host, 1.0, threads)
+            nbytes += cpu_layer_step(W, qs, 1.0, threads)
             n += 1
         dt = time.perf_counter() - t0
         cpu = {"value": nbytes / dt / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": "%d full layer-set steps (quantise + threaded int64 sums + restore), %.1f s" % (n, dt)}
+               "sample": "%d full layer-set steps (threaded int64 sums from the quantised inputs + restore), "
+                         "%.1f s" % (n, dt)}
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "strong" if tp_mode else "weak",
@@ -470,8 +500,8 @@ def run_b200(args, rank, world, local_rank):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
                          "traffic": GEMV_TRAFFIC.get((args.bits, M)) if not tp_mode else None,
-                         "kernel": "trellis_sums_kernel (fused operator: quantise + weighted sums + restore; the 6 launches "
-                                   "of each step, timed over the timed region)" + (
+                         "kernel": "trellis_sums_kernel (fused operator from int8 input: weighted sums + restore; the 6 "
+                                   "launches of each step, timed over the timed region)" + (
                                        "; rank 0's shards, row-parallel calls exchanging over NVLink in-kernel"
                                        if tp_mode else "; per rank" if world > 1 else ""),
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
@@ -998,7 +1028,7 @@ def run_reference_stack(args, rank, world):
     import oracle as O
     W = make_weights(args.bits, signs=O.signs)
     prepare_cpu(W, args.bits)
-    xs = make_inputs(1)
+    xs = cpu_inputs(W, make_inputs(1))
     threads = os.cpu_count() or 1
     tb = S.token_bytes(args.layers, S.VOCAB, args.stack_ctx, args.bits)
     for _ in range(max(1, min(args.warmup, 3))):
@@ -1046,7 +1076,7 @@ def run_stack(args, rank, world, local_rank):
     if world == 1 and not args.skip_cpu:
         W = make_weights(args.bits)
         prepare_cpu(W, args.bits)
-        xs = make_inputs(1)
+        xs = cpu_inputs(W, make_inputs(1))
         threads = os.cpu_count() or 1
         t0 = time.perf_counter()
         n, nbytes = 0, 0

@@ -394,6 +394,12 @@ YSKN_B200_API int yskn_b200_linear_rowpar(yskn_b200_tp* tp, const yskn_b200_matr
  * writes the whole next input (d_act_out, d_alpha_out, d_bss_out, d_gate_out as in
  * yskn_b200_linear_residual), bit-identical to one GPU's yskn_b200_linear_residual. The
  * matrix's rows are a multiple of 512 (physical rows = rows). */
+/* The row-parallel operator from this rank's int8 input columns d_act_local [M][cols of the
+ * shard] with group scales d_alpha_local (the local output of yskn_b200_gated_product_q8),
+ * the whole output d_y f32 [M][rows] on every rank, bit-identical to one GPU's
+ * yskn_b200_linear_q8 (no counterpart in the reference, whose engine runs on one GPU). */
+YSKN_B200_API int yskn_b200_linear_rowpar_q8(yskn_b200_tp* tp, const yskn_b200_matrix* mat, const int8_t* d_act_local,
+                                             const float* d_alpha_local, int M, float* d_y, void* stream);
 YSKN_B200_API int yskn_b200_linear_rowpar_residual(yskn_b200_tp* tp, const yskn_b200_matrix* mat,
                                                    const float* d_x_local, const int8_t* d_act_local,
                                                    const float* d_alpha_local, int M, uint16_t* d_hidden,
@@ -433,6 +439,22 @@ YSKN_B200_API int yskn_b200_linear_q8(const yskn_b200_matrix* const* mats, int n
                                       float* const* d_y, void* stream);
 YSKN_B200_API int yskn_b200_gated_product_q8(const float* d_gate, const float* d_up, int M, int n,
                                              const int8_t* d_signs, int8_t* d_act, float* d_alpha, void* stream);
+/* The same chain with the residual step at the start of the NEXT operator instead of the
+ * end of the previous one (replaces the same reference epilogue, src/q35_kernels.cu:1427-1474;
+ * scalar order as above): the operator of up to 3 matrices sharing one input, whose input
+ * is formed in the launch from the previous projection's restored rows d_y_prev f32 [M][cols]:
+ * h = bf16(h_in + bf16(y)) (d_hidden_in bf16 [M][cols]), x = h * (1 + w) (d_norm_weight
+ * bf16 [cols]), quantised with the matrices' input signs, 1/rms = rsqrt(sum of the block
+ * sums of squares / cols + eps) applied in the restore. It stores h to d_hidden_out (another
+ * buffer than d_hidden_in), and if given the bf16 copy of x to d_gate_out and 1/rms to
+ * d_inv_rms_out; d_y[i] f32 [M][rows_i] as yskn_b200_linear. Bit-identical to
+ * yskn_b200_residual_prepare followed by yskn_b200_linear. The previous projection restores
+ * in its own launch (yskn_b200_linear / _q8 / _rowpar), so no launch ends with a serial
+ * residual step. Decode shapes only (M = 1..16). */
+YSKN_B200_API int yskn_b200_linear_from_residual(const yskn_b200_matrix* const* mats, int n_mats, const float* d_y_prev,
+                                                 const uint16_t* d_hidden_in, uint16_t* d_hidden_out,
+                                                 const uint16_t* d_norm_weight, float eps, int M, uint16_t* d_gate_out,
+                                                 float* d_inv_rms_out, float* const* d_y, void* stream);
 
 /* Restore + output rotation (replaces src/a8_prologue.cuh:10-15 xsum_combine and the
  * restore part of src/q35_kernels.cu:1402-1474; compressed_linear.rs:288-370):

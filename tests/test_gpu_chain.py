@@ -183,3 +183,47 @@ def test_fused_chain_equals_the_separate_calls(cuda, M):
         tot = (tot + b3f.cpu().numpy()[:, bidx]).astype(np.float32)
     inv_from_blocks = O.pm("rsqrt", ((tot / np.float32(H)).astype(np.float32) + np.float32(eps)).astype(np.float32))
     assert np.array_equal(inv_from_blocks.view(np.uint32), inv3.cpu().numpy().view(np.uint32)), "block sums"
+
+
+@pytest.mark.parametrize("M", [1, 3])
+def test_residual_prologue_equals_residual_prepare_then_linear(cuda, M):
+    """yskn_b200_linear_from_residual (the residual add, normalisation and quantiser formed in
+    every CTA of the next operator's launch) against residual_prepare followed by the
+    operator, bit for bit: the outputs of two matrices sharing the input, the updated
+    residual stream (in the other buffer, the input buffer untouched), the dense-gate copy
+    and the 1/rms; three calls in a row, so the scratch is reused."""
+    import torch
+    import yskn_b200
+    H, F = 1024, 2048
+    eps = 1e-6
+    rng = np.random.default_rng(21 + M)
+    gate, _, _k1 = _matrix(F, H, 61, 0)
+    up, _, _k2 = _matrix(F, H, 62, 0)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    f32 = lambda *s: torch.empty(s, dtype=torch.float32, device="cuda")  # noqa: E731
+    i16 = lambda *s: torch.empty(s, dtype=torch.int16, device="cuda")  # noqa: E731
+    wk = torch.empty(yskn_b200.linear_work_bytes([gate, up], M), dtype=torch.uint8, device="cuda")
+    for call in range(3):
+        hidden0 = O.bf16_bits(rng.standard_normal((M, H)).astype(np.float32) * np.float32(0.5))
+        y = (rng.standard_normal((M, H)) * 0.3).astype(np.float32)
+        w = O.bf16_bits((rng.standard_normal(H) * 0.1).astype(np.float32))
+        # separate calls
+        h = dev(hidden0.view(np.int16))
+        x, inv, xg = f32(M, H), f32(M), i16(M, H)
+        yskn_b200.residual_prepare(h, dev(y), dev(w.view(np.int16)), eps, x, inv, gate=xg)
+        g, u = f32(M, F), f32(M, F)
+        yskn_b200.linear([gate, up], x, wk, [g, u], inv_rms=inv)
+        # the residual prologue
+        h_in = dev(hidden0.view(np.int16))
+        h_out, xg2, inv2 = i16(M, H), i16(M, H), f32(M)
+        g2, u2 = f32(M, F), f32(M, F)
+        yskn_b200.linear_from_residual([gate, up], dev(y), h_in, h_out, dev(w.view(np.int16)), eps, [g2, u2],
+                                       gate_out=xg2, inv_rms_out=inv2)
+        torch.cuda.synchronize()
+        assert yskn_b200.status() == 0
+        assert torch.equal(h_out, h), call
+        assert np.array_equal(h_in.cpu().numpy().view(np.uint16), hidden0), call
+        assert torch.equal(xg2, xg), call
+        assert torch.equal(inv2.view(torch.int32), inv.view(torch.int32)), call
+        assert torch.equal(g2.view(torch.int32), g.view(torch.int32)), call
+        assert torch.equal(u2.view(torch.int32), u.view(torch.int32)), call

@@ -524,6 +524,18 @@ YSKN_B200_API int yskn_b200_linear_rowpar(yskn_b200_tp* t, const yskn_b200_matri
   return launch_linear_rowpar(mat->dev, t->view, d_x_local, M, d_inv_rms, d_y, *sc, as_stream(stream));
 }
 
+YSKN_B200_API int yskn_b200_linear_rowpar_q8(yskn_b200_tp* t, const yskn_b200_matrix* mat, const int8_t* d_act_local,
+                                             const float* d_alpha_local, int M, float* d_y, void* stream) {
+  if (!t || !t->connected || !mat || !d_act_local || !d_alpha_local || !d_y || !aligned16(d_act_local))
+    return fail(YSKN_EINVAL, "linear_rowpar_q8: bad arguments (connected exchange, matrix, aligned input, output)");
+  const GemvScratch* sc = current_scratch();
+  if (!sc) return fail(YSKN_EINVAL, "linear_rowpar_q8: no matrix was created on this device");
+  FusedIO io;
+  io.q_act = d_act_local;
+  io.q_alpha = d_alpha_local;
+  return launch_linear_rowpar(mat->dev, t->view, nullptr, M, nullptr, d_y, *sc, as_stream(stream), io);
+}
+
 YSKN_B200_API int yskn_b200_linear_rowpar_residual(yskn_b200_tp* t, const yskn_b200_matrix* mat,
                                                    const float* d_x_local, const int8_t* d_act_local,
                                                    const float* d_alpha_local, int M, uint16_t* d_hidden,
@@ -782,6 +794,38 @@ YSKN_B200_API int yskn_b200_linear_residual(const yskn_b200_matrix* mat, const f
   float* no_y[1] = {nullptr};
   if (int rc = launch_linear_fused(&d, 1, d_x, M, nullptr, no_y, *sc, as_stream(stream), io)) return rc;
   return finish_checked(d.cols, stream);
+}
+
+YSKN_B200_API int yskn_b200_linear_from_residual(const yskn_b200_matrix* const* mats, int n_mats, const float* d_y_prev,
+                                                 const uint16_t* d_hidden_in, uint16_t* d_hidden_out,
+                                                 const uint16_t* d_norm_weight, float eps, int M, uint16_t* d_gate_out,
+                                                 float* d_inv_rms_out, float* const* d_y, void* stream) {
+  if (int rc = check_group(mats, n_mats)) return rc;
+  const int Kc = mats[0]->dev.cols;
+  if (M < 1 || !d_y_prev || !d_hidden_in || !d_hidden_out || !d_norm_weight || !d_y || !(eps > 0.0f) ||
+      d_hidden_in == d_hidden_out || !aligned16(d_y_prev) || (reinterpret_cast<uintptr_t>(d_hidden_in) & 3) ||
+      (reinterpret_cast<uintptr_t>(d_hidden_out) & 3) || (reinterpret_cast<uintptr_t>(d_norm_weight) & 3) ||
+      (d_gate_out && (reinterpret_cast<uintptr_t>(d_gate_out) & 3)))
+    return fail(YSKN_EINVAL, "linear_from_residual: bad arguments (aligned buffers, two residual buffers, eps > 0)");
+  if (!fused_linear_fits(M, Kc))
+    return fail(YSKN_EINVAL, "linear_from_residual: M must be 1..16 with the input in shared memory");
+  MatrixDev devs[3];
+  for (int i = 0; i < n_mats; ++i) {
+    if (!d_y[i]) return fail(YSKN_EINVAL, "linear_from_residual: null output");
+    devs[i] = mats[i]->dev;
+  }
+  const GemvScratch* sc = current_scratch();
+  if (!sc) return fail(YSKN_EINVAL, "linear_from_residual: no matrix was created on this device");
+  FusedIO io;
+  io.rin_y = d_y_prev;
+  io.rin_h_in = d_hidden_in;
+  io.rin_h_out = d_hidden_out;
+  io.rin_norm_w = d_norm_weight;
+  io.rin_gate_out = d_gate_out;
+  io.rin_inv_out = d_inv_rms_out;
+  io.rin_eps = eps;
+  if (int rc = launch_linear_fused(devs, n_mats, nullptr, M, nullptr, d_y, *sc, as_stream(stream), io)) return rc;
+  return finish_checked(Kc, stream);
 }
 
 static int kv_check(int M, int n_qh, int n_kvh, int length, int capacity, int kb, int n_splits) {

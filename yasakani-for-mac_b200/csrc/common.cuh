@@ -186,6 +186,13 @@ struct FusedIO {
   float* res_alpha = nullptr;
   float* res_bss = nullptr;
   uint16_t* res_gate = nullptr;
+  const float* rin_y = nullptr;  // residual prologue (GemvParams::rin)
+  const uint16_t* rin_h_in = nullptr;
+  uint16_t* rin_h_out = nullptr;
+  const uint16_t* rin_norm_w = nullptr;
+  uint16_t* rin_gate_out = nullptr;
+  float* rin_inv_out = nullptr;
+  float rin_eps = 0.0f;
 };
 int launch_linear_fused(const MatrixDev* mats, int n_mats, const float* x, int M, const float* inv_rms,
                         float* const* y, const GemvScratch& scratch, cudaStream_t st, const FusedIO& io = FusedIO());

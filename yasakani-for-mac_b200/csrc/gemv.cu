@@ -106,6 +106,12 @@ struct GemvParams {
   // restored rows go into the residual stream and become the next operator's quantised
   // input (residual_block512), token m's arrays at m * rows (alpha, bss at m * rows / 512).
   ResidualOut res;
+  // Residual prologue (rin.y != nullptr): the input is formed in every CTA from the previous
+  // projection's restored rows (residual_block512 per 512-group: the residual stream plus y,
+  // times 1 + norm weight, quantised with the matrix's input signs); each row's 1/rms from
+  // its block sums of squares. CTA 0 stores the updated stream to h_out (a buffer other than
+  // h_in, which every CTA reads), the gate copy and 1/rms.
+  ResidualIn rin;
   // Row-parallel tensor-parallel operator (tp.world > 1): exchange areas of all ranks.
   TpView tp;
 };
@@ -141,6 +147,13 @@ __device__ __forceinline__ void load_unit(Unit<BITS>& u, const uint32_t* tile0, 
       }
     }
   }
+}
+
+// One unit's codes (2 tiles, 256 * BITS bytes) requested into L2, a 128-byte line per lane.
+template <int BITS>
+__device__ __forceinline__ void l2_prefetch_unit(const uint32_t* unit, int lane) {
+  constexpr int LINES = 2 * BITS * 32 * 4 / 128;
+  if (lane < LINES) asm volatile("prefetch.global.L2 [%0];" ::"l"(unit + lane * 32));
 }
 
 template <int BITS>
@@ -317,6 +330,35 @@ struct Ranges {
   }
 };
 
+// Residual prologue of the fused operator (GemvParams::rin): warp w forms input groups
+// w, w + 16, ... from the previous projection's rows (every load of a group issued before
+// its arithmetic) into the CTA's int8 rows, group scales and block sums. Kept out of line:
+// its registers stay out of the streaming loop's allocation.
+__device__ __noinline__ void residual_prologue(const ResidualIn rin, const int8_t* s_in, int Kc, int items,
+                                               int8_t* s_act, int act_ld, float* s_alpha, float* s_bss,
+                                               unsigned* err, int warp, int lane) {
+  const int G = Kc / 512;
+  bool bad = false;
+  const bool writer = blockIdx.x == 0;
+  for (int k = warp; k < items; k += GEMV_WARPS) {
+    const int m = k / G, r0 = (k - m * G) * 512;
+    float v[16];
+    uint32_t hws[8], wws[8], sws[8];
+    const float* yr = rin.y + (size_t)m * Kc + r0;
+#pragma unroll
+    for (int k2 = 0; k2 < 8; ++k2) {
+      const float2 t = __ldcg(reinterpret_cast<const float2*>(yr + 64 * k2 + 2 * lane));
+      v[2 * k2] = t.x;
+      v[2 * k2 + 1] = t.y;
+    }
+    load_residual_words512(rin.h_in + (size_t)m * Kc, rin.norm_w, s_in, r0, lane, hws, wws, sws);
+    residual_block512(v, hws, wws, sws, writer ? rin.h_out + (size_t)m * Kc + r0 : nullptr,
+                      writer && rin.gate_out ? rin.gate_out + (size_t)m * Kc + r0 : nullptr,
+                      s_act + (size_t)m * act_ld + r0, s_alpha + k, s_bss + k, lane, bad);
+  }
+  if (writer && __any_sync(0xffffffffu, bad) && lane == 0) raise_device_error(err, DERR_NONFINITE);
+}
+
 // ACT_SMEM: activations and scales staged once per CTA in shared memory after
 // the table (rows padded by 16 bytes so the 8 token rows fall in different banks).
 // FUSED (implies ACT_SMEM): the whole operator. Every CTA quantises the f32 input
@@ -339,6 +381,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
   int32_t* s_scale = reinterpret_cast<int32_t*>(s_lut + LUT_COPY_BYTES + LUT_BAR_BYTES + (size_t)p.mv * act_ld);
   float* s_alpha = reinterpret_cast<float*>(s_scale + p.mv * G);  // FUSED: group scales
   float* s_rq = s_alpha + p.mv * G;                                // FUSED: row quanta
+  float* s_bss = s_rq + TP_MAX_M;                                  // FUSED, residual prologue: block sums
 
   // Programmatic dependent launch: the next kernel on the stream may be scheduled as
   // SMs free up; it waits (griddepcontrol.wait) before it reads anything this grid writes.
@@ -371,6 +414,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
   const uint32_t* ptr = S.codes + (size_t)u * 2 * TILE_WORDS;
   Unit<BITS> ua, ub;
   if (u < u_end) load_unit<BITS>(ua, ptr, lane);
+  if (u + 1 < u_end) l2_prefetch_unit<BITS>(ptr + 2 * TILE_WORDS, lane);
 
   // 16 copies of the int8-pair table: slot s (32 bytes) holds entry s 16 times. The
   // matrix keeps this image prebuilt (MatrixDev::lutx); one thread starts bulk
@@ -424,7 +468,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
   // do not all read the same input lines at the same moment.
   const int item_rot = FUSED ? (int)(blockIdx.x % (unsigned)items) : 0;
   auto item_of = [&](int k) { return k + item_rot < items ? k + item_rot : k + item_rot - items; };
-  if (FUSED && !p.q_act && warp < items) {
+  if (FUSED && !p.q_act && !p.rin.y && warp < items) {
     const int it = item_of(warp);
     load_group512(p.x + (size_t)(it / G) * Kc + (it % G) * 512, p.s_in + (it % G) * 512, lane, nxt);
   }
@@ -447,14 +491,12 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
           if (idx < total) reinterpret_cast<uint4*>(s_act + (idx / vec) * act_ld)[idx % vec] = v[k];
         }
       }
-      for (int idx = threadIdx.x; idx < p.mv * G; idx += blockDim.x) s_alpha[idx] = __ldcg(p.q_alpha + idx);
-      if (p.q_bss && threadIdx.x < p.mv) {
-        float total_sq = 0.0f;
-        for (int g = 0; g < G; ++g) total_sq = __fadd_rn(total_sq, __ldcg(p.q_bss + threadIdx.x * G + g));
-        const float inv = pm_rsqrt(__fadd_rn(__fdiv_rn(total_sq, (float)Kc), p.q_eps));
-        s_inv[threadIdx.x] = inv;
-        if (p.inv_out && blockIdx.x == 0) p.inv_out[threadIdx.x] = inv;
+      for (int idx = threadIdx.x; idx < p.mv * G; idx += blockDim.x) {
+        s_alpha[idx] = __ldcg(p.q_alpha + idx);
+        if (p.q_bss) s_bss[idx] = __ldcg(p.q_bss + idx);  // summed per row after the barrier
       }
+    } else if (FUSED && p.rin.y) {
+      residual_prologue(p.rin, p.s_in, Kc, items, s_act, act_ld, s_alpha, s_bss, p.err, warp, lane);
     } else if (FUSED) {
       // A warp's groups in turn, each one's inputs requested before the previous is quantised.
       bool bad = false;
@@ -510,6 +552,14 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
       float mx = 0.0f;
       for (int g = 0; g < G; ++g) mx = fmaxf(mx, s_alpha[threadIdx.x * G + g]);
       s_rowmax[threadIdx.x] = mx;
+      if (p.rin.y || (p.q_act && p.q_bss)) {  // the row's 1/rms from its block sums, added in order from +0
+        float total_sq = 0.0f;
+        for (int g = 0; g < G; ++g) total_sq = __fadd_rn(total_sq, s_bss[threadIdx.x * G + g]);
+        const float inv = pm_rsqrt(__fadd_rn(__fdiv_rn(total_sq, (float)Kc), p.rin.y ? p.rin.eps : p.q_eps));
+        s_inv[threadIdx.x] = inv;
+        float* inv_out = p.rin.y ? p.rin.inv_out : p.inv_out;
+        if (inv_out && blockIdx.x == 0) inv_out[threadIdx.x] = inv;
+      }
     }
     if (tp) {
       // The grid of a row is set by its largest group scale over all ranks' groups:
@@ -584,7 +634,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
   unsigned done_mask = 0;
 
   // The rows' 1/rms for the restore: formed here from a quantised input's block sums, or given.
-  const float* inv_base = (FUSED && p.q_act && p.q_bss) ? s_inv : p.inv_rms;
+  const float* inv_base = (FUSED && ((p.q_act && p.q_bss) || p.rin.y)) ? s_inv : p.inv_rms;
   // Final sums of rows row0, row0 + 1 for tokens n, n + 8 (the C fragment): stored
   // as int64, or (fused operator, rows without an output rotation) restored to f32.
   auto emit = [&](const long long (&v)[4], int row0) {
@@ -698,6 +748,9 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
     }
     ptr += 2 * TILE_WORDS;
     if (has_next) load_unit<BITS>(nxt, ptr, lane);
+    // The unit after the next one into L2 now, so its load next step waits on L2, not HBM
+    // (one unit in registers per warp is too few bytes in flight to cover HBM latency).
+    if (u + 2 < u_end) l2_prefetch_unit<BITS>(ptr + 2 * TILE_WORDS, lane);
     int c[4] = {0, 0, 0, 0};
     const int col = g * 512 + q * 64;
     const uint4* a0p = reinterpret_cast<const uint4*>(act0 + col);
@@ -792,6 +845,36 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
     g = gn;
     return !has_next;
   };
+  // Row-parallel: the peers' sums of block blk added to this rank's, then the restore.
+  auto recv_restore = [&](int blk, long long deadline, bool& ok) {
+    const unsigned epoch = s_epoch, par = epoch & 1u;
+    const int W = p.tp.world, me = p.tp.rank;
+    const size_t slot = (size_t)p.tp.max_blocks * 512 * 2;
+    const uint64_t* recv = tp_at<uint64_t>(p.tp, me, p.tp.off_recv);
+    for (int tok = 0; tok < p.mv; ++tok) {
+      int64_t* mine = S.out + (size_t)tok * S.out_ld + blk * 512;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int r = 64 * k + 2 * lane;
+        longlong2 s = __ldcg(reinterpret_cast<const longlong2*>(mine + r));
+        for (int src = 0; src < W; ++src) {
+          if (src == me) continue;
+          const uint64_t* w = recv + (((size_t)par * W + src) * TP_MAX_M + tok) * slot + (size_t)blk * 1024 + 2 * r;
+          s.x += recv_sum(w, epoch, deadline, &s_abort, ok);
+          s.y += recv_sum(w + 2, epoch, deadline, &s_abort, ok);
+        }
+        __stcg(reinterpret_cast<longlong2*>(mine + r), s);
+      }
+    }
+    if (__any_sync(0xffffffffu, !ok)) {
+      ok = false;
+      if (lane == 0) {
+        s_abort = 1;
+        raise_device_error(p.err, DERR_TIMEOUT);
+      }
+    }
+    restore_block(blk);
+  };
   for (;;) {
     if (step(ua, ub)) break;
     if (step(ub, ua)) break;
@@ -799,41 +882,15 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
   if (tp) {
     // Every peer's sums of the blocks this warp completed: wait for them (their warps
     // send as soon as each block completes there, without waiting on anything), add
-    // them to this rank's, restore the whole block.
-    const unsigned epoch = s_epoch, par = epoch & 1u;
-    const int W = p.tp.world, me = p.tp.rank;
-    const size_t slot = (size_t)p.tp.max_blocks * 512 * 2;
-    const uint64_t* recv = tp_at<uint64_t>(p.tp, me, p.tp.off_recv);
-    // One deadline for all of this warp's blocks; after a timeout (here or in another
-    // warp of the CTA) the remaining words are not polled.
+    // them to this rank's, restore the whole block. One deadline for all of this warp's
+    // blocks; after a timeout (here or in another warp of the CTA) the remaining words
+    // are not polled.
     const long long deadline = clock64() + p.tp.wait_cycles;
     bool ok = true;
     while (done_mask) {
       const int blk = blk_lo + __ffs(done_mask) - 1;
       done_mask &= done_mask - 1;
-      for (int tok = 0; tok < p.mv; ++tok) {
-        int64_t* mine = S.out + (size_t)tok * S.out_ld + blk * 512;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int r = 64 * k + 2 * lane;
-          longlong2 s = __ldcg(reinterpret_cast<const longlong2*>(mine + r));
-          for (int src = 0; src < W; ++src) {
-            if (src == me) continue;
-            const uint64_t* w = recv + (((size_t)par * W + src) * TP_MAX_M + tok) * slot + (size_t)blk * 1024 + 2 * r;
-            s.x += recv_sum(w, epoch, deadline, &s_abort, ok);
-            s.y += recv_sum(w + 2, epoch, deadline, &s_abort, ok);
-          }
-          __stcg(reinterpret_cast<longlong2*>(mine + r), s);
-        }
-      }
-      if (__any_sync(0xffffffffu, !ok)) {
-        ok = false;
-        if (lane == 0) {
-          s_abort = 1;
-          raise_device_error(p.err, DERR_TIMEOUT);
-        }
-      }
-      restore_block(blk);
+      recv_restore(blk, deadline, ok);
     }
   }
   if constexpr (FUSED) {
@@ -868,7 +925,8 @@ constexpr int SMEM_LIMIT = 232448 - 1024;
 
 static size_t act_smem_bytes(int mv, int Kc, bool fused) {
   const size_t G = Kc / 512;
-  return (size_t)mv * (Kc + 16) + 4 * (size_t)mv * G + (fused ? 4 * (size_t)mv * G + 64 : 0);
+  // int8 rows | integer scales | fused: group scales, row quanta (TP_MAX_M), block sums
+  return (size_t)mv * (Kc + 16) + 4 * (size_t)mv * G + (fused ? 8 * (size_t)mv * G + 4 * TP_MAX_M : 0);
 }
 static size_t table_smem_bytes() { return LUT_COPY_BYTES + LUT_BAR_BYTES; }
 
@@ -1043,6 +1101,7 @@ int launch_linear_fused(const MatrixDev* mats, int n_mats, const float* x, int M
   p.inv_out = io.inv_out;
   p.res = ResidualOut{io.res_hidden, io.res_norm_w, io.res_next_signs, io.res_act, io.res_alpha, io.res_bss,
                       io.res_gate};
+  p.rin = ResidualIn{io.rin_y, io.rin_h_in, io.rin_h_out, io.rin_norm_w, io.rin_gate_out, io.rin_inv_out, io.rin_eps};
   int64_t sums_used = 0;  // rotated rows add into the zero-kept scratch sums
   for (int i = 0; i < n_mats; ++i) {
     GemvSeg& s = p.seg[i];

@@ -267,38 +267,35 @@ struct ResidualOut {
   uint16_t* gate;          // bf16 [rows] of this token, or nullptr
 };
 
+// The residual prologue's inputs (see GemvParams::rin).
+struct ResidualIn {
+  const float* y;           // f32 [M][cols]: the previous projection's restored rows
+  const uint16_t* h_in;     // bf16 [M][cols]: the residual stream before it
+  uint16_t* h_out;          // bf16 [M][cols]: after it (CTA 0)
+  const uint16_t* norm_w;   // bf16 [cols]
+  uint16_t* gate_out;       // bf16 [M][cols] copy of h * (1 + w), or nullptr (CTA 0)
+  float* inv_out;           // f32 [M] 1/rms, or nullptr (CTA 0)
+  float eps;
+};
+
 __device__ __forceinline__ float bf16_round(float x) {
   return __uint_as_float((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(x)) << 16);
 }
 
-// Restores token block r0 of the int64 sums wsr (restore_values512) and applies the
-// residual epilogue to it. Every load the block needs is issued first, together: the sums,
-// the row scales and output signs, and the residual-stream, norm-weight and next-sign words
-// (the stores below go through some of the same pointers, so the compiler could not move
-// the later loads ahead of them). The caller clears the sums afterwards.
-__device__ __forceinline__ void residual_restore512(const int64_t* wsr, const float* __restrict__ tau,
-                                                        const int8_t* __restrict__ s_out, float rq,
-                                                        const float* inv_rms_m, const ResidualOut o, int r0, int lane,
-                                                        bool& bad) {
-  longlong2 ws[8];
-  Rows512 rr;
-  load_sums512(wsr, r0, lane, ws);
-  load_rows512(tau, s_out, r0, lane, rr);
-  uint32_t hws[8], wws[8], sws[8];
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const int r = r0 + 64 * k + 2 * lane;
-    hws[k] = __ldcg(reinterpret_cast<const unsigned int*>(o.hidden + r));
-    wws[k] = __ldg(reinterpret_cast<const unsigned int*>(o.norm_w + r));
-    sws[k] = (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(o.s_next + r));
-  }
-  float v[16];  // the block's outputs y; then the updated residual stream h
-  restore_values512(ws, rr, rq, inv_rms_m, lane, bad, v);
+// The residual epilogue of one token's 512-row block from its projection values v (the
+// restore's lane mapping) and the block's residual-stream, norm-weight and next-sign words
+// (hws, wws, sws: rows r + 2l, r + 2l + 1 at k = 0..7, r = 64k), in the scalar order above.
+// Writes the updated residual words to hidden_out and the gate copy to gate_out (each if
+// non-null; rows 64k + 2l + b from each pointer), the block's int8 input to act (same
+// rows), and lane 0 writes the block's group scale to *alpha and its sum of squares to *bss.
+__device__ __forceinline__ void residual_block512(float (&v)[16], const uint32_t (&hws)[8], const uint32_t (&wws)[8],
+                                                  const uint32_t (&sws)[8], uint16_t* hidden_out, uint16_t* gate_out,
+                                                  int8_t* act, float* alpha, float* bss, int lane, bool& bad) {
   float x[16];  // the next operator's unnormalised input h * (1 + w)
   // residual and the next normalisation's input
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    const int r = r0 + 64 * k + 2 * lane;
+    const int r = 64 * k + 2 * lane;
     const uint32_t hw = hws[k], ww = wws[k];
     uint32_t hn = 0, gw = 0;
 #pragma unroll
@@ -313,8 +310,8 @@ __device__ __forceinline__ void residual_restore512(const int64_t* wsr, const fl
       gw |= (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(xv)) << (16 * b);
       bad |= !finite32(nh) | !finite32(xv);
     }
-    *reinterpret_cast<uint32_t*>(o.hidden + r) = hn;
-    if (o.gate) *reinterpret_cast<uint32_t*>(o.gate + r) = gw;
+    if (hidden_out) *reinterpret_cast<uint32_t*>(hidden_out + r) = hn;
+    if (gate_out) *reinterpret_cast<uint32_t*>(gate_out + r) = gw;
   }
   // block sum of squares of h: lane l holds partials 2l + b (k even) and 64 + 2l + b (k odd)
   float pt[2][2];
@@ -394,12 +391,47 @@ __device__ __forceinline__ void residual_restore512(const int64_t* wsr, const fl
       q = max(-127, min(127, q));
       w2 |= (uint32_t)(q & 0xff) << (8 * b);
     }
-    *reinterpret_cast<uint16_t*>(o.act + r0 + 64 * k + 2 * lane) = (uint16_t)w2;
+    *reinterpret_cast<uint16_t*>(act + 64 * k + 2 * lane) = (uint16_t)w2;
   }
   if (lane == 0) {
-    o.alpha[r0 / 512] = scale;
-    o.bss[r0 / 512] = block;
+    *alpha = scale;
+    *bss = block;
   }
+}
+
+// The block's residual-stream, norm-weight and next-sign words (residual_block512's
+// inputs) for rows r0 + 64k + 2l + b.
+__device__ __forceinline__ void load_residual_words512(const uint16_t* hidden, const uint16_t* __restrict__ norm_w,
+                                                       const int8_t* __restrict__ s_next, int r0, int lane,
+                                                       uint32_t (&hws)[8], uint32_t (&wws)[8], uint32_t (&sws)[8]) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int r = r0 + 64 * k + 2 * lane;
+    hws[k] = __ldcg(reinterpret_cast<const unsigned int*>(hidden + r));
+    wws[k] = __ldg(reinterpret_cast<const unsigned int*>(norm_w + r));
+    sws[k] = (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(s_next + r));
+  }
+}
+
+// Restores token block r0 of the int64 sums wsr (restore_values512) and applies the
+// residual epilogue to it. Every load the block needs is issued first, together: the sums,
+// the row scales and output signs, and the residual-stream, norm-weight and next-sign words
+// (the stores below go through some of the same pointers, so the compiler could not move
+// the later loads ahead of them). The caller clears the sums afterwards.
+__device__ __forceinline__ void residual_restore512(const int64_t* wsr, const float* __restrict__ tau,
+                                                        const int8_t* __restrict__ s_out, float rq,
+                                                        const float* inv_rms_m, const ResidualOut o, int r0, int lane,
+                                                        bool& bad) {
+  longlong2 ws[8];
+  Rows512 rr;
+  load_sums512(wsr, r0, lane, ws);
+  load_rows512(tau, s_out, r0, lane, rr);
+  uint32_t hws[8], wws[8], sws[8];
+  load_residual_words512(o.hidden, o.norm_w, o.s_next, r0, lane, hws, wws, sws);
+  float v[16];  // the block's outputs y; then the updated residual stream h
+  restore_values512(ws, rr, rq, inv_rms_m, lane, bad, v);
+  residual_block512(v, hws, wws, sws, o.hidden + r0, o.gate ? o.gate + r0 : nullptr, o.act + r0, o.alpha + r0 / 512,
+                    o.bss + r0 / 512, lane, bad);
 }
 
 __device__ __forceinline__ void restore_block512(const int64_t* wsr, float rq, const float* inv_rms_m,

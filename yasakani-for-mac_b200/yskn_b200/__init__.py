@@ -87,6 +87,8 @@ _SIGNATURES = {
     "yskn_b200_gdn_step_heads": (_i, [_vp] * 7 + [C.c_float, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "yskn_b200_linear_rowpar_residual": (_i, [_vp] * 5 + [_i] + [_vp] * 8),
     "yskn_b200_head_merge": (_i, [_vp, _vp, _i64, _vp, _i, _i, _vp, _vp, _vp, _vp]),
+    "yskn_b200_linear_from_residual": (_i, [_vp, _i, _vp, _vp, _vp, _vp, C.c_float, _i, _vp, _vp, _vp, _vp]),
+    "yskn_b200_linear_rowpar_q8": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp]),
 }
 
 _lib = None
@@ -517,6 +519,13 @@ def linear_rowpar(exchange, mat, x_local, y, inv_rms=None, stream=None):
                                         _ptr(y), _stream(stream)), "linear_rowpar")
 
 
+def linear_rowpar_q8(exchange, mat, act_local, alpha_local, y, stream=None):
+    """yskn_b200_linear_rowpar_q8: the whole output of a row-parallel shard from this rank's
+    int8 input columns, on every rank."""
+    check(lib().yskn_b200_linear_rowpar_q8(exchange.handle, mat.handle, _ptr(act_local), _ptr(alpha_local),
+                                           act_local.shape[0], _ptr(y), _stream(stream)), "linear_rowpar_q8")
+
+
 def linear_rowpar_residual(exchange, mat, hidden, norm_weight, next_signs, act_out, alpha_out, bss_out, x=None,
                            act=None, alpha=None, gate_out=None, stream=None):
     """yskn_b200_linear_rowpar_residual: the row-parallel operator from this rank's input
@@ -558,6 +567,18 @@ def linear_q8(mats, act, alpha, ys, bss=None, eps=0.0, inv_rms_out=None, stream=
     yp = (C.c_void_p * len(ys))(*[y.data_ptr() for y in ys])
     check(lib().yskn_b200_linear_q8(_handles(mats), len(mats), _ptr(act), _ptr(alpha), _ptr(bss), float(eps),
                                     act.shape[0], _ptr(inv_rms_out), yp, _stream(stream)), "linear_q8")
+
+
+def linear_from_residual(mats, y_prev, hidden_in, hidden_out, norm_weight, eps, ys, gate_out=None, inv_rms_out=None,
+                         stream=None):
+    """yskn_b200_linear_from_residual: the operator whose input is the residual stream
+    hidden_in plus the previous projection's rows y_prev, normalised (norm_weight, eps) and
+    quantised in the launch; the updated stream goes to hidden_out."""
+    yp = (C.c_void_p * len(ys))(*[y.data_ptr() for y in ys])
+    check(lib().yskn_b200_linear_from_residual(_handles(mats), len(mats), _ptr(y_prev), _ptr(hidden_in),
+                                               _ptr(hidden_out), _ptr(norm_weight), float(eps), y_prev.shape[0],
+                                               _ptr(gate_out), _ptr(inv_rms_out), yp, _stream(stream)),
+          "linear_from_residual")
 
 
 def gated_product_q8(gate, up, signs, act, alpha, stream=None):

@@ -119,6 +119,7 @@ class Stack:
         i16 = lambda *s: torch.zeros(s, dtype=torch.int16, device=device)  # noqa: E731
         self.token = torch.zeros(1, dtype=torch.int32, device=device)
         self.h, self.xg = i16(1, HIDDEN), i16(1, HIDDEN)
+        self.h_alt = i16(1, HIDDEN)  # the residual stream's second buffer (linear_from_residual)
         self.x, self.inv, self.proj = f32(1, HIDDEN), f32(1), f32(1, HIDDEN)
         self.qkv_o, self.z_o, self.gates, self.g_out = f32(1, QKV), f32(1, ZDIM), f32(1, 96), f32(1, ZDIM)
         self.q_o, self.k_o, self.v_o = f32(1, N_QH, 2 * HEAD), f32(1, N_KVH, HEAD), f32(1, N_KVH, HEAD)
@@ -173,20 +174,26 @@ class Stack:
 
     def decode(self, stream=None, fused=True):
         """One token: reads self.token, writes the next greedy token into it. fused: the
-        chain between projections inside the operators (residual, normalisation and the next
-        quantiser in the restore of o/out/down; the MLP product quantised for down), else the
-        separate residual_prepare / gated_product calls; both give the same bits."""
+        chain between projections inside the operators (each operator that follows a
+        residual add forms its input in its own launch: residual, normalisation and quantiser,
+        yskn_b200_linear_from_residual; the MLP product quantised for down), else the
+        separate residual_prepare / gated_product calls; both give the same bits. The
+        residual stream alternates between two buffers and ends each token in self.h."""
         if not fused:
             return self._decode_separate(stream)
         s = stream
+        hs = [self.h, self.h_alt]
+        cur = 0
+
+        def from_residual(mats, norm, outs, gate=None, inv=None):
+            nonlocal cur
+            Y.linear_from_residual(mats, self.proj, hs[cur], hs[1 - cur], norm, EPS, outs, gate_out=gate,
+                                   inv_rms_out=inv, stream=s)
+            cur = 1 - cur
+
         self.embedding.lookup(self.token, self.h, stream=s)
         Y.residual_prepare(self.h, None, self.L[0]["in_norm"], EPS, self.x, self.inv, gate=self.xg, stream=s)
         for i, L in enumerate(self.L):
-            if i + 1 < len(self.L):
-                nL = self.L[i + 1]
-                next_norm, next_first = nL["in_norm"], nL["qkv"] if nL["kind"] == "gdn" else nL["q"]
-            else:
-                next_norm, next_first = self.final_norm, self.head
             if L["kind"] == "gdn":
                 mats, outs = [L["qkv"], L["z"]], [self.qkv_o, self.z_o]
             else:
@@ -194,23 +201,35 @@ class Stack:
             if i == 0:
                 Y.linear(mats, self.x, self.work, outs, inv_rms=self.inv, stream=s)
             else:
-                Y.linear_q8(mats, self.act, self.alpha, outs, bss=self.bss, eps=EPS, inv_rms_out=self.inv, stream=s)
+                from_residual(mats, L["in_norm"], outs, gate=self.xg, inv=self.inv)
             if L["kind"] == "gdn":
-                Y.gdn_gates(self.xg, self.inv, L["wb"], L["wa"], self.gates, stream=s)
-                Y.gdn_step(self.qkv_o, self.z_o, self.gates, L["conv"], L["a_log"], L["dt_bias"], L["norm_w"], EPS,
-                           L["state"], L["history"], self.g_out, stream=s)
-                mixer_out, mixer_in = L["out"], self.g_out
+                self._gdn(L, s)
+                self._project(L["out"], self.g_out, s)
             else:
                 self._attention(L, s)
-                mixer_out, mixer_in = L["o"], self.a_in
-            Y.linear_residual(mixer_out, self.h, L["post_norm"], L["gate"].signs_in_ptr, self.act, self.alpha,
-                              self.bss, x=mixer_in, stream=s)
-            Y.linear_q8([L["gate"], L["up"]], self.act, self.alpha, [self.g_o, self.u_o], bss=self.bss, eps=EPS,
-                        stream=s)
+                self._project(L["o"], self.a_in, s)
+            from_residual([L["gate"], L["up"]], L["post_norm"], [self.g_o, self.u_o])
             Y.gated_product_q8(self.g_o, self.u_o, L["down"].signs_in_ptr, self.act_m, self.alpha_m, stream=s)
-            Y.linear_residual(L["down"], self.h, next_norm, next_first.signs_in_ptr, self.act, self.alpha, self.bss,
-                              act=self.act_m, alpha=self.alpha_m, gate_out=self.xg, stream=s)
-        Y.linear_q8([self.head], self.act, self.alpha, [self.logits], bss=self.bss, eps=EPS, stream=s)
+            self._project_q8(L["down"], s)
+        from_residual([self.head], self.final_norm, [self.logits])
+        assert cur == 0  # an even number of residual adds per token: the stream ends in self.h
+        self._select(s)
+
+    def _gdn(self, L, s):
+        """The Gated DeltaNet mixer between in_proj and out_proj: gates, then the step."""
+        Y.gdn_gates(self.xg, self.inv, L["wb"], L["wa"], self.gates, stream=s)
+        Y.gdn_step(self.qkv_o, self.z_o, self.gates, L["conv"], L["a_log"], L["dt_bias"], L["norm_w"], EPS,
+                   L["state"], L["history"], self.g_out, stream=s)
+
+    def _project(self, mat, x, s):
+        """A mixer's output projection into self.proj (f32 input)."""
+        Y.linear([mat], x, self.work, [self.proj], stream=s)
+
+    def _project_q8(self, mat, s):
+        """The down projection into self.proj from the quantised MLP product."""
+        Y.linear_q8([mat], self.act_m, self.alpha_m, [self.proj], stream=s)
+
+    def _select(self, s):
         Y.head_select(self.logits, token=self.token, stream=s)
 
     def _attention(self, L, s):
@@ -263,9 +282,10 @@ class Stack:
     def launches_per_token(self, fused=True):
         """This library's kernel launches in decode(), one per call except the GDN step
         (step + history). Fused chain: embedding, the first layer's normalisation, head
-        operator, head select; per layer the mixer's input operator, the mixer's output
-        operator (with the residual and the next quantiser), gate/up, the quantised product
-        and down (with the residual); GDN mixer in between: gates, step (2); attention:
+        operator (with the last residual add), head select; per layer the mixer's input
+        operator (with the residual add before it, after the first layer), the mixer's output
+        operator, gate/up (with the residual add), the quantised product and down; GDN mixer
+        in between: gates, step (2); attention:
         preparation, KV encode, attention, widening. Separate calls: embedding, final
         norm, head operator, head select; per layer the input norm and the MLP (post norm,
         gate/up operator, gated product, down operator); GDN mixer: operator, gates, step

@@ -16,9 +16,9 @@ split follows the format's 512-blocks:
   many heads a launch holds.
 * The MLP splits gate/up by 512-row blocks and down by the same 512-column groups.
 * o_proj, out_proj and down are row-parallel: one launch per rank with the exchange over
-  NVLink inside the kernel and the residual epilogue on every rank
-  (yskn_b200_linear_rowpar_residual), so the residual stream and the next operator's
-  int8 input are the same bits on every rank.
+  NVLink inside the kernel (yskn_b200_linear_rowpar, _rowpar_q8 for down's quantised
+  input), the whole projection on every rank; the next operator adds it to the residual
+  stream in its own launch on every rank, so the stream is the same bits everywhere.
 * The head splits over vocabulary rows; each rank's first eight are gathered (NCCL) and
   merged (yskn_b200_head_merge) into the same greedy token on every rank.
 
@@ -179,41 +179,29 @@ class TPStack(S.Stack):
             self.exchange = None
 
     def decode(self, stream=None, fused=True):
-        """One token on this rank: reads self.token, writes the next greedy token (the same
-        on every rank). Every rank issues the same launches and collectives in order."""
-        P, s, ex = self.plan, stream, self.exchange
-        self.embedding.lookup(self.token, self.h, stream=s)
-        Y.residual_prepare(self.h, None, self.L[0]["in_norm"], S.EPS, self.x, self.inv, gate=self.xg, stream=s)
-        for i, L in enumerate(self.L):
-            if i + 1 < len(self.L):
-                nL = self.L[i + 1]
-                next_norm, next_first = nL["in_norm"], nL["qkv"] if nL["kind"] == "gdn" else nL["q"]
-            else:
-                next_norm, next_first = self.final_norm, self.head
-            if L["kind"] == "gdn":
-                mats, outs = [L["qkv"], L["z"]], [self.qkv_o, self.z_o]
-            else:
-                mats, outs = [L["q"], L["k"], L["v"]], [self.q_o, self.k_o, self.v_o]
-            if i == 0:
-                Y.linear(mats, self.x, self.work, outs, inv_rms=self.inv, stream=s)
-            else:
-                Y.linear_q8(mats, self.act, self.alpha, outs, bss=self.bss, eps=S.EPS, inv_rms_out=self.inv, stream=s)
-            if L["kind"] == "gdn":
-                Y.gdn_gates_heads(self.xg, self.inv, L["wb"], L["wa"], self.gates, stream=s)
-                Y.gdn_step_heads(self.qkv_o, self.z_o, self.gates, L["conv"], L["a_log"], L["dt_bias"], L["norm_w"],
-                                 S.EPS, L["state"], L["history"], self.g_out, P.v0, P.qk0, P.qk_ch, stream=s)
-                mixer_out, mixer_in = L["out"], self.g_out
-            else:
-                self._attention(L, s)
-                mixer_out, mixer_in = L["o"], self.a_in
-            Y.linear_rowpar_residual(ex, mixer_out, self.h, L["post_norm"], L["gate"].signs_in_ptr, self.act,
-                                     self.alpha, self.bss, x=mixer_in, stream=s)
-            Y.linear_q8([L["gate"], L["up"]], self.act, self.alpha, [self.g_o, self.u_o], bss=self.bss, eps=S.EPS,
-                        stream=s)
-            Y.gated_product_q8(self.g_o, self.u_o, L["down"].signs_in_ptr, self.act_m, self.alpha_m, stream=s)
-            Y.linear_rowpar_residual(ex, L["down"], self.h, next_norm, next_first.signs_in_ptr, self.act, self.alpha,
-                                     self.bss, act=self.act_m, alpha=self.alpha_m, gate_out=self.xg, stream=s)
-        Y.linear_q8([self.head], self.act, self.alpha, [self.logits], bss=self.bss, eps=S.EPS, stream=s)
+        """One token on this rank: S.Stack.decode's fused chain with this rank's part of each
+        step; every rank issues the same launches and collectives in order and ends with the
+        same greedy token."""
+        if not fused:
+            raise ValueError("the tensor-parallel pass runs the fused chain only")
+        return super().decode(stream)
+
+    # The one-GPU pass (S.Stack.decode) with this rank's parts of each step.
+    def _gdn(self, L, s):
+        P = self.plan
+        Y.gdn_gates_heads(self.xg, self.inv, L["wb"], L["wa"], self.gates, stream=s)
+        Y.gdn_step_heads(self.qkv_o, self.z_o, self.gates, L["conv"], L["a_log"], L["dt_bias"], L["norm_w"], S.EPS,
+                         L["state"], L["history"], self.g_out, P.v0, P.qk0, P.qk_ch, stream=s)
+
+    def _project(self, mat, x, s):
+        """Row-parallel: this rank's input columns; the whole projection on every rank."""
+        Y.linear_rowpar(self.exchange, mat, x, self.proj, stream=s)
+
+    def _project_q8(self, mat, s):
+        Y.linear_rowpar_q8(self.exchange, mat, self.act_m, self.alpha_m, self.proj, stream=s)
+
+    def _select(self, s):
+        """This rank's first eight of its vocabulary part, gathered from every rank and merged."""
         Y.head_select(self.logits, top_logits=self.cand[0].view(torch.float32), top_ids=self.cand[1], stream=s)
         with torch.cuda.stream(s) if s is not None else contextlib.nullcontext():
             dist.all_gather_into_tensor(self.gathered, self.cand, group=self.group)
