@@ -350,12 +350,7 @@ static yskn_b200_matrix* create_matrix(const uint32_t* d_codes, int layout, int 
   // The GEMV's shared-memory image of the table (MatrixDev::lutx).
   std::vector<uint16_t> lutx(4096 * 16);
   auto pair = [&](uint32_t s) { return (uint16_t)((uint8_t)lut8[2 * s] | ((uint8_t)lut8[2 * s + 1] << 8)); };
-  if (bits == 8) {
-    for (uint32_t e = 0; e < 4096 * 16; ++e) lutx[e] = pair(lutx8_state(2 * e));
-  } else {
-    for (int s = 0; s < 4096; ++s)
-      for (int c = 0; c < 16; ++c) lutx[16 * s + c] = pair(s);
-  }
+  for (uint32_t e = 0; e < 4096 * 16; ++e) lutx[e] = pair(bits == 8 ? lutx8_state(2 * e) : lutx_split_state(2 * e));
   cudaError_t e = cudaMalloc(&m->codes, (size_t)packed);
   if (e == cudaSuccess) e = cudaMalloc(&m->small, small_bytes);
   if (e != cudaSuccess) {

@@ -85,12 +85,19 @@ __host__ __device__ inline uint32_t lutx8_state(uint32_t a) {
   return (b_prev >> 4) | (b_cur << 4);
 }
 
+// The state whose entry the table image of the other widths holds at byte address a
+// (even, < 128 KiB): address bits 1, 2 are state bits 0, 1, bits 7..16 state bits 2..11;
+// bits 3..6 pick the copy.
+__host__ __device__ inline uint32_t lutx_split_state(uint32_t a) {
+  return ((a >> 1) & 3u) | (((a >> 7) & 0x3ffu) << 2);
+}
+
 struct MatrixDev {
   const uint32_t* codes;  // B200 streaming layout (see pack.cu)
   const uint16_t* lut8;   // 4096 entries: int8 pair (component 0 low byte, component 1 high byte)
   // The GEMV's shared-memory image of lut8 (128 KiB, 16 copies). bits = 8: the entry of
   // lutx8_state(a) at every even byte address a, copy (a >> 3) & 15 in banks 2c, 2c+1;
-  // other bits: 4096 slots of 32 bytes, entry s 16 times in slot s.
+  // other bits: the same with lutx_split_state(a).
   const uint8_t* lutx;
   const float* tau;       // effective row scale, f32[physical_rows]
   const int8_t* s_in;     // i8[cols]

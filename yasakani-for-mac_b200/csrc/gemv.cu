@@ -158,7 +158,7 @@ __device__ __forceinline__ void l2_prefetch_unit(const uint32_t* unit, int lane)
 
 template <int BITS>
 __device__ __forceinline__ uint32_t lut_copy_off(int lane) {
-  return BITS == 8 ? (uint32_t)(lane >> 1) << 3 : (uint32_t)(lane >> 1) << 1;
+  return (uint32_t)(lane >> 1) << 3;
 }
 
 // hi32(a * b) + c and lo32(a * b) + c in one instruction each: with b a power of two they
@@ -190,9 +190,11 @@ __device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
 //   address bits 1,2 and 7..16 around the copy (lane/2) in bits 3..6, so copy c sits
 //   in banks 2c and 2c+1 and only the two lanes of a copy can conflict: ~2 shared-
 //   memory wavefronts per 32 random lookups.
-// * other bits: 4096 slots of 32 bytes (slot s holds 16 copies of entry s), the state
-//   in address bits 5..16, the copy in bits 1..4. Four lanes share the 4 banks
-//   {c, c+8, c+16, c+24} picked by the state's two low bits: ~3 wavefronts.
+// * other bits: the same image layout (copy c in banks 2c, 2c+1; state bits 0,1 at
+//   address bits 1,2 and bits 2..11 at 7..16, lutx_split_state in common.cuh), so the
+//   same ~2 wavefronts per lookup; the stored stream has no spare bits between the two
+//   parts of a state, so the address takes the state's window shifted to bit 1, two
+//   masks and a multiply-add.
 // base is the image's shared address plus the lane's copy offset (the masked state
 // bits never overlap the copy field, so adding the copy equals or-ing it). Where the
 // state's bits come from one word, the mask and one multiply-add form the address
@@ -201,8 +203,16 @@ __device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
 // amounts are compile-time constants after unrolling.
 template <int BITS>
 __device__ __forceinline__ uint32_t lut_abs(uint32_t carry, const uint32_t (&w)[BITS], int i, uint32_t base) {
-  constexpr uint32_t MASK = BITS == 8 ? 0x1ff86u : 0x1ffe0u;
-  constexpr int LO = BITS == 8 ? 1 : 5, HI = 17;
+  if constexpr (BITS != 8) {
+    const int p = 32 + BITS * (i + 1) - 12 - 1;  // the bit of V below the state's first
+    const int wi = p >> 5, sh = p & 31;
+    const uint32_t lo = wi == 0 ? carry : w[wi - 1];
+    const uint32_t hi = wi >= BITS ? 0u : w[wi];
+    const uint32_t x = sh == 0 ? lo : sh + 13 <= 32 ? lo >> sh : __funnelshift_r(lo, hi, sh);  // state at 1..12
+    return mad_lo(x & 0x1ff8u, 16u, (x & 6u) | base);
+  }
+  constexpr uint32_t MASK = 0x1ff86u;
+  constexpr int LO = 1, HI = 17;
   const int p = 32 + BITS * (i + 1) - 12 - 5;
   const int wi = p >> 5, sh = p & 31;
   const uint32_t lo = wi == 0 ? carry : w[wi - 1];
@@ -416,7 +426,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
   if (u < u_end) load_unit<BITS>(ua, ptr, lane);
   if (u + 1 < u_end) l2_prefetch_unit<BITS>(ptr + 2 * TILE_WORDS, lane);
 
-  // 16 copies of the int8-pair table: slot s (32 bytes) holds entry s 16 times. The
+  // 16 copies of the int8-pair table, copy c in banks 2c, 2c+1 (lut_abs). The
   // matrix keeps this image prebuilt (MatrixDev::lutx); one thread starts bulk
   // asynchronous copies of it at once, and they land while the warps quantise the
   // input (fused) or stage the activations. (Expanding the stored 8 KiB table in
