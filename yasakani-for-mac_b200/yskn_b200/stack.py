@@ -127,10 +127,8 @@ class Stack:
         self.kv_rows = f32(2 * N_KVH, HEAD)
         self.a_in = f32(1, N_QH * HEAD)
         self.g_o, self.u_o, self.m_o = f32(1, FFN), f32(1, FFN), f32(1, FFN)
-        # the chain between projections (yskn_b200_linear_residual / linear_q8 / gated_product_q8):
-        # the next operator's int8 input, group scales and block sums of squares
+        # the MLP product quantised for down (yskn_b200_gated_product_q8): int8 rows, group scales
         i8 = lambda *s: torch.zeros(s, dtype=torch.int8, device=device)  # noqa: E731
-        self.act, self.alpha, self.bss = i8(1, HIDDEN), f32(1, HIDDEN // 512), f32(1, HIDDEN // 512)
         self.act_m, self.alpha_m = i8(1, FFN), f32(1, FFN // 512)
         self.logits = f32(1, vocab)
         first = {k: next(L for L in self.L if L["kind"] == k) for k in set(self.kinds)}
