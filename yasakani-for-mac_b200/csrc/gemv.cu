@@ -863,18 +863,33 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
     const uint64_t* recv = tp_at<uint64_t>(p.tp, me, p.tp.off_recv);
     for (int tok = 0; tok < p.mv; ++tok) {
       int64_t* mine = S.out + (size_t)tok * S.out_ld + blk * 512;
+      longlong2 s[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int r = 64 * k + 2 * lane;
-        longlong2 s = __ldcg(reinterpret_cast<const longlong2*>(mine + r));
-        for (int src = 0; src < W; ++src) {
-          if (src == me) continue;
-          const uint64_t* w = recv + (((size_t)par * W + src) * TP_MAX_M + tok) * slot + (size_t)blk * 1024 + 2 * r;
-          s.x += recv_sum(w, epoch, deadline, &s_abort, ok);
-          s.y += recv_sum(w + 2, epoch, deadline, &s_abort, ok);
+      for (int k = 0; k < 8; ++k) s[k] = __ldcg(reinterpret_cast<const longlong2*>(mine + 64 * k + 2 * lane));
+      for (int src = 0; src < W; ++src) {
+        if (src == me) continue;
+        // All 16 tagged word pairs of this lane requested at once (one round trip when the
+        // peer's block has arrived, instead of one per pair); a pair whose tag is not yet
+        // this epoch's is polled on its own, against the same deadline.
+        const uint64_t* w = recv + (((size_t)par * W + src) * TP_MAX_M + tok) * slot + (size_t)blk * 1024 + 4 * lane;
+        ulonglong2 v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = ld_ll2(w + 128 * (j >> 1) + 2 * (j & 1));
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          long long add;
+          if ((uint32_t)(v[j].x >> 32) == epoch && (uint32_t)(v[j].y >> 32) == epoch)
+            add = (long long)(((uint64_t)(uint32_t)v[j].y << 32) | (uint32_t)v[j].x);
+          else
+            add = recv_sum(w + 128 * (j >> 1) + 2 * (j & 1), epoch, deadline, &s_abort, ok);
+          if (j & 1)
+            s[j >> 1].y += add;
+          else
+            s[j >> 1].x += add;
         }
-        __stcg(reinterpret_cast<longlong2*>(mine + r), s);
       }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) __stcg(reinterpret_cast<longlong2*>(mine + 64 * k + 2 * lane), s[k]);
     }
     if (__any_sync(0xffffffffu, !ok)) {
       ok = false;
