@@ -486,7 +486,20 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
   {
     if (FUSED && p.q_act) {
       // Quantised input: stage the int8 rows and the group scales (8 independent 16-byte
-      // loads per thread before their stores); each row's 1/rms from its block sums.
+      // loads per thread before their stores); each row's 1/rms from its block sums. The
+      // first two scales (and block sums) of each thread are requested before the rows, so
+      // all of the staging is one round of loads.
+      const int n_sc = p.mv * G;
+      const int i0 = threadIdx.x, i1 = threadIdx.x + GEMV_WARPS * 32;
+      float al0 = 0.0f, al1 = 0.0f, bs0 = 0.0f, bs1 = 0.0f;
+      if (i0 < n_sc) {
+        al0 = __ldcg(p.q_alpha + i0);
+        if (p.q_bss) bs0 = __ldcg(p.q_bss + i0);
+      }
+      if (i1 < n_sc) {
+        al1 = __ldcg(p.q_alpha + i1);
+        if (p.q_bss) bs1 = __ldcg(p.q_bss + i1);
+      }
       const int vec = Kc / 16, total = p.mv * vec;
       for (int base = 0; base < total; base += 8 * GEMV_WARPS * 32) {
         uint4 v[8];
@@ -501,9 +514,17 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) trellis_sums_kernel(const 
           if (idx < total) reinterpret_cast<uint4*>(s_act + (idx / vec) * act_ld)[idx % vec] = v[k];
         }
       }
-      for (int idx = threadIdx.x; idx < p.mv * G; idx += blockDim.x) {
+      if (i0 < n_sc) {
+        s_alpha[i0] = al0;
+        s_bss[i0] = bs0;  // summed per row after the barrier
+      }
+      if (i1 < n_sc) {
+        s_alpha[i1] = al1;
+        s_bss[i1] = bs1;
+      }
+      for (int idx = threadIdx.x + 2 * GEMV_WARPS * 32; idx < n_sc; idx += blockDim.x) {
         s_alpha[idx] = __ldcg(p.q_alpha + idx);
-        if (p.q_bss) s_bss[idx] = __ldcg(p.q_bss + idx);  // summed per row after the barrier
+        if (p.q_bss) s_bss[idx] = __ldcg(p.q_bss + idx);
       }
     } else if (FUSED && p.rin.y) {
       residual_prologue(p.rin, p.s_in, Kc, items, s_act, act_ld, s_alpha, s_bss, p.err, warp, lane);
