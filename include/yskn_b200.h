@@ -293,6 +293,23 @@ YSKN_B200_API int yskn_b200_gdn_step_heads(const float* d_qkv, const float* d_z,
                                            const uint16_t* d_dt_bias, const uint16_t* d_norm_w, float eps, int M,
                                            int n_commit, int n_v_heads, int v_head0, int qk_head0, int qk_channels,
                                            float* d_state, uint16_t* d_history, float* d_out, void* stream);
+/* The whole mixer in one launch (the reference's dense-gate and recurrence kernels,
+ * src/q35_kernels.cu:746-820 and :864-980): yskn_b200_gdn_gates (here from d_hidden bf16
+ * [M][hidden], d_inv_rms, d_wb, d_wa bf16 [heads][hidden], hidden a multiple of 1024) and
+ * yskn_b200_gdn_step with the history update, bit-identical to the two calls; M = 1..64.
+ * _heads: a run of value heads as yskn_b200_gdn_step_heads, d_wb / d_wa the run's rows.
+ * One mixer launch in flight per device (its key-head arrival counters are the device's). */
+YSKN_B200_API int yskn_b200_gdn_mixer(const uint16_t* d_hidden, const float* d_inv_rms, const uint16_t* d_wb,
+                                      const uint16_t* d_wa, int hidden, const float* d_qkv, const float* d_z,
+                                      const uint16_t* d_conv_w, const uint16_t* d_a_log, const uint16_t* d_dt_bias,
+                                      const uint16_t* d_norm_w, float eps, int M, int n_commit, float* d_state,
+                                      uint16_t* d_history, float* d_out, void* stream);
+YSKN_B200_API int yskn_b200_gdn_mixer_heads(const uint16_t* d_hidden, const float* d_inv_rms, const uint16_t* d_wb,
+                                            const uint16_t* d_wa, int hidden, const float* d_qkv, const float* d_z,
+                                            const uint16_t* d_conv_w, const uint16_t* d_a_log,
+                                            const uint16_t* d_dt_bias, const uint16_t* d_norm_w, float eps, int M,
+                                            int n_commit, int n_v_heads, int v_head0, int qk_head0, int qk_channels,
+                                            float* d_state, uint16_t* d_history, float* d_out, void* stream);
 
 /* bf16 -> f32 copy of n values (exact): an operator's f32 input from a bf16 producer, such as
  * the attention output before o_proj (the reference quantises that bf16 vector directly,

@@ -227,3 +227,4 @@ def test_residual_prologue_equals_residual_prepare_then_linear(cuda, M):
         assert torch.equal(inv2.view(torch.int32), inv.view(torch.int32)), call
         assert torch.equal(g2.view(torch.int32), g.view(torch.int32)), call
         assert torch.equal(u2.view(torch.int32), u.view(torch.int32)), call
+

@@ -14,7 +14,10 @@ import oracle as O
 pytestmark = pytest.mark.gpu
 
 
-def test_gdn_gates_and_steps(cuda):
+@pytest.mark.parametrize("mixer", [False, True])
+def test_gdn_gates_and_steps(cuda, mixer):
+    """mixer: yskn_b200_gdn_mixer (gates, step and history in one launch) in place of the
+    gates and step calls, against the same oracle."""
     import torch
     import yskn_b200
     rng = np.random.default_rng(17)
@@ -32,18 +35,24 @@ def test_gdn_gates_and_steps(cuda):
     for call, (M, n_commit) in enumerate([(1, 1), (4, 0), (4, 2)]):
         x = O.bf16_bits(rng.standard_normal((M, hidden)).astype(np.float32))
         inv = (0.5 + rng.random(M)).astype(np.float32)
-        gates = torch.empty((M, 96), dtype=torch.float32, device="cuda")
-        yskn_b200.gdn_gates(dev(x.view(np.int16)), dev(inv), dev(wb.view(np.int16)), dev(wa.view(np.int16)), gates)
-        g = gates.cpu().numpy()
-        for m in range(M):
-            assert np.array_equal(g[m].view(np.uint32), O.gdn_gates(x[m], inv[m], wb, wa).view(np.uint32)), (call, m)
         qkv = rng.standard_normal((M, 10240)).astype(np.float32)
         z = rng.standard_normal((M, 6144)).astype(np.float32)
         out = torch.empty((M, 6144), dtype=torch.float32, device="cuda")
         before = d_state.cpu().numpy()
-        yskn_b200.gdn_step(dev(qkv), dev(z), gates, dev(conv.view(np.int16)), dev(a_log.view(np.int16)),
-                           dev(dt_bias.view(np.int16)), dev(norm_w.view(np.int16)), eps, d_state, d_hist, out,
-                           n_commit=n_commit)
+        step_args = (dev(conv.view(np.int16)), dev(a_log.view(np.int16)), dev(dt_bias.view(np.int16)),
+                     dev(norm_w.view(np.int16)), eps, d_state, d_hist, out)
+        want_g = np.stack([O.gdn_gates(x[m], inv[m], wb, wa) for m in range(M)])
+        if mixer:
+            yskn_b200.gdn_mixer(dev(x.view(np.int16)), dev(inv), dev(wb.view(np.int16)), dev(wa.view(np.int16)),
+                                dev(qkv), dev(z), *step_args, n_commit=n_commit)
+            g = want_g
+        else:
+            gates = torch.empty((M, 96), dtype=torch.float32, device="cuda")
+            yskn_b200.gdn_gates(dev(x.view(np.int16)), dev(inv), dev(wb.view(np.int16)), dev(wa.view(np.int16)),
+                                gates)
+            g = gates.cpu().numpy()
+            assert np.array_equal(g.view(np.uint32), want_g.view(np.uint32)), call
+            yskn_b200.gdn_step(dev(qkv), dev(z), gates, *step_args, n_commit=n_commit)
         assert yskn_b200.status() == 0
         want_out, state, history = O.gdn_step(qkv, z, g, conv, a_log, dt_bias, norm_w, eps, state, history, n_commit)
         got = out.cpu().numpy()

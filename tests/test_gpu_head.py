@@ -89,3 +89,27 @@ def test_both_selection_levels_and_repeated_calls(cuda, M, n):
     for m in range(M):
         t, v, i = O.head_select(logits[m])
         assert tok[m] == t and np.array_equal(ti[m], i) and np.array_equal(tv[m], v), m
+
+
+@pytest.mark.parametrize("M,n", [(1, 151936), (5, 3000), (64, 151936), (2, 300)])
+def test_greedy_token_alone_equals_the_oracle(cuda, M, n):
+    """With no top-8 output requested, the selection takes one candidate per thread and one
+    block-wide round per level; the token equals the oracle's over ties inside and across
+    chunks, NaN and -inf logits, a row of only NaN, and two calls in a row."""
+    import torch
+    import yskn_b200
+    rng = np.random.default_rng(M * 13 + n)
+    logits = rng.standard_normal((M, n)).astype(np.float32)
+    logits[:, rng.integers(0, n, 5)] = 3.25  # ties
+    logits[0, : n // 3] = np.nan
+    logits[-1, n // 2:] = -np.inf
+    if M > 2:
+        logits[1, :] = np.nan
+    d = torch.from_numpy(logits).cuda()
+    for _ in range(2):
+        tok = torch.full((M,), -1, dtype=torch.int32, device="cuda")
+        yskn_b200.head_select(d, token=tok)
+        assert yskn_b200.status() == 0
+        got = tok.cpu().numpy()
+        for m in range(M):
+            assert got[m] == O.head_select(logits[m])[0], m

@@ -251,7 +251,7 @@ def test_two_layer_stack_matches_the_composed_oracle(cuda):
 
 
 def test_fused_chain_pass_equals_the_separate_calls(cuda):
-    """The decode pass with the chain between projections inside the operators (532 launches
+    """The decode pass with the chain between projections inside the operators (436 launches
     per token) and with the separate residual/normalisation and product calls (660): the
     same tokens, hidden rows, logits and recurrent states, bit for bit, over three tokens."""
     import torch

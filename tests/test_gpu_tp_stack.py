@@ -68,7 +68,10 @@ def test_row_ranges_shard_is_the_whole_sums_of_those_rows(cuda):
     assert yskn_b200.status() == 0
 
 
-def test_gdn_head_runs_equal_the_whole_layer(cuda):
+@pytest.mark.parametrize("mixer", [False, True])
+def test_gdn_head_runs_equal_the_whole_layer(cuda, mixer):
+    """Every rank's run of value heads (gates + step, or the one-launch mixer) gives the whole
+    layer's outputs, states and history for those heads, for 2, 4 and 8 ranks."""
     import torch
     import yskn_b200
     from yskn_b200.tp_stack import TPPlan
@@ -103,7 +106,16 @@ def test_gdn_head_runs_equal_the_whole_layer(cuda):
             nh = hv.stop - hv.start
             gates = torch.empty((M, 2 * nh), dtype=torch.float32, device="cuda")
             out = torch.empty((M, 128 * nh), dtype=torch.float32, device="cuda")
-            if whole:
+            if mixer and not whole:
+                yskn_b200.gdn_mixer_heads(i16(c["x"]), _dev(c["inv"]), i16(np.ascontiguousarray(wb[hv])),
+                                          i16(np.ascontiguousarray(wa[hv])),
+                                          _dev(np.ascontiguousarray(c["qkv"][:, chans])),
+                                          _dev(np.ascontiguousarray(c["z"][:, 128 * v0:128 * (v0 + n_v)])),
+                                          i16(np.ascontiguousarray(conv[chans])), i16(np.ascontiguousarray(a_log[hv])),
+                                          i16(np.ascontiguousarray(dt_bias[hv])), i16(norm_w), eps, d_state, d_hist,
+                                          out, v0, qk0, qk_ch, n_commit=c["n_commit"])
+                gates = None
+            elif whole:
                 yskn_b200.gdn_gates(i16(c["x"]), _dev(c["inv"]), i16(wb), i16(wa), gates)
                 yskn_b200.gdn_step(_dev(c["qkv"]), _dev(c["z"]), gates, i16(conv), i16(a_log), i16(dt_bias),
                                    i16(norm_w), eps, d_state, d_hist, out, n_commit=c["n_commit"])
@@ -115,7 +127,7 @@ def test_gdn_head_runs_equal_the_whole_layer(cuda):
                                          i16(np.ascontiguousarray(conv[chans])), i16(np.ascontiguousarray(a_log[hv])),
                                          i16(np.ascontiguousarray(dt_bias[hv])), i16(norm_w), eps, d_state, d_hist,
                                          out, v0, qk0, qk_ch, n_commit=c["n_commit"])
-            res.append((gates.cpu().numpy(), out.cpu().numpy()))
+            res.append((None if gates is None else gates.cpu().numpy(), out.cpu().numpy()))
         return res, d_state.cpu().numpy(), d_hist.cpu().numpy().view(np.uint16)
 
     ref, ref_state, ref_hist = run(None, None, None, None, np.arange(10240))
@@ -127,7 +139,7 @@ def test_gdn_head_runs_equal_the_whole_layer(cuda):
             hv = slice(p.v0, p.v0 + p.n_v)
             for (g, o), (rg, ro) in zip(got, ref):
                 rgates = np.concatenate([rg[:, hv], rg[:, 48 + p.v0:48 + p.v0 + p.n_v]], axis=1)
-                assert np.array_equal(g.view(np.uint32), rgates.view(np.uint32)), (world, r)
+                assert g is None or np.array_equal(g.view(np.uint32), rgates.view(np.uint32)), (world, r)
                 assert np.array_equal(o.view(np.uint32), ro[:, 128 * p.v0:128 * (p.v0 + p.n_v)].view(np.uint32)), \
                     (world, r)
             assert np.array_equal(st.view(np.uint32), ref_state[hv].view(np.uint32)), (world, r)

@@ -1,6 +1,6 @@
 """Host-side arithmetic of the 27B-shape decode pass (yskn_b200/stack.py): the layer pattern,
 the code bytes of the stack against the reference's config-5 figure, the algorithmic bytes of
-one token and the launch count (532 per token with the chain between projections inside the
+one token and the launch count (436 per token with the chain between projections inside the
 operators, 660 with separate calls)."""
 import types
 
@@ -26,5 +26,6 @@ def test_launches_per_token():
     fake = types.SimpleNamespace(kinds=S.layer_kinds(64), layers=64)
     assert S.Stack.launches_per_token(fake, fused=False) == 660
     # the chain inside the operators: no residual_prepare after the first layer's, no
-    # separate quantiser for down (the MLP product is quantised in place)
-    assert S.Stack.launches_per_token(fake) == 532
+    # separate quantiser for down (the MLP product is quantised in place), the GDN mixer
+    # (gates, step, history) in one launch
+    assert S.Stack.launches_per_token(fake) == 436

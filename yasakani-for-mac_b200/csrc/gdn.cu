@@ -27,6 +27,12 @@
 //    (q/k of the key head are recomputed by its three value heads: 128 channels each).
 //  * history: the three newest projected rows are written after the step, in place (another
 //    launch, since three CTAs read each key head's history).
+//  * the whole mixer in one launch (yskn_b200_gdn_mixer[_heads]): the step CTA of value head h
+//    also forms its two dense gates (thread groups 0 and 1 in the gates kernel's order, every
+//    row's before the first) and, once every row is done, writes its value channels' history;
+//    the query/key history of a key head is written by the last of the key head's value-head
+//    CTAs to finish (an arrival counter per key head), after every reader has used its taps;
+//    CTA 0 writes that of the run's key heads that none of its value heads reads.
 //  * tensor parallelism: a rank runs a run of value heads with the key heads they read
 //    (the *_heads entry points); every head's arithmetic is the whole layer's, so the runs
 //    of all ranks together give the whole layer's bits.
@@ -41,6 +47,11 @@ constexpr int GDN_DK = 128;   // channels per head
 constexpr int GDN_QK_HEADS = 16;
 constexpr int GDN_V_HEADS = 48;
 constexpr int GDN_GATE_ROWS = 8;  // rows per gates CTA
+constexpr int GDN_MIXER_MAX_M = 64;  // rows per call of the one-launch mixer (gates in shared memory)
+
+// Arrivals of the one-launch mixer's value-head CTAs per key head (zero between launches;
+// the last arriver resets its counter): one such launch in flight per device.
+__device__ unsigned g_gdn_arrivals[GDN_QK_HEADS];
 
 __device__ __forceinline__ float bf(float x) {
   return __uint_as_float((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(x)) << 16);
@@ -111,9 +122,15 @@ struct GdnParams {
   float eps;
   int M, n_commit;
   float* state;              // [n_v][128][128]
-  const uint16_t* history;   // bf16 [3][W], oldest first
+  uint16_t* history;         // bf16 [3][W], oldest first (written by the one-launch mixer)
   float* out;                // [M][128 n_v]: the gated output (bf16 values), out_proj's x
   int n_v, v0, qk0, qk_ch, W;
+  // One-launch mixer only: the dense gates' input rows and weights (rows of the run's heads).
+  const uint16_t* x;         // bf16 [M][hidden]
+  const float* inv_rms;      // [M]
+  const uint16_t* wb;        // bf16 [n_v][hidden]
+  const uint16_t* wa;
+  int hidden;
 };
 
 constexpr int GDN_STEP_THREADS = 4 * GDN_DK;  // four threads per state column, one per 32-row group
@@ -126,7 +143,9 @@ struct GdnRowIn {
   float z, gb, ga;
 };
 
-__device__ __forceinline__ void gdn_load_row(const GdnParams& p, int row, int c, int vh, int j, GdnRowIn& in) {
+// The gates come from gsrc: [row][gstride], b at gb_off and a at gb_off + ga_step.
+__device__ __forceinline__ void gdn_load_row(const GdnParams& p, int row, int c, int vh, int j, const float* gsrc,
+                                             int gstride, int gb_off, int ga_step, GdnRowIn& in) {
   if (c >= 0) {
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
@@ -135,8 +154,20 @@ __device__ __forceinline__ void gdn_load_row(const GdnParams& p, int row, int c,
     }
   }
   if (c >= 0 && c < p.qk_ch) in.z = p.z[(size_t)row * p.n_v * GDN_DK + GDN_DK * vh + j];
-  in.gb = p.gates[(size_t)row * 2 * p.n_v + vh];
-  in.ga = p.gates[(size_t)row * 2 * p.n_v + p.n_v + vh];
+  in.gb = gsrc[(size_t)row * gstride + gb_off];
+  in.ga = gsrc[(size_t)row * gstride + gb_off + ga_step];
+}
+
+// The history of channel c after a call that commits n_commit rows: row a takes the newest
+// committed row n_commit - 3 + a, or old row n_commit + a when fewer than 3 - a new rows
+// exist (a later row than a, read before anything overwrites it).
+__device__ __forceinline__ void gdn_history_channel(const float* qkv, int n_commit, int W, int c, uint16_t* history) {
+#pragma unroll
+  for (int a = 0; a < 3; ++a) {
+    const int r = n_commit - 3 + a;
+    history[(size_t)a * W + c] = r < 0 ? history[(size_t)(3 + r) * W + c]
+                                       : __bfloat16_as_ushort(__float2bfloat16_rn(qkv[(size_t)r * W + c]));
+  }
 }
 
 // bf(silu(bf(conv))) of one channel from its taps and weights.
@@ -148,7 +179,11 @@ __device__ __forceinline__ float gdn_conv(const float (&x)[4], const float (&w)[
   return bf(pm_silu(bf(a)));
 }
 
+template <bool MIXER>
 __global__ void __launch_bounds__(GDN_STEP_THREADS) gdn_step_kernel(const __grid_constant__ GdnParams p) {
+  __shared__ float s_gate[MIXER ? GDN_MIXER_MAX_M : 1][2];  // mixer: every row's b, a
+  __shared__ float s_g4[2][4];
+  __shared__ bool s_last;
   __shared__ __align__(16) float s_q[GDN_DK];
   __shared__ __align__(16) float s_k[GDN_DK];
   __shared__ float s_v[GDN_DK];
@@ -173,11 +208,37 @@ __global__ void __launch_bounds__(GDN_STEP_THREADS) gdn_step_kernel(const __grid
     cw[2] = __uint_as_float(w4.y << 16), cw[3] = __uint_as_float(w4.y & 0xffff0000u);
   }
   const float a_log = bf16f(p.a_log[vh]), dt_bias = bf16f(p.dt_bias[vh]);
+  if constexpr (MIXER) {
+    // 03_GATED_DELTANET.md:57-76: this head's dense gates of every row, in gdn_gates_kernel's
+    // order: group 0 forms b, group 1 a; thread j adds its 40 products (5120 columns), each
+    // warp is one xor_sum32 group, the four groups meet in sum4 order.
+    const uint16_t* w = (grp == 0 ? p.wb : p.wa) + (size_t)vh * p.hidden;
+    const int chunks = p.hidden / 1024;
+    for (int row = 0; row < p.M; ++row) {
+      if (grp < 2) {
+        const uint16_t* xr = p.x + (size_t)row * p.hidden;
+        float partial = 0.0f;
+#pragma unroll 5
+        for (int chunk = 0; chunk < chunks; ++chunk) {
+          const int i = 1024 * chunk + 8 * j;
+          partial =
+              dot8(partial, __ldg(reinterpret_cast<const uint4*>(w + i)), __ldg(reinterpret_cast<const uint4*>(xr + i)));
+        }
+        const float g = xor_sum32(partial);
+        if (lane == 0) s_g4[grp][warp & 3] = g;
+      }
+      __syncthreads();
+      if (j == 0 && grp < 2) s_gate[row][grp] = bf(__fmul_rn(sum4(s_g4[grp]), p.inv_rms[row]));
+      __syncthreads();
+    }
+  }
+  const float* gsrc = MIXER ? &s_gate[0][0] : p.gates;
+  const int gstride = MIXER ? 2 : 2 * p.n_v, gb_off = MIXER ? 0 : vh, ga_step = MIXER ? 1 : p.n_v;
   GdnRowIn cur;
-  gdn_load_row(p, 0, c, vh, j, cur);
+  gdn_load_row(p, 0, c, vh, j, gsrc, gstride, gb_off, ga_step, cur);
   for (int row = 0; row < p.M; ++row) {
     GdnRowIn nxt;
-    if (row + 1 < p.M) gdn_load_row(p, row + 1, c, vh, j, nxt);
+    if (row + 1 < p.M) gdn_load_row(p, row + 1, c, vh, j, gsrc, gstride, gb_off, ga_step, nxt);
     // 03_GATED_DELTANET.md:102-116: the convolved channel; squares of query and key per warp.
     const float y = c >= 0 ? gdn_conv(cur.x, cw) : 0.0f;
     if (grp < 2) {
@@ -244,22 +305,44 @@ __global__ void __launch_bounds__(GDN_STEP_THREADS) gdn_step_kernel(const __grid
       for (int r = 0; r < 32; ++r) state[r * GDN_DK] = R[r];
     cur = nxt;
   }
+  if constexpr (MIXER) {
+    if (p.n_commit > 0) {
+      // Every tap of every row has been used. This head alone reads its value channels;
+      // the query/key channels of its key head are read by up to three heads, so the last
+      // of them to get here writes those.
+      if (grp == 2) gdn_history_channel(p.qkv, p.n_commit, p.W, c, p.history);
+      __syncthreads();
+      const int kg = p.v0 + vh;  // global value head; its key head kg / 3
+      if (t == 0) {
+        const int k3 = kg / 3 * 3;
+        const unsigned readers = (unsigned)(min(p.v0 + p.n_v, k3 + 3) - max(p.v0, k3));
+        __threadfence();
+        s_last = atomicAdd(&g_gdn_arrivals[kg / 3], 1u) == readers - 1u;
+      }
+      __syncthreads();
+      if (s_last) {
+        if (grp < 2) gdn_history_channel(p.qkv, p.n_commit, p.W, c, p.history);
+        if (t == 0) g_gdn_arrivals[kg / 3] = 0u;
+      }
+      // Key heads of the run that no value head of the run reads (a run's query/key
+      // channels come in whole 512-column blocks): nobody reads them here, CTA 0 writes them.
+      if (vh == 0 && grp < 2)
+        for (int kl = 0; kl < p.qk_ch / GDN_DK; ++kl) {
+          const int k3 = 3 * (p.qk0 + kl);
+          if (k3 + 2 < p.v0 || k3 >= p.v0 + p.n_v)
+            gdn_history_channel(p.qkv, p.n_commit, p.W, grp * p.qk_ch + GDN_DK * kl + j, p.history);
+        }
+    }
+  }
 }
 
 // The three newest committed rows (bf16, M = n_commit here) become the history, in place
-// after the step: row a takes old row M + a when fewer than 3 - a new rows exist, a later
-// row than a, so
-// each thread (one channel) reads every old value before it writes over it.
+// after the step; each thread (one channel) reads every old value before it writes over it.
 __global__ void gdn_history_kernel(const float* qkv, int M, int W, uint16_t* history) {
   pdl_begin();
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= W) return;
-#pragma unroll
-  for (int a = 0; a < 3; ++a) {
-    const int r = M - 3 + a;
-    history[(size_t)a * W + c] = r < 0 ? history[(size_t)(3 + r) * W + c]
-                                       : __bfloat16_as_ushort(__float2bfloat16_rn(qkv[(size_t)r * W + c]));
-  }
+  gdn_history_channel(qkv, M, W, c, history);
 }
 
 }  // namespace yskn
@@ -280,13 +363,26 @@ static int gdn_gates(const uint16_t* d_hidden, const float* d_inv_rms, const uin
                    "gdn_gates_kernel");
 }
 
+// The one-launch mixer's dense-gate inputs (gdn_step with them: gates and history in the launch).
+struct MixerIn {
+  const uint16_t* x;
+  const float* inv_rms;
+  const uint16_t* wb;
+  const uint16_t* wa;
+  int hidden;
+};
+
 static int gdn_step(const float* d_qkv, const float* d_z, const float* d_gates, const uint16_t* d_conv_w,
                     const uint16_t* d_a_log, const uint16_t* d_dt_bias, const uint16_t* d_norm_w, float eps, int M,
                     int n_commit, int n_v, int v0, int qk0, int qk_ch, float* d_state, uint16_t* d_history,
-                    float* d_out, void* stream) {
-  if (!d_qkv || !d_z || !d_gates || !d_conv_w || !d_a_log || !d_dt_bias || !d_norm_w || !d_state || !d_history ||
-      !d_out || M < 1 || n_commit < 0 || n_commit > M)
+                    float* d_out, void* stream, const MixerIn* mixer = nullptr) {
+  if (!d_qkv || !d_z || !(d_gates || mixer) || !d_conv_w || !d_a_log || !d_dt_bias || !d_norm_w || !d_state ||
+      !d_history || !d_out || M < 1 || n_commit < 0 || n_commit > M)
     return fail(YSKN_EINVAL, "gdn_step: null argument, M < 1 or n_commit outside 0..M");
+  if (mixer && (!mixer->x || !mixer->inv_rms || !mixer->wb || !mixer->wa || mixer->hidden <= 0 ||
+                mixer->hidden % 1024 || M > GDN_MIXER_MAX_M ||
+                (((uintptr_t)mixer->x | (uintptr_t)mixer->wb | (uintptr_t)mixer->wa) & 15)))
+    return fail(YSKN_EINVAL, "gdn_mixer: null or unaligned gate input, hidden not a multiple of 1024, or M above 64");
   if (n_v < 1 || v0 < 0 || v0 + n_v > GDN_V_HEADS || qk0 < 0 || qk_ch < GDN_DK || qk_ch % GDN_DK ||
       qk0 * GDN_DK + qk_ch > GDN_QK_HEADS * GDN_DK || v0 / 3 < qk0 || (v0 + n_v - 1) / 3 >= qk0 + qk_ch / GDN_DK)
     return fail(YSKN_EINVAL, "gdn_step: the value heads need their key heads among the given query/key channels");
@@ -295,7 +391,17 @@ static int gdn_step(const float* d_qkv, const float* d_z, const float* d_gates, 
   const int W = 2 * qk_ch + GDN_DK * n_v;
   GdnParams p{d_qkv, d_z, d_gates, d_conv_w, d_a_log, d_dt_bias, d_norm_w, eps, M, n_commit, d_state, d_history,
               d_out, n_v, v0, qk0, qk_ch, W};
-  if (cudaError_t e = launch_pdl(gdn_step_kernel, n_v, GDN_STEP_THREADS, 0, st, p)) return cuda_fail(e, "gdn_step_kernel");
+  if (mixer) {  // the gates and the history in the step's launch
+    p.gates = nullptr;
+    p.x = mixer->x;
+    p.inv_rms = mixer->inv_rms;
+    p.wb = mixer->wb;
+    p.wa = mixer->wa;
+    p.hidden = mixer->hidden;
+    return cuda_fail(launch_pdl(gdn_step_kernel<true>, n_v, GDN_STEP_THREADS, 0, st, p), "gdn_step_kernel");
+  }
+  if (cudaError_t e = launch_pdl(gdn_step_kernel<false>, n_v, GDN_STEP_THREADS, 0, st, p))
+    return cuda_fail(e, "gdn_step_kernel");
   if (n_commit == 0) return YSKN_OK;
   // After the step (the same stream): every head has read the old history.
   return cuda_fail(launch_pdl(gdn_history_kernel, (W + 255) / 256, 256, 0, st, d_qkv, n_commit, W, d_history),
@@ -320,6 +426,30 @@ extern "C" YSKN_B200_API int yskn_b200_gdn_step(const float* d_qkv, const float*
                                                int n_commit, float* d_state, uint16_t* d_history, float* d_out, void* stream) {
   return gdn_step(d_qkv, d_z, d_gates, d_conv_w, d_a_log, d_dt_bias, d_norm_w, eps, M, n_commit, GDN_V_HEADS, 0, 0,
                   GDN_QK_HEADS * GDN_DK, d_state, d_history, d_out, stream);
+}
+
+extern "C" YSKN_B200_API int yskn_b200_gdn_mixer_heads(const uint16_t* d_hidden, const float* d_inv_rms,
+                                                      const uint16_t* d_wb, const uint16_t* d_wa, int hidden,
+                                                      const float* d_qkv, const float* d_z, const uint16_t* d_conv_w,
+                                                      const uint16_t* d_a_log, const uint16_t* d_dt_bias,
+                                                      const uint16_t* d_norm_w, float eps, int M, int n_commit,
+                                                      int n_v_heads, int v_head0, int qk_head0, int qk_channels,
+                                                      float* d_state, uint16_t* d_history, float* d_out,
+                                                      void* stream) {
+  const MixerIn in{d_hidden, d_inv_rms, d_wb, d_wa, hidden};
+  return gdn_step(d_qkv, d_z, nullptr, d_conv_w, d_a_log, d_dt_bias, d_norm_w, eps, M, n_commit, n_v_heads, v_head0,
+                  qk_head0, qk_channels, d_state, d_history, d_out, stream, &in);
+}
+
+extern "C" YSKN_B200_API int yskn_b200_gdn_mixer(const uint16_t* d_hidden, const float* d_inv_rms,
+                                                const uint16_t* d_wb, const uint16_t* d_wa, int hidden,
+                                                const float* d_qkv, const float* d_z, const uint16_t* d_conv_w,
+                                                const uint16_t* d_a_log, const uint16_t* d_dt_bias,
+                                                const uint16_t* d_norm_w, float eps, int M, int n_commit,
+                                                float* d_state, uint16_t* d_history, float* d_out, void* stream) {
+  return yskn_b200_gdn_mixer_heads(d_hidden, d_inv_rms, d_wb, d_wa, hidden, d_qkv, d_z, d_conv_w, d_a_log, d_dt_bias,
+                                   d_norm_w, eps, M, n_commit, GDN_V_HEADS, 0, 0, GDN_QK_HEADS * GDN_DK, d_state,
+                                   d_history, d_out, stream);
 }
 
 extern "C" YSKN_B200_API int yskn_b200_gdn_step_heads(const float* d_qkv, const float* d_z, const float* d_gates,

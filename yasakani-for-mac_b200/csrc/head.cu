@@ -205,6 +205,58 @@ __global__ void head_merge_kernel(const float* part_v, const int32_t* part_id, i
   }
 }
 
+// Greedy token only (no top-8 requested): the same two levels with one candidate per
+// thread and one block-wide round per level instead of eight. The first of the order is
+// the best of the first candidates of any partition, so the token is the same.
+__device__ Cand g_head_best[HEAD_SPLIT_ROWS][HEAD_CHUNKS];
+__device__ unsigned g_head_best_arrivals[HEAD_SPLIT_ROWS];
+
+__global__ void __launch_bounds__(HEAD_SPLIT_THREADS) head_greedy_split_kernel(const float* logits, int n,
+                                                                                int32_t* token) {
+  __shared__ Cand s_warp[HEAD_SPLIT_THREADS / 32];
+  __shared__ bool s_last;
+  pdl_begin();
+  const int c = blockIdx.x, m = blockIdx.y;
+  const int chunk = (n + HEAD_CHUNKS - 1) / HEAD_CHUNKS;
+  const int lo = min(n, c * chunk), hi = min(n, lo + chunk);
+  const float* row = logits + (size_t)m * n;
+  Cand mine{-FLT_MAX, INT_MAX};
+  constexpr int BATCH = 8;
+  for (int i0 = lo + threadIdx.x; i0 < hi; i0 += BATCH * HEAD_SPLIT_THREADS) {
+    float xs[BATCH];
+#pragma unroll
+    for (int u = 0; u < BATCH; ++u) {
+      const int i = i0 + u * HEAD_SPLIT_THREADS;
+      xs[u] = i < hi ? __ldg(row + i) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < BATCH; ++u) {  // in increasing index order, as one element at a time
+      const int i = i0 + u * HEAD_SPLIT_THREADS;
+      if (i < hi && before(xs[u], i, mine.v, mine.id)) mine = {xs[u], i};
+    }
+  }
+  const Cand best = block_best<HEAD_SPLIT_THREADS>(mine, s_warp);
+  if (threadIdx.x == 0) {
+    g_head_best[m][c] = best;
+    __threadfence();  // this chunk's best before the arrival
+    s_last = atomicAdd(&g_head_best_arrivals[m], 1u) == HEAD_CHUNKS - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();  // the other chunks' bests after seeing the final count
+  Cand cand{-FLT_MAX, INT_MAX};
+  for (int i = threadIdx.x; i < HEAD_CHUNKS; i += HEAD_SPLIT_THREADS) {
+    const Cand* q = &g_head_best[m][i];
+    const Cand o{__ldcg(&q->v), __ldcg(&q->id)};  // through L2: other SMs wrote them in this launch
+    if (before(o.v, o.id, cand.v, cand.id)) cand = o;
+  }
+  const Cand total = block_best<HEAD_SPLIT_THREADS>(cand, s_warp);
+  if (threadIdx.x == 0) {
+    token[m] = total.id;
+    g_head_best_arrivals[m] = 0u;
+  }
+}
+
 }  // namespace yskn
 
 using namespace yskn;
@@ -232,6 +284,10 @@ extern "C" YSKN_B200_API int yskn_b200_head_select(const float* d_logits, int M,
   if (!d_logits || M < 1 || n < 1 || (!d_token && !d_top8_logits && !d_top8_ids))
     return fail(YSKN_EINVAL, "head_select: null logits, M < 1, n < 1 or no output");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (M <= HEAD_SPLIT_ROWS && n >= 4 * HEAD_CHUNKS && !d_top8_logits && !d_top8_ids)
+    return cuda_fail(launch_pdl(head_greedy_split_kernel, dim3(HEAD_CHUNKS, M), HEAD_SPLIT_THREADS, 0, st, d_logits,
+                                n, d_token),
+                     "head_greedy_split_kernel");
   if (M <= HEAD_SPLIT_ROWS && n >= 4 * HEAD_CHUNKS)
     return cuda_fail(launch_pdl(head_select_split_kernel, dim3(HEAD_CHUNKS, M), HEAD_SPLIT_THREADS, 0, st, d_logits, n,
                                 d_token, d_top8_logits, d_top8_ids),

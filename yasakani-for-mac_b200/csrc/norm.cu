@@ -100,10 +100,7 @@ __global__ void __launch_bounds__(256) gated_product_kernel(const float* gate, c
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     if (k >= k_end) break;
-    const float g = bf16_to_f32(f32_to_bf16(gate[i0 + k]));
-    const float u = bf16_to_f32(f32_to_bf16(up[i0 + k]));
-    const float silu = bf16_to_f32(f32_to_bf16(pm_silu(g)));
-    out[i0 + k] = bf16_to_f32(f32_to_bf16(__fmul_rn(silu, u)));
+    out[i0 + k] = gated_product_value(gate[i0 + k], up[i0 + k]);
   }
 }
 
@@ -126,11 +123,7 @@ __global__ void __launch_bounds__(128) gated_product_q8_kernel(const float* gate
     const float gs[4] = {gv.x, gv.y, gv.z, gv.w}, us[4] = {uv.x, uv.y, uv.z, uv.w};
     float o[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float gg = bf16_to_f32(f32_to_bf16(gs[e]));
-      const float uu = bf16_to_f32(f32_to_bf16(us[e]));
-      o[e] = bf16_to_f32(f32_to_bf16(__fmul_rn(bf16_to_f32(f32_to_bf16(pm_silu(gg))), uu)));
-    }
+    for (int e = 0; e < 4; ++e) o[e] = gated_product_value(gs[e], us[e]);
     reinterpret_cast<float4*>(s_prod)[threadIdx.x] = make_float4(o[0], o[1], o[2], o[3]);
   }
   __syncthreads();

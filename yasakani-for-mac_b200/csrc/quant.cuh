@@ -18,6 +18,7 @@
 #include <cuda_fp16.h>
 
 #include "common.cuh"
+#include "pmath.cuh"
 
 namespace yskn {
 
@@ -280,6 +281,12 @@ struct ResidualIn {
 
 __device__ __forceinline__ float bf16_round(float x) {
   return __uint_as_float((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(x)) << 16);
+}
+
+// The MLP's gated product of one element in the scalar order of the reference
+// (residual_norm_mlp.rs; docs/spec/05_RESIDUAL_NORM_MLP.md): bf16(bf16(silu(bf16(g))) * bf16(u)).
+__device__ __forceinline__ float gated_product_value(float g, float u) {
+  return bf16_round(__fmul_rn(bf16_round(pm_silu(bf16_round(g))), bf16_round(u)));
 }
 
 // The residual epilogue of one token's 512-row block from its projection values v (the

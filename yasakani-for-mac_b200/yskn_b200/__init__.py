@@ -85,6 +85,9 @@ _SIGNATURES = {
     "yskn_b200_matrix_create_rows": (_vp, [_vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _i, _vp, _i, _i]),
     "yskn_b200_gdn_gates_heads": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
     "yskn_b200_gdn_step_heads": (_i, [_vp] * 7 + [C.c_float, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
+    "yskn_b200_gdn_mixer": (_i, [_vp] * 4 + [_i] + [_vp] * 6 + [C.c_float, _i, _i, _vp, _vp, _vp, _vp]),
+    "yskn_b200_gdn_mixer_heads": (_i, [_vp] * 4 + [_i] + [_vp] * 6 + [C.c_float, _i, _i, _i, _i, _i, _i, _vp, _vp,
+                                                                        _vp, _vp]),
     "yskn_b200_linear_rowpar_residual": (_i, [_vp] * 5 + [_i] + [_vp] * 8),
     "yskn_b200_head_merge": (_i, [_vp, _vp, _i64, _vp, _i, _i, _vp, _vp, _vp, _vp]),
     "yskn_b200_linear_from_residual": (_i, [_vp, _i, _vp, _vp, _vp, _vp, C.c_float, _i, _vp, _vp, _vp, _vp]),
@@ -417,6 +420,27 @@ def gdn_step(qkv, z, gates, conv_w, a_log, dt_bias, norm_w, eps, state, history,
     check(lib().yskn_b200_gdn_step(_ptr(qkv), _ptr(z), _ptr(gates), _ptr(conv_w), _ptr(a_log), _ptr(dt_bias),
                                    _ptr(norm_w), eps, qkv.shape[0], n_commit, _ptr(state), _ptr(history), _ptr(out),
                                    _stream(stream)), "gdn_step")
+
+
+def gdn_mixer(hidden, inv_rms, wb, wa, qkv, z, conv_w, a_log, dt_bias, norm_w, eps, state, history, out,
+              n_commit=None, stream=None):
+    """yskn_b200_gdn_mixer: gdn_gates then gdn_step (with the history) in one launch."""
+    n_commit = qkv.shape[0] if n_commit is None else n_commit
+    check(lib().yskn_b200_gdn_mixer(_ptr(hidden), _ptr(inv_rms), _ptr(wb), _ptr(wa), hidden.shape[1], _ptr(qkv),
+                                    _ptr(z), _ptr(conv_w), _ptr(a_log), _ptr(dt_bias), _ptr(norm_w), eps,
+                                    qkv.shape[0], n_commit, _ptr(state), _ptr(history), _ptr(out), _stream(stream)),
+          "gdn_mixer")
+
+
+def gdn_mixer_heads(hidden, inv_rms, wb, wa, qkv, z, conv_w, a_log, dt_bias, norm_w, eps, state, history, out,
+                    v_head0, qk_head0, qk_channels, n_commit=None, stream=None):
+    """yskn_b200_gdn_mixer_heads: gdn_gates_heads then gdn_step_heads in one launch."""
+    n_commit = qkv.shape[0] if n_commit is None else n_commit
+    check(lib().yskn_b200_gdn_mixer_heads(_ptr(hidden), _ptr(inv_rms), _ptr(wb), _ptr(wa), hidden.shape[1],
+                                          _ptr(qkv), _ptr(z), _ptr(conv_w), _ptr(a_log), _ptr(dt_bias), _ptr(norm_w),
+                                          eps, qkv.shape[0], n_commit, state.shape[0], v_head0, qk_head0,
+                                          qk_channels, _ptr(state), _ptr(history), _ptr(out), _stream(stream)),
+          "gdn_mixer_heads")
 
 
 def _handles(mats):

@@ -174,8 +174,9 @@ class Stack:
         """One token: reads self.token, writes the next greedy token into it. fused: the
         chain between projections inside the operators (each operator that follows a
         residual add forms its input in its own launch: residual, normalisation and quantiser,
-        yskn_b200_linear_from_residual; the MLP product quantised for down), else the
-        separate residual_prepare / gated_product calls; both give the same bits. The
+        yskn_b200_linear_from_residual; the MLP product quantised for down; the GDN mixer in
+        one launch), else the separate residual_prepare / gated_product / gates calls; both
+        give the same bits. The
         residual stream alternates between two buffers and ends each token in self.h."""
         if not fused:
             return self._decode_separate(stream)
@@ -214,10 +215,10 @@ class Stack:
         self._select(s)
 
     def _gdn(self, L, s):
-        """The Gated DeltaNet mixer between in_proj and out_proj: gates, then the step."""
-        Y.gdn_gates(self.xg, self.inv, L["wb"], L["wa"], self.gates, stream=s)
-        Y.gdn_step(self.qkv_o, self.z_o, self.gates, L["conv"], L["a_log"], L["dt_bias"], L["norm_w"], EPS,
-                   L["state"], L["history"], self.g_out, stream=s)
+        """The Gated DeltaNet mixer between in_proj and out_proj: gates, step and history in
+        one launch."""
+        Y.gdn_mixer(self.xg, self.inv, L["wb"], L["wa"], self.qkv_o, self.z_o, L["conv"], L["a_log"], L["dt_bias"],
+                    L["norm_w"], EPS, L["state"], L["history"], self.g_out, stream=s)
 
     def _project(self, mat, x, s):
         """A mixer's output projection into self.proj (f32 input)."""
@@ -278,12 +279,12 @@ class Stack:
         Y.head_select(self.logits, token=self.token, stream=s)
 
     def launches_per_token(self, fused=True):
-        """This library's kernel launches in decode(), one per call except the GDN step
-        (step + history). Fused chain: embedding, the first layer's normalisation, head
+        """This library's kernel launches in decode(), one per call except the separate
+        GDN step (step + history). Fused chain: embedding, the first layer's normalisation, head
         operator (with the last residual add), head select; per layer the mixer's input
         operator (with the residual add before it, after the first layer), the mixer's output
         operator, gate/up (with the residual add), the quantised product and down; GDN mixer
-        in between: gates, step (2); attention:
+        in between: one launch (gates, step, history); attention:
         preparation, KV encode, attention, widening. Separate calls: embedding, final
         norm, head operator, head select; per layer the input norm and the MLP (post norm,
         gate/up operator, gated product, down operator); GDN mixer: operator, gates, step
@@ -291,5 +292,5 @@ class Stack:
         widening, o operator."""
         gdn, attn = self.kinds.count("gdn"), self.kinds.count("attn")
         if fused:
-            return 4 + self.layers * 5 + gdn * 3 + attn * 4
+            return 4 + self.layers * 5 + gdn + attn * 4
         return 4 + self.layers * 5 + gdn * 5 + attn * 6

@@ -189,9 +189,9 @@ class TPStack(S.Stack):
     # The one-GPU pass (S.Stack.decode) with this rank's parts of each step.
     def _gdn(self, L, s):
         P = self.plan
-        Y.gdn_gates_heads(self.xg, self.inv, L["wb"], L["wa"], self.gates, stream=s)
-        Y.gdn_step_heads(self.qkv_o, self.z_o, self.gates, L["conv"], L["a_log"], L["dt_bias"], L["norm_w"], S.EPS,
-                         L["state"], L["history"], self.g_out, P.v0, P.qk0, P.qk_ch, stream=s)
+        Y.gdn_mixer_heads(self.xg, self.inv, L["wb"], L["wa"], self.qkv_o, self.z_o, L["conv"], L["a_log"],
+                          L["dt_bias"], L["norm_w"], S.EPS, L["state"], L["history"], self.g_out, P.v0, P.qk0,
+                          P.qk_ch, stream=s)
 
     def _project(self, mat, x, s):
         """Row-parallel: this rank's input columns; the whole projection on every rank."""
