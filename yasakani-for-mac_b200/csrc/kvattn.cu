@@ -397,14 +397,20 @@ __global__ void __launch_bounds__(KV_THREADS, 1) kv4_attention_kernel(const __gr
     S.lut[1][i] = raw_v[i >> 5];
   }
   if (tid < 8) S.run[tid] = -1e30f;
-  // The cache rows (the newest one may come from the encoder just before), the queries
-  // and the gate may be the previous kernel's output: wait for it (a no-op without a
-  // programmatic launch).
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-
   // First requests: the chunk's first two blocks of this warp (K, V, scales) and the self row.
+  // Blocks wholly before the call's M new rows hold earlier steps' rows, which no kernel
+  // just before this one writes: they are requested before the wait.
   int nb = n_tiles > 0 ? blocks_of(0) : 0;
-  for (int j = 0; j < min(nb, 2); ++j) {
+  int j0 = 0;
+  for (; j0 < min(nb, 2) && block_pos(0, j0) + 16 <= p.length - p.M; ++j0) {
+    copy_rows(0, block_pos(0, j0), j0);
+    copy_rows(1, block_pos(0, j0), j0);
+    cp_commit();
+  }
+  // The new rows (from the encoder just before), the queries and the gate may be the
+  // previous kernel's output: wait for it (a no-op without a programmatic launch).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  for (int j = j0; j < min(nb, 2); ++j) {
     copy_rows(0, block_pos(0, j), j);
     copy_rows(1, block_pos(0, j), j);
     cp_commit();

@@ -260,6 +260,7 @@ __global__ void __launch_bounds__(ENC_THREADS) kv_encode_kernel(const __grid_con
   const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const bool chan = tid < 256;
   const int c = tid & 255;
+  pdl_begin();  // the rows may be the previous kernel's output; the attention may start its set-up
   const int grp = p.row_group[row];
   const float x = chan ? p.rows[(size_t)row * 256 + c] : 0.0f;
   bool bad = false;
@@ -391,8 +392,7 @@ int launch_kv_encode(const KvEncArgs& a, cudaStream_t st) {
     if (e != cudaSuccess) return cuda_fail(e, "kv encode attributes");
     attr[dev] = true;
   }
-  kv_encode_kernel<<<a.n_rows, ENC_THREADS, sizeof(EncSmem), st>>>(p);
-  return cuda_fail(cudaGetLastError(), "kv_encode_kernel");
+  return cuda_fail(launch_pdl(kv_encode_kernel, a.n_rows, ENC_THREADS, sizeof(EncSmem), st, p), "kv_encode_kernel");
 }
 
 }  // namespace yskn
