@@ -526,7 +526,10 @@ YSKN_B200_API int yskn_b200_linear(const yskn_b200_matrix* const* mats, int n_ma
  * last CTA of each (query row, KV head) combines the splits, counting arrivals in a
  * static device array of 4096 counters that the launch leaves at zero; so M *
  * n_kv_heads <= 4096, and calls on one device must not overlap (issue them in order
- * on one stream, as a decode loop does).
+ * on one stream, as a decode loop does). Launched as a programmatic dependent of the
+ * previous kernel on the stream: the codebooks and the cache rows before the call's M new
+ * rows are read before it waits for that kernel, so that kernel must not write them (it
+ * may write the M new rows, the queries and the gate).
  * d_attended: optional f32 [M][n_query_heads][256] (before the inverse rotation).
  * d_out: bf16 [M][n_query_heads][256]. d_work: yskn_b200_kv4_attention_work_bytes(). */
 YSKN_B200_API int64_t yskn_b200_kv4_attention_work_bytes(int M, int n_query_heads, int length, int n_splits);
