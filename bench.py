@@ -755,12 +755,13 @@ def run_kv(args, rank, world, local_rank):
             "data": "synthetic", "config": kv_config(args, copies),
             "roofline": {"bound": "hbm", "achieved": value, "peak": peak, "unit": "GB/s", "frac": value / peak,
                          "traffic": None,
-                         "kernel": "kv4_split_kernel + kv4_combine_kernel (the step's 32 launches, device time)",
+                         "kernel": "kv4_attention_kernel (splits, combine, inverse rotation and gate in one "
+                                   "launch; the step's 16 launches, device time)",
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
             "cpu_baseline": cpu,
             "e2e": {"value": step_bytes / (e2e_ms_step * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h)},
-            "gpu_launches": steps * 2 * KV_LAYERS,
+            "gpu_launches": steps * KV_LAYERS,
             "clocks": sampler.summary(), "step_bytes": step_bytes}
     return line
 
